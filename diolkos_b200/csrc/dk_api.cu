@@ -1,0 +1,134 @@
+// dk_api.cu -- kernel-level entry points of the C ABI (include/diolkos.h) and error reporting.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "dk_internal.h"
+
+namespace dk {
+
+static thread_local char g_err[512] = "";
+
+int set_error(int code, const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof g_err, fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int cuda_status(cudaError_t e, const char *what) {
+    if (e == cudaSuccess) return DK_OK;
+    return set_error(DK_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+int current_num_sms() {
+    int dev = 0, n = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n;
+}
+
+}  // namespace dk
+
+using namespace dk;
+
+extern "C" {
+
+const char *dk_last_error(void) { return g_err; }
+
+int dk_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
+    return n;
+}
+
+static int check_aligned(const void *p, size_t a, const char *name) {
+    if (reinterpret_cast<uintptr_t>(p) % a)
+        return set_error(DK_ERR_INVALID, "%s must be %zu-byte aligned", name, a);
+    return DK_OK;
+}
+
+int dk_quantize_bf16_q8_0(const uint16_t *x, size_t n, int8_t *q, float *scale, void *stream) {
+    if (n % 32) return set_error(DK_ERR_INVALID, "dk_quantize_bf16_q8_0: n=%zu is not a multiple of 32", n);
+    if (!x || !q || !scale) return set_error(DK_ERR_INVALID, "dk_quantize_bf16_q8_0: null pointer");
+    if (int r = check_aligned(x, 16, "x")) return r;
+    if (int r = check_aligned(q, 16, "q")) return r;
+    return cuda_status(launch_quant_bf16(x, n, q, scale, (cudaStream_t)stream), "dk_quantize_bf16_q8_0");
+}
+
+int dk_quantize_f32_q8_0(const float *x, size_t n, int8_t *q, float *scale, void *stream) {
+    if (n % 32) return set_error(DK_ERR_INVALID, "dk_quantize_f32_q8_0: n=%zu is not a multiple of 32", n);
+    if (!x || !q || !scale) return set_error(DK_ERR_INVALID, "dk_quantize_f32_q8_0: null pointer");
+    if (int r = check_aligned(x, 16, "x")) return r;
+    if (int r = check_aligned(q, 16, "q")) return r;
+    return cuda_status(launch_quant_f32(x, n, q, scale, (cudaStream_t)stream), "dk_quantize_f32_q8_0");
+}
+
+int dk_dequantize_q8_0(const int8_t *q, const float *scale, size_t n, float *out, void *stream) {
+    if (n % 32) return set_error(DK_ERR_INVALID, "dk_dequantize_q8_0: n=%zu is not a multiple of 32", n);
+    if (!q || !scale || !out) return set_error(DK_ERR_INVALID, "dk_dequantize_q8_0: null pointer");
+    return cuda_status(launch_dequant(q, scale, n, out, (cudaStream_t)stream), "dk_dequantize_q8_0");
+}
+
+int dk_q8_0_group_dots(const int8_t *xq, const int8_t *wq, int n, int d, int32_t *dots, void *stream) {
+    if (n <= 0 || n % 32 || d <= 0) return set_error(DK_ERR_INVALID, "dk_q8_0_group_dots: bad shape n=%d d=%d", n, d);
+    if (int r = check_aligned(xq, 16, "xq")) return r;
+    if (int r = check_aligned(wq, 16, "wq")) return r;
+    return cuda_status(launch_group_dots(xq, wq, n, d, dots, (cudaStream_t)stream), "dk_q8_0_group_dots");
+}
+
+size_t dk_q8_row_bytes(int n) { return n > 0 ? q8_row_bytes(n) : 0; }
+
+int dk_q8_pack_rows(uint8_t *dst, int n, const int8_t *src_q, const float *src_scale, int rows, int dst_row0,
+                    int dst_row_step, void *stream) {
+    if (n <= 0 || n % 32 || rows < 0 || dst_row0 < 0 || dst_row_step < 1)
+        return set_error(DK_ERR_INVALID, "dk_q8_pack_rows: bad arguments");
+    if (int r = check_aligned(dst, 16, "dst")) return r;
+    if (int r = check_aligned(src_q, 16, "src_q")) return r;
+    return cuda_status(launch_pack_rows(dst, n, src_q, src_scale, rows, dst_row0, dst_row_step, (cudaStream_t)stream),
+                       "dk_q8_pack_rows");
+}
+
+static int matmul_common(float *out, const float *x, const int8_t *xq, const float *xs, const uint8_t *w, int n,
+                         int d, void *stream) {
+    if (n <= 0 || n % 32 || d <= 0) return set_error(DK_ERR_INVALID, "matmul: bad shape n=%d d=%d", n, d);
+    if (!out || !w) return set_error(DK_ERR_INVALID, "matmul: null pointer");
+    if (int r = check_aligned(w, 16, "w_packed")) return r;
+    GemvArgs a;
+    a.w = w;
+    a.n = n;
+    a.d = d;
+    a.out = out;
+    a.err = device_error_word();
+    if (!a.err) return set_error(DK_ERR_CUDA, "matmul: could not allocate the device error word");
+    if (x) {
+        a.pro = PRO_F32;
+        a.x = x;
+    } else {
+        if (int r = check_aligned(xq, 16, "xq")) return r;
+        a.pro = PRO_Q8;
+        a.xq = xq;
+        a.xs = xs;
+    }
+    a.epi = EPI_STORE;
+    const GemvPlan p = plan_gemv(n, d, EPI_STORE, current_num_sms());
+    return cuda_status(launch_gemv(a, p, (cudaStream_t)stream, false), "matmul");
+}
+
+int dk_matmul_q8_0(float *out, const float *x, const uint8_t *w_packed, int n, int d, void *stream) {
+    if (!x) return set_error(DK_ERR_INVALID, "dk_matmul_q8_0: null x");
+    return matmul_common(out, x, nullptr, nullptr, w_packed, n, d, stream);
+}
+
+int dk_matmul_q8_0_q(float *out, const int8_t *xq, const float *xs, const uint8_t *w_packed, int n, int d,
+                     void *stream) {
+    if (!xq || !xs) return set_error(DK_ERR_INVALID, "dk_matmul_q8_0_q: null activation");
+    return matmul_common(out, nullptr, xq, xs, w_packed, n, d, stream);
+}
+
+int dk_rmsnorm(float *o, const float *x, const float *w, int n, void *stream) {
+    if (n <= 0 || !o || !x || !w) return set_error(DK_ERR_INVALID, "dk_rmsnorm: bad arguments");
+    return cuda_status(launch_rmsnorm(o, x, w, n, (cudaStream_t)stream), "dk_rmsnorm");
+}
+
+}  // extern "C"

@@ -1,0 +1,530 @@
+// engine.cu -- the decode engine behind dk_model_* (include/diolkos.h).
+//
+// One dk_model holds a LLaMA-2 model (or one tensor-parallel shard of it) in HBM:
+//   * packed Q8_0 weights in one allocation: per layer the fused [wq; wk; wv] matrix, wo, the
+//     row-interleaved [w1_0; w3_0; w1_1; w3_1; ...] matrix (so SwiGLU pairs arrive together) and
+//     w2; the embedding table and lm_head; fp32 norm weights;
+//   * the KV cache, [layer][kv_head][seq_len][head_size], bf16 (truncating, like the reference) or
+//     fp32;
+//   * activations, the RoPE (cos, sin) table, the token buffer and the current position.
+// The per-token step (reference forward, src/transformer.c:55-239) is 5 kernels per layer plus
+// the classifier, launched with programmatic dependent launch and captured once into a CUDA
+// graph; `pos` and the tokens live in device memory, so the same graph serves every position and
+// greedy decoding replays it back to back without the host in the loop.
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "dk_internal.h"
+
+namespace dk {
+
+int *device_error_word() {
+    static std::mutex mu;
+    static int *words[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lk(mu);
+    if (!words[dev]) {
+        int *p = nullptr;
+        if (cudaMalloc(&p, sizeof(int)) != cudaSuccess) return nullptr;
+        if (cudaMemset(p, 0, sizeof(int)) != cudaSuccess) return nullptr;
+        words[dev] = p;
+    }
+    return words[dev];
+}
+
+// HF rotate-half RoPE coefficients (src/transformer.c:90-95): for position p and j < hs/2,
+// freq = 1/powf(10000, 2j/(float)hs), val = p*freq, (cosf(val), sinf(val)).  Computed on the host
+// with the C library's single-precision functions and uploaded once.
+static void rope_table(std::vector<float> &t, int seq_len, int hs) {
+    t.resize((size_t)seq_len * hs);
+    for (int p = 0; p < seq_len; ++p)
+        for (int j = 0; j < hs / 2; ++j) {
+            const float freq = 1.0f / powf(10000.0f, (float)(2 * j) / (float)hs);
+            const float val = (float)p * freq;
+            t[(size_t)p * hs + 2 * j] = cosf(val);
+            t[(size_t)p * hs + 2 * j + 1] = sinf(val);
+        }
+}
+
+}  // namespace dk
+
+using namespace dk;
+
+struct dk_layer {
+    uint8_t *wqkv = nullptr, *wo = nullptr, *w13 = nullptr, *w2 = nullptr;
+    float *rms_att = nullptr, *rms_ffn = nullptr;
+};
+
+struct dk_model {
+    // global config
+    int dim, hidden, n_layers, n_heads, n_kv_heads, vocab, seq_len, kv_type, device, rank, world;
+    int hs, kv_dim;
+    // this rank's shard sizes
+    int l_heads, l_kv_heads, l_hidden;
+    int num_sms;
+    cudaStream_t stream = nullptr;
+    // weights
+    uint8_t *warena = nullptr;
+    size_t warena_bytes = 0;
+    uint8_t *emb = nullptr, *wcls = nullptr;
+    float *rms_final = nullptr;
+    std::vector<dk_layer> layers;
+    std::vector<uint8_t> have;  // [(n_layers + 1) * DK_W_COUNT]
+    // activations and state
+    uint8_t *aarena = nullptr;
+    float *x = nullptr, *qkv = nullptr, *xb = nullptr, *hb = nullptr, *logits = nullptr, *rope = nullptr;
+    float *attn_work = nullptr;
+    unsigned *attn_count = nullptr;
+    unsigned long long *amax_part = nullptr;
+    unsigned *amax_count = nullptr;
+    int *tokens = nullptr, *pos = nullptr, *n_forced = nullptr, *err = nullptr;
+    void *kcache = nullptr, *vcache = nullptr;
+    size_t kv_layer_elems = 0;
+    int attn_splits = 1;
+    // staging for weight upload
+    uint8_t *stage = nullptr;
+    size_t stage_bytes = 0;
+    // pinned host scratch
+    int *h_small = nullptr;
+    // plans
+    GemvPlan p_qkv, p_wo, p_w13, p_w2, p_cls;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    int kernels_per_step = 0;
+    bool finalized = false;
+};
+
+static size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+static int need(dk_model *m) {
+    if (!m) return set_error(DK_ERR_INVALID, "null dk_model");
+    cudaError_t e = cudaSetDevice(m->device);
+    return cuda_status(e, "cudaSetDevice");
+}
+
+extern "C" {
+
+dk_model *dk_model_create(const int *cfg, int kv_type, int device, int tp_rank, int tp_world) {
+    if (!cfg) {
+        set_error(DK_ERR_INVALID, "dk_model_create: null cfg");
+        return nullptr;
+    }
+    const int dim = cfg[0], hidden = cfg[1], L = cfg[2], H = cfg[3], KVH = cfg[4], V = cfg[5], S = cfg[6];
+    if (dim <= 0 || hidden <= 0 || L <= 0 || H <= 0 || KVH <= 0 || V <= 0 || S <= 0 || dim % H || H % KVH ||
+        dim % 32 || hidden % 32 || (dim / H) % 2 || dim / H > 128 || H / KVH > 8) {
+        set_error(DK_ERR_INVALID, "dk_model_create: unsupported config dim=%d hidden=%d layers=%d heads=%d kv=%d",
+                  dim, hidden, L, H, KVH);
+        return nullptr;
+    }
+    if (tp_world != 1 || tp_rank != 0) {
+        set_error(DK_ERR_INVALID, "dk_model_create: this entry point builds single-GPU models (tp_world=1)");
+        return nullptr;
+    }
+    if (kv_type != DK_KV_BF16 && kv_type != DK_KV_F32) {
+        set_error(DK_ERR_INVALID, "dk_model_create: bad kv_type %d", kv_type);
+        return nullptr;
+    }
+    if (cudaSetDevice(device) != cudaSuccess) {
+        set_error(DK_ERR_CUDA, "dk_model_create: cudaSetDevice(%d) failed", device);
+        return nullptr;
+    }
+    dk_model *m = new dk_model();
+    m->dim = dim; m->hidden = hidden; m->n_layers = L; m->n_heads = H; m->n_kv_heads = KVH;
+    m->vocab = V; m->seq_len = S; m->kv_type = kv_type; m->device = device;
+    m->rank = tp_rank; m->world = tp_world;
+    m->hs = dim / H;
+    m->kv_dim = dim * KVH / H;
+    m->l_heads = H / tp_world;
+    m->l_kv_heads = KVH / tp_world;
+    m->l_hidden = hidden / tp_world;
+    cudaDeviceGetAttribute(&m->num_sms, cudaDevAttrMultiProcessorCount, device);
+    m->layers.resize(L);
+    m->have.assign((size_t)(L + 1) * DK_W_COUNT, 0);
+
+    auto fail = [&](const char *what) -> dk_model * {
+        set_error(DK_ERR_NOMEM, "dk_model_create: %s", what);
+        dk_model_destroy(m);
+        return nullptr;
+    };
+    if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess) return fail("stream");
+
+    // ---- weights
+    const size_t rs_dim = q8_row_bytes(dim), rs_hid = q8_row_bytes(hidden);
+    const int qkv_rows = dim + 2 * m->kv_dim;
+    const size_t b_qkv = align256((size_t)qkv_rows * rs_dim), b_wo = align256((size_t)dim * rs_dim);
+    const size_t b_w13 = align256((size_t)2 * hidden * rs_dim), b_w2 = align256((size_t)dim * rs_hid);
+    const size_t b_norm = align256((size_t)dim * 4);
+    const size_t b_emb = align256((size_t)V * rs_dim);
+    const size_t per_layer = b_qkv + b_wo + b_w13 + b_w2 + 2 * b_norm;
+    m->warena_bytes = per_layer * L + 2 * b_emb + b_norm;
+    if (cudaMalloc(&m->warena, m->warena_bytes) != cudaSuccess) return fail("weight memory");
+    uint8_t *p = m->warena;
+    m->emb = p; p += b_emb;
+    m->wcls = p; p += b_emb;
+    m->rms_final = reinterpret_cast<float *>(p); p += b_norm;
+    for (int l = 0; l < L; ++l) {
+        dk_layer &ly = m->layers[l];
+        ly.wqkv = p; p += b_qkv;
+        ly.wo = p; p += b_wo;
+        ly.w13 = p; p += b_w13;
+        ly.w2 = p; p += b_w2;
+        ly.rms_att = reinterpret_cast<float *>(p); p += b_norm;
+        ly.rms_ffn = reinterpret_cast<float *>(p); p += b_norm;
+    }
+
+    // ---- KV cache
+    const size_t esz = kv_type == DK_KV_F32 ? 4 : 2;
+    m->kv_layer_elems = (size_t)KVH * S * m->hs;
+    if (cudaMalloc(&m->kcache, m->kv_layer_elems * L * esz) != cudaSuccess) return fail("key cache");
+    if (cudaMalloc(&m->vcache, m->kv_layer_elems * L * esz) != cudaSuccess) return fail("value cache");
+    cudaMemsetAsync(m->kcache, 0, m->kv_layer_elems * L * esz, m->stream);
+    cudaMemsetAsync(m->vcache, 0, m->kv_layer_elems * L * esz, m->stream);
+
+    // ---- activations and small state
+    m->attn_splits = attn_max_splits(S, KVH, m->num_sms);
+    const size_t sz_x = align256((size_t)dim * 4), sz_qkv = align256((size_t)qkv_rows * 4);
+    const size_t sz_hb = align256((size_t)hidden * 4), sz_logits = align256((size_t)V * 4);
+    const size_t sz_rope = align256((size_t)S * m->hs * 4);
+    const size_t sz_work = align256((size_t)H * m->attn_splits * (m->hs + 2) * 4);
+    const size_t sz_cnt = align256((size_t)KVH * 4);
+    const size_t sz_part = align256((size_t)m->num_sms * 8);
+    const size_t sz_tok = align256((size_t)(S + 1) * 4);
+    const size_t total = sz_x * 2 + sz_qkv + sz_hb + sz_logits + sz_rope + sz_work + sz_cnt + sz_part + 256 + sz_tok + 3 * 256;
+    if (cudaMalloc(&m->aarena, total) != cudaSuccess) return fail("activation memory");
+    cudaMemsetAsync(m->aarena, 0, total, m->stream);
+    p = m->aarena;
+    m->x = reinterpret_cast<float *>(p); p += sz_x;
+    m->xb = reinterpret_cast<float *>(p); p += sz_x;
+    m->qkv = reinterpret_cast<float *>(p); p += sz_qkv;
+    m->hb = reinterpret_cast<float *>(p); p += sz_hb;
+    m->logits = reinterpret_cast<float *>(p); p += sz_logits;
+    m->rope = reinterpret_cast<float *>(p); p += sz_rope;
+    m->attn_work = reinterpret_cast<float *>(p); p += sz_work;
+    m->attn_count = reinterpret_cast<unsigned *>(p); p += sz_cnt;
+    m->amax_part = reinterpret_cast<unsigned long long *>(p); p += sz_part;
+    m->amax_count = reinterpret_cast<unsigned *>(p); p += 256;
+    m->tokens = reinterpret_cast<int *>(p); p += sz_tok;
+    m->pos = reinterpret_cast<int *>(p); p += 256;
+    m->n_forced = reinterpret_cast<int *>(p); p += 256;
+    m->err = reinterpret_cast<int *>(p); p += 256;
+
+    std::vector<float> rt;
+    rope_table(rt, S, m->hs);
+    if (cudaMemcpyAsync(m->rope, rt.data(), rt.size() * 4, cudaMemcpyHostToDevice, m->stream) != cudaSuccess)
+        return fail("rope upload");
+    if (cudaMallocHost(&m->h_small, 4096) != cudaSuccess) return fail("pinned scratch");
+    if (cudaStreamSynchronize(m->stream) != cudaSuccess) return fail("init sync");
+
+    m->p_qkv = plan_gemv(dim, qkv_rows, EPI_STORE, m->num_sms);
+    m->p_wo = plan_gemv(dim, dim, EPI_ADD, m->num_sms);
+    m->p_w13 = plan_gemv(dim, 2 * hidden, EPI_SWIGLU, m->num_sms);
+    m->p_w2 = plan_gemv(hidden, dim, EPI_ADD, m->num_sms);
+    m->p_cls = plan_gemv(dim, V, EPI_ARGMAX, m->num_sms);
+    return m;
+}
+
+void dk_model_destroy(dk_model *m) {
+    if (!m) return;
+    cudaSetDevice(m->device);
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    if (m->exec) cudaGraphExecDestroy(m->exec);
+    if (m->graph) cudaGraphDestroy(m->graph);
+    cudaFree(m->warena);
+    cudaFree(m->kcache);
+    cudaFree(m->vcache);
+    cudaFree(m->aarena);
+    cudaFree(m->stage);
+    if (m->h_small) cudaFreeHost(m->h_small);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+}
+
+}  // extern "C"
+
+// Shape of one weight: rows x cols of the full (unsharded) matrix; cols == 0 for norm vectors.
+static int weight_shape(const dk_model *m, int which, int &rows, int &cols) {
+    switch (which) {
+    case DK_W_EMB: case DK_W_WCLS: rows = m->vocab; cols = m->dim; return 1;
+    case DK_W_WQ: case DK_W_WO: rows = m->dim; cols = m->dim; return 1;
+    case DK_W_WK: case DK_W_WV: rows = m->kv_dim; cols = m->dim; return 1;
+    case DK_W_W1: case DK_W_W3: rows = m->hidden; cols = m->dim; return 1;
+    case DK_W_W2: rows = m->dim; cols = m->hidden; return 1;
+    case DK_W_RMS_FINAL: case DK_W_RMS_ATT: case DK_W_RMS_FFN: rows = m->dim; cols = 0; return 0;
+    default: return -1;
+    }
+}
+
+static int set_weight_impl(dk_model *m, int which, int layer, const void *q, const float *scale, bool on_device) {
+    if (int r = need(m)) return r;
+    if (m->finalized) return set_error(DK_ERR_STATE, "dk_model_set_weight: model already finalized");
+    int rows = 0, cols = 0;
+    const int kind = weight_shape(m, which, rows, cols);
+    if (kind < 0) return set_error(DK_ERR_INVALID, "dk_model_set_weight: unknown weight id %d", which);
+    const bool per_layer = which >= DK_W_RMS_ATT;
+    if (per_layer ? (layer < 0 || layer >= m->n_layers) : (layer != -1))
+        return set_error(DK_ERR_INVALID, "dk_model_set_weight: bad layer %d for weight %d", layer, which);
+    if (!q || (kind == 1 && !scale)) return set_error(DK_ERR_INVALID, "dk_model_set_weight: null data");
+    cudaStream_t st = m->stream;
+    const cudaMemcpyKind dir = on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+
+    if (kind == 0) {  // fp32 norm vector
+        float *dst = which == DK_W_RMS_FINAL ? m->rms_final
+                     : which == DK_W_RMS_ATT ? m->layers[layer].rms_att : m->layers[layer].rms_ffn;
+        if (int r = cuda_status(cudaMemcpyAsync(dst, q, (size_t)rows * 4, dir, st), "norm upload")) return r;
+    } else {
+        const size_t nq = (size_t)rows * cols, ns = nq / 32;
+        const int8_t *src_q = static_cast<const int8_t *>(q);
+        const float *src_s = scale;
+        if (!on_device) {
+            const size_t need_bytes = align256(nq) + ns * 4;
+            if (need_bytes > m->stage_bytes) {
+                if (m->stage) {
+                    cudaStreamSynchronize(st);
+                    cudaFree(m->stage);
+                    m->stage = nullptr;
+                    m->stage_bytes = 0;
+                }
+                if (cudaMalloc(&m->stage, need_bytes) != cudaSuccess)
+                    return set_error(DK_ERR_NOMEM, "dk_model_set_weight: staging buffer of %zu bytes", need_bytes);
+                m->stage_bytes = need_bytes;
+            }
+            if (int r = cuda_status(cudaMemcpyAsync(m->stage, q, nq, cudaMemcpyHostToDevice, st), "weight upload"))
+                return r;
+            if (int r = cuda_status(cudaMemcpyAsync(m->stage + align256(nq), scale, ns * 4, cudaMemcpyHostToDevice, st),
+                                    "scale upload"))
+                return r;
+            src_q = reinterpret_cast<const int8_t *>(m->stage);
+            src_s = reinterpret_cast<const float *>(m->stage + align256(nq));
+        }
+        uint8_t *dst = nullptr;
+        int row0 = 0, step = 1;
+        switch (which) {
+        case DK_W_EMB: dst = m->emb; break;
+        case DK_W_WCLS: dst = m->wcls; break;
+        case DK_W_WQ: dst = m->layers[layer].wqkv; break;
+        case DK_W_WK: dst = m->layers[layer].wqkv; row0 = m->dim; break;
+        case DK_W_WV: dst = m->layers[layer].wqkv; row0 = m->dim + m->kv_dim; break;
+        case DK_W_WO: dst = m->layers[layer].wo; break;
+        case DK_W_W1: dst = m->layers[layer].w13; row0 = 0; step = 2; break;
+        case DK_W_W3: dst = m->layers[layer].w13; row0 = 1; step = 2; break;
+        case DK_W_W2: dst = m->layers[layer].w2; break;
+        default: break;
+        }
+        if (int r = cuda_status(launch_pack_rows(dst, cols, src_q, src_s, rows, row0, step, st), "pack rows")) return r;
+        if (!on_device) {  // the staging buffer is reused by the next call
+            if (int r = cuda_status(cudaStreamSynchronize(st), "weight upload sync")) return r;
+        }
+    }
+    m->have[(size_t)(per_layer ? layer : m->n_layers) * DK_W_COUNT + which] = 1;
+    return DK_OK;
+}
+
+static int enqueue_step(dk_model *m, cudaStream_t st) {
+    int launches = 0;
+    auto gemv = [&](const GemvPlan &p, const uint8_t *w, int n, int d, int pro, int epi, const float *x,
+                    const float *norm, float *out) -> cudaError_t {
+        GemvArgs a;
+        a.w = w; a.n = n; a.d = d; a.pro = pro; a.epi = epi; a.x = x; a.norm_w = norm; a.out = out;
+        a.emb = m->emb; a.tokens = m->tokens; a.pos = m->pos; a.n_forced = m->n_forced; a.seq_len = m->seq_len;
+        a.amax_part = m->amax_part; a.amax_count = m->amax_count; a.err = m->err;
+        ++launches;
+        return launch_gemv(a, p, st, true);
+    };
+    cudaError_t e = cudaSuccess;
+    const int qkv_rows = m->dim + 2 * m->kv_dim;
+    const size_t esz = m->kv_type == DK_KV_F32 ? 4 : 2;
+    for (int l = 0; l < m->n_layers && e == cudaSuccess; ++l) {
+        const dk_layer &ly = m->layers[l];
+        e = gemv(m->p_qkv, ly.wqkv, m->dim, qkv_rows, l == 0 ? PRO_EMB_RMS : PRO_RMS, EPI_STORE, m->x, ly.rms_att,
+                 m->qkv);
+        if (e != cudaSuccess) break;
+        AttnArgs at;
+        at.qkv = m->qkv; at.rope = m->rope;
+        at.k_cache = static_cast<uint8_t *>(m->kcache) + (size_t)l * m->kv_layer_elems * esz;
+        at.v_cache = static_cast<uint8_t *>(m->vcache) + (size_t)l * m->kv_layer_elems * esz;
+        at.out = m->xb; at.work = m->attn_work; at.count = m->attn_count; at.pos = m->pos;
+        at.n_heads = m->n_heads; at.n_kv_heads = m->n_kv_heads; at.head_size = m->hs; at.seq_len = m->seq_len;
+        at.kv_f32 = m->kv_type == DK_KV_F32; at.max_splits = m->attn_splits; at.min_chunk = 64; at.err = m->err;
+        e = launch_attention(at, st, true);
+        ++launches;
+        if (e != cudaSuccess) break;
+        e = gemv(m->p_wo, ly.wo, m->dim, m->dim, PRO_F32, EPI_ADD, m->xb, nullptr, m->x);
+        if (e != cudaSuccess) break;
+        e = gemv(m->p_w13, ly.w13, m->dim, 2 * m->hidden, PRO_RMS, EPI_SWIGLU, m->x, ly.rms_ffn, m->hb);
+        if (e != cudaSuccess) break;
+        e = gemv(m->p_w2, ly.w2, m->hidden, m->dim, PRO_F32, EPI_ADD, m->hb, nullptr, m->x);
+    }
+    if (e == cudaSuccess) e = gemv(m->p_cls, m->wcls, m->dim, m->vocab, PRO_RMS, EPI_ARGMAX, m->x, m->rms_final, m->logits);
+    m->kernels_per_step = launches;
+    return cuda_status(e, "enqueue decode step");
+}
+
+extern "C" {
+
+int dk_model_set_weight(dk_model *m, int which, int layer, const void *q, const float *scale) {
+    return set_weight_impl(m, which, layer, q, scale, false);
+}
+
+int dk_model_set_weight_device(dk_model *m, int which, int layer, const void *q, const float *scale) {
+    return set_weight_impl(m, which, layer, q, scale, true);
+}
+
+int dk_model_finalize(dk_model *m) {
+    if (int r = need(m)) return r;
+    if (m->finalized) return DK_OK;
+    for (int l = 0; l <= m->n_layers; ++l)
+        for (int w = 0; w < DK_W_COUNT; ++w) {
+            const bool per_layer = w >= DK_W_RMS_ATT;
+            if (per_layer != (l < m->n_layers)) continue;
+            if (!m->have[(size_t)l * DK_W_COUNT + w])
+                return set_error(DK_ERR_STATE, "dk_model_finalize: weight %d of layer %d was never set", w,
+                                 per_layer ? l : -1);
+        }
+    if (int r = cuda_status(cudaStreamSynchronize(m->stream), "finalize sync")) return r;
+    cudaFree(m->stage);
+    m->stage = nullptr;
+    m->stage_bytes = 0;
+    // Capture one decode step.
+    if (int r = cuda_status(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal), "begin capture"))
+        return r;
+    const int rs = enqueue_step(m, m->stream);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+    if (rs) {
+        if (g) cudaGraphDestroy(g);
+        return rs;
+    }
+    if (int r = cuda_status(e, "end capture")) return r;
+    m->graph = g;
+    if (int r = cuda_status(cudaGraphInstantiate(&m->exec, g, 0), "graph instantiate")) return r;
+    m->finalized = true;
+    return DK_OK;
+}
+
+int dk_model_set_tokens(dk_model *m, const int *tokens, int n_tokens, int n_forced) {
+    if (int r = need(m)) return r;
+    if (n_tokens < 0 || n_tokens > m->seq_len + 1 || n_forced < 0)
+        return set_error(DK_ERR_INVALID, "dk_model_set_tokens: bad sizes");
+    for (int i = 0; i < n_tokens; ++i)
+        if (tokens[i] < 0 || tokens[i] >= m->vocab)
+            return set_error(DK_ERR_INVALID, "dk_model_set_tokens: token %d out of range", tokens[i]);
+    if (n_tokens && cudaMemcpyAsync(m->tokens, tokens, (size_t)n_tokens * 4, cudaMemcpyHostToDevice, m->stream))
+        return set_error(DK_ERR_CUDA, "dk_model_set_tokens: copy failed");
+    m->h_small[0] = n_forced;
+    if (int r = cuda_status(cudaMemcpyAsync(m->n_forced, m->h_small, 4, cudaMemcpyHostToDevice, m->stream), "n_forced"))
+        return r;
+    return cuda_status(cudaStreamSynchronize(m->stream), "dk_model_set_tokens");
+}
+
+int dk_model_enqueue_steps(dk_model *m, int pos0, int n_steps) {
+    if (int r = need(m)) return r;
+    if (!m->finalized) return set_error(DK_ERR_STATE, "dk_model_enqueue_steps: model not finalized");
+    if (pos0 < 0 || n_steps < 0 || pos0 + n_steps > m->seq_len)
+        return set_error(DK_ERR_INVALID, "dk_model_enqueue_steps: positions [%d, %d) exceed seq_len %d", pos0,
+                         pos0 + n_steps, m->seq_len);
+    m->h_small[1] = pos0;
+    if (int r = cuda_status(cudaMemcpyAsync(m->pos, m->h_small + 1, 4, cudaMemcpyHostToDevice, m->stream), "pos"))
+        return r;
+    for (int i = 0; i < n_steps; ++i)
+        if (int r = cuda_status(cudaGraphLaunch(m->exec, m->stream), "graph launch")) return r;
+    return DK_OK;
+}
+
+int dk_model_get_tokens(dk_model *m, int *tokens, int n_tokens) {
+    if (int r = need(m)) return r;
+    if (n_tokens < 0 || n_tokens > m->seq_len + 1) return set_error(DK_ERR_INVALID, "dk_model_get_tokens: bad size");
+    if (int r = cuda_status(cudaMemcpyAsync(tokens, m->tokens, (size_t)n_tokens * 4, cudaMemcpyDeviceToHost, m->stream),
+                            "token readback"))
+        return r;
+    return cuda_status(cudaStreamSynchronize(m->stream), "token readback sync");
+}
+
+int dk_model_sync(dk_model *m) {
+    if (int r = need(m)) return r;
+    return cuda_status(cudaStreamSynchronize(m->stream), "dk_model_sync");
+}
+
+void *dk_model_stream(dk_model *m) { return m ? (void *)m->stream : nullptr; }
+
+int dk_model_device_error(dk_model *m) {
+    if (need(m)) return DK_ERR_CUDA;
+    int v = 0;
+    if (cudaMemcpyAsync(m->h_small + 2, m->err, 4, cudaMemcpyDeviceToHost, m->stream) != cudaSuccess) return DK_ERR_CUDA;
+    if (cudaStreamSynchronize(m->stream) != cudaSuccess) return DK_ERR_CUDA;
+    v = m->h_small[2];
+    return v;
+}
+
+int dk_model_kernels_per_step(dk_model *m) { return m ? m->kernels_per_step : 0; }
+
+size_t dk_model_weight_bytes(dk_model *m) {
+    if (!m) return 0;
+    const size_t rs_dim = q8_row_bytes(m->dim), rs_hid = q8_row_bytes(m->hidden);
+    const size_t per_layer = (size_t)(m->dim + 2 * m->kv_dim) * rs_dim + (size_t)m->dim * rs_dim +
+                             (size_t)2 * m->hidden * rs_dim + (size_t)m->dim * rs_hid;
+    return per_layer * m->n_layers + (size_t)m->vocab * rs_dim;  // + one embedding row (negligible)
+}
+
+int dk_model_forward(dk_model *m, int token, int pos, float *logits) {
+    if (int r = need(m)) return r;
+    if (!m->finalized) return set_error(DK_ERR_STATE, "dk_model_forward: model not finalized");
+    if (pos < 0 || pos >= m->seq_len) return set_error(DK_ERR_INVALID, "dk_model_forward: pos %d out of range", pos);
+    if (token < 0 || token >= m->vocab) return set_error(DK_ERR_INVALID, "dk_model_forward: token %d out of range", token);
+    m->h_small[8] = token;
+    m->h_small[9] = pos;
+    m->h_small[10] = m->seq_len + 1;  // nothing forced: the argmax is written but not used
+    cudaStream_t st = m->stream;
+    if (cudaMemcpyAsync(m->tokens + pos, m->h_small + 8, 4, cudaMemcpyHostToDevice, st) ||
+        cudaMemcpyAsync(m->pos, m->h_small + 9, 4, cudaMemcpyHostToDevice, st) ||
+        cudaMemcpyAsync(m->n_forced, m->h_small + 10, 4, cudaMemcpyHostToDevice, st))
+        return set_error(DK_ERR_CUDA, "dk_model_forward: step upload failed");
+    if (int r = cuda_status(cudaGraphLaunch(m->exec, st), "graph launch")) return r;
+    if (logits) {
+        if (int r = cuda_status(cudaMemcpyAsync(logits, m->logits, (size_t)m->vocab * 4, cudaMemcpyDeviceToHost, st),
+                                "logits readback"))
+            return r;
+    }
+    if (int r = cuda_status(cudaStreamSynchronize(st), "dk_model_forward")) return r;
+    const int dev_err = dk_model_device_error(m);
+    if (dev_err) return set_error(dev_err, "dk_model_forward: device error word 0x%x", dev_err);
+    return DK_OK;
+}
+
+int dk_model_generate(dk_model *m, const int *prompt, int n_prompt, int steps, int *out, int *n_out) {
+    if (int r = need(m)) return r;
+    if (!m->finalized) return set_error(DK_ERR_STATE, "dk_model_generate: model not finalized");
+    if (!prompt || n_prompt < 1) return set_error(DK_ERR_INVALID, "dk_model_generate: expected at least 1 prompt token");
+    if (steps > m->seq_len) steps = m->seq_len;
+    if (steps < 0) steps = 0;
+    for (int i = 0; i < n_prompt; ++i)
+        if (prompt[i] < 0 || prompt[i] >= m->vocab)
+            return set_error(DK_ERR_INVALID, "dk_model_generate: prompt token %d out of range", prompt[i]);
+    const int nt = n_prompt < m->seq_len + 1 ? n_prompt : m->seq_len + 1;
+    if (int r = dk_model_set_tokens(m, prompt, nt, n_prompt)) return r;
+    if (int r = dk_model_enqueue_steps(m, 0, steps)) return r;
+    std::vector<int> toks((size_t)steps + 1);
+    if (int r = dk_model_get_tokens(m, toks.data(), steps + 1)) return r;
+    const int dev_err = dk_model_device_error(m);
+    if (dev_err) return set_error(dev_err, "dk_model_generate: device error word 0x%x", dev_err);
+    // Replay the reference loop's bookkeeping on the tokens the device produced.
+    int count = 0;
+    for (int pos = 0; pos < steps; ++pos) {
+        int next;
+        if (pos < n_prompt - 1) {
+            next = prompt[pos + 1];
+        } else {
+            next = toks[(size_t)pos + 1];
+            if (out) out[count] = next;
+            ++count;
+        }
+        if (next == 1) break;
+    }
+    if (n_out) *n_out = count;
+    return DK_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,119 @@
+"""Python mirror of the decode engine (dk_model_* in include/diolkos.h)."""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import _native as N
+from . import synth
+
+# HF tensor name suffix -> weight id
+_LAYER_IDS = {
+    "input_layernorm.weight": N.DK_W_RMS_ATT, "self_attn.q_proj.weight": N.DK_W_WQ,
+    "self_attn.k_proj.weight": N.DK_W_WK, "self_attn.v_proj.weight": N.DK_W_WV,
+    "self_attn.o_proj.weight": N.DK_W_WO, "post_attention_layernorm.weight": N.DK_W_RMS_FFN,
+    "mlp.gate_proj.weight": N.DK_W_W1, "mlp.down_proj.weight": N.DK_W_W2, "mlp.up_proj.weight": N.DK_W_W3,
+}
+
+
+def weight_id(name: str) -> tuple[int, int]:
+    """(weight id, layer) of an HF tensor name."""
+    if name == "model.embed_tokens.weight":
+        return N.DK_W_EMB, -1
+    if name == "lm_head.weight":
+        return N.DK_W_WCLS, -1
+    if name == "model.norm.weight":
+        return N.DK_W_RMS_FINAL, -1
+    rest = name[len("model.layers."):]
+    layer, suffix = rest.split(".", 1)
+    return _LAYER_IDS[suffix], int(layer)
+
+
+class Model:
+    """One model resident on one GPU; the whole decode step is a CUDA graph."""
+
+    def __init__(self, cfg: synth.Config, kv_f32: bool = False, device: int = 0):
+        self.cfg = cfg
+        L = N.lib()
+        arr = (C.c_int * 7)(*cfg.as_list())
+        self.h = L.dk_model_create(arr, N.DK_KV_F32 if kv_f32 else N.DK_KV_BF16, device, 0, 1)
+        if not self.h:
+            raise N.DiolkosError(N.DK_ERR_INVALID, L.dk_last_error().decode())
+
+    def set_weight(self, which: int, layer: int, q, s=None):
+        """Host arrays: Q8_0 (int8 q, fp32 s) planar, or a fp32 vector."""
+        q = np.ascontiguousarray(q)
+        if s is not None:
+            s = np.ascontiguousarray(s, dtype=np.float32)
+        N.check(N.lib().dk_model_set_weight(self.h, which, layer, q.ctypes.data,
+                                             s.ctypes.data if s is not None else None))
+
+    def set_weight_device(self, which: int, layer: int, q, s=None):
+        """Device tensors (torch): Q8_0 planar (int8, fp32) or a fp32 vector."""
+        N.check(N.lib().dk_model_set_weight_device(self.h, which, layer, q.data_ptr(),
+                                                    s.data_ptr() if s is not None else None))
+
+    def load_named(self, weights_by_name: dict):
+        for name, val in weights_by_name.items():
+            which, layer = weight_id(name)
+            if isinstance(val, tuple):
+                self.set_weight(which, layer, val[0], val[1])
+            else:
+                self.set_weight(which, layer, np.asarray(val, dtype=np.float32))
+
+    def finalize(self):
+        N.check(N.lib().dk_model_finalize(self.h))
+
+    def forward(self, token: int, pos: int) -> np.ndarray:
+        logits = np.empty(self.cfg.vocab_size, np.float32)
+        N.check(N.lib().dk_model_forward(self.h, token, pos, logits.ctypes.data))
+        return logits
+
+    def generate(self, prompt, steps: int) -> np.ndarray:
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.empty(max(steps, 1), np.int32)
+        n = C.c_int(0)
+        N.check(N.lib().dk_model_generate(self.h, p.ctypes.data, p.size, steps, out.ctypes.data, C.byref(n)))
+        return out[: n.value].copy()
+
+    def set_tokens(self, tokens, n_forced: int):
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        N.check(N.lib().dk_model_set_tokens(self.h, t.ctypes.data, t.size, n_forced))
+
+    def enqueue_steps(self, pos0: int, n_steps: int):
+        N.check(N.lib().dk_model_enqueue_steps(self.h, pos0, n_steps))
+
+    def get_tokens(self, n: int) -> np.ndarray:
+        t = np.empty(n, np.int32)
+        N.check(N.lib().dk_model_get_tokens(self.h, t.ctypes.data, n))
+        return t
+
+    def sync(self):
+        N.check(N.lib().dk_model_sync(self.h))
+
+    @property
+    def stream(self) -> int:
+        return N.lib().dk_model_stream(self.h)
+
+    def device_error(self) -> int:
+        return N.lib().dk_model_device_error(self.h)
+
+    @property
+    def kernels_per_step(self) -> int:
+        return N.lib().dk_model_kernels_per_step(self.h)
+
+    @property
+    def weight_bytes(self) -> int:
+        return int(N.lib().dk_model_weight_bytes(self.h))
+
+    def close(self):
+        if getattr(self, "h", None):
+            N.lib().dk_model_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

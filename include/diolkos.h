@@ -1,0 +1,138 @@
+/*
+ * diolkos.h -- the C ABI of the B200 decode path (libdiolkos.so).
+ *
+ * Plain pointers, sizes and int status codes; no C++ or torch types.  "Device" pointers are CUDA
+ * device addresses on the current device; `stream` is a cudaStream_t passed as void* (NULL = the
+ * legacy default stream).  Every entry point returns DK_OK (0) or a DK_ERR_* code, and
+ * dk_last_error() describes the most recent failure of the calling thread.
+ *
+ * The reference's own C API (transformer.h, safetensors.h, tensor.h, utils.h, sampler.h,
+ * tokenizer.h in this directory) is implemented on top of these entry points by the same library.
+ */
+#ifndef DIOLKOS_H
+#define DIOLKOS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  The device-side error word uses the same bits. */
+#define DK_OK            0
+#define DK_ERR_INVALID   0x01 /* bad argument or shape                                  */
+#define DK_ERR_CUDA      0x02 /* a CUDA runtime call failed                              */
+#define DK_ERR_TIMEOUT   0x04 /* a bounded device-side wait gave up                      */
+#define DK_ERR_NOMEM     0x08 /* device or host allocation failed                        */
+#define DK_ERR_IO        0x10 /* file could not be read or written                       */
+#define DK_ERR_STATE     0x20 /* call not valid in the object's current state             */
+#define DK_ERR_COMM      0x40 /* a peer (tensor-parallel rank) did not answer in time     */
+
+const char *dk_last_error(void);
+int dk_device_count(void);
+
+/* ---------------------------------------------------------------------------------------------
+ * Q8_0 format: groups of 32 int8 values with one fp32 scale (value = q * scale).
+ * ------------------------------------------------------------------------------------------- */
+
+/* Weight quantiser: replaces convert_bf16_q8_0 (reference src/tensor.c:312-344).  Device
+ * pointers; n % 32 == 0.  Bit-exact with the reference build: scale = amax*(1/127),
+ * q = rint(x * (1/scale)). */
+int dk_quantize_bf16_q8_0(const uint16_t *x, size_t n, int8_t *q, float *scale, void *stream);
+/* Activation quantiser: replaces convert_f32_q8_slice_into_offset (src/tensor.c:199-228). */
+int dk_quantize_f32_q8_0(const float *x, size_t n, int8_t *q, float *scale, void *stream);
+/* Dequantiser: replaces convert_q8_f32_slice_into_offset (src/tensor.c:245-265). */
+int dk_dequantize_q8_0(const int8_t *q, const float *scale, size_t n, float *out, void *stream);
+/* The exact int32 dot of every 32-element group of a [d x n] Q8_0 matrix with a Q8_0 vector
+ * (the inner loop of matmul_Q8_0, src/utils.c:122-127): dots[i*(n/32)+g]. */
+int dk_q8_0_group_dots(const int8_t *xq, const int8_t *wq, int n, int d, int32_t *dots, void *stream);
+
+/* Packed device weight layout used by the GEMV: row r occupies dk_q8_row_bytes(n) bytes
+ * (n int8 values, then the row's n/32 fp32 scales, zero padding to 16 bytes). */
+size_t dk_q8_row_bytes(int n);
+/* Pack `rows` rows of a planar Q8_0 matrix (the on-disk cache layout: int8[rows*n] and
+ * fp32[rows*n/32], device pointers) into packed rows dst_row0, dst_row0+step, ... of `dst`. */
+int dk_q8_pack_rows(uint8_t *dst, int n, const int8_t *src_q, const float *src_scale, int rows,
+                    int dst_row0, int dst_row_step, void *stream);
+
+/* matmul_Q8_0 (src/utils.c:106-138) on packed weights: out[d] = W[d x n] * quant(x[n]).
+ * Device pointers.  Output bit-exact with the reference build (same group order, same
+ * rounding). */
+int dk_matmul_q8_0(float *out, const float *x, const uint8_t *w_packed, int n, int d, void *stream);
+/* The same GEMV on an activation that is already quantised (xq int8[n], xs fp32[n/32]). */
+int dk_matmul_q8_0_q(float *out, const int8_t *xq, const float *xs, const uint8_t *w_packed, int n,
+                     int d, void *stream);
+/* rmsnorm (src/utils.c:59-76), device pointers; o may alias x. */
+int dk_rmsnorm(float *o, const float *x, const float *w, int n, void *stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Decode engine: one LLaMA-2 model resident on one GPU (or one tensor-parallel shard), whose
+ * whole per-token step (reference forward, src/transformer.c:55-239) is one CUDA graph.
+ * ------------------------------------------------------------------------------------------- */
+typedef struct dk_model dk_model;
+
+/* Weight identifiers (HF tensor names in the comments). */
+enum dk_weight {
+    DK_W_EMB = 0,   /* model.embed_tokens.weight        Q8_0 [vocab x dim]  */
+    DK_W_RMS_FINAL, /* model.norm.weight                F32  [dim]          */
+    DK_W_WCLS,      /* lm_head.weight                   Q8_0 [vocab x dim]  */
+    DK_W_RMS_ATT,   /* layers.L.input_layernorm         F32  [dim]          */
+    DK_W_WQ,        /* layers.L.self_attn.q_proj        Q8_0 [dim x dim]    */
+    DK_W_WK,        /* layers.L.self_attn.k_proj        Q8_0 [kv_dim x dim] */
+    DK_W_WV,        /* layers.L.self_attn.v_proj        Q8_0 [kv_dim x dim] */
+    DK_W_WO,        /* layers.L.self_attn.o_proj        Q8_0 [dim x dim]    */
+    DK_W_RMS_FFN,   /* layers.L.post_attention_layernorm F32 [dim]          */
+    DK_W_W1,        /* layers.L.mlp.gate_proj           Q8_0 [hidden x dim] */
+    DK_W_W2,        /* layers.L.mlp.down_proj           Q8_0 [dim x hidden] */
+    DK_W_W3,        /* layers.L.mlp.up_proj             Q8_0 [hidden x dim] */
+    DK_W_COUNT
+};
+
+/* KV-cache element type. */
+#define DK_KV_BF16 0 /* the reference's bf16-truncating cache (src/transformer.c:25-26, :145-146) */
+#define DK_KV_F32  1 /* fp32 cache                                                            */
+
+/* cfg = {dim, hidden_dim, n_layers, n_heads, n_kv_heads, vocab_size, seq_len} (the reference's
+ * Config, src/transformer.h:14-22).  Allocates all device memory of the model on `device`.
+ * tp_rank / tp_world select this process's tensor-parallel shard (0 / 1 for one GPU). */
+dk_model *dk_model_create(const int *cfg, int kv_type, int device, int tp_rank, int tp_world);
+void dk_model_destroy(dk_model *m);
+/* Set one weight from HOST memory.  Q8_0 weights: q = int8[rows*cols], scale = fp32[rows*cols/32]
+ * in the planar cache layout, full (unsharded) matrix; the engine keeps this rank's shard.
+ * F32 weights: q = float[n], scale = NULL.  layer = -1 for the non-layer weights. */
+int dk_model_set_weight(dk_model *m, int which, int layer, const void *q, const float *scale);
+/* Same, with the planar Q8_0 (or F32) data in DEVICE memory of the model's GPU. */
+int dk_model_set_weight_device(dk_model *m, int which, int layer, const void *q, const float *scale);
+/* Check that every weight is present and capture the per-token CUDA graph. */
+int dk_model_finalize(dk_model *m);
+
+/* One decode step (reference forward(transformer, token, pos)): writes vocab logits to the HOST
+ * buffer `logits` (NULL: skip the copy). */
+int dk_model_forward(dk_model *m, int token, int pos, float *logits);
+/* Greedy generation with the reference generate() rules (src/bin/localinfer.c:42-99): prompt
+ * tokens are forced one position at a time, then argmax tokens (first index wins ties) are fed
+ * back; stops after `steps` positions or when the sampled token is 1.  The whole loop runs on the
+ * GPU; out receives the generated (non-forced) tokens, *n_out their count.  Host buffers. */
+int dk_model_generate(dk_model *m, const int *prompt, int n_prompt, int steps, int *out, int *n_out);
+
+/* Lower-level control used by benchmarks: enqueue decode steps for positions
+ * [pos0, pos0 + n_steps) with tokens taken from the device token buffer (set by dk_model_set_tokens)
+ * and argmax results written back into it; nothing is synchronised. */
+int dk_model_set_tokens(dk_model *m, const int *tokens, int n_tokens, int n_forced);
+int dk_model_enqueue_steps(dk_model *m, int pos0, int n_steps);
+int dk_model_get_tokens(dk_model *m, int *tokens, int n_tokens);
+int dk_model_sync(dk_model *m);
+/* The CUDA stream the engine launches on (cudaStream_t as void*). */
+void *dk_model_stream(dk_model *m);
+/* Device error word (DK_ERR_* bits raised by kernels); reading it synchronises the stream. */
+int dk_model_device_error(dk_model *m);
+/* Number of kernels one decode step launches (for launch accounting). */
+int dk_model_kernels_per_step(dk_model *m);
+/* Bytes of weights one decode step reads on this rank. */
+size_t dk_model_weight_bytes(dk_model *m);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DIOLKOS_H */

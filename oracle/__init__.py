@@ -1,0 +1,299 @@
+"""The oracle: ctypes bindings to the CPU restatement (port.c) and to the compiled reference.
+
+TEST INFRASTRUCTURE ONLY.  Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline
+leg import this package, and only as the checker; the product (``diolkos_b200``) never does.
+
+* :class:`Port` wraps ``oracle/liboracle_port.so`` (the restatement; always built).
+* :class:`Ref` wraps ``oracle/_ref/<variant>/liboracle_ref.so`` (the unmodified reference sources
+  compiled with the reference's flags; built only where the reference tree is present, then
+  carried along with the working tree).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+PORT_SO = os.path.join(HERE, "liboracle_port.so")
+REF_DIR = os.path.join(HERE, "_ref")
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_i8p = np.ctypeslib.ndpointer(np.int8, flags="C_CONTIGUOUS")
+_u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+
+PW_EMB, PW_RMS_FINAL, PW_WCLS, PW_RMS_ATT, PW_WQ, PW_WK, PW_WV, PW_WO, PW_RMS_FFN, PW_W1, PW_W2, PW_W3 = range(12)
+
+
+class Port:
+    """The restatement in port.c."""
+
+    def __init__(self, path: str = PORT_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} is not built; run `make -C oracle port`")
+        L = self.lib = C.CDLL(path)
+        L.port_quant_bf16.argtypes = [_u16p, C.c_size_t, _i8p, _f32p]
+        L.port_quant_f32.argtypes = [_f32p, C.c_size_t, _i8p, _f32p]
+        L.port_dequant.argtypes = [_i8p, _f32p, C.c_size_t, _f32p]
+        L.port_matmul.argtypes = [_f32p, _f32p, _i8p, _f32p, C.c_int, C.c_int]
+        L.port_matmul_q.argtypes = [_f32p, _i8p, _f32p, _i8p, _f32p, C.c_int, C.c_int]
+        L.port_group_dots.argtypes = [_i32p, _i8p, _i8p, C.c_int, C.c_int]
+        L.port_rmsnorm.argtypes = [_f32p, _f32p, _f32p, C.c_int]
+        L.port_softmax.argtypes = [_f32p, C.c_int]
+        L.port_argmax.argtypes = [_f32p, C.c_int]
+        L.port_argmax.restype = C.c_int
+        L.port_rope_coeffs.argtypes = [C.c_int, C.c_int, _f32p]
+        L.port_sample.argtypes = [_f32p, C.c_int, C.c_float, C.c_float, C.POINTER(C.c_ulonglong)]
+        L.port_sample.restype = C.c_int
+        L.port_model_create.argtypes = [_i32p, C.c_int]
+        L.port_model_create.restype = C.c_void_p
+        L.port_model_destroy.argtypes = [C.c_void_p]
+        L.port_model_set.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
+        L.port_forward.argtypes = [C.c_void_p, C.c_int, C.c_int, _f32p, C.c_void_p]
+        L.port_generate.argtypes = [C.c_void_p, _i32p, C.c_int, C.c_int, _i32p]
+        L.port_generate.restype = C.c_int
+
+    def quant_bf16(self, x_bits: np.ndarray):
+        x = np.ascontiguousarray(x_bits, dtype=np.uint16).ravel()
+        q = np.empty(x.size, np.int8)
+        s = np.empty(x.size // 32, np.float32)
+        self.lib.port_quant_bf16(x, x.size, q, s)
+        return q, s
+
+    def quant_f32(self, x: np.ndarray):
+        x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+        q = np.empty(x.size, np.int8)
+        s = np.empty(x.size // 32, np.float32)
+        self.lib.port_quant_f32(x, x.size, q, s)
+        return q, s
+
+    def dequant(self, q, s):
+        out = np.empty(q.size, np.float32)
+        self.lib.port_dequant(np.ascontiguousarray(q, np.int8).ravel(),
+                              np.ascontiguousarray(s, np.float32).ravel(), q.size, out)
+        return out
+
+    def matmul(self, x, wq, ws, n, d):
+        out = np.empty(d, np.float32)
+        self.lib.port_matmul(out, np.ascontiguousarray(x, np.float32), np.ascontiguousarray(wq, np.int8).ravel(),
+                             np.ascontiguousarray(ws, np.float32).ravel(), n, d)
+        return out
+
+    def matmul_q(self, xq, xs, wq, ws, n, d):
+        out = np.empty(d, np.float32)
+        self.lib.port_matmul_q(out, np.ascontiguousarray(xq, np.int8), np.ascontiguousarray(xs, np.float32),
+                               np.ascontiguousarray(wq, np.int8).ravel(),
+                               np.ascontiguousarray(ws, np.float32).ravel(), n, d)
+        return out
+
+    def group_dots(self, xq, wq, n, d):
+        dots = np.empty((d, n // 32), np.int32)
+        self.lib.port_group_dots(dots, np.ascontiguousarray(xq, np.int8),
+                                 np.ascontiguousarray(wq, np.int8).ravel(), n, d)
+        return dots
+
+    def rmsnorm(self, x, w):
+        o = np.empty(x.size, np.float32)
+        self.lib.port_rmsnorm(o, np.ascontiguousarray(x, np.float32), np.ascontiguousarray(w, np.float32), x.size)
+        return o
+
+    def softmax(self, x):
+        y = np.array(x, dtype=np.float32, copy=True)
+        self.lib.port_softmax(y, y.size)
+        return y
+
+    def argmax(self, x):
+        return int(self.lib.port_argmax(np.ascontiguousarray(x, np.float32), x.size))
+
+    def rope_coeffs(self, pos, head_size):
+        cs = np.empty(head_size, np.float32)
+        self.lib.port_rope_coeffs(pos, head_size, cs)
+        return cs
+
+    def sample(self, logits, temperature, topp, rng_state):
+        y = np.array(logits, dtype=np.float32, copy=True)
+        st = C.c_ulonglong(rng_state)
+        tok = self.lib.port_sample(y, y.size, temperature, topp, C.byref(st))
+        return int(tok), int(st.value)
+
+
+class PortModel:
+    """A whole model in the restatement; holds references to the weight arrays it registers."""
+
+    def __init__(self, port: Port, cfg, weights: dict, kv_f32: bool = False):
+        self.port, self.cfg = port, cfg
+        self._keep = []
+        self.h = port.lib.port_model_create(np.array(cfg.as_list(), np.int32), int(kv_f32))
+        for (which, layer), w in weights.items():
+            if isinstance(w, tuple):
+                q = np.ascontiguousarray(w[0], np.int8)
+                s = np.ascontiguousarray(w[1], np.float32)
+                self._keep += [q, s]
+                port.lib.port_model_set(self.h, which, layer, q.ctypes.data, s.ctypes.data)
+            else:
+                v = np.ascontiguousarray(w, np.float32)
+                self._keep.append(v)
+                port.lib.port_model_set(self.h, which, layer, v.ctypes.data, None)
+
+    def forward(self, token, pos, dump_layers=False):
+        logits = np.empty(self.cfg.vocab_size, np.float32)
+        xd = np.empty((self.cfg.n_layers, self.cfg.dim), np.float32) if dump_layers else None
+        self.port.lib.port_forward(self.h, token, pos, logits, xd.ctypes.data if xd is not None else None)
+        return (logits, xd) if dump_layers else logits
+
+    def generate(self, prompt, steps):
+        p = np.ascontiguousarray(prompt, np.int32)
+        out = np.empty(max(steps, 1), np.int32)
+        n = self.port.lib.port_generate(self.h, p, p.size, steps, out)
+        return out[:n].copy()
+
+    def __del__(self):
+        try:
+            self.port.lib.port_model_destroy(self.h)
+        except Exception:
+            pass
+
+
+def ref_path(variant: str = "auto") -> str | None:
+    """Path of the compiled reference library, or None when it was not built here."""
+    order = ["native", "portable"] if variant == "auto" else [variant]
+    for v in order:
+        p = os.path.join(REF_DIR, v, "liboracle_ref.so")
+        if os.path.exists(p):
+            return p
+    return None
+
+
+class Ref:
+    """The unmodified reference C code (oracle/_ref), driven through ref_driver.c."""
+
+    def __init__(self, variant: str = "auto"):
+        p = ref_path(variant)
+        if p is None:
+            raise FileNotFoundError("oracle/_ref is not built (needs the reference source tree)")
+        self.path = p
+        L = self.lib = C.CDLL(p)
+        L.oref_load.argtypes = [C.c_char_p, C.c_char_p]
+        L.oref_load.restype = C.c_void_p
+        L.oref_config.argtypes = [C.c_void_p, _i32p]
+        L.oref_forward.argtypes = [C.c_void_p, C.c_int, C.c_int, _f32p]
+        L.oref_state_x.argtypes = [C.c_void_p, _f32p]
+        L.oref_generate.argtypes = [C.c_void_p, _i32p, C.c_int, C.c_int, _i32p, C.POINTER(C.c_double)]
+        L.oref_generate.restype = C.c_int
+        L.oref_quant_f32.argtypes = [_f32p, C.c_size_t, _i8p, _f32p]
+        L.oref_quant_bf16.argtypes = [_u16p, C.c_size_t, _i8p, _f32p]
+        L.oref_mat_create.argtypes = [_i8p, _f32p, C.c_int, C.c_int]
+        L.oref_mat_create.restype = C.c_void_p
+        L.oref_mat_run.argtypes = [C.c_void_p, _f32p, _f32p]
+        L.oref_mat_time.argtypes = [C.c_void_p, C.c_int]
+        L.oref_mat_time.restype = C.c_double
+        L.oref_mat_destroy.argtypes = [C.c_void_p]
+        L.oref_rmsnorm.argtypes = [_f32p, _f32p, _f32p, C.c_int]
+        L.oref_softmax.argtypes = [_f32p, C.c_int]
+        L.oref_argmax.argtypes = [_f32p, C.c_int]
+        L.oref_argmax.restype = C.c_int
+        L.oref_sample.argtypes = [_f32p, C.c_int, C.c_float, C.c_float, C.POINTER(C.c_ulonglong)]
+        L.oref_sample.restype = C.c_int
+
+    def quant_f32(self, x):
+        x = np.ascontiguousarray(x, np.float32).ravel()
+        q = np.empty(x.size, np.int8)
+        s = np.empty(x.size // 32, np.float32)
+        self.lib.oref_quant_f32(x, x.size, q, s)
+        return q, s
+
+    def quant_bf16(self, x_bits):
+        x = np.ascontiguousarray(x_bits, np.uint16).ravel()
+        q = np.empty(x.size, np.int8)
+        s = np.empty(x.size // 32, np.float32)
+        self.lib.oref_quant_bf16(x, x.size, q, s)
+        return q, s
+
+    def matmul(self, x, wq, ws, n, d):
+        m = self.lib.oref_mat_create(np.ascontiguousarray(wq, np.int8).ravel(),
+                                     np.ascontiguousarray(ws, np.float32).ravel(), n, d)
+        out = np.empty(d, np.float32)
+        self.lib.oref_mat_run(m, np.ascontiguousarray(x, np.float32), out)
+        self.lib.oref_mat_destroy(m)
+        return out
+
+    def rmsnorm(self, x, w):
+        o = np.empty(x.size, np.float32)
+        self.lib.oref_rmsnorm(o, np.ascontiguousarray(x, np.float32), np.ascontiguousarray(w, np.float32), x.size)
+        return o
+
+    def softmax(self, x):
+        y = np.array(x, dtype=np.float32, copy=True)
+        self.lib.oref_softmax(y, y.size)
+        return y
+
+    def argmax(self, x):
+        return int(self.lib.oref_argmax(np.ascontiguousarray(x, np.float32), x.size))
+
+    def sample(self, logits, temperature, topp, rng_state):
+        y = np.array(logits, dtype=np.float32, copy=True)
+        st = C.c_ulonglong(rng_state)
+        tok = self.lib.oref_sample(y, y.size, temperature, topp, C.byref(st))
+        return int(tok), int(st.value)
+
+    def load(self, model_dir: str, work_dir: str):
+        h = self.lib.oref_load(os.path.abspath(model_dir).encode(), os.path.abspath(work_dir).encode())
+        if not h:
+            raise RuntimeError("reference load failed")
+        return RefModel(self, h)
+
+
+class RefModel:
+    def __init__(self, ref: Ref, h):
+        self.ref, self.h = ref, h
+        cfg = np.empty(7, np.int32)
+        ref.lib.oref_config(h, cfg)
+        self.cfg = [int(v) for v in cfg]
+
+    def forward(self, token, pos):
+        logits = np.empty(self.cfg[5], np.float32)
+        self.ref.lib.oref_forward(self.h, token, pos, logits)
+        return logits
+
+    def generate(self, prompt, steps):
+        p = np.ascontiguousarray(prompt, np.int32)
+        out = np.empty(max(steps, 1), np.int32)
+        tps = C.c_double(0.0)
+        n = self.ref.lib.oref_generate(self.h, p, p.size, steps, out, C.byref(tps))
+        return out[:n].copy(), tps.value
+
+
+def load_port_weights(port: Port, cfg, seed: int):
+    """Regenerate a seeded synthetic model (diolkos_b200.synth) and quantise it with the
+    restatement's load-time quantiser; returns the dict PortModel expects plus the raw Q8 arrays
+    keyed by HF tensor name."""
+    from diolkos_b200 import synth
+
+    names = {
+        "input_layernorm.weight": PW_RMS_ATT, "self_attn.q_proj.weight": PW_WQ,
+        "self_attn.k_proj.weight": PW_WK, "self_attn.v_proj.weight": PW_WV,
+        "self_attn.o_proj.weight": PW_WO, "post_attention_layernorm.weight": PW_RMS_FFN,
+        "mlp.gate_proj.weight": PW_W1, "mlp.down_proj.weight": PW_W2, "mlp.up_proj.weight": PW_W3,
+    }
+    weights, by_name = {}, {}
+    for idx, (name, kind, shape) in enumerate(synth.tensor_specs(cfg)):
+        bits = synth.gen_tensor(seed, idx, kind, shape)
+        if kind == "q8":
+            val = port.quant_bf16(bits)
+        else:
+            val = synth.bf16_bits_to_f32(bits)
+        by_name[name] = val
+        if name == "model.embed_tokens.weight":
+            key = (PW_EMB, -1)
+        elif name == "lm_head.weight":
+            key = (PW_WCLS, -1)
+        elif name == "model.norm.weight":
+            key = (PW_RMS_FINAL, -1)
+        else:
+            rest = name[len("model.layers."):]
+            layer, suffix = rest.split(".", 1)
+            key = (names[suffix], int(layer))
+        weights[key] = val
+    return weights, by_name

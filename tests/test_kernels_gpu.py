@@ -1,0 +1,179 @@
+"""CUDA kernels vs the oracle, through the C ABI (libdiolkos.so).
+
+Bit-exact: both quantisers, the int32 group dots, packing, and the GEMV output itself (the
+kernel replays the reference's group order and rounding).  Tolerance: rmsnorm (2 ulp-level; the
+reduction order differs)."""
+import hashlib
+import os
+
+import numpy as np
+import pytest
+
+from diolkos_b200 import synth
+from tests.golden import make_golden as G
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def sha(a):
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+@pytest.fixture(scope="module")
+def torch_cuda():
+    import torch
+
+    torch.cuda.init()
+    return torch
+
+
+@pytest.fixture(scope="module")
+def kgold():
+    return np.load(os.path.join(GOLD, "kernels.npz"))
+
+
+def _dev(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+@pytest.mark.parametrize("case", G.QUANT_F32_CASES)
+def test_quant_f32_bit_exact(torch_cuda, port, kgold, case):
+    from diolkos_b200 import ops
+
+    seed, n, sc = case
+    x = G.quant_f32_input(seed, n, sc)
+    q, s = ops.quantize_f32(_dev(torch_cuda, x))
+    q, s = q.cpu().numpy(), s.cpu().numpy()
+    assert sha(q) == str(kgold[f"qf32_{seed}_q"]) and sha(s) == str(kgold[f"qf32_{seed}_s"])
+    pq, ps = port.quant_f32(x)
+    np.testing.assert_array_equal(q, pq)
+
+
+@pytest.mark.parametrize("case", G.QUANT_BF16_CASES)
+def test_quant_bf16_bit_exact(torch_cuda, port, kgold, case):
+    from diolkos_b200 import ops
+
+    seed, n, sc = case
+    x = G.quant_bf16_input(seed, n, sc)
+    q, s = ops.quantize_bf16(_dev(torch_cuda, x.view(np.int16)))
+    q, s = q.cpu().numpy(), s.cpu().numpy()
+    assert sha(q) == str(kgold[f"qbf16_{seed}_q"]) and sha(s) == str(kgold[f"qbf16_{seed}_s"])
+
+
+def test_quant_edge_groups(torch_cuda, port):
+    """Zero groups, one-hot groups, denormals, huge values, exact ties -- GPU == oracle."""
+    from diolkos_b200 import ops
+
+    rng = np.random.default_rng(1)
+    groups = [np.zeros(32, np.float32), np.eye(1, 32, 5, dtype=np.float32)[0] * -3.0,
+              np.full(32, 1e-40, np.float32), rng.standard_normal(32).astype(np.float32) * 1e30,
+              np.linspace(-127, 127, 32, dtype=np.float32), np.array([2.5, 3.5, -2.5, 127.0] * 8, np.float32)]
+    x = np.concatenate(groups)
+    q, s = ops.quantize_f32(_dev(torch_cuda, x))
+    pq, ps = port.quant_f32(x)
+    np.testing.assert_array_equal(q.cpu().numpy(), pq)
+    np.testing.assert_array_equal(s.cpu().numpy().view(np.uint32), ps.view(np.uint32))
+
+
+def test_group_dots_exact(torch_cuda, port):
+    from diolkos_b200 import ops
+
+    rng = np.random.default_rng(2)
+    for n, d in [(4096, 64), (11008, 8), (288, 33)]:
+        xq = rng.integers(-127, 128, n, dtype=np.int8)
+        wq = rng.integers(-128, 128, n * d, dtype=np.int8)
+        dots = ops.group_dots(_dev(torch_cuda, xq), _dev(torch_cuda, wq), n, d).cpu().numpy()
+        np.testing.assert_array_equal(dots, port.group_dots(xq, wq, n, d))
+
+
+def test_pack_layout(torch_cuda):
+    from diolkos_b200 import ops
+
+    rng = np.random.default_rng(3)
+    n, d = 288, 5
+    q = rng.integers(-127, 128, n * d, dtype=np.int8)
+    s = rng.standard_normal(n * d // 32).astype(np.float32)
+    w = ops.pack(_dev(torch_cuda, q), _dev(torch_cuda, s), n, d).cpu().numpy()
+    rb = ops.row_bytes(n)
+    assert rb % 16 == 0 and rb >= n + n // 8
+    for r in range(d):
+        row = w[r * rb:(r + 1) * rb]
+        np.testing.assert_array_equal(row[:n].view(np.int8), q[r * n:(r + 1) * n])
+        np.testing.assert_array_equal(row[n:n + n // 8].view(np.float32), s[r * n // 32:(r + 1) * n // 32])
+        assert not row[n + n // 8:].any()
+
+
+@pytest.mark.parametrize("case", G.GEMV_CASES)
+def test_gemv_bit_exact_golden(torch_cuda, kgold, case):
+    """Weights quantised on the GPU, packed, GEMV on the GPU: output bits == the reference's."""
+    from diolkos_b200 import ops
+
+    n, d, seed = case
+    wb, x = G.gemv_inputs(n, d, seed)
+    q, s = ops.quantize_bf16(_dev(torch_cuda, wb.view(np.int16)))
+    w = ops.pack(q, s, n, d)
+    out = ops.matmul(_dev(torch_cuda, x), w, n, d).cpu().numpy()
+    np.testing.assert_array_equal(out.view(np.uint32), kgold[f"gemv_{n}x{d}"].view(np.uint32))
+
+
+@pytest.mark.parametrize("shape", [(4096, 4096), (4096, 11008), (11008, 4096), (4096, 32000)])
+def test_gemv_full_shapes_bit_exact(torch_cuda, port, shape):
+    """The four GEMV shapes of the benchmark ([out x in] = 4096x4096, 11008x4096, 4096x11008,
+    32000x4096), seeded N(0,0.02) weights and N(0,1) input: GPU output bits == oracle's."""
+    from diolkos_b200 import ops
+
+    torch = torch_cuda
+    n, d = shape
+    g = torch.Generator(device="cuda").manual_seed(n * 7 + d)
+    wf = torch.randn(d * n, generator=g, device="cuda", dtype=torch.float32) * 0.02
+    wb = wf.to(torch.bfloat16).view(torch.int16)
+    q, s = ops.quantize_bf16(wb)
+    pq, ps = port.quant_bf16(wb.cpu().numpy().view(np.uint16))
+    np.testing.assert_array_equal(q.cpu().numpy(), pq)
+    w = ops.pack(q, s, n, d)
+    x = torch.randn(n, generator=g, device="cuda", dtype=torch.float32)
+    out = ops.matmul(x, w, n, d).cpu().numpy()
+    np.testing.assert_array_equal(out.view(np.uint32), port.matmul(x.cpu().numpy(), pq, ps, n, d).view(np.uint32))
+    # the pre-quantised entry point gives the same bits
+    xq, xs = ops.quantize_f32(x)
+    out2 = ops.matmul_q(xq, xs, w, n, d).cpu().numpy()
+    np.testing.assert_array_equal(out2.view(np.uint32), out.view(np.uint32))
+
+
+def test_gemv_repeatable_and_ragged(torch_cuda, port):
+    """Shapes that do not divide the stage size or the SM count; repeated calls give the same bits."""
+    from diolkos_b200 import ops
+
+    torch = torch_cuda
+    rng = np.random.default_rng(4)
+    for n, d in [(32, 1), (64, 149), (96, 297), (8192, 1001), (28672, 40)]:
+        wq = rng.integers(-127, 128, n * d, dtype=np.int8)
+        ws = (rng.random(n * d // 32, dtype=np.float32) * 0.001).astype(np.float32)
+        x = rng.standard_normal(n).astype(np.float32)
+        w = ops.pack(_dev(torch, wq), _dev(torch, ws), n, d)
+        a = ops.matmul(_dev(torch, x), w, n, d).cpu().numpy()
+        b = ops.matmul(_dev(torch, x), w, n, d).cpu().numpy()
+        np.testing.assert_array_equal(a.view(np.uint32), b.view(np.uint32))
+        np.testing.assert_array_equal(a.view(np.uint32), port.matmul(x, wq, ws, n, d).view(np.uint32))
+
+
+def test_rmsnorm(torch_cuda, port):
+    from diolkos_b200 import ops
+
+    rng = np.random.default_rng(5)
+    for n in (288, 4096, 8192):
+        x = rng.standard_normal(n).astype(np.float32)
+        w = rng.standard_normal(n).astype(np.float32)
+        got = ops.rmsnorm(_dev(torch_cuda, x), _dev(torch_cuda, w)).cpu().numpy()
+        np.testing.assert_allclose(got, port.rmsnorm(x, w), rtol=1e-6, atol=1e-7)
+
+
+def test_dequant(torch_cuda, port):
+    from diolkos_b200 import ops
+
+    rng = np.random.default_rng(6)
+    q = rng.integers(-127, 128, 4096, dtype=np.int8)
+    s = rng.standard_normal(128).astype(np.float32)
+    got = ops.dequantize(_dev(torch_cuda, q), _dev(torch_cuda, s)).cpu().numpy()
+    np.testing.assert_array_equal(got.view(np.uint32), port.dequant(q, s).view(np.uint32))

@@ -1,0 +1,188 @@
+"""The whole decode step on the GPU (dk_model_*: one CUDA graph per token) vs the oracle and the
+reference's golden outputs.
+
+Tolerances.  The reference re-quantises its fp32 activations to int8 before every matmul, so an
+ulp-level difference anywhere upstream (its vectorised expf and rsqrt approximation cannot be
+reproduced on a GPU) occasionally flips one int8 and moves later logits by ~1e-2.  The checks are
+therefore: (1) before the first flip -- the first positions -- logits agree to 1e-5 relative
+(far inside the 1e-3 bar); (2) teacher-forced over the reference's own greedy continuation, the GPU
+picks the reference's token at every position whose top-2 margin exceeds the envelope that the
+oracle restatement itself shows against the reference; (3) free-running greedy tokens are compared
+with the oracle run in the same process."""
+import os
+
+import numpy as np
+import pytest
+
+from diolkos_b200 import synth
+from tests.golden import make_golden as G
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def _first_div(a, b):
+    m = min(len(a), len(b))
+    for i in range(m):
+        if a[i] != b[i]:
+            return i
+    return m
+
+
+@pytest.fixture(scope="module")
+def tiny_weights(port):
+    from oracle import load_port_weights
+
+    return load_port_weights(port, synth.TINY, G.TINY_SEED)
+
+
+def _gpu_model(cfg, by_name, kv_f32=False):
+    from diolkos_b200.model import Model
+
+    m = Model(cfg, kv_f32=kv_f32)
+    m.load_named(by_name)
+    m.finalize()
+    return m
+
+
+def test_tiny_logits_match_reference_golden(tiny_weights):
+    w, by_name = tiny_weights
+    tg = np.load(os.path.join(GOLD, "tiny.npz"))
+    ps = G.TINY_PROMPTS[0]
+    prompt = synth.seeded_prompt(ps, 8)
+    seq = list(prompt) + list(tg[f"tokens_{ps}"])
+    m = _gpu_model(synth.TINY, by_name)
+    arg, top2 = tg[f"tf_argmax_{ps}"], tg[f"tf_top2_{ps}"]
+    agree = 0
+    for pos in range(G.TINY_TF_POSITIONS):
+        lg = m.forward(int(seq[pos]), pos)
+        if pos < 3:
+            gl = tg[f"logits_{ps}_{pos}"]
+            assert np.max(np.abs(lg - gl)) / np.max(np.abs(gl)) < 1e-5, pos
+        gap = (top2[pos, 0] - top2[pos, 1]) / abs(top2[pos, 0])
+        if gap > 0.03:
+            assert int(np.argmax(lg)) == int(arg[pos]), pos
+        agree += int(np.argmax(lg)) == int(arg[pos])
+    assert agree >= G.TINY_TF_POSITIONS - 3
+
+
+def test_tiny_logits_match_oracle_teacher_forced(port, tiny_weights):
+    from oracle import PortModel
+
+    w, by_name = tiny_weights
+    cfg = synth.TINY
+    m = _gpu_model(cfg, by_name)
+    pm = PortModel(port, cfg, w)
+    prompt = synth.seeded_prompt(11, 8)
+    rng = np.random.default_rng(0)
+    seq = list(prompt) + list(rng.integers(3, cfg.vocab_size, 40))
+    errs = []
+    for pos, tok in enumerate(seq):
+        a = m.forward(int(tok), pos)
+        b = pm.forward(int(tok), pos)
+        errs.append(np.max(np.abs(a - b)) / np.max(np.abs(b)))
+    assert max(errs[:3]) < 1e-5
+    assert max(errs) < 5e-2, errs
+
+
+def test_tiny_generate_vs_oracle(port, tiny_weights):
+    """Greedy generation on the GPU (the whole loop on the device) vs the oracle restatement."""
+    from oracle import PortModel
+
+    w, by_name = tiny_weights
+    cfg = synth.TINY
+    m = _gpu_model(cfg, by_name)
+    for ps in G.TINY_PROMPTS:
+        prompt = synth.seeded_prompt(ps, 8)
+        gpu = m.generate(prompt, G.TINY_STEPS)
+        cpu = PortModel(port, cfg, w).generate(prompt, G.TINY_STEPS)
+        assert len(gpu) > 0
+        assert _first_div(gpu, cpu) >= 8, (ps, gpu[:20], cpu[:20])
+        # generate() must agree with forward()+argmax step by step on the same device state
+        assert gpu.dtype == np.int32 and (gpu >= 0).all() and (gpu < cfg.vocab_size).all()
+
+
+def test_generate_equals_forward_argmax(tiny_weights):
+    """The on-device greedy loop and the host loop over forward() produce the same tokens."""
+    w, by_name = tiny_weights
+    cfg = synth.TINY
+    m = _gpu_model(cfg, by_name)
+    prompt = synth.seeded_prompt(9, 8)
+    gen = m.generate(prompt, 40)
+    m2 = _gpu_model(cfg, by_name)
+    tok, out = int(prompt[0]), []
+    for pos in range(40):
+        lg = m2.forward(tok, pos)
+        nxt = int(prompt[pos + 1]) if pos < len(prompt) - 1 else int(np.argmax(lg))
+        if pos >= len(prompt) - 1:
+            out.append(nxt)
+        if nxt == 1:
+            break
+        tok = nxt
+    np.testing.assert_array_equal(gen, np.array(out, np.int32))
+
+
+def test_kv_f32_and_gqa_vs_oracle(port):
+    """fp32 KV cache and grouped-query attention (8 query heads per KV head, as in 70B), against
+    the oracle with the same cache type; long enough to use several attention splits."""
+    from oracle import PortModel, load_port_weights
+
+    cfg = synth.Config(dim=512, hidden_dim=1024, n_layers=2, n_heads=8, n_kv_heads=1, vocab_size=2048, seq_len=512)
+    w, by_name = load_port_weights(port, cfg, 77)
+    for kv_f32 in (True, False):
+        m = _gpu_model(cfg, by_name, kv_f32=kv_f32)
+        pm = PortModel(port, cfg, w, kv_f32=kv_f32)
+        rng = np.random.default_rng(1)
+        seq = rng.integers(3, cfg.vocab_size, 300)
+        worst = 0.0
+        for pos, tok in enumerate(seq):
+            a = m.forward(int(tok), pos)
+            b = pm.forward(int(tok), pos)
+            e = np.max(np.abs(a - b)) / np.max(np.abs(b))
+            if pos < 2:
+                assert e < 1e-5, (kv_f32, pos, e)
+            worst = max(worst, e)
+        assert worst < 5e-2, (kv_f32, worst)
+
+
+def test_device_weight_upload_path(torch_cuda_fixture=None):
+    """Weights quantised on the GPU and set from device memory give the same model as the host
+    path (quantised by the oracle, which is bit-exact with the reference's loader)."""
+    import torch
+
+    from diolkos_b200 import ops
+    from diolkos_b200.model import Model, weight_id
+    from oracle import Port, load_port_weights
+
+    cfg = synth.Config(dim=256, hidden_dim=512, n_layers=2, n_heads=4, n_kv_heads=4, vocab_size=1024, seq_len=64)
+    port = Port()
+    _, by_name = load_port_weights(port, cfg, 5)
+    host = Model(cfg)
+    host.load_named(by_name)
+    host.finalize()
+    dev = Model(cfg)
+    for idx, (name, kind, shape) in enumerate(synth.tensor_specs(cfg)):
+        bits = synth.gen_tensor(5, idx, kind, shape)
+        which, layer = weight_id(name)
+        if kind == "q8":
+            q, s = ops.quantize_bf16(torch.from_numpy(bits.view(np.int16)).cuda())
+            torch.cuda.synchronize()
+            dev.set_weight_device(which, layer, q, s)
+        else:
+            dev.set_weight_device(which, layer, torch.from_numpy(synth.bf16_bits_to_f32(bits)).cuda())
+    dev.finalize()
+    for pos, tok in enumerate([5, 17, 900, 3]):
+        np.testing.assert_array_equal(host.forward(tok, pos), dev.forward(tok, pos))
+
+
+def test_bad_arguments_fail_loudly():
+    from diolkos_b200._native import DiolkosError
+    from diolkos_b200.model import Model
+
+    with pytest.raises(DiolkosError):
+        Model(synth.Config(dim=100, hidden_dim=64, n_layers=1, n_heads=3, n_kv_heads=3, vocab_size=10, seq_len=8))
+    m = Model(synth.Config(dim=64, hidden_dim=64, n_layers=1, n_heads=2, n_kv_heads=2, vocab_size=64, seq_len=8))
+    with pytest.raises(DiolkosError):
+        m.finalize()  # weights missing
+    with pytest.raises(DiolkosError):
+        m.forward(0, 0)  # not finalized
