@@ -1,0 +1,433 @@
+#!/usr/bin/env python3
+"""Benchmark: batch-1 Q8_0 decode of a LLaMA-2-7B-shape model on B200, plus the Q8_0 GEMV shapes.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload decode|gemv]
+
+Decode workload (N=1): LLaMA-2-7B shape (dim 4096, hidden 11008, 32 layers, 32 heads, 32 KV heads,
+vocab 32000, seq_len 4096), random-init weights N(0, 0.02) generated on the GPU from a seed, rounded
+to bf16 and quantised to Q8_0 by the library's load-time quantiser; fp32 KV cache.  One step = a
+seeded 32-token prompt forced position by position, then 256 greedy tokens (287 decode positions).
+`value` = generated tokens per second of the 256-token decode phase, timed with CUDA events on the
+engine's stream, inputs resident in HBM; the weights (7.4 GB) are far larger than L2, so every token
+streams them from HBM.  `e2e` = the same tokens per second through the C-ABI generate entry point
+(dk_model_generate: host prompt in, host tokens out, copies included), wall clock, prompt positions
+included.
+
+Reference arm (--impl reference): the reference's own CPU forward (its unmodified sources compiled
+with its own flags, oracle/_ref) on the host cores, on a bounded sample of the same workload: the
+7B-shape model with 1 and with 3 layers (Q8_0 cache files written from the same distribution),
+per-token time extrapolated linearly to 32 layers.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PROMPT_LEN = 32
+GEN_LEN = 256
+SEED = 20260
+GEMV_SHAPES = [(4096, 4096), (11008, 4096), (4096, 11008), (32000, 4096)]  # [out x in]
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["decode", "gemv"], default="decode")
+    ap.add_argument("--kv", choices=["f32", "bf16"], default="f32")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------ clocks during the timed region
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-f", self.path], stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        try:
+            with open(self.path) as f:
+                for line in f:
+                    parts = [x.strip() for x in line.split(",")]
+                    if len(parts) >= 9:
+                        rows.append(parts)
+        finally:
+            os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for name, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+# ------------------------------------------------------------------ model construction on the GPU
+def weight_bytes_per_token(cfg) -> float:
+    """Algorithmic bytes a decode step reads: every matmul weight at 1.125 B per value (int8 + fp32
+    scale per 32), the activation vectors, one embedding row, the norm weights."""
+    mats = [(cfg.dim, cfg.dim), (cfg.kv_dim, cfg.dim), (cfg.kv_dim, cfg.dim), (cfg.dim, cfg.dim),
+            (cfg.hidden_dim, cfg.dim), (cfg.dim, cfg.hidden_dim), (cfg.hidden_dim, cfg.dim)]
+    per_layer = sum(d * n * 1.125 + n * 1.125 + d * 4 for d, n in mats) + 2 * cfg.dim * 4
+    cls = cfg.vocab_size * cfg.dim * 1.125 + cfg.dim * 1.125 + cfg.vocab_size * 4
+    return cfg.n_layers * per_layer + cls + cfg.dim * 1.125 + cfg.dim * 4
+
+
+def kv_bytes_read(cfg, pos0: int, pos1: int, elem: int) -> float:
+    """KV-cache bytes the attention reads over positions [pos0, pos1): 2 * (pos+1) * kv_dim per layer."""
+    tot = sum(pos + 1 for pos in range(pos0, pos1))
+    return 2.0 * tot * cfg.kv_dim * elem * cfg.n_layers
+
+
+def build_model(cfg, kv_f32: bool, seed: int):
+    import torch
+
+    from diolkos_b200 import ops, synth
+    from diolkos_b200.model import Model, weight_id
+
+    m = Model(cfg, kv_f32=kv_f32)
+    g = torch.Generator(device="cuda")
+    for idx, (name, kind, shape) in enumerate(synth.tensor_specs(cfg)):
+        which, layer = weight_id(name)
+        n = 1
+        for s in shape:
+            n *= s
+        if kind == "norm":
+            m.set_weight_device(which, layer, torch.ones(n, device="cuda", dtype=torch.float32))
+            continue
+        g.manual_seed(seed * 1000003 + idx)
+        w = (torch.randn(n, generator=g, device="cuda", dtype=torch.float32) * 0.02).to(torch.bfloat16)
+        q, s = ops.quantize_bf16(w.view(torch.int16))
+        del w
+        torch.cuda.synchronize()
+        m.set_weight_device(which, layer, q, s)
+        del q, s
+    m.finalize()
+    return m
+
+
+# ------------------------------------------------------------------ CPU baseline: the reference
+def _write_cpu_model(dirpath, cfg, seed, port, layers_from=None):
+    """Q8_0 cache files + header-only safetensors for the reference loader (quantised with the
+    oracle's load-time quantiser, bit-exact with the reference's)."""
+    from diolkos_b200 import synth
+
+    name = os.path.basename(dirpath)
+    synth.write_model(dirpath, cfg, seed, header_only=True)
+    cache = os.path.join(os.path.dirname(dirpath), "cache", name)
+    os.makedirs(cache, exist_ok=True)
+    for idx, (tname, kind, shape) in enumerate(synth.tensor_specs(cfg)):
+        if layers_from is not None:
+            src_f = os.path.join(layers_from, f"{tname}-{'Q8_0' if kind == 'q8' else 'F32'}.tensor")
+            dst_f = os.path.join(cache, os.path.basename(src_f))
+            if os.path.exists(src_f):
+                os.symlink(src_f, dst_f)
+                continue
+        bits = synth.gen_tensor(seed, idx, kind, shape)
+        if kind == "q8":
+            q, s = port.quant_bf16(bits)
+            synth.write_q8_cache(cache, tname, q, s)
+        else:
+            synth.write_f32_cache(cache, tname, synth.bf16_bits_to_f32(bits))
+    return cache
+
+
+class CpuReference:
+    """Bounded sample of the 7B decode on the reference's CPU path (oracle/_ref, all host cores)."""
+
+    def __init__(self, cfg, positions: int = 12):
+        os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
+        from oracle import Port, Ref, ref_path
+
+        self.kind = "reference" if ref_path() else "port"
+        self.cores = int(os.environ["OMP_NUM_THREADS"])
+        self.tmp = tempfile.mkdtemp(prefix="dk_cpu_")
+        port = Port()
+        c3 = cfg.replace(n_layers=3)
+        c1 = cfg.replace(n_layers=1)
+        d3 = os.path.join(self.tmp, "llama7b_l3")
+        d1 = os.path.join(self.tmp, "llama7b_l1")
+        cache3 = _write_cpu_model(d3, c3, SEED, port)
+        _write_cpu_model(d1, c1, SEED, port, layers_from=cache3)
+        self.positions = positions
+        from diolkos_b200 import synth
+
+        self.prompt = synth.seeded_prompt(SEED, PROMPT_LEN)
+        if self.kind == "reference":
+            ref = Ref()
+            self.m1 = ref.load(d1, self.tmp)
+            self.m3 = ref.load(d3, self.tmp)
+        else:  # the restatement, when the reference build is not present
+            from oracle import PortModel, load_port_weights
+
+            self.m1 = PortModel(port, c1, load_port_weights(port, c1, SEED)[0])
+            self.m3 = PortModel(port, c3, load_port_weights(port, c3, SEED)[0])
+        self.n_layers = cfg.n_layers
+
+    def _tok_time(self, m) -> float:
+        toks = list(self.prompt[: self.positions])
+        t0 = time.perf_counter()
+        for pos, tok in enumerate(toks):
+            m.forward(int(tok), pos)
+        return (time.perf_counter() - t0) / len(toks)
+
+    def sample(self) -> float:
+        """Extrapolated decode tokens/s of the 32-layer model."""
+        t1 = self._tok_time(self.m1)
+        t3 = self._tok_time(self.m3)
+        per_layer = (t3 - t1) / 2.0
+        t32 = t1 + (self.n_layers - 1) * per_layer
+        return 1.0 / t32
+
+    def describe(self) -> str:
+        return (f"7B-shape model with 1 and 3 layers (Q8_0, bf16 KV as in the reference), {self.positions} "
+                f"positions each; per-token time extrapolated linearly to {self.n_layers} layers")
+
+
+# ------------------------------------------------------------------ GEMV microbenchmark (config 2)
+def gemv_bench(reps: int = 50):
+    import torch
+
+    from diolkos_b200 import ops
+
+    out = {}
+    for d, n in GEMV_SHAPES:
+        rb = ops.row_bytes(n)
+        copies = max(2, int(3 * 126e6 // (d * rb)) + 1)
+        g = torch.Generator(device="cuda").manual_seed(d * 31 + n)
+        ws = []
+        for _ in range(copies):
+            wf = (torch.randn(d * n, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+            q, s = ops.quantize_bf16(wf.view(torch.int16))
+            ws.append(ops.pack(q, s, n, d))
+            del wf, q, s
+        x = torch.randn(n, generator=g, device="cuda")
+        y = torch.empty(d, device="cuda")
+        for i in range(5):
+            ops.matmul(x, ws[i % copies], n, d, y)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(reps):
+            ops.matmul(x, ws[i % copies], n, d, y)
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / reps
+        alg = d * n * 1.125 + n * 1.125 + d * 4
+        out[f"{d}x{n}"] = {"us": round(us, 2), "GBps": round(alg / us / 1e3, 1)}
+        del ws
+        torch.cuda.empty_cache()
+    return out
+
+
+# ------------------------------------------------------------------ main arms
+def run_reference(args):
+    from diolkos_b200 import synth
+
+    cfg = synth.LLAMA7B
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    cpu = CpuReference(cfg)
+    for _ in range(args.warmup):
+        cpu.sample()
+    vals = [cpu.sample() for _ in range(args.steps)]
+    v = statistics.mean(vals)
+    line = {
+        "impl": "reference", "metric": "Q8_0 decode tok/s batch 1", "value": round(v, 3), "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 / v, 2),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic (seeded N(0,0.02) weights, seeded prompt)",
+        "config": {"workload": "llama2-7b-shape q8_0 decode, 32-token prompt + 256 greedy tokens",
+                   "model": "llama2-7b-shape", "kv_cache": "bf16 (the reference's)"},
+        "cpu_baseline": {"value": round(v, 3), "unit": "tok/s", "cores": cpu.cores, "kind": cpu.kind,
+                         "sample": cpu.describe()},
+        "e2e": {"value": round(v, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_decode(args):
+    import torch
+
+    from diolkos_b200 import synth
+
+    cfg = synth.LLAMA7B
+    kv_f32 = args.kv == "f32"
+    torch.cuda.set_device(0)
+    m = build_model(cfg, kv_f32, SEED)
+    stream = torch.cuda.ExternalStream(m.stream)
+    prompt = synth.seeded_prompt(SEED, PROMPT_LEN, cfg.vocab_size)
+    P, G = PROMPT_LEN, GEN_LEN
+
+    def one_step(record=None):
+        m.set_tokens(prompt, n_forced=P)
+        m.enqueue_steps(0, P - 1)
+        if record:
+            record[0].record(stream)
+        m.enqueue_steps(P - 1, G)
+        if record:
+            record[1].record(stream)
+
+    for _ in range(args.warmup):
+        one_step()
+    m.sync()
+    if m.device_error():
+        raise RuntimeError(f"device error word 0x{m.device_error():x} after warm-up")
+
+    sampler = ClockSampler(0)
+    sampler.start()
+    torch.cuda.synchronize()
+    m.sync()
+    t_all0 = time.perf_counter()
+    evs = []
+    for _ in range(args.steps):
+        e = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        one_step(e)
+        evs.append(e)
+    m.sync()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t_all0
+    clocks = sampler.stop()
+    decode_ms = sum(a.elapsed_time(b) for a, b in evs)
+    if m.device_error():
+        raise RuntimeError(f"device error word 0x{m.device_error():x}")
+    toks = m.get_tokens(P + G)
+
+    value = G * args.steps / (decode_ms / 1e3)
+    ms_per_tok = decode_ms / (G * args.steps)
+    elem = 4 if kv_f32 else 2
+    bytes_tok = weight_bytes_per_token(cfg) + kv_bytes_read(cfg, P - 1, P - 1 + G, elem) / G
+    hbm, peak_kind = peaks()
+    achieved = bytes_tok / (ms_per_tok / 1e3) / 1e9
+
+    # end to end through the public C-ABI generate entry point (host buffers)
+    e2e_times = []
+    n_gen = 0
+    for _ in range(max(1, args.steps)):
+        t0 = time.perf_counter()
+        gen = m.generate(prompt, P - 1 + G)
+        e2e_times.append(time.perf_counter() - t0)
+        n_gen = len(gen)
+    e2e = n_gen * len(e2e_times) / sum(e2e_times)
+
+    gemv = gemv_bench()
+    cpu = None
+    if not args.no_cpu_baseline:
+        try:
+            cb = CpuReference(cfg)
+            cb.sample()
+            v = statistics.mean(cb.sample() for _ in range(2))
+            cpu = {"value": round(v, 3), "unit": "tok/s", "cores": cb.cores, "kind": cb.kind, "sample": cb.describe()}
+        except Exception as ex:  # the baseline is reported, never required
+            cpu = {"value": None, "unit": "tok/s", "cores": os.cpu_count(), "kind": "reference",
+                   "sample": f"not run: {ex}"}
+
+    line = {
+        "metric": "Q8_0 decode tok/s batch 1", "value": round(value, 2), "unit": "tok/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(decode_ms / args.steps, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic (seeded N(0,0.02) weights, seeded prompt)",
+        "config": {"workload": "llama2-7b-shape q8_0 decode: 32-token prompt, then 256 greedy tokens timed",
+                   "model": "llama2-7b-shape", "dim": cfg.dim, "hidden": cfg.hidden_dim, "layers": cfg.n_layers,
+                   "heads": cfg.n_heads, "kv_heads": cfg.n_kv_heads, "vocab": cfg.vocab_size,
+                   "seq_len": cfg.seq_len, "kv_cache": args.kv, "global_batch": 1, "parallelism": "single GPU",
+                   "l2": "weights (7.4 GB) exceed L2; every token streams them from HBM"},
+        "ms_per_token": round(ms_per_tok, 4),
+        "gpu_launches": m.kernels_per_step * G * args.steps,
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "traffic": None,
+                     "what": f"whole decode step: weight + KV bytes per token ({bytes_tok / 1e9:.3f} GB) / "
+                             f"time per token; peak = {peak_kind} HBM copy bandwidth"},
+        "gemv": gemv,
+        "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * P + 12,
+                "d2h_bytes_per_step": 4 * (P + G) + 4,
+                "how": "dk_model_generate (C ABI): host prompt -> host tokens, wall clock, prompt positions included"},
+        "cpu_baseline": cpu,
+        "clocks": clocks,
+        "wall_s_timed_region": round(wall, 3),
+        "tokens_sample": [int(t) for t in toks[P:P + 8]],
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_gemv(args):
+    import torch
+
+    torch.cuda.set_device(0)
+    g = gemv_bench(reps=max(20, args.steps * 10))
+    hbm, kind = peaks()
+    best = max(g.items(), key=lambda kv: kv[1]["GBps"])
+    line = {"metric": "Q8_0 GEMV HBM GB/s", "value": best[1]["GBps"], "unit": "GB/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": "isolated Q8_0 GEMV, batch 1", "shapes": g}, "peak": hbm, "peak_kind": kind}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    if args.gpus > 1:
+        print(json.dumps({"error": "tensor-parallel decode is not available in this build"}), flush=True)
+        return 1
+    if args.workload == "gemv":
+        return run_gemv(args)
+    return run_decode(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

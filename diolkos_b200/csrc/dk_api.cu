@@ -111,6 +111,8 @@ static int matmul_common(float *out, const float *x, const int8_t *xq, const flo
         a.xs = xs;
     }
     a.epi = EPI_STORE;
+    if (!gemv_supported(n, d, EPI_STORE))
+        return set_error(DK_ERR_INVALID, "matmul: unsupported shape n=%d d=%d (n must be a multiple of 32, <= 32768)", n, d);
     const GemvPlan p = plan_gemv(n, d, EPI_STORE, current_num_sms());
     return cuda_status(launch_gemv(a, p, (cudaStream_t)stream, false), "matmul");
 }

@@ -25,7 +25,7 @@ enum GemvEpi : int {
 };
 
 struct GemvArgs {
-    const uint8_t *w = nullptr;  // packed rows (dk_q8_row_bytes(n) each)
+    const uint8_t *w = nullptr;  // packed rows (q8_row_bytes(n) each)
     int n = 0, d = 0;
     int pro = PRO_F32, epi = EPI_STORE;
     const float *x = nullptr;       // PRO_F32 / PRO_RMS input; PRO_EMB_RMS: x is written here
@@ -45,18 +45,97 @@ struct GemvArgs {
 };
 
 struct GemvPlan {
-    int R = 1;        // rows per stage
-    int S = 8;        // stages == consumer warps
-    int RS = 0;       // packed row bytes
-    int grid = 1;
-    size_t smem = 0;  // dynamic shared memory bytes
-    size_t ring = 0;  // bytes of the stage ring
-    size_t stage = 0; // bytes of one stage
+    int RS = 0;        // packed row bytes
+    int grid = 1;      // CTAs (one contiguous row range each)
+    int CW = 4;        // consumer warps
+    int SPW = 1;       // stage slots per consumer warp (warp w owns slots w*SPW .. w*SPW+SPW-1)
+    size_t stage = 0;  // bytes of one stage (R packed rows)
+    size_t ring = 0;   // bytes of all stages
+    size_t xoff = 0;   // shared-memory offset of the activation
+    size_t smem = 0;   // dynamic shared memory bytes
 };
 
-// Packed row bytes of an n-column Q8_0 matrix: n int8 + n/32 fp32 scales, padded to 16 bytes.
-__host__ __device__ inline size_t q8_row_bytes(int n) { return ((size_t)n + (size_t)n / 8 + 15) & ~(size_t)15; }
-GemvPlan plan_gemv(int n, int d, int epi, int num_sms, size_t smem_budget = 0);
+// ---- packed Q8_0 weight layout --------------------------------------------------------------
+// A packed row is a sequence of 512-column blocks, padded to a multiple of 128 bytes.  Block b
+// holds w_b = min(512, n - 512b) int8 values (w_b/16 chunks of 16 bytes) followed by their w_b/32
+// fp32 scales, padded to 16 bytes; a full block is 576 bytes.  Inside a block the 16-byte chunks
+// are XOR-swizzled by a row/segment key so that the GEMV's lanes read shared memory without bank
+// conflicts (q8_swz_q / q8_swz_s).
+//
+// GEMV geometry of an n-column matrix: L lanes cooperate on one row (lane j handles the BL
+// consecutive blocks starting at j*BL), R = 32/L rows per warp-stage.
+struct Q8Geom {
+    int nblk, L, BL, R;
+};
+__host__ __device__ inline size_t q8_row_bytes(int n);
+// L is the smallest power of two (>= 8 when the row has more than 2 blocks, so an 8-lane shared
+// memory phase stays inside one row) with at most 2 blocks per lane and a stage of R = 32/L rows
+// of at most 25 KB.
+__host__ __device__ inline Q8Geom q8_geom(int n) {
+    Q8Geom g;
+    g.nblk = (n + 511) / 512;
+    const size_t rs = q8_row_bytes(n);
+    g.L = g.nblk > 2 ? 8 : 1;
+    while (g.L < 32 && ((g.nblk + g.L - 1) / g.L > 2 || (size_t)(32 / g.L) * rs > 25 * 1024)) g.L *= 2;
+    g.BL = (g.nblk + g.L - 1) / g.L;
+    g.R = 32 / g.L;
+    return g;
+}
+__host__ __device__ inline int q8_blk_width(int n, int b) { return (n - 512 * b) < 512 ? (n - 512 * b) : 512; }
+__host__ __device__ inline size_t q8_blk_bytes(int w) { return ((size_t)w + (size_t)w / 8 + 15) & ~(size_t)15; }
+__host__ __device__ inline size_t q8_blk_off(int b) { return (size_t)b * 576; }
+// Bytes of one packed row of an n-column matrix.
+__host__ __device__ inline size_t q8_row_bytes(int n) {
+    const size_t raw = (size_t)(n / 512) * 576 + ((n % 512) ? q8_blk_bytes(n % 512) : 0);
+    return (raw + 127) & ~(size_t)127;
+}
+// Swizzle key of (packed row, block).
+__host__ __device__ inline int q8_swz_key(const Q8Geom &g, int row, int b) { return (row * g.L + b / g.BL) & 7; }
+// Physical position of value chunk c / scale chunk s of a block of width wb.
+__host__ __device__ inline int q8_swz_q(int c, int key, int wb) { return ((wb / 16) % 8 == 0) ? (c ^ key) : c; }
+__host__ __device__ inline int q8_swz_s(int s, int key, int wb) {
+    const int nsc = wb / 128;  // scale chunks of a width that is a multiple of 128
+    return (wb % 128 == 0 && (nsc == 1 || nsc == 2 || nsc == 4)) ? (s ^ (key & (nsc - 1))) : s;
+}
+// Element i of packed row `row` (dequantised): q * scale.
+__host__ __device__ inline float q8_packed_elem(const uint8_t *rowp, int n, int row, int i) {
+    const Q8Geom g = q8_geom(n);
+    const int b = i >> 9, wb = q8_blk_width(n, b), key = q8_swz_key(g, row, b);
+    const uint8_t *seg = rowp + q8_blk_off(b);
+    const int within = i & 511;
+    const int8_t q = (int8_t)seg[q8_swz_q(within >> 4, key, wb) * 16 + (within & 15)];
+    const int grp = within >> 5;
+    const float s = *reinterpret_cast<const float *>(seg + wb + q8_swz_s(grp >> 2, key, wb) * 16 + (grp & 3) * 4);
+#ifdef __CUDA_ARCH__
+    return __fmul_rn((float)q, s);
+#else
+    return (float)q * s;
+#endif
+}
+// The 32 dequantised values of group g of packed row `row` (its two 16-byte chunks and one scale).
+__host__ __device__ inline void q8_packed_group(const uint8_t *rowp, int n, int row, int g, float *f) {
+    const Q8Geom gm = q8_geom(n);
+    const int b = g >> 4, wb = q8_blk_width(n, b), key = q8_swz_key(gm, row, b), w = g & 15;
+    const uint8_t *seg = rowp + q8_blk_off(b);
+    const int8_t *c0 = reinterpret_cast<const int8_t *>(seg + 16 * q8_swz_q(2 * w, key, wb));
+    const int8_t *c1 = reinterpret_cast<const int8_t *>(seg + 16 * q8_swz_q(2 * w + 1, key, wb));
+    const float s = *reinterpret_cast<const float *>(seg + wb + 16 * q8_swz_s(w >> 2, key, wb) + 4 * (w & 3));
+    for (int k = 0; k < 16; ++k) {
+#ifdef __CUDA_ARCH__
+        f[k] = __fmul_rn((float)c0[k], s);
+        f[16 + k] = __fmul_rn((float)c1[k], s);
+#else
+        f[k] = (float)c0[k] * s;
+        f[16 + k] = (float)c1[k] * s;
+#endif
+    }
+}
+size_t gemv_x_bytes(int n);
+// ctas_per_sm: CTAs per SM (1 or 2); smem_budget: shared memory per SM for the stage rings
+// (0 = default).  The ring of each CTA gets as many stage slots as fit, 1-3 per consumer warp.
+GemvPlan plan_gemv(int n, int d, int epi, int num_sms, int ctas_per_sm = 1, size_t smem_budget = 0);
+// Whether plan_gemv can serve this shape/epilogue (SwiGLU needs an even number of rows per stage).
+bool gemv_supported(int n, int d, int epi);
 cudaError_t launch_gemv(const GemvArgs &a, const GemvPlan &p, cudaStream_t st, bool pdl);
 
 // ---------------- Q8_0 conversions ----------------------------------------------------------

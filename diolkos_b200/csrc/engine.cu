@@ -99,6 +99,8 @@ struct dk_model {
 };
 
 static size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+// Capacity of the per-CTA argmax partials, in CTAs per SM (plan_gemv never launches more).
+static constexpr int kMaxGemvGrid = 4;
 
 static int need(dk_model *m) {
     if (!m) return set_error(DK_ERR_INVALID, "null dk_model");
@@ -191,7 +193,7 @@ dk_model *dk_model_create(const int *cfg, int kv_type, int device, int tp_rank, 
     const size_t sz_rope = align256((size_t)S * m->hs * 4);
     const size_t sz_work = align256((size_t)H * m->attn_splits * (m->hs + 2) * 4);
     const size_t sz_cnt = align256((size_t)KVH * 4);
-    const size_t sz_part = align256((size_t)m->num_sms * 8);
+    const size_t sz_part = align256((size_t)kMaxGemvGrid * m->num_sms * 8);
     const size_t sz_tok = align256((size_t)(S + 1) * 4);
     const size_t total = sz_x * 2 + sz_qkv + sz_hb + sz_logits + sz_rope + sz_work + sz_cnt + sz_part + 256 + sz_tok + 3 * 256;
     if (cudaMalloc(&m->aarena, total) != cudaSuccess) return fail("activation memory");
@@ -275,6 +277,7 @@ static int set_weight_impl(dk_model *m, int which, int layer, const void *q, con
         float *dst = which == DK_W_RMS_FINAL ? m->rms_final
                      : which == DK_W_RMS_ATT ? m->layers[layer].rms_att : m->layers[layer].rms_ffn;
         if (int r = cuda_status(cudaMemcpyAsync(dst, q, (size_t)rows * 4, dir, st), "norm upload")) return r;
+        if (int r = cuda_status(cudaStreamSynchronize(st), "norm upload sync")) return r;
     } else {
         const size_t nq = (size_t)rows * cols, ns = nq / 32;
         const int8_t *src_q = static_cast<const int8_t *>(q);
@@ -315,9 +318,9 @@ static int set_weight_impl(dk_model *m, int which, int layer, const void *q, con
         default: break;
         }
         if (int r = cuda_status(launch_pack_rows(dst, cols, src_q, src_s, rows, row0, step, st), "pack rows")) return r;
-        if (!on_device) {  // the staging buffer is reused by the next call
-            if (int r = cuda_status(cudaStreamSynchronize(st), "weight upload sync")) return r;
-        }
+        // The staging buffer is reused by the next call, and a caller may free its device source
+        // buffers as soon as this returns: wait for the copy.
+        if (int r = cuda_status(cudaStreamSynchronize(st), "weight upload sync")) return r;
     }
     m->have[(size_t)(per_layer ? layer : m->n_layers) * DK_W_COUNT + which] = 1;
     return DK_OK;
@@ -325,23 +328,26 @@ static int set_weight_impl(dk_model *m, int which, int layer, const void *q, con
 
 static int enqueue_step(dk_model *m, cudaStream_t st) {
     int launches = 0;
-    auto gemv = [&](const GemvPlan &p, const uint8_t *w, int n, int d, int pro, int epi, const float *x,
-                    const float *norm, float *out) -> cudaError_t {
+    // The first kernel of the step has no kernel predecessor inside the graph, so it is launched
+    // without the programmatic-dependency attribute; every later kernel overlaps its weight
+    // prefetch with the tail of the previous one.
+    auto gemv = [&](const char *what, const GemvPlan &p, const uint8_t *w, int n, int d, int pro, int epi,
+                    const float *x, const float *norm, float *out) -> int {
         GemvArgs a;
         a.w = w; a.n = n; a.d = d; a.pro = pro; a.epi = epi; a.x = x; a.norm_w = norm; a.out = out;
         a.emb = m->emb; a.tokens = m->tokens; a.pos = m->pos; a.n_forced = m->n_forced; a.seq_len = m->seq_len;
         a.amax_part = m->amax_part; a.amax_count = m->amax_count; a.err = m->err;
+        const bool pdl = launches > 0;
         ++launches;
-        return launch_gemv(a, p, st, true);
+        return cuda_status(launch_gemv(a, p, st, pdl), what);
     };
-    cudaError_t e = cudaSuccess;
     const int qkv_rows = m->dim + 2 * m->kv_dim;
     const size_t esz = m->kv_type == DK_KV_F32 ? 4 : 2;
-    for (int l = 0; l < m->n_layers && e == cudaSuccess; ++l) {
+    for (int l = 0; l < m->n_layers; ++l) {
         const dk_layer &ly = m->layers[l];
-        e = gemv(m->p_qkv, ly.wqkv, m->dim, qkv_rows, l == 0 ? PRO_EMB_RMS : PRO_RMS, EPI_STORE, m->x, ly.rms_att,
-                 m->qkv);
-        if (e != cudaSuccess) break;
+        if (int r = gemv("qkv gemv", m->p_qkv, ly.wqkv, m->dim, qkv_rows, l == 0 ? PRO_EMB_RMS : PRO_RMS,
+                         EPI_STORE, m->x, ly.rms_att, m->qkv))
+            return r;
         AttnArgs at;
         at.qkv = m->qkv; at.rope = m->rope;
         at.k_cache = static_cast<uint8_t *>(m->kcache) + (size_t)l * m->kv_layer_elems * esz;
@@ -349,18 +355,22 @@ static int enqueue_step(dk_model *m, cudaStream_t st) {
         at.out = m->xb; at.work = m->attn_work; at.count = m->attn_count; at.pos = m->pos;
         at.n_heads = m->n_heads; at.n_kv_heads = m->n_kv_heads; at.head_size = m->hs; at.seq_len = m->seq_len;
         at.kv_f32 = m->kv_type == DK_KV_F32; at.max_splits = m->attn_splits; at.min_chunk = 64; at.err = m->err;
-        e = launch_attention(at, st, true);
         ++launches;
-        if (e != cudaSuccess) break;
-        e = gemv(m->p_wo, ly.wo, m->dim, m->dim, PRO_F32, EPI_ADD, m->xb, nullptr, m->x);
-        if (e != cudaSuccess) break;
-        e = gemv(m->p_w13, ly.w13, m->dim, 2 * m->hidden, PRO_RMS, EPI_SWIGLU, m->x, ly.rms_ffn, m->hb);
-        if (e != cudaSuccess) break;
-        e = gemv(m->p_w2, ly.w2, m->hidden, m->dim, PRO_F32, EPI_ADD, m->hb, nullptr, m->x);
+        if (int r = cuda_status(launch_attention(at, st, true), "attention")) return r;
+        if (int r = gemv("wo gemv", m->p_wo, ly.wo, m->dim, m->dim, PRO_F32, EPI_ADD, m->xb, nullptr, m->x)) return r;
+        if (int r = gemv("w1/w3 gemv", m->p_w13, ly.w13, m->dim, 2 * m->hidden, PRO_RMS, EPI_SWIGLU, m->x,
+                         ly.rms_ffn, m->hb))
+            return r;
+        if (int r = gemv("w2 gemv", m->p_w2, ly.w2, m->hidden, m->dim, PRO_F32, EPI_ADD, m->hb, nullptr, m->x))
+            return r;
     }
-    if (e == cudaSuccess) e = gemv(m->p_cls, m->wcls, m->dim, m->vocab, PRO_RMS, EPI_ARGMAX, m->x, m->rms_final, m->logits);
+    if (m->p_cls.grid > kMaxGemvGrid * m->num_sms)
+        return set_error(DK_ERR_INVALID, "classifier grid %d exceeds the argmax partials", m->p_cls.grid);
+    if (int r = gemv("classifier gemv", m->p_cls, m->wcls, m->dim, m->vocab, PRO_RMS, EPI_ARGMAX, m->x,
+                     m->rms_final, m->logits))
+        return r;
     m->kernels_per_step = launches;
-    return cuda_status(e, "enqueue decode step");
+    return DK_OK;
 }
 
 extern "C" {

@@ -103,17 +103,28 @@ __global__ void group_dots_kernel(const int8_t *__restrict__ xq, const int8_t *_
     }
 }
 
+// Planar source row i -> packed destination row (row0 + i*step): per 512-column block, the block's
+// int8 values then its fp32 scales (16-byte chunks placed by the layout's XOR swizzle), zero
+// padding to 16 bytes per block and to 128 bytes per row.
 __global__ void pack_rows_kernel(uint8_t *__restrict__ dst, int n, size_t rs, const int8_t *__restrict__ q,
                                  const float *__restrict__ s, int row0, int step) {
     const int i = blockIdx.x;  // source row
-    uint8_t *drow = dst + (size_t)(row0 + (size_t)i * step) * rs;
-    const uint4 *qs = reinterpret_cast<const uint4 *>(q + (size_t)i * n);
-    for (int c = threadIdx.x; c < n / 16; c += blockDim.x) reinterpret_cast<uint4 *>(drow)[c] = qs[c];
-    float *ds = reinterpret_cast<float *>(drow + n);
-    const float *ss = s + (size_t)i * (n / 32);
-    for (int g = threadIdx.x; g < n / 32; g += blockDim.x) ds[g] = ss[g];
-    const int pad = (int)(rs - (size_t)n - (size_t)(n / 8));
-    for (int b = threadIdx.x; b < pad; b += blockDim.x) drow[n + n / 8 + b] = 0;
+    const int drow = row0 + i * step;
+    uint8_t *d = dst + (size_t)drow * rs;
+    const int8_t *qrow = q + (size_t)i * n;
+    const float *srow = s + (size_t)i * (n / 32);
+    for (size_t c = threadIdx.x; c < rs / 16; c += blockDim.x) reinterpret_cast<uint4 *>(d)[c] = make_uint4(0, 0, 0, 0);
+    __syncthreads();
+    const Q8Geom G = q8_geom(n);
+    for (int b = 0; b < G.nblk; ++b) {
+        const int wb = q8_blk_width(n, b), key = q8_swz_key(G, drow, b);
+        uint8_t *seg = d + q8_blk_off(b);
+        const uint4 *qs = reinterpret_cast<const uint4 *>(qrow + 512 * b);
+        for (int c = threadIdx.x; c < wb / 16; c += blockDim.x)
+            reinterpret_cast<uint4 *>(seg)[q8_swz_q(c, key, wb)] = qs[c];
+        for (int g = threadIdx.x; g < wb / 32; g += blockDim.x)
+            reinterpret_cast<float *>(seg + wb + 16 * q8_swz_s(g >> 2, key, wb))[g & 3] = srow[16 * b + g];
+    }
 }
 
 // One CTA: ss by tree reduction, scale = 1/sqrt(ss/n + 1e-5), o = (w*x)*scale.
@@ -142,10 +153,9 @@ __global__ void embed_kernel(const uint8_t *__restrict__ emb, int dim, size_t rs
                              float *__restrict__ x) {
     pdl_wait();
     const int tok = tokens[*pos];
-    const int8_t *q = reinterpret_cast<const int8_t *>(emb + (size_t)tok * rs);
-    const float *s = reinterpret_cast<const float *>(emb + (size_t)tok * rs + dim);
+    const uint8_t *row = emb + (size_t)tok * rs;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x)
-        x[i] = __fmul_rn((float)q[i], s[i >> 5]);
+        x[i] = q8_packed_elem(row, dim, tok, i);
     pdl_trigger();
 }
 

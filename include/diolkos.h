@@ -102,7 +102,8 @@ void dk_model_destroy(dk_model *m);
  * in the planar cache layout, full (unsharded) matrix; the engine keeps this rank's shard.
  * F32 weights: q = float[n], scale = NULL.  layer = -1 for the non-layer weights. */
 int dk_model_set_weight(dk_model *m, int which, int layer, const void *q, const float *scale);
-/* Same, with the planar Q8_0 (or F32) data in DEVICE memory of the model's GPU. */
+/* Same, with the planar Q8_0 (or F32) data in DEVICE memory of the model's GPU.  Both calls return
+ * once the data has been copied: the caller may free or reuse its buffers afterwards. */
 int dk_model_set_weight_device(dk_model *m, int which, int layer, const void *q, const float *scale);
 /* Check that every weight is present and capture the per-token CUDA graph. */
 int dk_model_finalize(dk_model *m);

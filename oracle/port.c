@@ -340,18 +340,19 @@ void port_forward(PortModel *m, int token, int pos, float *logits, float *xdump)
         port_matmul(m->v, m->xb, L->wv.q, L->wv.s, dim, kv_dim);
 
         /* HF rotate-half RoPE (src/transformer.c:87-119): pairs (j, j + hs/2) per head; keys
-         * are rotated where the pair lies inside kv_dim. */
+         * are rotated where the pair lies inside kv_dim.  The reference's -Ofast build contracts
+         * the rotation into fused multiply-adds: a' = fma(a, c, -(b*s)), b' = fma(a, s, b*c). */
         for (int i = 0; i < m->n_heads; i++) {
             for (int j = 0; j < hs / 2; j++) {
                 const float fcr = cs[2 * j], fci = cs[2 * j + 1];
                 const int i1 = i * hs + j, i2 = i * hs + j + hs / 2;
                 const float q0 = m->q[i1], q1 = m->q[i2];
-                m->q[i1] = q0 * fcr - q1 * fci;
-                m->q[i2] = q0 * fci + q1 * fcr;
+                m->q[i1] = fmaf(q0, fcr, -(q1 * fci));
+                m->q[i2] = fmaf(q0, fci, q1 * fcr);
                 if (i2 < kv_dim) {
                     const float k0 = m->k[i1], k1 = m->k[i2];
-                    m->k[i1] = k0 * fcr - k1 * fci;
-                    m->k[i2] = k0 * fci + k1 * fcr;
+                    m->k[i1] = fmaf(k0, fcr, -(k1 * fci));
+                    m->k[i2] = fmaf(k0, fci, k1 * fcr);
                 }
             }
         }

@@ -87,21 +87,55 @@ def test_group_dots_exact(torch_cuda, port):
         np.testing.assert_array_equal(dots, port.group_dots(xq, wq, n, d))
 
 
+def _geom(n):
+    """Packed-layout geometry (restated from diolkos_b200/csrc/dk_kernels.h)."""
+    nblk = (n + 511) // 512
+    raw = (n // 512) * 576 + ((n % 512 + (n % 512) // 8 + 15) // 16 * 16 if n % 512 else 0)
+    rs = (raw + 127) // 128 * 128
+    L = 8 if nblk > 2 else 1
+    while L < 32 and ((nblk + L - 1) // L > 2 or (32 // L) * rs > 25 * 1024):
+        L *= 2
+    return nblk, rs, L, (nblk + L - 1) // L
+
+
+def _unpack_row(row, n, r):
+    """Decode packed row r: per 512-column block, value chunk c sits at c ^ key and scale chunk s at
+    s ^ (key & (nsc-1)), key = (r*L + b//BL) & 7 (when the block width allows it)."""
+    nblk, rs, L, BL = _geom(n)
+    q = np.empty(n, np.int8)
+    sc = np.empty(n // 32, np.float32)
+    for b in range(nblk):
+        wb = min(512, n - 512 * b)
+        seg = row[576 * b:]
+        key = (r * L + b // BL) & 7
+        swq = (wb // 16) % 8 == 0
+        for c in range(wb // 16):
+            pc = c ^ key if swq else c
+            q[512 * b + 16 * c:512 * b + 16 * c + 16] = seg[16 * pc:16 * pc + 16].view(np.int8)
+        nsc = wb // 128
+        sws = wb % 128 == 0 and nsc in (1, 2, 4)
+        for g in range(wb // 32):
+            ps = ((g >> 2) ^ (key & (nsc - 1))) if sws else (g >> 2)
+            sc[16 * b + g] = seg[wb + 16 * ps + 4 * (g & 3):wb + 16 * ps + 4 * (g & 3) + 4].view(np.float32)[0]
+    return q, sc
+
+
 def test_pack_layout(torch_cuda):
+    """Packed rows: 512-column blocks of int8 values + fp32 scales, 16-byte chunks XOR-swizzled, rows
+    padded to 128 bytes; decoding every row gives back the planar input."""
     from diolkos_b200 import ops
 
     rng = np.random.default_rng(3)
-    n, d = 288, 5
-    q = rng.integers(-127, 128, n * d, dtype=np.int8)
-    s = rng.standard_normal(n * d // 32).astype(np.float32)
-    w = ops.pack(_dev(torch_cuda, q), _dev(torch_cuda, s), n, d).cpu().numpy()
-    rb = ops.row_bytes(n)
-    assert rb % 16 == 0 and rb >= n + n // 8
-    for r in range(d):
-        row = w[r * rb:(r + 1) * rb]
-        np.testing.assert_array_equal(row[:n].view(np.int8), q[r * n:(r + 1) * n])
-        np.testing.assert_array_equal(row[n:n + n // 8].view(np.float32), s[r * n // 32:(r + 1) * n // 32])
-        assert not row[n + n // 8:].any()
+    for n, d in [(288, 5), (1056, 3), (4096, 9), (11008, 3)]:
+        q = rng.integers(-127, 128, n * d, dtype=np.int8)
+        s = rng.standard_normal(n * d // 32).astype(np.float32)
+        w = ops.pack(_dev(torch_cuda, q), _dev(torch_cuda, s), n, d).cpu().numpy()
+        rb = ops.row_bytes(n)
+        assert rb == _geom(n)[1] and rb % 128 == 0
+        for r in range(d):
+            gq, gs = _unpack_row(w[r * rb:(r + 1) * rb], n, r)
+            np.testing.assert_array_equal(gq, q[r * n:(r + 1) * n])
+            np.testing.assert_array_equal(gs, s[r * n // 32:(r + 1) * n // 32])
 
 
 @pytest.mark.parametrize("case", G.GEMV_CASES)

@@ -85,21 +85,31 @@ def test_tiny_logits_match_oracle_teacher_forced(port, tiny_weights):
     assert max(errs) < 5e-2, errs
 
 
-def test_tiny_generate_vs_oracle(port, tiny_weights):
-    """Greedy generation on the GPU (the whole loop on the device) vs the oracle restatement."""
-    from oracle import PortModel
+def _first_near_tie(tg, ps, eps=5e-3):
+    """Index of the first generated token whose position has a reference top-2 gap below eps
+    (relative to the top logit): from there on any implementation may legitimately diverge."""
+    top2 = tg[f"tf_top2_{ps}"]
+    for pos in range(7, G.TINY_TF_POSITIONS):
+        if (top2[pos, 0] - top2[pos, 1]) / abs(top2[pos, 0]) < eps:
+            return pos - 7
+    return G.TINY_TF_POSITIONS - 7
 
+
+def test_tiny_generate_vs_reference(tiny_weights):
+    """Greedy generation with the whole loop on the GPU follows the reference's own greedy tokens
+    (golden) at least up to the first position where the reference's two best logits are within
+    0.5% of each other."""
     w, by_name = tiny_weights
+    tg = np.load(os.path.join(GOLD, "tiny.npz"))
     cfg = synth.TINY
     m = _gpu_model(cfg, by_name)
     for ps in G.TINY_PROMPTS:
         prompt = synth.seeded_prompt(ps, 8)
         gpu = m.generate(prompt, G.TINY_STEPS)
-        cpu = PortModel(port, cfg, w).generate(prompt, G.TINY_STEPS)
-        assert len(gpu) > 0
-        assert _first_div(gpu, cpu) >= 8, (ps, gpu[:20], cpu[:20])
-        # generate() must agree with forward()+argmax step by step on the same device state
-        assert gpu.dtype == np.int32 and (gpu >= 0).all() and (gpu < cfg.vocab_size).all()
+        ref = tg[f"tokens_{ps}"]
+        assert len(gpu) > 0 and (gpu >= 0).all() and (gpu < cfg.vocab_size).all()
+        bound = _first_near_tie(tg, ps)
+        assert _first_div(gpu, ref) >= bound, (ps, bound, gpu[:20], ref[:20])
 
 
 def test_generate_equals_forward_argmax(tiny_weights):
