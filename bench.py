@@ -189,6 +189,7 @@ class CpuReference:
         from oracle import Port, Ref, ref_path
 
         self.kind = "reference" if ref_path() else "port"
+        self.variant = "native" if ref_path("native") else "portable"
         self.cores = int(os.environ["OMP_NUM_THREADS"])
         self.tmp = tempfile.mkdtemp(prefix="dk_cpu_")
         port = Port()
@@ -203,7 +204,7 @@ class CpuReference:
 
         self.prompt = synth.seeded_prompt(SEED, PROMPT_LEN)
         if self.kind == "reference":
-            ref = Ref()
+            ref = Ref(self.variant)  # the reference's own flags (-march=native) for timing
             self.m1 = ref.load(d1, self.tmp)
             self.m3 = ref.load(d3, self.tmp)
         else:  # the restatement, when the reference build is not present
@@ -241,8 +242,7 @@ def gemv_bench(reps: int = 50):
 
     out = {}
     for d, n in GEMV_SHAPES:
-        rb = ops.row_bytes(n)
-        copies = max(2, int(3 * 126e6 // (d * rb)) + 1)
+        copies = max(2, int(3 * 126e6 // ops.packed_bytes(n, d)) + 1)
         g = torch.Generator(device="cuda").manual_seed(d * 31 + n)
         ws = []
         for _ in range(copies):

@@ -28,7 +28,9 @@ SIGNATURES = {
     "dk_dequantize_q8_0": (_i, [_vp, _vp, _sz, _vp, _vp]),
     "dk_q8_0_group_dots": (_i, [_vp, _vp, _i, _i, _vp, _vp]),
     "dk_q8_row_bytes": (_sz, [_i]),
-    "dk_q8_pack_rows": (_i, [_vp, _i, _vp, _vp, _i, _i, _i, _vp]),
+    "dk_q8_tile_rows": (_i, [_i]),
+    "dk_q8_packed_bytes": (_sz, [_i, _i]),
+    "dk_q8_pack": (_i, [_vp, _i, _i, _vp, _vp, _vp]),
     "dk_matmul_q8_0": (_i, [_vp, _vp, _vp, _i, _i, _vp]),
     "dk_matmul_q8_0_q": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp]),
     "dk_rmsnorm": (_i, [_vp, _vp, _vp, _i, _vp]),

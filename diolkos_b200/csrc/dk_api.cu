@@ -77,16 +77,25 @@ int dk_q8_0_group_dots(const int8_t *xq, const int8_t *wq, int n, int d, int32_t
     return cuda_status(launch_group_dots(xq, wq, n, d, dots, (cudaStream_t)stream), "dk_q8_0_group_dots");
 }
 
-size_t dk_q8_row_bytes(int n) { return n > 0 ? q8_row_bytes(n) : 0; }
+size_t dk_q8_row_bytes(int n) { return (n > 0 && n % 32 == 0) ? q8_row_bytes(n) : 0; }
 
-int dk_q8_pack_rows(uint8_t *dst, int n, const int8_t *src_q, const float *src_scale, int rows, int dst_row0,
-                    int dst_row_step, void *stream) {
-    if (n <= 0 || n % 32 || rows < 0 || dst_row0 < 0 || dst_row_step < 1)
-        return set_error(DK_ERR_INVALID, "dk_q8_pack_rows: bad arguments");
+int dk_q8_tile_rows(int d) { return d > 0 ? gemv_tile_rows(d, EPI_STORE, current_num_sms()) : 0; }
+
+size_t dk_q8_packed_bytes(int n, int d) {
+    if (n <= 0 || n % 32 || d <= 0) return 0;
+    return q8_packed_bytes(n, d, gemv_tile_rows(d, EPI_STORE, current_num_sms()));
+}
+
+int dk_q8_pack(uint8_t *dst, int n, int d, const int8_t *src_q, const float *src_scale, void *stream) {
+    if (n <= 0 || n % 32 || d <= 0) return set_error(DK_ERR_INVALID, "dk_q8_pack: bad shape n=%d d=%d", n, d);
+    if (!dst || !src_q || !src_scale) return set_error(DK_ERR_INVALID, "dk_q8_pack: null pointer");
     if (int r = check_aligned(dst, 16, "dst")) return r;
     if (int r = check_aligned(src_q, 16, "src_q")) return r;
-    return cuda_status(launch_pack_rows(dst, n, src_q, src_scale, rows, dst_row0, dst_row_step, (cudaStream_t)stream),
-                       "dk_q8_pack_rows");
+    if (int r = check_aligned(src_scale, 4, "src_scale")) return r;
+    const int T = gemv_tile_rows(d, EPI_STORE, current_num_sms());
+    cudaStream_t st = (cudaStream_t)stream;
+    if (int r = cuda_status(cudaMemsetAsync(dst, 0, q8_packed_bytes(n, d, T), st), "dk_q8_pack: memset")) return r;
+    return cuda_status(launch_pack_rows(dst, n, T, src_q, src_scale, d, 0, 1, st), "dk_q8_pack");
 }
 
 static int matmul_common(float *out, const float *x, const int8_t *xq, const float *xs, const uint8_t *w, int n,
@@ -112,7 +121,7 @@ static int matmul_common(float *out, const float *x, const int8_t *xq, const flo
     }
     a.epi = EPI_STORE;
     if (!gemv_supported(n, d, EPI_STORE))
-        return set_error(DK_ERR_INVALID, "matmul: unsupported shape n=%d d=%d (n must be a multiple of 32, <= 32768)", n, d);
+        return set_error(DK_ERR_INVALID, "matmul: unsupported shape n=%d d=%d (n must be a multiple of 32 and fit the shared-memory budget)", n, d);
     const GemvPlan p = plan_gemv(n, d, EPI_STORE, current_num_sms());
     return cuda_status(launch_gemv(a, p, (cudaStream_t)stream, false), "matmul");
 }

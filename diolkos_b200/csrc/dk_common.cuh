@@ -85,6 +85,12 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         : "memory");
 }
 
+// Ask the bulk-copy engine to bring [src, src+bytes) into L2 (no shared memory, no completion
+// signal).  src 16-byte aligned, bytes % 16 == 0.
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // ---- programmatic dependent launch ------------------------------------------------------------
 // Wait until the preceding kernel in the stream has completed and its writes are visible.  Every
 // kernel calls this before it reads anything an earlier kernel wrote or writes anything an
@@ -93,6 +99,20 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 // Allow the next kernel in the stream to be scheduled (its pre-wait prologue may then overlap
 // with the rest of this kernel).
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+// ---- shared-memory loads through 32-bit shared addresses ---------------------------------------
+// Explicit ld.shared: a load through a generic pointer that the compiler cannot prove to be shared
+// is issued as a generic load and waited on like a global one.
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ float4 lds_f4(uint32_t a) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a));
+    return v;
+}
 
 // ---- small helpers ------------------------------------------------------------------------------
 __device__ __forceinline__ float warp_max(float v) {

@@ -25,14 +25,15 @@ enum GemvEpi : int {
 };
 
 struct GemvArgs {
-    const uint8_t *w = nullptr;  // packed rows (q8_row_bytes(n) each)
+    const uint8_t *w = nullptr;  // packed matrix (tile layout)
     int n = 0, d = 0;
     int pro = PRO_F32, epi = EPI_STORE;
     const float *x = nullptr;       // PRO_F32 / PRO_RMS input; PRO_EMB_RMS: x is written here
     const float *norm_w = nullptr;  // PRO_RMS / PRO_EMB_RMS
     const int8_t *xq = nullptr;     // PRO_Q8
     const float *xs = nullptr;
-    const uint8_t *emb = nullptr;   // PRO_EMB_RMS: packed embedding rows
+    const uint8_t *emb = nullptr;   // PRO_EMB_RMS: packed embedding table
+    int emb_T = 32;                 // its tile height
     float *out = nullptr;
     // greedy-token epilogue and embedding prologue state (device memory)
     unsigned long long *amax_part = nullptr;  // >= grid entries
@@ -45,96 +46,76 @@ struct GemvArgs {
 };
 
 struct GemvPlan {
-    int RS = 0;        // packed row bytes
-    int grid = 1;      // CTAs (one contiguous row range each)
-    int CW = 4;        // consumer warps
-    int SPW = 1;       // stage slots per consumer warp (warp w owns slots w*SPW .. w*SPW+SPW-1)
-    size_t stage = 0;  // bytes of one stage (R packed rows)
-    size_t ring = 0;   // bytes of all stages
+    int T = 32;        // rows per tile (the packed layout's tile height)
+    int ntiles = 0;    // tiles of the matrix
+    int grid = 1;      // CTAs (one contiguous tile range each)
+    int CW = 1;        // consumer warps (warp w takes the CTA's tiles w, w+CW, ...)
+    int SPW = 1;       // stage slots per consumer warp
+    int PF = 0;        // stages prefetched into L2 ahead of the shared-memory rings
+    size_t slot = 0;   // bytes of one stage slot (T * 576)
     size_t xoff = 0;   // shared-memory offset of the activation
     size_t smem = 0;   // dynamic shared memory bytes
 };
 
-// ---- packed Q8_0 weight layout --------------------------------------------------------------
-// A packed row is a sequence of 512-column blocks, padded to a multiple of 128 bytes.  Block b
-// holds w_b = min(512, n - 512b) int8 values (w_b/16 chunks of 16 bytes) followed by their w_b/32
-// fp32 scales, padded to 16 bytes; a full block is 576 bytes.  Inside a block the 16-byte chunks
-// are XOR-swizzled by a row/segment key so that the GEMV's lanes read shared memory without bank
-// conflicts (q8_swz_q / q8_swz_s).
-//
-// GEMV geometry of an n-column matrix: L lanes cooperate on one row (lane j handles the BL
-// consecutive blocks starting at j*BL), R = 32/L rows per warp-stage.
-struct Q8Geom {
-    int nblk, L, BL, R;
-};
-__host__ __device__ inline size_t q8_row_bytes(int n);
-// L is the smallest power of two (>= 8 when the row has more than 2 blocks, so an 8-lane shared
-// memory phase stays inside one row) with at most 2 blocks per lane and a stage of R = 32/L rows
-// of at most 25 KB.
-__host__ __device__ inline Q8Geom q8_geom(int n) {
-    Q8Geom g;
-    g.nblk = (n + 511) / 512;
-    const size_t rs = q8_row_bytes(n);
-    g.L = g.nblk > 2 ? 8 : 1;
-    while (g.L < 32 && ((g.nblk + g.L - 1) / g.L > 2 || (size_t)(32 / g.L) * rs > 25 * 1024)) g.L *= 2;
-    g.BL = (g.nblk + g.L - 1) / g.L;
-    g.R = 32 / g.L;
-    return g;
-}
+// ---- packed Q8_0 weight layout ----------------------------------------------------------------
+// An n-column matrix is cut into 512-column blocks; block b holds w_b = min(512, n - 512b) columns
+// and, per row, a SEGMENT of q8_blk_bytes(w_b) bytes: the row's w_b int8 values (16-byte chunks)
+// followed by its w_b/32 fp32 scales, padded to 16 bytes (576 bytes for a full block).  Rows are
+// grouped into tiles of T rows (T depends on the row count and the GPU's SM count so that every SM
+// gets the same number of rows); a tile stores block 0 of its T rows, then block 1, ... so that
+// (tile, block) -- one STAGE of the GEMV -- is one contiguous range of T segments.  Inside a
+// segment the chunks are XOR-swizzled by the row's index in the tile so that lanes reading "their"
+// rows hit distinct shared-memory banks.  The last tile is padded with zero rows.
 __host__ __device__ inline int q8_blk_width(int n, int b) { return (n - 512 * b) < 512 ? (n - 512 * b) : 512; }
 __host__ __device__ inline size_t q8_blk_bytes(int w) { return ((size_t)w + (size_t)w / 8 + 15) & ~(size_t)15; }
-__host__ __device__ inline size_t q8_blk_off(int b) { return (size_t)b * 576; }
-// Bytes of one packed row of an n-column matrix.
+// Bytes of all segments of one row.
 __host__ __device__ inline size_t q8_row_bytes(int n) {
-    const size_t raw = (size_t)(n / 512) * 576 + ((n % 512) ? q8_blk_bytes(n % 512) : 0);
-    return (raw + 127) & ~(size_t)127;
+    return (size_t)(n / 512) * 576 + ((n % 512) ? q8_blk_bytes(n % 512) : 0);
 }
-// Swizzle key of (packed row, block).
-__host__ __device__ inline int q8_swz_key(const Q8Geom &g, int row, int b) { return (row * g.L + b / g.BL) & 7; }
-// Physical position of value chunk c / scale chunk s of a block of width wb.
-__host__ __device__ inline int q8_swz_q(int c, int key, int wb) { return ((wb / 16) % 8 == 0) ? (c ^ key) : c; }
-__host__ __device__ inline int q8_swz_s(int s, int key, int wb) {
-    const int nsc = wb / 128;  // scale chunks of a width that is a multiple of 128
-    return (wb % 128 == 0 && (nsc == 1 || nsc == 2 || nsc == 4)) ? (s ^ (key & (nsc - 1))) : s;
+// Tile height for a d-row matrix on num_sms SMs (unit = 2 keeps SwiGLU row pairs in one tile).
+__host__ __device__ inline int q8_tile_rows(int d, int num_sms, int unit) {
+    const long per = 32L * num_sms;
+    const long k = (d + per - 1) / per;  // tiles per SM
+    long t = (d + (long)num_sms * k - 1) / ((long)num_sms * k);
+    t = (t + unit - 1) / unit * unit;
+    return (int)(t < 1 ? 1 : (t > 32 ? 32 : t));
 }
-// Element i of packed row `row` (dequantised): q * scale.
-__host__ __device__ inline float q8_packed_elem(const uint8_t *rowp, int n, int row, int i) {
-    const Q8Geom g = q8_geom(n);
-    const int b = i >> 9, wb = q8_blk_width(n, b), key = q8_swz_key(g, row, b);
-    const uint8_t *seg = rowp + q8_blk_off(b);
-    const int within = i & 511;
-    const int8_t q = (int8_t)seg[q8_swz_q(within >> 4, key, wb) * 16 + (within & 15)];
-    const int grp = within >> 5;
-    const float s = *reinterpret_cast<const float *>(seg + wb + q8_swz_s(grp >> 2, key, wb) * 16 + (grp & 3) * 4);
+__host__ __device__ inline size_t q8_packed_bytes(int n, int d, int T) {
+    return (size_t)((d + T - 1) / T) * (size_t)T * q8_row_bytes(n);
+}
+// Byte offset of the segment (row, block b).
+__host__ __device__ inline size_t q8_seg_off(int n, int T, int row, int b) {
+    return (size_t)(row / T) * (size_t)T * q8_row_bytes(n) + (size_t)T * 576 * b +
+           (size_t)(row % T) * q8_blk_bytes(q8_blk_width(n, b));
+}
+// Physical 16-byte position of value chunk c / scale chunk s in the segment of tile row r.
+__host__ __device__ inline int q8_swz_q(int c, int r, int wb) { return ((wb / 16) % 8 == 0) ? (c ^ (r & 7)) : c; }
+__host__ __device__ inline int q8_swz_s(int s, int r, int wb) {
+    if (wb == 512) return s ^ ((r >> 1) & 3);
+    if (wb == 256) return s ^ (r & 1);
+    return s;
+}
+// The 32 dequantised values (q * scale) of group g of packed row `row`.
+__host__ __device__ inline void q8_packed_group(const uint8_t *w, int n, int T, int row, int g, float *f) {
+    const int b = g >> 4, wb = q8_blk_width(n, b), r = row % T, k = g & 15;
+    const uint8_t *seg = w + q8_seg_off(n, T, row, b);
+    const int8_t *c0 = reinterpret_cast<const int8_t *>(seg + 16 * q8_swz_q(2 * k, r, wb));
+    const int8_t *c1 = reinterpret_cast<const int8_t *>(seg + 16 * q8_swz_q(2 * k + 1, r, wb));
+    const float s = *reinterpret_cast<const float *>(seg + wb + 16 * q8_swz_s(k >> 2, r, wb) + 4 * (k & 3));
+    for (int i = 0; i < 16; ++i) {
 #ifdef __CUDA_ARCH__
-    return __fmul_rn((float)q, s);
+        f[i] = __fmul_rn((float)c0[i], s);
+        f[16 + i] = __fmul_rn((float)c1[i], s);
 #else
-    return (float)q * s;
-#endif
-}
-// The 32 dequantised values of group g of packed row `row` (its two 16-byte chunks and one scale).
-__host__ __device__ inline void q8_packed_group(const uint8_t *rowp, int n, int row, int g, float *f) {
-    const Q8Geom gm = q8_geom(n);
-    const int b = g >> 4, wb = q8_blk_width(n, b), key = q8_swz_key(gm, row, b), w = g & 15;
-    const uint8_t *seg = rowp + q8_blk_off(b);
-    const int8_t *c0 = reinterpret_cast<const int8_t *>(seg + 16 * q8_swz_q(2 * w, key, wb));
-    const int8_t *c1 = reinterpret_cast<const int8_t *>(seg + 16 * q8_swz_q(2 * w + 1, key, wb));
-    const float s = *reinterpret_cast<const float *>(seg + wb + 16 * q8_swz_s(w >> 2, key, wb) + 4 * (w & 3));
-    for (int k = 0; k < 16; ++k) {
-#ifdef __CUDA_ARCH__
-        f[k] = __fmul_rn((float)c0[k], s);
-        f[16 + k] = __fmul_rn((float)c1[k], s);
-#else
-        f[k] = (float)c0[k] * s;
-        f[16 + k] = (float)c1[k] * s;
+        f[i] = (float)c0[i] * s;
+        f[16 + i] = (float)c1[i] * s;
 #endif
     }
 }
 size_t gemv_x_bytes(int n);
-// ctas_per_sm: CTAs per SM (1 or 2); smem_budget: shared memory per SM for the stage rings
-// (0 = default).  The ring of each CTA gets as many stage slots as fit, 1-3 per consumer warp.
-GemvPlan plan_gemv(int n, int d, int epi, int num_sms, int ctas_per_sm = 1, size_t smem_budget = 0);
-// Whether plan_gemv can serve this shape/epilogue (SwiGLU needs an even number of rows per stage).
+// Tile height of the matrix a GEMV with this epilogue runs on (d rows, num_sms SMs).
+int gemv_tile_rows(int d, int epi, int num_sms);
+GemvPlan plan_gemv(int n, int d, int epi, int num_sms);
 bool gemv_supported(int n, int d, int epi);
 cudaError_t launch_gemv(const GemvArgs &a, const GemvPlan &p, cudaStream_t st, bool pdl);
 
@@ -143,10 +124,12 @@ cudaError_t launch_quant_bf16(const uint16_t *x, size_t n, int8_t *q, float *s, 
 cudaError_t launch_quant_f32(const float *x, size_t n, int8_t *q, float *s, cudaStream_t st);
 cudaError_t launch_dequant(const int8_t *q, const float *s, size_t n, float *out, cudaStream_t st);
 cudaError_t launch_group_dots(const int8_t *xq, const int8_t *wq, int n, int d, int32_t *dots, cudaStream_t st);
-cudaError_t launch_pack_rows(uint8_t *dst, int n, const int8_t *q, const float *s, int rows, int row0,
+// Pack `rows` planar rows (int8 q[rows*n], fp32 s[rows*n/32]) into packed rows row0, row0+step, ...
+// of a matrix with tile height T (the destination must be zeroed beforehand: padding stays zero).
+cudaError_t launch_pack_rows(uint8_t *dst, int n, int T, const int8_t *q, const float *s, int rows, int row0,
                              int step, cudaStream_t st);
 cudaError_t launch_rmsnorm(float *o, const float *x, const float *w, int n, cudaStream_t st);
-cudaError_t launch_embed(const uint8_t *emb_packed, int dim, const int *tokens, const int *pos, float *x,
+cudaError_t launch_embed(const uint8_t *emb_packed, int dim, int T, const int *tokens, const int *pos, float *x,
                          cudaStream_t st, bool pdl);
 
 // ---------------- attention ------------------------------------------------------------------

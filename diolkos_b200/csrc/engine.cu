@@ -92,6 +92,7 @@ struct dk_model {
     int *h_small = nullptr;
     // plans
     GemvPlan p_qkv, p_wo, p_w13, p_w2, p_cls;
+    int emb_T = 32;  // tile height of the packed embedding table
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     int kernels_per_step = 0;
@@ -154,19 +155,36 @@ dk_model *dk_model_create(const int *cfg, int kv_type, int device, int tp_rank, 
     };
     if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess) return fail("stream");
 
-    // ---- weights
-    const size_t rs_dim = q8_row_bytes(dim), rs_hid = q8_row_bytes(hidden);
+    // ---- GEMV plans (they fix each matrix's tile height, hence its packed size)
     const int qkv_rows = dim + 2 * m->kv_dim;
-    const size_t b_qkv = align256((size_t)qkv_rows * rs_dim), b_wo = align256((size_t)dim * rs_dim);
-    const size_t b_w13 = align256((size_t)2 * hidden * rs_dim), b_w2 = align256((size_t)dim * rs_hid);
+    m->p_qkv = plan_gemv(dim, qkv_rows, EPI_STORE, m->num_sms);
+    m->p_wo = plan_gemv(dim, dim, EPI_ADD, m->num_sms);
+    m->p_w13 = plan_gemv(dim, 2 * hidden, EPI_SWIGLU, m->num_sms);
+    m->p_w2 = plan_gemv(hidden, dim, EPI_ADD, m->num_sms);
+    m->p_cls = plan_gemv(dim, V, EPI_ARGMAX, m->num_sms);
+    m->emb_T = gemv_tile_rows(V, EPI_STORE, m->num_sms);
+    if (!gemv_supported(dim, qkv_rows, EPI_STORE) || !gemv_supported(dim, 2 * hidden, EPI_SWIGLU) ||
+        !gemv_supported(hidden, dim, EPI_ADD) || !gemv_supported(dim, V, EPI_ARGMAX)) {
+        set_error(DK_ERR_INVALID, "dk_model_create: matrix shapes exceed the GEMV's shared-memory budget");
+        dk_model_destroy(m);
+        return nullptr;
+    }
+
+    // ---- weights (zeroed: the pad rows of ragged last tiles and the pad bytes of segments stay 0)
+    const size_t b_qkv = align256(q8_packed_bytes(dim, qkv_rows, m->p_qkv.T));
+    const size_t b_wo = align256(q8_packed_bytes(dim, dim, m->p_wo.T));
+    const size_t b_w13 = align256(q8_packed_bytes(dim, 2 * hidden, m->p_w13.T));
+    const size_t b_w2 = align256(q8_packed_bytes(hidden, dim, m->p_w2.T));
     const size_t b_norm = align256((size_t)dim * 4);
-    const size_t b_emb = align256((size_t)V * rs_dim);
+    const size_t b_emb = align256(q8_packed_bytes(dim, V, m->emb_T));
+    const size_t b_cls = align256(q8_packed_bytes(dim, V, m->p_cls.T));
     const size_t per_layer = b_qkv + b_wo + b_w13 + b_w2 + 2 * b_norm;
-    m->warena_bytes = per_layer * L + 2 * b_emb + b_norm;
+    m->warena_bytes = per_layer * L + b_emb + b_cls + b_norm;
     if (cudaMalloc(&m->warena, m->warena_bytes) != cudaSuccess) return fail("weight memory");
+    if (cudaMemsetAsync(m->warena, 0, m->warena_bytes, m->stream) != cudaSuccess) return fail("weight memset");
     uint8_t *p = m->warena;
     m->emb = p; p += b_emb;
-    m->wcls = p; p += b_emb;
+    m->wcls = p; p += b_cls;
     m->rms_final = reinterpret_cast<float *>(p); p += b_norm;
     for (int l = 0; l < L; ++l) {
         dk_layer &ly = m->layers[l];
@@ -221,11 +239,6 @@ dk_model *dk_model_create(const int *cfg, int kv_type, int device, int tp_rank, 
     if (cudaMallocHost(&m->h_small, 4096) != cudaSuccess) return fail("pinned scratch");
     if (cudaStreamSynchronize(m->stream) != cudaSuccess) return fail("init sync");
 
-    m->p_qkv = plan_gemv(dim, qkv_rows, EPI_STORE, m->num_sms);
-    m->p_wo = plan_gemv(dim, dim, EPI_ADD, m->num_sms);
-    m->p_w13 = plan_gemv(dim, 2 * hidden, EPI_SWIGLU, m->num_sms);
-    m->p_w2 = plan_gemv(hidden, dim, EPI_ADD, m->num_sms);
-    m->p_cls = plan_gemv(dim, V, EPI_ARGMAX, m->num_sms);
     return m;
 }
 
@@ -304,20 +317,21 @@ static int set_weight_impl(dk_model *m, int which, int layer, const void *q, con
             src_s = reinterpret_cast<const float *>(m->stage + align256(nq));
         }
         uint8_t *dst = nullptr;
-        int row0 = 0, step = 1;
+        int row0 = 0, step = 1, T = 32;
         switch (which) {
-        case DK_W_EMB: dst = m->emb; break;
-        case DK_W_WCLS: dst = m->wcls; break;
-        case DK_W_WQ: dst = m->layers[layer].wqkv; break;
-        case DK_W_WK: dst = m->layers[layer].wqkv; row0 = m->dim; break;
-        case DK_W_WV: dst = m->layers[layer].wqkv; row0 = m->dim + m->kv_dim; break;
-        case DK_W_WO: dst = m->layers[layer].wo; break;
-        case DK_W_W1: dst = m->layers[layer].w13; row0 = 0; step = 2; break;
-        case DK_W_W3: dst = m->layers[layer].w13; row0 = 1; step = 2; break;
-        case DK_W_W2: dst = m->layers[layer].w2; break;
+        case DK_W_EMB: dst = m->emb; T = m->emb_T; break;
+        case DK_W_WCLS: dst = m->wcls; T = m->p_cls.T; break;
+        case DK_W_WQ: dst = m->layers[layer].wqkv; T = m->p_qkv.T; break;
+        case DK_W_WK: dst = m->layers[layer].wqkv; row0 = m->dim; T = m->p_qkv.T; break;
+        case DK_W_WV: dst = m->layers[layer].wqkv; row0 = m->dim + m->kv_dim; T = m->p_qkv.T; break;
+        case DK_W_WO: dst = m->layers[layer].wo; T = m->p_wo.T; break;
+        case DK_W_W1: dst = m->layers[layer].w13; row0 = 0; step = 2; T = m->p_w13.T; break;
+        case DK_W_W3: dst = m->layers[layer].w13; row0 = 1; step = 2; T = m->p_w13.T; break;
+        case DK_W_W2: dst = m->layers[layer].w2; T = m->p_w2.T; break;
         default: break;
         }
-        if (int r = cuda_status(launch_pack_rows(dst, cols, src_q, src_s, rows, row0, step, st), "pack rows")) return r;
+        if (int r = cuda_status(launch_pack_rows(dst, cols, T, src_q, src_s, rows, row0, step, st), "pack rows"))
+            return r;
         // The staging buffer is reused by the next call, and a caller may free its device source
         // buffers as soon as this returns: wait for the copy.
         if (int r = cuda_status(cudaStreamSynchronize(st), "weight upload sync")) return r;
@@ -335,7 +349,7 @@ static int enqueue_step(dk_model *m, cudaStream_t st) {
                     const float *x, const float *norm, float *out) -> int {
         GemvArgs a;
         a.w = w; a.n = n; a.d = d; a.pro = pro; a.epi = epi; a.x = x; a.norm_w = norm; a.out = out;
-        a.emb = m->emb; a.tokens = m->tokens; a.pos = m->pos; a.n_forced = m->n_forced; a.seq_len = m->seq_len;
+        a.emb = m->emb; a.emb_T = m->emb_T; a.tokens = m->tokens; a.pos = m->pos; a.n_forced = m->n_forced; a.seq_len = m->seq_len;
         a.amax_part = m->amax_part; a.amax_count = m->amax_count; a.err = m->err;
         const bool pdl = launches > 0;
         ++launches;
@@ -473,10 +487,12 @@ int dk_model_kernels_per_step(dk_model *m) { return m ? m->kernels_per_step : 0;
 
 size_t dk_model_weight_bytes(dk_model *m) {
     if (!m) return 0;
-    const size_t rs_dim = q8_row_bytes(m->dim), rs_hid = q8_row_bytes(m->hidden);
-    const size_t per_layer = (size_t)(m->dim + 2 * m->kv_dim) * rs_dim + (size_t)m->dim * rs_dim +
-                             (size_t)2 * m->hidden * rs_dim + (size_t)m->dim * rs_hid;
-    return per_layer * m->n_layers + (size_t)m->vocab * rs_dim;  // + one embedding row (negligible)
+    // Bytes the GEMVs of one step stream (pad rows included): every layer's four matrices + lm_head.
+    const size_t per_layer = q8_packed_bytes(m->dim, m->dim + 2 * m->kv_dim, m->p_qkv.T) +
+                             q8_packed_bytes(m->dim, m->dim, m->p_wo.T) +
+                             q8_packed_bytes(m->dim, 2 * m->hidden, m->p_w13.T) +
+                             q8_packed_bytes(m->hidden, m->dim, m->p_w2.T);
+    return per_layer * m->n_layers + q8_packed_bytes(m->dim, m->vocab, m->p_cls.T);
 }
 
 int dk_model_forward(dk_model *m, int token, int pos, float *logits) {

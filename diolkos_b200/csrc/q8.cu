@@ -103,27 +103,25 @@ __global__ void group_dots_kernel(const int8_t *__restrict__ xq, const int8_t *_
     }
 }
 
-// Planar source row i -> packed destination row (row0 + i*step): per 512-column block, the block's
-// int8 values then its fp32 scales (16-byte chunks placed by the layout's XOR swizzle), zero
-// padding to 16 bytes per block and to 128 bytes per row.
-__global__ void pack_rows_kernel(uint8_t *__restrict__ dst, int n, size_t rs, const int8_t *__restrict__ q,
+// Planar source row i -> packed row (row0 + i*step) of a tile-layout matrix with tile height T: per
+// 512-column block, the row's segment (int8 values then fp32 scales, 16-byte chunks placed by the
+// swizzle of the row's index in its tile).  The destination is zeroed beforehand, so the pad bytes of
+// each segment and the rows of a ragged last tile stay zero.
+__global__ void pack_rows_kernel(uint8_t *__restrict__ dst, int n, int T, const int8_t *__restrict__ q,
                                  const float *__restrict__ s, int row0, int step) {
     const int i = blockIdx.x;  // source row
-    const int drow = row0 + i * step;
-    uint8_t *d = dst + (size_t)drow * rs;
+    const int drow = row0 + i * step, r = drow % T;
     const int8_t *qrow = q + (size_t)i * n;
     const float *srow = s + (size_t)i * (n / 32);
-    for (size_t c = threadIdx.x; c < rs / 16; c += blockDim.x) reinterpret_cast<uint4 *>(d)[c] = make_uint4(0, 0, 0, 0);
-    __syncthreads();
-    const Q8Geom G = q8_geom(n);
-    for (int b = 0; b < G.nblk; ++b) {
-        const int wb = q8_blk_width(n, b), key = q8_swz_key(G, drow, b);
-        uint8_t *seg = d + q8_blk_off(b);
+    const int nblk = (n + 511) / 512;
+    for (int b = 0; b < nblk; ++b) {
+        const int wb = q8_blk_width(n, b);
+        uint8_t *seg = dst + q8_seg_off(n, T, drow, b);
         const uint4 *qs = reinterpret_cast<const uint4 *>(qrow + 512 * b);
         for (int c = threadIdx.x; c < wb / 16; c += blockDim.x)
-            reinterpret_cast<uint4 *>(seg)[q8_swz_q(c, key, wb)] = qs[c];
+            reinterpret_cast<uint4 *>(seg)[q8_swz_q(c, r, wb)] = qs[c];
         for (int g = threadIdx.x; g < wb / 32; g += blockDim.x)
-            reinterpret_cast<float *>(seg + wb + 16 * q8_swz_s(g >> 2, key, wb))[g & 3] = srow[16 * b + g];
+            reinterpret_cast<float *>(seg + wb + 16 * q8_swz_s(g >> 2, r, wb))[g & 3] = srow[16 * b + g];
     }
 }
 
@@ -149,13 +147,18 @@ __global__ void rmsnorm_kernel(float *o, const float *x, const float *w, int n) 
     for (int i = tid; i < n; i += blockDim.x) o[i] = __fmul_rn(__fmul_rn(w[i], x[i]), r);
 }
 
-__global__ void embed_kernel(const uint8_t *__restrict__ emb, int dim, size_t rs, const int *tokens, const int *pos,
+// Dequantised embedding row tokens[*pos] (src/transformer.c:69), one thread per 32-value group.
+__global__ void embed_kernel(const uint8_t *__restrict__ emb, int dim, int T, const int *tokens, const int *pos,
                              float *__restrict__ x) {
     pdl_wait();
     const int tok = tokens[*pos];
-    const uint8_t *row = emb + (size_t)tok * rs;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x)
-        x[i] = q8_packed_elem(row, dim, tok, i);
+    for (int g = blockIdx.x * blockDim.x + threadIdx.x; g < dim / 32; g += gridDim.x * blockDim.x) {
+        float f[32];
+        q8_packed_group(emb, dim, T, tok, g, f);
+        float4 *o = reinterpret_cast<float4 *>(x + 32 * g);
+        #pragma unroll
+        for (int k = 0; k < 8; ++k) o[k] = make_float4(f[4 * k], f[4 * k + 1], f[4 * k + 2], f[4 * k + 3]);
+    }
     pdl_trigger();
 }
 
@@ -188,10 +191,11 @@ cudaError_t launch_group_dots(const int8_t *xq, const int8_t *wq, int n, int d, 
     return cudaGetLastError();
 }
 
-cudaError_t launch_pack_rows(uint8_t *dst, int n, const int8_t *q, const float *s, int rows, int row0, int step,
-                             cudaStream_t st) {
+cudaError_t launch_pack_rows(uint8_t *dst, int n, int T, const int8_t *q, const float *s, int rows, int row0,
+                             int step, cudaStream_t st) {
     if (rows <= 0) return cudaSuccess;
-    pack_rows_kernel<<<rows, 128, 0, st>>>(dst, n, q8_row_bytes(n), q, s, row0, step);
+    if (n <= 0 || n % 32 || T < 1 || T > 32) return cudaErrorInvalidValue;
+    pack_rows_kernel<<<rows, 128, 0, st>>>(dst, n, T, q, s, row0, step);
     return cudaGetLastError();
 }
 
@@ -200,10 +204,10 @@ cudaError_t launch_rmsnorm(float *o, const float *x, const float *w, int n, cuda
     return cudaGetLastError();
 }
 
-cudaError_t launch_embed(const uint8_t *emb_packed, int dim, const int *tokens, const int *pos, float *x,
+cudaError_t launch_embed(const uint8_t *emb_packed, int dim, int T, const int *tokens, const int *pos, float *x,
                          cudaStream_t st, bool pdl) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((dim + 255) / 256);
+    cfg.gridDim = dim3((dim / 32 + 255) / 256);
     cfg.blockDim = dim3(256);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -211,7 +215,7 @@ cudaError_t launch_embed(const uint8_t *emb_packed, int dim, const int *tokens, 
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, embed_kernel, emb_packed, dim, q8_row_bytes(dim), tokens, pos, x);
+    return cudaLaunchKernelEx(&cfg, embed_kernel, emb_packed, dim, T, tokens, pos, x);
 }
 
 }  // namespace dk

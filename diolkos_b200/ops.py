@@ -51,10 +51,19 @@ def row_bytes(n: int) -> int:
     return int(lib().dk_q8_row_bytes(n))
 
 
+def tile_rows(d: int) -> int:
+    """Tile height of a packed d-row matrix on the current device."""
+    return int(lib().dk_q8_tile_rows(d))
+
+
+def packed_bytes(n: int, d: int) -> int:
+    return int(lib().dk_q8_packed_bytes(n, d))
+
+
 def pack(q: torch.Tensor, s: torch.Tensor, n: int, d: int) -> torch.Tensor:
-    """Planar Q8_0 [d x n] (cache layout) -> packed GEMV rows."""
-    w = torch.empty(d * row_bytes(n), dtype=torch.uint8, device=q.device)
-    check(lib().dk_q8_pack_rows(_ptr(w), n, _ptr(q), _ptr(s), d, 0, 1, stream_ptr()))
+    """Planar Q8_0 [d x n] (cache layout) -> the GEMV's packed tile layout."""
+    w = torch.empty(packed_bytes(n, d), dtype=torch.uint8, device=q.device)
+    check(lib().dk_q8_pack(_ptr(w), n, d, _ptr(q), _ptr(s), stream_ptr()))
     return w
 
 

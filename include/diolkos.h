@@ -48,13 +48,25 @@ int dk_dequantize_q8_0(const int8_t *q, const float *scale, size_t n, float *out
  * (the inner loop of matmul_Q8_0, src/utils.c:122-127): dots[i*(n/32)+g]. */
 int dk_q8_0_group_dots(const int8_t *xq, const int8_t *wq, int n, int d, int32_t *dots, void *stream);
 
-/* Packed device weight layout used by the GEMV: row r occupies dk_q8_row_bytes(n) bytes
- * (n int8 values, then the row's n/32 fp32 scales, zero padding to 16 bytes). */
+/* Packed device weight layout used by the GEMV (no reference counterpart: the reference keeps
+ * the planar cache layout in host memory).  A [d x n] matrix is cut into 512-column blocks; per
+ * row and block a SEGMENT holds the block's int8 values then its fp32 scales, padded to 16 bytes
+ * (576 bytes for a full block).  Rows are grouped into tiles of dk_q8_tile_rows(d) rows (chosen so
+ * that every SM of the current device streams the same number of rows); a tile stores block 0 of
+ * its rows, then block 1, ..., and the 16-byte chunks inside a segment are XOR-swizzled by the
+ * row's index in its tile.  The last tile is zero-padded.  The layout depends on the SM count, so
+ * pack on the device that runs the GEMV.
+ * dk_q8_row_bytes: bytes of all segments of one row (0 for n not a positive multiple of 32). */
 size_t dk_q8_row_bytes(int n);
-/* Pack `rows` rows of a planar Q8_0 matrix (the on-disk cache layout: int8[rows*n] and
- * fp32[rows*n/32], device pointers) into packed rows dst_row0, dst_row0+step, ... of `dst`. */
-int dk_q8_pack_rows(uint8_t *dst, int n, const int8_t *src_q, const float *src_scale, int rows,
-                    int dst_row0, int dst_row_step, void *stream);
+/* Tile height (1..32) of a d-row matrix on the current device. */
+int dk_q8_tile_rows(int d);
+/* Bytes of the packed [d x n] matrix on the current device (0 for bad shapes). */
+size_t dk_q8_packed_bytes(int n, int d);
+/* Pack a planar Q8_0 [d x n] matrix (the on-disk cache layout: int8[d*n] then fp32[d*n/32];
+ * device pointers, src_q 16-byte aligned) into dst (dk_q8_packed_bytes(n, d) bytes, 16-byte
+ * aligned), replacing the reference's load of a Q8_0 tensor from its cache file
+ * (src/tensor.c:346-397).  Asynchronous on `stream`. */
+int dk_q8_pack(uint8_t *dst, int n, int d, const int8_t *src_q, const float *src_scale, void *stream);
 
 /* matmul_Q8_0 (src/utils.c:106-138) on packed weights: out[d] = W[d x n] * quant(x[n]).
  * Device pointers.  Output bit-exact with the reference build (same group order, same

@@ -157,8 +157,12 @@ class PortModel:
 
 
 def ref_path(variant: str = "auto") -> str | None:
-    """Path of the compiled reference library, or None when it was not built here."""
-    order = ["native", "portable"] if variant == "auto" else [variant]
+    """Path of the compiled reference library, or None when it was not built here.
+
+    "auto" prefers the portable (-march=x86-64-v3) build: its arithmetic is the same on every
+    AVX2+FMA host, whereas -march=native lets the compiler pick a host-dependent vector shape that
+    changes the order of the GEMV's fp32 sums."""
+    order = ["portable", "native"] if variant == "auto" else [variant]
     for v in order:
         p = os.path.join(REF_DIR, v, "liboracle_ref.so")
         if os.path.exists(p):

@@ -54,5 +54,6 @@ def test_library_loads_via_ctypes():
     for name in _native.SIGNATURES:
         assert hasattr(L, name)
     assert L.dk_q8_row_bytes(4096) == 4608
-    assert L.dk_q8_row_bytes(288) == 384
-    assert L.dk_q8_row_bytes(11008) == 12416
+    assert L.dk_q8_row_bytes(288) == 336
+    assert L.dk_q8_row_bytes(11008) == 12384
+    assert L.dk_q8_row_bytes(100) == 0

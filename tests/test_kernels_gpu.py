@@ -87,55 +87,63 @@ def test_group_dots_exact(torch_cuda, port):
         np.testing.assert_array_equal(dots, port.group_dots(xq, wq, n, d))
 
 
-def _geom(n):
-    """Packed-layout geometry (restated from diolkos_b200/csrc/dk_kernels.h)."""
-    nblk = (n + 511) // 512
-    raw = (n // 512) * 576 + ((n % 512 + (n % 512) // 8 + 15) // 16 * 16 if n % 512 else 0)
-    rs = (raw + 127) // 128 * 128
-    L = 8 if nblk > 2 else 1
-    while L < 32 and ((nblk + L - 1) // L > 2 or (32 // L) * rs > 25 * 1024):
-        L *= 2
-    return nblk, rs, L, (nblk + L - 1) // L
+def _row_bytes(n):
+    """Bytes of one packed row: per 512-column block, values + scales padded to 16 bytes."""
+    blk = lambda w: (w + w // 8 + 15) // 16 * 16
+    return (n // 512) * 576 + (blk(n % 512) if n % 512 else 0)
 
 
-def _unpack_row(row, n, r):
-    """Decode packed row r: per 512-column block, value chunk c sits at c ^ key and scale chunk s at
-    s ^ (key & (nsc-1)), key = (r*L + b//BL) & 7 (when the block width allows it)."""
-    nblk, rs, L, BL = _geom(n)
-    q = np.empty(n, np.int8)
-    sc = np.empty(n // 32, np.float32)
-    for b in range(nblk):
-        wb = min(512, n - 512 * b)
-        seg = row[576 * b:]
-        key = (r * L + b // BL) & 7
-        swq = (wb // 16) % 8 == 0
-        for c in range(wb // 16):
-            pc = c ^ key if swq else c
-            q[512 * b + 16 * c:512 * b + 16 * c + 16] = seg[16 * pc:16 * pc + 16].view(np.int8)
-        nsc = wb // 128
-        sws = wb % 128 == 0 and nsc in (1, 2, 4)
-        for g in range(wb // 32):
-            ps = ((g >> 2) ^ (key & (nsc - 1))) if sws else (g >> 2)
-            sc[16 * b + g] = seg[wb + 16 * ps + 4 * (g & 3):wb + 16 * ps + 4 * (g & 3) + 4].view(np.float32)[0]
+def _unpack(w, n, d, T):
+    """Decode the tile layout (restated from diolkos_b200/csrc/dk_kernels.h): tile t of T rows stores
+    block b of its rows at t*T*row_bytes + T*576*b, row r of the tile at + r*blk_bytes(w_b); inside a
+    segment value chunk c sits at c ^ (r & 7) (when w_b/16 is a multiple of 8) and scale chunk s at
+    s ^ ((r >> 1) & 3) (w_b == 512) or s ^ (r & 1) (w_b == 256)."""
+    rb = _row_bytes(n)
+    q = np.empty((d, n), np.int8)
+    sc = np.empty((d, n // 32), np.float32)
+    for row in range(d):
+        t, r = divmod(row, T)
+        for b in range((n + 511) // 512):
+            wb = min(512, n - 512 * b)
+            bb = (wb + wb // 8 + 15) // 16 * 16
+            off = t * T * rb + T * 576 * b + r * bb
+            seg = w[off:off + bb]
+            for c in range(wb // 16):
+                pc = c ^ (r & 7) if (wb // 16) % 8 == 0 else c
+                q[row, 512 * b + 16 * c:512 * b + 16 * c + 16] = seg[16 * pc:16 * pc + 16].view(np.int8)
+            for g in range(wb // 32):
+                s4 = g >> 2
+                ps = s4 ^ ((r >> 1) & 3) if wb == 512 else (s4 ^ (r & 1) if wb == 256 else s4)
+                o = wb + 16 * ps + 4 * (g & 3)
+                sc[row, 16 * b + g] = seg[o:o + 4].view(np.float32)[0]
     return q, sc
 
 
 def test_pack_layout(torch_cuda):
-    """Packed rows: 512-column blocks of int8 values + fp32 scales, 16-byte chunks XOR-swizzled, rows
-    padded to 128 bytes; decoding every row gives back the planar input."""
+    """Packed tile layout: decoding every row gives back the planar input; pad rows stay zero."""
     from diolkos_b200 import ops
 
     rng = np.random.default_rng(3)
-    for n, d in [(288, 5), (1056, 3), (4096, 9), (11008, 3)]:
+    for n, d in [(288, 5), (1056, 37), (4096, 70), (11008, 9), (4096, 4096 + 2 * 1024)]:
         q = rng.integers(-127, 128, n * d, dtype=np.int8)
         s = rng.standard_normal(n * d // 32).astype(np.float32)
         w = ops.pack(_dev(torch_cuda, q), _dev(torch_cuda, s), n, d).cpu().numpy()
-        rb = ops.row_bytes(n)
-        assert rb == _geom(n)[1] and rb % 128 == 0
-        for r in range(d):
-            gq, gs = _unpack_row(w[r * rb:(r + 1) * rb], n, r)
-            np.testing.assert_array_equal(gq, q[r * n:(r + 1) * n])
-            np.testing.assert_array_equal(gs, s[r * n // 32:(r + 1) * n // 32])
+        T = ops.tile_rows(d)
+        assert 1 <= T <= 32 and ops.row_bytes(n) == _row_bytes(n)
+        tiles = (d + T - 1) // T
+        assert w.size == tiles * T * _row_bytes(n) == ops.packed_bytes(n, d)
+        rows = d if d < 300 else 300  # decode a prefix of the large case (pure-Python loops)
+        gq, gs = _unpack(w, n, rows, T)
+        np.testing.assert_array_equal(gq, q.reshape(d, n)[:rows])
+        np.testing.assert_array_equal(gs, s.reshape(d, n // 32)[:rows])
+        if tiles * T > d:  # the ragged last tile's pad rows are zero
+            t = tiles - 1
+            for r in range(d - t * T, T):
+                for b in range((n + 511) // 512):
+                    wb = min(512, n - 512 * b)
+                    bb = (wb + wb // 8 + 15) // 16 * 16
+                    off = t * T * _row_bytes(n) + T * 576 * b + r * bb
+                    assert not w[off:off + bb].any()
 
 
 @pytest.mark.parametrize("case", G.GEMV_CASES)

@@ -153,18 +153,25 @@ def test_port_tiny_model_vs_golden(port, tgold):
     assert _first_div(gen, toks) >= 8
 
 
-def test_reference_builds_agree(ref):
-    """The two compiled reference variants (native and portable -march) produce identical logits
-    (they share the same 256-bit vector code), so the reference's own numerics are pinned."""
+def test_reference_native_build(ref):
+    """The reference's -march=native build follows the portable build up to the order of its fp32
+    sums, which depends on the host CPU: quantised bytes are identical, logits agree within the
+    activation-requantisation envelope (and are identical on hosts whose native vector shape is the
+    portable one)."""
     from oracle import Ref, ref_path
 
     if ref_path("portable") is None or ref_path("native") is None:
         pytest.skip("both reference variants are needed")
     a, b = Ref("native"), Ref("portable")
+    rng = np.random.default_rng(12)
+    x = rng.standard_normal(32 * 2000, dtype=np.float32)
+    for u, v in zip(a.quant_f32(x), b.quant_f32(x)):
+        np.testing.assert_array_equal(u.view(np.uint8), v.view(np.uint8))
     tmp = tempfile.mkdtemp()
     md = os.path.join(tmp, "tiny")
     synth.write_model(md, synth.TINY, G.TINY_SEED)
     ma, mb = a.load(md, tmp), b.load(md, tmp)
     prompt = synth.seeded_prompt(7, 8)
     for pos in range(6):
-        np.testing.assert_array_equal(ma.forward(int(prompt[pos]), pos), mb.forward(int(prompt[pos]), pos))
+        la, lb = ma.forward(int(prompt[pos]), pos), mb.forward(int(prompt[pos]), pos)
+        assert np.max(np.abs(la - lb)) / np.max(np.abs(lb)) < 5e-2
