@@ -227,9 +227,21 @@ size_t attn_smem_bytes(const AttnArgs &a) {
     return sizeof(float) * ((size_t)kv_mul * a.head_size + (size_t)kv_mul * chunk_max + 2 * (size_t)kv_mul);
 }
 
+size_t attn_count_offset(int n_heads, int head_size, int max_splits) {
+    return ((size_t)n_heads * max_splits * (head_size + 2) * sizeof(float) + 255) & ~(size_t)255;
+}
+
+size_t attn_work_bytes(int n_heads, int n_kv_heads, int head_size, int max_splits) {
+    return attn_count_offset(n_heads, head_size, max_splits) + (((size_t)n_kv_heads * 4 + 255) & ~(size_t)255);
+}
+
+bool attn_supported(int n_heads, int n_kv_heads, int head_size) {
+    return n_heads > 0 && n_kv_heads > 0 && head_size > 0 && head_size <= 128 && !(head_size & 1) &&
+           n_heads % n_kv_heads == 0 && n_heads / n_kv_heads <= 8;
+}
+
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st, bool pdl) {
-    if (a.head_size > 128 || (a.head_size & 1) || a.n_heads % a.n_kv_heads || a.n_heads / a.n_kv_heads > 8)
-        return cudaErrorInvalidValue;
+    if (!attn_supported(a.n_heads, a.n_kv_heads, a.head_size)) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.n_kv_heads, a.max_splits);
     cfg.blockDim = dim3(kAttnThreads);

@@ -137,6 +137,36 @@ int dk_matmul_q8_0_q(float *out, const int8_t *xq, const float *xs, const uint8_
     return matmul_common(out, nullptr, xq, xs, w_packed, n, d, stream);
 }
 
+size_t dk_attention_work_bytes(int n_heads, int n_kv_heads, int head_size, int seq_len) {
+    if (!attn_supported(n_heads, n_kv_heads, head_size) || seq_len <= 0) return 0;
+    return attn_work_bytes(n_heads, n_kv_heads, head_size, attn_max_splits(seq_len, n_kv_heads, current_num_sms()));
+}
+
+int dk_attention_decode(float *out, const float *qkv, const float *rope, void *k_cache, void *v_cache, int kv_type,
+                        const int *pos, int n_heads, int n_kv_heads, int head_size, int seq_len, void *work,
+                        void *stream) {
+    if (!attn_supported(n_heads, n_kv_heads, head_size) || seq_len <= 0)
+        return set_error(DK_ERR_INVALID, "dk_attention_decode: unsupported shape heads=%d kv_heads=%d head_size=%d",
+                         n_heads, n_kv_heads, head_size);
+    if (kv_type != DK_KV_BF16 && kv_type != DK_KV_F32)
+        return set_error(DK_ERR_INVALID, "dk_attention_decode: bad kv_type %d", kv_type);
+    if (!out || !qkv || !rope || !k_cache || !v_cache || !pos || !work)
+        return set_error(DK_ERR_INVALID, "dk_attention_decode: null pointer");
+    if (int r = check_aligned(work, 256, "work")) return r;
+    AttnArgs a;
+    a.qkv = qkv; a.rope = rope; a.k_cache = k_cache; a.v_cache = v_cache; a.out = out; a.pos = pos;
+    a.n_heads = n_heads; a.n_kv_heads = n_kv_heads; a.head_size = head_size; a.seq_len = seq_len;
+    a.kv_f32 = kv_type == DK_KV_F32;
+    a.max_splits = attn_max_splits(seq_len, n_kv_heads, current_num_sms());
+    a.min_chunk = 64;
+    a.work = static_cast<float *>(work);
+    a.count = reinterpret_cast<unsigned *>(static_cast<uint8_t *>(work) +
+                                           attn_count_offset(n_heads, head_size, a.max_splits));
+    a.err = device_error_word();
+    if (!a.err) return set_error(DK_ERR_CUDA, "dk_attention_decode: could not allocate the device error word");
+    return cuda_status(launch_attention(a, (cudaStream_t)stream, false), "dk_attention_decode");
+}
+
 int dk_rmsnorm(float *o, const float *x, const float *w, int n, void *stream) {
     if (n <= 0 || !o || !x || !w) return set_error(DK_ERR_INVALID, "dk_rmsnorm: bad arguments");
     return cuda_status(launch_rmsnorm(o, x, w, n, (cudaStream_t)stream), "dk_rmsnorm");

@@ -149,6 +149,13 @@ struct AttnArgs {
 };
 int attn_max_splits(int seq_len, int n_kv_heads, int num_sms);
 size_t attn_smem_bytes(const AttnArgs &a);
+// Scratch of one attention launch: split partials (n_heads * max_splits * (head_size + 2) floats)
+// at offset 0, then n_kv_heads arrival counters at attn_count_offset(); both 256-byte aligned.
+size_t attn_count_offset(int n_heads, int head_size, int max_splits);
+size_t attn_work_bytes(int n_heads, int n_kv_heads, int head_size, int max_splits);
+// Shape checks of launch_attention (head_size even and <= 128, n_heads a multiple of n_kv_heads
+// with at most 8 query heads per KV head).
+bool attn_supported(int n_heads, int n_kv_heads, int head_size);
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st, bool pdl);
 
 }  // namespace dk

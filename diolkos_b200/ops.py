@@ -89,3 +89,21 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     o = torch.empty_like(x)
     check(lib().dk_rmsnorm(_ptr(o), _ptr(x), _ptr(w), x.numel(), stream_ptr()))
     return o
+
+
+def attention_work_bytes(n_heads: int, n_kv_heads: int, head_size: int, seq_len: int) -> int:
+    return int(lib().dk_attention_work_bytes(n_heads, n_kv_heads, head_size, seq_len))
+
+
+def attention_decode(qkv: torch.Tensor, rope: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                     pos: torch.Tensor, n_heads: int, n_kv_heads: int, head_size: int, seq_len: int,
+                     work: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """The attention block of forward (src/transformer.c:87-193) for one position: RoPE, KV-cache write
+    at pos (an int32 device tensor), softmax attention over 0..pos.  The cache type follows the cache
+    tensors' dtype (float32, or bfloat16/int16 bit patterns)."""
+    kv_type = 1 if k_cache.dtype == torch.float32 else 0
+    if out is None:
+        out = torch.empty(n_heads * head_size, dtype=torch.float32, device=qkv.device)
+    check(lib().dk_attention_decode(_ptr(out), _ptr(qkv), _ptr(rope), _ptr(k_cache), _ptr(v_cache), kv_type,
+                                    _ptr(pos), n_heads, n_kv_heads, head_size, seq_len, _ptr(work), stream_ptr()))
+    return out

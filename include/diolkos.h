@@ -78,6 +78,24 @@ int dk_matmul_q8_0_q(float *out, const int8_t *xq, const float *xs, const uint8_
 /* rmsnorm (src/utils.c:59-76), device pointers; o may alias x. */
 int dk_rmsnorm(float *o, const float *x, const float *w, int n, void *stream);
 
+/* The attention block of one decode step of one layer: replaces src/transformer.c:87-193 of
+ * forward (RoPE on q and k, k and v written into the cache at pos, then softmax(q.k/sqrt(hs))
+ * weighted sum of v for every query head over positions 0..pos), as split-K flash-decoding.
+ * Device pointers:
+ *   qkv     fp32 [n_heads*hs + 2*n_kv_heads*hs] = q | k | v, the wq/wk/wv outputs before RoPE;
+ *   rope    fp32 [seq_len][hs/2][2] = (cosf(p*f_j), sinf(p*f_j)), f_j = 1/powf(10000, 2j/(float)hs);
+ *   k_cache, v_cache  [n_kv_heads][seq_len][hs] of kv_type (DK_KV_BF16 truncating, or DK_KV_F32);
+ *   pos     int, the position (0 <= pos < seq_len; read on the device, so a captured call can be
+ *           replayed for every position);
+ *   out     fp32 [n_heads*hs];
+ *   work    scratch of dk_attention_work_bytes(...) bytes, 256-byte aligned, zero-filled before its
+ *           first use; every call leaves it ready for the next one.
+ * Calls that share `work` must be ordered (one stream). */
+size_t dk_attention_work_bytes(int n_heads, int n_kv_heads, int head_size, int seq_len);
+int dk_attention_decode(float *out, const float *qkv, const float *rope, void *k_cache, void *v_cache,
+                        int kv_type, const int *pos, int n_heads, int n_kv_heads, int head_size,
+                        int seq_len, void *work, void *stream);
+
 /* ---------------------------------------------------------------------------------------------
  * Decode engine: one LLaMA-2 model resident on one GPU (or one tensor-parallel shard), whose
  * whole per-token step (reference forward, src/transformer.c:55-239) is one CUDA graph.

@@ -219,3 +219,59 @@ def test_dequant(torch_cuda, port):
     s = rng.standard_normal(128).astype(np.float32)
     got = ops.dequantize(_dev(torch_cuda, q), _dev(torch_cuda, s)).cpu().numpy()
     np.testing.assert_array_equal(got.view(np.uint32), port.dequant(q, s).view(np.uint32))
+
+
+def _rope_table(seq_len, hs):
+    """(cos, sin) of p * 1/10000^(2j/hs) in float32, [seq_len][hs/2][2] (src/transformer.c:90-95)."""
+    j = np.arange(hs // 2, dtype=np.float32)
+    freq = (np.float32(1.0) / np.power(np.float32(10000.0), (2 * j) / np.float32(hs))).astype(np.float32)
+    val = (np.arange(seq_len, dtype=np.float32)[:, None] * freq[None, :]).astype(np.float32)
+    return np.stack([np.cos(val), np.sin(val)], axis=-1).astype(np.float32)
+
+
+def _attention_ref(qkv, rope, kc, vc, pos, H, KVH, hs):
+    """float64 restatement of src/transformer.c:87-193 on a cache already holding 0..pos-1."""
+    dim, kvd, half = H * hs, KVH * hs, hs // 2
+    c, s = rope[pos, :, 0].astype(np.float64), rope[pos, :, 1].astype(np.float64)
+    def rot(v):
+        v = v.astype(np.float64).reshape(-1, hs)
+        a, b = v[:, :half], v[:, half:]
+        return np.concatenate([a * c - b * s, a * s + b * c], axis=1)
+    q = rot(qkv[:dim])
+    k = rot(qkv[dim:dim + kvd])
+    v = qkv[dim + kvd:].astype(np.float64).reshape(KVH, hs)
+    K = kc.astype(np.float64).copy()
+    V = vc.astype(np.float64).copy()
+    K[:, pos], V[:, pos] = k, v
+    out = np.empty((H, hs))
+    for h in range(H):
+        g = h // (H // KVH)
+        sc = K[g, :pos + 1] @ q[h] / np.sqrt(hs)
+        e = np.exp(sc - sc.max())
+        out[h] = (e / e.sum()) @ V[g, :pos + 1]
+    return out.reshape(-1)
+
+
+@pytest.mark.parametrize("H,KVH,hs,seq,pos", [(32, 32, 128, 4096, 0), (32, 32, 128, 4096, 1000),
+                                              (8, 1, 64, 512, 300), (6, 6, 48, 256, 63)])
+def test_attention_decode_vs_fp64(torch_cuda, H, KVH, hs, seq, pos):
+    """dk_attention_decode (fp32 cache) against a float64 numpy attention, 1e-5 relative; the cache
+    row at pos holds the rotated k and v afterwards."""
+    from diolkos_b200 import ops
+
+    torch = torch_cuda
+    rng = np.random.default_rng(H * 1000 + pos)
+    qkv = rng.standard_normal((H + 2 * KVH) * hs).astype(np.float32)
+    kc = np.zeros((KVH, seq, hs), np.float32)
+    vc = np.zeros((KVH, seq, hs), np.float32)
+    kc[:, :pos] = rng.standard_normal((KVH, pos, hs))
+    vc[:, :pos] = rng.standard_normal((KVH, pos, hs))
+    rope = _rope_table(seq, hs)
+    dk, dv = _dev(torch, kc), _dev(torch, vc)
+    work = torch.zeros(ops.attention_work_bytes(H, KVH, hs, seq), dtype=torch.uint8, device="cuda")
+    p = torch.tensor([pos], dtype=torch.int32, device="cuda")
+    out = ops.attention_decode(_dev(torch, qkv), _dev(torch, rope), dk, dv, p, H, KVH, hs, seq, work).cpu().numpy()
+    ref = _attention_ref(qkv, rope, kc, vc, pos, H, KVH, hs)
+    np.testing.assert_allclose(out, ref, rtol=1e-5, atol=1e-5 * np.abs(ref).max())
+    np.testing.assert_array_equal(dv[:, pos].cpu().numpy(), qkv[(H + KVH) * hs:].reshape(KVH, hs))
+    assert not work[ops.attention_work_bytes(H, KVH, hs, seq) - 256:].any()  # counters back at zero
