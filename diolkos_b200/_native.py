@@ -36,6 +36,7 @@ SIGNATURES = {
     "dk_rmsnorm": (_i, [_vp, _vp, _vp, _i, _vp]),
     "dk_attention_work_bytes": (_sz, [_i, _i, _i, _i]),
     "dk_attention_decode": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _vp, _vp]),
+    "dk_attention_decode_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _vp]),
     "dk_model_create": (_vp, [C.POINTER(C.c_int), _i, _i, _i, _i]),
     "dk_model_destroy": (None, [_vp]),
     "dk_model_set_weight": (_i, [_vp, _i, _i, _vp, _vp]),

@@ -107,3 +107,14 @@ def attention_decode(qkv: torch.Tensor, rope: torch.Tensor, k_cache: torch.Tenso
     check(lib().dk_attention_decode(_ptr(out), _ptr(qkv), _ptr(rope), _ptr(k_cache), _ptr(v_cache), kv_type,
                                     _ptr(pos), n_heads, n_kv_heads, head_size, seq_len, _ptr(work), stream_ptr()))
     return out
+
+
+def attention_decode_noalloc(qkv: torch.Tensor, rope: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                             pos: torch.Tensor, n_heads: int, n_kv_heads: int, head_size: int, seq_len: int,
+                             out: torch.Tensor) -> torch.Tensor:
+    """attention_decode with the library's static device scratch (no allocation anywhere: `out` is
+    the caller's)."""
+    kv_type = 1 if k_cache.dtype == torch.float32 else 0
+    check(lib().dk_attention_decode_noalloc(_ptr(out), _ptr(qkv), _ptr(rope), _ptr(k_cache), _ptr(v_cache), kv_type,
+                                            _ptr(pos), n_heads, n_kv_heads, head_size, seq_len, stream_ptr()))
+    return out

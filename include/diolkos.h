@@ -95,6 +95,20 @@ size_t dk_attention_work_bytes(int n_heads, int n_kv_heads, int head_size, int s
 int dk_attention_decode(float *out, const float *qkv, const float *rope, void *k_cache, void *v_cache,
                         int kv_type, const int *pos, int n_heads, int n_kv_heads, int head_size,
                         int seq_len, void *work, void *stream);
+/* dk_attention_decode without a `work` argument and without allocating anything.  No reference
+ * counterpart: the reference's attention needs no scratch.  The scratch lives in a static device
+ * array of 4 MiB (4194304 bytes) per device, holding the split partials, the arrival counters and
+ * an error word; shapes that need more (dk_attention_work_bytes(...) + 256 bytes) are rejected
+ * with DK_ERR_INVALID.  The same arguments give the same bits as dk_attention_decode.
+ *   - The first call on each device does setup: it looks up the array's device address (which may
+ *     load this module onto the device).  Make that first call before any stream capture.
+ *   - Every call clears the counters and the error word with cudaMemsetAsync on `stream`; it calls
+ *     no cudaMalloc, cudaFree or other allocating routine.
+ *   - All calls on one device share the one array: calls that overlap in time (other streams,
+ *     other threads) race on it and give wrong results.  Order them on one stream. */
+int dk_attention_decode_noalloc(float *out, const float *qkv, const float *rope, void *k_cache,
+                                void *v_cache, int kv_type, const int *pos, int n_heads,
+                                int n_kv_heads, int head_size, int seq_len, void *stream);
 
 /* ---------------------------------------------------------------------------------------------
  * Decode engine: one LLaMA-2 model resident on one GPU (or one tensor-parallel shard), whose
