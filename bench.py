@@ -235,7 +235,10 @@ class CpuReference:
 
 
 # ------------------------------------------------------------------ GEMV microbenchmark (config 2)
-def gemv_bench(reps: int = 50):
+def gemv_bench(reps: int = 64):
+    """The four GEMV shapes through dk_matmul_q8_0_batch: `reps` GEMVs back to back, rotating over
+    enough packed copies of the matrix that the working set is over 3x the L2, timed with CUDA
+    events on the launching stream (best of 3 batches)."""
     import torch
 
     from diolkos_b200 import ops
@@ -251,20 +254,21 @@ def gemv_bench(reps: int = 50):
             ws.append(ops.pack(q, s, n, d))
             del wf, q, s
         x = torch.randn(n, generator=g, device="cuda")
-        y = torch.empty(d, device="cuda")
-        for i in range(5):
-            ops.matmul(x, ws[i % copies], n, d, y)
+        batch = [ws[i % copies] for i in range(reps)]
+        y = torch.empty((reps, d), device="cuda")
+        ops.matmul_batch(x, batch, n, d, y)
         torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for i in range(reps):
-            ops.matmul(x, ws[i % copies], n, d, y)
-        e1.record()
-        torch.cuda.synchronize()
-        us = e0.elapsed_time(e1) * 1e3 / reps
+        best = float("inf")
+        for _ in range(3):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            ops.matmul_batch(x, batch, n, d, y)
+            e1.record()
+            torch.cuda.synchronize()
+            best = min(best, e0.elapsed_time(e1) * 1e3 / reps)
         alg = d * n * 1.125 + n * 1.125 + d * 4
-        out[f"{d}x{n}"] = {"us": round(us, 2), "GBps": round(alg / us / 1e3, 1)}
-        del ws
+        out[f"{d}x{n}"] = {"us": round(best, 2), "GBps": round(alg / best / 1e3, 1)}
+        del ws, batch, y
         torch.cuda.empty_cache()
     return out
 

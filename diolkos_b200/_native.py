@@ -33,6 +33,7 @@ SIGNATURES = {
     "dk_q8_pack": (_i, [_vp, _i, _i, _vp, _vp, _vp]),
     "dk_matmul_q8_0": (_i, [_vp, _vp, _vp, _i, _i, _vp]),
     "dk_matmul_q8_0_q": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp]),
+    "dk_matmul_q8_0_batch": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
     "dk_rmsnorm": (_i, [_vp, _vp, _vp, _i, _vp]),
     "dk_attention_work_bytes": (_sz, [_i, _i, _i, _i]),
     "dk_attention_decode": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _vp, _vp]),

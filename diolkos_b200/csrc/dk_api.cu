@@ -167,6 +167,35 @@ int dk_attention_decode(float *out, const float *qkv, const float *rope, void *k
     return cuda_status(launch_attention(a, (cudaStream_t)stream, false), "dk_attention_decode");
 }
 
+int dk_matmul_q8_0_batch(float *out, const float *x, const uint8_t *const *w_packed, int count, int n, int d,
+                         void *stream) {
+    if (count < 0 || (count && !w_packed)) return set_error(DK_ERR_INVALID, "dk_matmul_q8_0_batch: bad count or list");
+    if (!x || !out) return set_error(DK_ERR_INVALID, "dk_matmul_q8_0_batch: null pointer");
+    if (n <= 0 || n % 32 || d <= 0 || !gemv_supported(n, d, EPI_STORE))
+        return set_error(DK_ERR_INVALID, "dk_matmul_q8_0_batch: unsupported shape n=%d d=%d", n, d);
+    for (int i = 0; i < count; ++i) {
+        if (!w_packed[i]) return set_error(DK_ERR_INVALID, "dk_matmul_q8_0_batch: null matrix %d", i);
+        if (int r = check_aligned(w_packed[i], 16, "w_packed[i]")) return r;
+    }
+    GemvArgs a;
+    a.n = n;
+    a.d = d;
+    a.pro = PRO_F32;
+    a.epi = EPI_STORE;
+    a.x = x;
+    a.err = device_error_word();
+    if (!a.err) return set_error(DK_ERR_CUDA, "dk_matmul_q8_0_batch: could not allocate the device error word");
+    const GemvPlan p = plan_gemv(n, d, EPI_STORE, current_num_sms());
+    for (int i = 0; i < count; ++i) {
+        a.w = w_packed[i];
+        a.out = out + (size_t)i * d;
+        // The first GEMV waits for whatever wrote its weights; the later ones may start streaming their
+        // weights while the previous GEMV of the batch runs (nothing in the batch writes weights).
+        if (int r = cuda_status(launch_gemv(a, p, (cudaStream_t)stream, i > 0), "dk_matmul_q8_0_batch")) return r;
+    }
+    return DK_OK;
+}
+
 int dk_rmsnorm(float *o, const float *x, const float *w, int n, void *stream) {
     if (n <= 0 || !o || !x || !w) return set_error(DK_ERR_INVALID, "dk_rmsnorm: bad arguments");
     return cuda_status(launch_rmsnorm(o, x, w, n, (cudaStream_t)stream), "dk_rmsnorm");

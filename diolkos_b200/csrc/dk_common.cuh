@@ -66,6 +66,33 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
     return true;
 }
 
+__device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait that also gives up as soon as another warp of the CTA has raised *abort.  spin = poll
+// with test_wait (lowest wake-up latency, for short hand-offs) instead of the suspending try_wait.
+__device__ __forceinline__ bool mbar_wait_abortable(uint64_t *bar, uint32_t parity, int *err, const int *abort,
+                                                    bool spin) {
+    if (spin ? mbar_test_wait(bar, parity) : mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    for (;;) {
+        if (spin ? mbar_test_wait(bar, parity) : mbar_try_wait(bar, parity)) return true;
+        if (*reinterpret_cast<const volatile int *>(abort)) return false;
+        if (clock64() - t0 > DK_WAIT_LIMIT_CYCLES) {
+            atomicOr(err, DK_ERR_TIMEOUT);
+            return false;
+        }
+    }
+}
+
 // ---- bulk copy engine (TMA, 1-D) --------------------------------------------------------------
 // L2 policy for streamed-once data (weights): evict first, so the KV cache and activations stay.
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
@@ -83,6 +110,12 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         "[%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
         "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
+}
+
+// Order this thread's earlier generic-proxy shared-memory accesses before its later async-proxy
+// (bulk-copy) accesses: used before a copy overwrites a slot that threads just read.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // Ask the bulk-copy engine to bring [src, src+bytes) into L2 (no shared memory, no completion
@@ -106,6 +139,11 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 __device__ __forceinline__ uint4 lds128(uint32_t a) {
     uint4 v;
     asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ float lds_f32(uint32_t a) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
     return v;
 }
 __device__ __forceinline__ float4 lds_f4(uint32_t a) {

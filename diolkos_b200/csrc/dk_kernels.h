@@ -49,9 +49,10 @@ struct GemvPlan {
     int T = 32;        // rows per tile (the packed layout's tile height)
     int ntiles = 0;    // tiles of the matrix
     int grid = 1;      // CTAs (one contiguous tile range each)
-    int CW = 1;        // consumer warps (warp w takes the CTA's tiles w, w+CW, ...)
-    int SPW = 1;       // stage slots per consumer warp
-    int PF = 0;        // stages prefetched into L2 ahead of the shared-memory rings
+    int NW = 1;        // consumer warps (stage s of the CTA goes to warp s % NW)
+    int S = 1;         // ring slots (stage s of the CTA lands in slot s % S); S >= NW, S % NP == 0
+    int NP = 1;        // producer threads (producer q issues the stages s = q mod NP)
+    int PF = 0;        // stages prefetched into L2 ahead of the ring
     size_t slot = 0;   // bytes of one stage slot (T * 576)
     size_t xoff = 0;   // shared-memory offset of the activation
     size_t smem = 0;   // dynamic shared memory bytes
@@ -113,6 +114,8 @@ __host__ __device__ inline void q8_packed_group(const uint8_t *w, int n, int T, 
     }
 }
 size_t gemv_x_bytes(int n);
+// Shared memory besides the ring: activation, reduction scratch, barriers, argmax keys.
+size_t gemv_smem_tail(int n);
 // Tile height of the matrix a GEMV with this epilogue runs on (d rows, num_sms SMs).
 int gemv_tile_rows(int d, int epi, int num_sms);
 GemvPlan plan_gemv(int n, int d, int epi, int num_sms);

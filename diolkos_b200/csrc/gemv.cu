@@ -5,21 +5,23 @@
 // block b of the T rows of one tile -- is one contiguous range of T row segments (about 16-18 KB for
 // the LLaMA shapes).
 //
-// Persistent kernel, one CTA per SM; CTA c owns a contiguous range of tiles.  Warp 4 is the
-// producer: it streams stages with the bulk-copy engine (cp.async.bulk, one copy per stage,
-// completion counted on an mbarrier, L2 evict-first) into per-consumer rings in shared memory and
-// keeps PF further stages prefetched into L2 (cp.async.bulk.prefetch.L2).  The shared-memory
-// footprint stays near 100 KB so that the next kernel's CTA fits beside this one.  The first stages
-// and prefetches are issued BEFORE griddepcontrol.wait, i.e. while the previous kernel in the stream
-// is still running: weights never depend on it.
+// Persistent kernel, one CTA per SM; CTA c owns a contiguous range of tiles, i.e. a sequence of
+// stages (its tiles in order, each tile's blocks in order).  NP producer threads (in separate warps:
+// under load the copy engine completes only a few copies per microsecond for each issuing thread)
+// stream the stages with the bulk-copy engine (cp.async.bulk, one copy per stage, completion counted on the slot's
+// mbarrier, L2 evict-first) through a ring of S shared-memory slots; the first S copies are issued
+// BEFORE griddepcontrol.wait, i.e. while the previous kernel in the stream is still running (weights
+// never depend on it).  Shared memory stays near 100 KB and registers at 128 per thread, so the next
+// kernel's CTA fits beside this one.
 //
-// Consumers: warp w takes the CTA's tiles w, w+CW, ...; LANE r OF THE WARP IS ROW r OF THE TILE.
-// For each stage the lane walks its row's 16 groups in order: exact int32 dot (dp4a against the
-// broadcast activation), then sum = sum + (float)dot * (w_scale * x_scale) with no FMA -- the
-// order and rounding of the reference's compiled loop, so the output is bit-identical to the
-// reference build.  The sum is carried in a register from block to block.  Only the warp that owns
-// a ring slot ever waits on it, so the mbarrier phases of a slot are always waited in order.  All
-// hot-loop loads are explicit ld.shared on 32-bit shared addresses.
+// NC consumer warps take the stages round-robin; LANE r OF A WARP IS ROW r OF THE TILE.  For its
+// stage a lane computes the row's 16 group terms (float)dot * (w_scale * x_scale) -- the exact int32
+// dot with dp4a against the broadcast activation, the products rounded as in the reference -- then
+// adds them to the row's running sum in group order, sum = sum + term with no FMA.  The running sums
+// travel from the warp of stage s to the warp of stage s+1 through shared memory, so the additions
+// of every row happen in the reference's order while the dot products of NC stages proceed in
+// parallel: the output is bit-identical to the reference build.  All hot-loop loads are explicit
+// ld.shared on 32-bit shared addresses.
 #include "dk_common.cuh"
 #include "dk_kernels.h"
 
@@ -29,13 +31,11 @@
 namespace dk {
 namespace {
 
-constexpr int kThreads = 160;  // warps 0..3 consume, warp 4 produces; all build the activation
-constexpr int kProducer = 4;
-constexpr int kMaxCW = 4;
-constexpr int kMaxSPW = 4;
-constexpr int kMaxSlots = kMaxCW * kMaxSPW;
+constexpr int kMaxConsumers = 6;
+constexpr int kMinWarps = 8;   // warps launched per CTA (consumers + producer + helpers for the activation)
+constexpr int kMaxSlots = 16;
 constexpr size_t kSmemBudget = 104 * 1024;    // two of these fit on an SM (this kernel + the next)
-constexpr size_t kPrefetchBytes = 40 * 1024;  // L2 prefetch distance ahead of the rings, per CTA
+constexpr int kPrefetchStages = 3;           // L2 prefetch distance beyond the ring, in stages
 
 __device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
     unsigned u = __float_as_uint(v);
@@ -74,12 +74,21 @@ __device__ __forceinline__ void build_activation(const GemvArgs &a, int8_t *xq, 
                 }
             }
         };
+        // The first group of each thread stays in registers between the two passes (with n <= 32 *
+        // threads that is every group, so x is read once).
+        float f0[32];
+        if (tid < ng) load_group(tid, f0);
         float r = 1.0f;
         if constexpr (PRO == PRO_RMS || PRO == PRO_EMB_RMS) {
             float ss = 0.0f;
             for (int g = tid; g < ng; g += nthreads) {
                 float f[32];
-                load_group(g, f);
+                if (g == tid) {
+                    #pragma unroll
+                    for (int k = 0; k < 32; ++k) f[k] = f0[k];
+                } else {
+                    load_group(g, f);
+                }
                 if constexpr (PRO == PRO_EMB_RMS) {
                     if (blockIdx.x == 0) {  // residual stream x
                         float4 *dst = reinterpret_cast<float4 *>(const_cast<float *>(a.x) + 32 * g);
@@ -102,7 +111,12 @@ __device__ __forceinline__ void build_activation(const GemvArgs &a, int8_t *xq, 
         }
         for (int g = tid; g < ng; g += nthreads) {
             float f[32];
-            load_group(g, f);
+            if (g == tid) {
+                #pragma unroll
+                for (int k = 0; k < 32; ++k) f[k] = f0[k];
+            } else {
+                load_group(g, f);
+            }
             if constexpr (PRO == PRO_RMS || PRO == PRO_EMB_RMS) {
                 // o = (w*x)*scale, the reference build's evaluation order (src/utils.c:73-75)
                 const float4 *wn = reinterpret_cast<const float4 *>(a.norm_w + 32 * g);
@@ -134,104 +148,160 @@ __device__ __forceinline__ void build_activation(const GemvArgs &a, int8_t *xq, 
     }
 }
 
-// One lane's reference-order sum over one block of its row (FULL: 512 columns).  seg, xq, xs are
-// 32-bit shared-memory addresses of the row's segment and of this block's activation values/scales.
-template <bool FULL>
-__device__ __forceinline__ float block_chain(float sum, uint32_t seg, uint32_t xq, uint32_t xs, int wb, int r) {
-    const int ng = FULL ? 16 : (wb >> 5);
-    const int cw = FULL ? 512 : wb;
-    const uint32_t scp = seg + cw;
-    #pragma unroll 4
-    for (int g4 = 0; g4 < ng; g4 += 4) {
-        const uint4 s4 = lds128(scp + 16 * q8_swz_s(g4 >> 2, r, cw));
-        const float wsc[4] = {__uint_as_float(s4.x), __uint_as_float(s4.y), __uint_as_float(s4.z),
-                              __uint_as_float(s4.w)};
-        const float4 x4 = lds_f4(xs + 4 * g4);
-        const float xsc[4] = {x4.x, x4.y, x4.z, x4.w};
-        #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int g = g4 + j;
-            if (!FULL && g >= ng) break;
-            const uint4 w0 = lds128(seg + 16 * q8_swz_q(2 * g, r, cw));
-            const uint4 w1 = lds128(seg + 16 * q8_swz_q(2 * g + 1, r, cw));
-            const uint4 x0 = lds128(xq + 32 * g), x1 = lds128(xq + 32 * g + 16);
-            const int dot = dp4a_16B(w1, x1) + dp4a_16B(w0, x0);
-            sum = __fadd_rn(sum, __fmul_rn(__int2float_rn(dot), __fmul_rn(wsc[j], xsc[j])));
-        }
-    }
-    return sum;
-}
-
-struct Sched {  // which stages exist, and where they come from
-    int t0, nt, CW, nblk, T, n;
-    size_t tile_bytes;
-    __device__ int nstages(int w) const { return nt > w ? ((nt - w + CW - 1) / CW) * nblk : 0; }
-    __device__ int tile_of(int w, int k) const { return t0 + w + CW * (k / nblk); }
-    __device__ const uint8_t *src(const uint8_t *base, int w, int k) const {
-        return base + (size_t)tile_of(w, k) * tile_bytes + (size_t)T * 576 * (k % nblk);
-    }
-    __device__ uint32_t bytes(int k) const { return (uint32_t)((size_t)T * q8_blk_bytes(q8_blk_width(n, k % nblk))); }
+// Data of 4 consecutive groups of one row: the 4 weight scales, the 4 activation scales, the 8
+// 16-byte weight chunks and the 8 16-byte activation chunks.
+struct Quad {
+    uint4 s;
+    float4 xs;
+    uint4 w[8], x[8];
 };
 
+// Load quad q (groups 4q..4q+3) of a full 512-column segment.  seg, xq, xs are 32-bit shared-memory
+// addresses of the row's segment and of this block's activation values/scales.
+__device__ __forceinline__ void load_quad(Quad &d, int q, uint32_t seg, uint32_t xq, uint32_t xs, int r) {
+    d.s = lds128(seg + 512 + 16 * q8_swz_s(q, r, 512));
+    d.xs = lds_f4(xs + 16 * q);
+    #pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        d.w[c] = lds128(seg + 16 * q8_swz_q(8 * q + c, r, 512));
+        d.x[c] = lds128(xq + 128 * q + 16 * c);
+    }
+}
+
+// Wait until the token flag says the running sums of stage s-1 have been handed to this warp (the flag
+// holds the index of the stage they are for).  A plain shared-memory flag: a hand-off is on the
+// critical path of every stage, and polling a volatile word sees it sooner than an mbarrier phase.
+// Bounded like every wait, and abandoned as soon as another warp raised the CTA's abort flag.
+__device__ __forceinline__ bool token_wait(const int *flag, int s, int *err, const int *abort) {
+    const volatile int *f = flag;
+    if (*f == s) {
+        __threadfence_block();
+        return true;
+    }
+    const long long t0 = clock64();
+    for (;;) {
+        if (*f == s) {
+            __threadfence_block();
+            return true;
+        }
+        if (*reinterpret_cast<const volatile int *>(abort)) return false;
+        if (clock64() - t0 > DK_WAIT_LIMIT_CYCLES) {
+            atomicOr(err, DK_ERR_TIMEOUT);
+            return false;
+        }
+    }
+}
+
+struct Sched {  // the CTA's stages: tile t0 + s / nblk, block s % nblk, for s < nst
+    int t0, nt, nblk, T, n, nst;
+    size_t tile_bytes;
+    __device__ const uint8_t *src(const uint8_t *base, int s) const {
+        return base + (size_t)(t0 + s / nblk) * tile_bytes + (size_t)T * 576 * (s % nblk);
+    }
+    __device__ uint32_t bytes(int s) const { return (uint32_t)((size_t)T * q8_blk_bytes(q8_blk_width(n, s % nblk))); }
+};
+
+// The 16 terms (float)dot_g * (ws_g * xs_g) of one row over one full block, each rounded exactly as
+// in the reference's loop.  Loads of quad q+1 are issued before quad q's arithmetic.
+__device__ __forceinline__ void quad_terms(float *t, const Quad &d) {
+    const float ws[4] = {__uint_as_float(d.s.x), __uint_as_float(d.s.y), __uint_as_float(d.s.z), __uint_as_float(d.s.w)};
+    const float xs[4] = {d.xs.x, d.xs.y, d.xs.z, d.xs.w};
+    #pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int dot = dp4a_16B(d.w[2 * j + 1], d.x[2 * j + 1]) + dp4a_16B(d.w[2 * j], d.x[2 * j]);
+        t[j] = __fmul_rn(__int2float_rn(dot), __fmul_rn(ws[j], xs[j]));
+    }
+}
+__device__ __forceinline__ void block_terms_full(float *t, uint32_t seg, uint32_t xq, uint32_t xs, int r) {
+    Quad A;
+    load_quad(A, 0, seg, xq, xs, r);
+    #pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        Quad B;
+        if (q < 3) load_quad(B, q + 1, seg, xq, xs, r);
+        quad_terms(t + 4 * q, A);
+        if (q < 3) A = B;
+    }
+}
+// Partial last block: wb/32 < 16 groups.
+__device__ __forceinline__ void block_terms_part(float *t, uint32_t seg, uint32_t xq, uint32_t xs, int wb, int r) {
+    const int ng = wb >> 5;
+    const uint32_t scp = seg + wb;
+    #pragma unroll
+    for (int g = 0; g < 16; ++g) {
+        if (g >= ng) break;
+        const float ws = lds_f32(scp + 16 * q8_swz_s(g >> 2, r, wb) + 4 * (g & 3));
+        const float xsg = lds_f32(xs + 4 * g);
+        const uint4 w0 = lds128(seg + 16 * q8_swz_q(2 * g, r, wb));
+        const uint4 w1 = lds128(seg + 16 * q8_swz_q(2 * g + 1, r, wb));
+        const uint4 x0 = lds128(xq + 32 * g), x1 = lds128(xq + 32 * g + 16);
+        const int dot = dp4a_16B(w1, x1) + dp4a_16B(w0, x0);
+        t[g] = __fmul_rn(__int2float_rn(dot), __fmul_rn(ws, xsg));
+    }
+}
+
+// Block layout (warps): 0 .. NC-1 consume, NC .. NC+NP-1 produce (one thread each), the rest (up to
+// kMinWarps) only help build the activation.  Stage s of the CTA sits in ring slot s % S and is consumed by warp s % NC.  A
+// consumer computes its stage's per-group terms as soon as the data is in, frees the slot, then
+// waits for the running row sums of stage s-1 (the TOKEN, passed warp to warp through shared
+// memory), folds its 16 terms into them in group order and passes them on to the warp of stage s+1.
+// So the fp32 additions of every row happen in exactly the reference's order, while the dot
+// products of consecutive stages run on different warps at the same time.  The token travels along
+// ALL stages of the CTA (across tile boundaries too, where the sums restart at 0), so a warp is never
+// handed a second token before it has taken the first.
 template <int PRO, int EPI>
-__global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const GemvArgs a, const GemvPlan p) {
+__global__ void __launch_bounds__(32 * kMinWarps, 2) gemv_q8_kernel(const GemvArgs a, const GemvPlan p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n = a.n;
+    const int n = a.n, NC = p.NW, S = p.S;
 
     uint8_t *ring = smem;
     int8_t *xq = reinterpret_cast<int8_t *>(smem + p.xoff);
     float *xs = reinterpret_cast<float *>(smem + p.xoff + ((n + 15) & ~15));
-    float *red = xs + ((n / 32 + 3) & ~3);
-    uint64_t *full = reinterpret_cast<uint64_t *>(red + 8);
-    uint64_t *empty = full + kMaxSlots;
-    int *flags = reinterpret_cast<int *>(empty + kMaxSlots);  // [0] abort, [1] last CTA
-    int *issued = flags + 2, *consumed = issued + kMaxSlots;
-    unsigned long long *wkey = reinterpret_cast<unsigned long long *>(consumed + kMaxSlots);
+    float *red = xs + ((n / 32 + 3) & ~3);                           // [kMinWarps]
+    uint64_t *full = reinterpret_cast<uint64_t *>(red + kMinWarps);  // [kMaxSlots]
+    uint64_t *empty = full + kMaxSlots;                              // [kMaxSlots]
+    int *tokflag = reinterpret_cast<int *>(empty + kMaxSlots);       // [kMaxConsumers] (padded to 8 B each)
+    float *tokval = reinterpret_cast<float *>(tokflag + 2 * kMaxConsumers);  // [kMaxConsumers][32]
+    unsigned long long *wkey = reinterpret_cast<unsigned long long *>(tokval + kMaxConsumers * 32);
+    int *flags = reinterpret_cast<int *>(wkey + kMaxConsumers);      // [0] abort, [1] last CTA
     const uint32_t ring_s = smem_u32(ring), xq_s = smem_u32(xq), xs_s = smem_u32(xs);
 
     Sched sc;
     sc.t0 = (int)((long long)blockIdx.x * p.ntiles / gridDim.x);
     sc.nt = (int)((long long)(blockIdx.x + 1) * p.ntiles / gridDim.x) - sc.t0;
-    sc.CW = p.CW;
     sc.nblk = (n + 511) >> 9;
     sc.T = p.T;
     sc.n = n;
+    sc.nst = sc.nt * sc.nblk;
     sc.tile_bytes = (size_t)p.T * q8_row_bytes(n);
-    const int SPW = p.SPW, CW = p.CW;
-    // Stage k of consumer warp w: its tile w + CW*(k / nblk), block k % nblk; slot w*SPW + k % SPW,
-    // use k / SPW of that slot.  The producer walks the stages round-robin over the warps.
-    const int kmax = sc.nstages(0);  // warp 0 has the most stages
 
     if (tid == 0) {
-        for (int i = 0; i < CW * SPW; ++i) {
+        for (int i = 0; i < S; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
-            issued[i] = 0;
-            consumed[i] = 0;
         }
+        for (int i = 0; i < NC; ++i) tokflag[2 * i] = -1;
         flags[0] = 0;
         flags[1] = 0;
         mbar_fence_init();
     }
     __syncthreads();
 
+    // Producer warps NC .. NC+NP-1: producer q issues the stages s = q (mod NP), into the slots
+    // s % S (S is a multiple of NP, so each slot has one producer).  Weights only, so the ring is filled
+    // (and PF more stages are prefetched into L2) before the dependency wait.
+    const int NP = p.NP, q = warp - NC;
+    const bool producer = q >= 0 && q < NP && lane == 0;
     uint64_t policy = 0;
-    if (warp == kProducer && lane == 0) {
-        // Weights only, so safe before the dependency wait: fill every ring slot, then prefetch the
-        // next PF stages of each warp into L2.
+    int next = q;  // this producer's next stage to issue
+    if (producer) {
         policy = l2_evict_first_policy();
-        for (int k = 0; k < min(SPW, kmax); ++k)
-            for (int w = 0; w < CW; ++w) {
-                if (k >= sc.nstages(w)) continue;
-                const int slot = w * SPW + k;
-                mbar_arrive_expect_tx(&full[slot], sc.bytes(k));
-                bulk_g2s(ring + (size_t)slot * p.slot, sc.src(a.w, w, k), sc.bytes(k), &full[slot], policy);
-                issued[slot] += 1;
-            }
-        for (int k = SPW; k < min(SPW + p.PF, kmax); ++k)
-            for (int w = 0; w < CW; ++w)
-                if (k < sc.nstages(w)) bulk_prefetch_l2(sc.src(a.w, w, k), sc.bytes(k));
+        for (; next < min(S, sc.nst); next += NP) {
+            mbar_arrive_expect_tx(&full[next], sc.bytes(next));
+            bulk_g2s(ring + (size_t)next * p.slot, sc.src(a.w, next), sc.bytes(next), &full[next], policy);
+        }
+        for (int s = S + q; s < min(S + p.PF, sc.nst); s += NP) bulk_prefetch_l2(sc.src(a.w, s), sc.bytes(s));
     }
 
     pdl_wait();
@@ -239,51 +309,67 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const GemvArgs a, 
     build_activation<PRO>(a, xq, xs, red);
     __syncthreads();
 
-    if (warp == kProducer) {
+    if (q >= 0 && q < NP) {
         if (lane == 0) {
-            bool stop = false;
-            for (int k = SPW; k < kmax && !stop; ++k) {
-                for (int w = 0; w < CW; ++w) {
-                    if (k >= sc.nstages(w)) continue;
-                    const int slot = w * SPW + (k % SPW);
-                    if (*reinterpret_cast<volatile int *>(flags) ||
-                        !mbar_wait(&empty[slot], (uint32_t)(((k / SPW) - 1) & 1), a.err)) {
-                        *reinterpret_cast<volatile int *>(flags) = 1;
-                        stop = true;
-                        break;
-                    }
-                    mbar_arrive_expect_tx(&full[slot], sc.bytes(k));
-                    bulk_g2s(ring + (size_t)slot * p.slot, sc.src(a.w, w, k), sc.bytes(k), &full[slot], policy);
-                    issued[slot] += 1;
-                    const int kp = k + p.PF;  // keep the L2 prefetch PF stages ahead
-                    if (kp < sc.nstages(w)) bulk_prefetch_l2(sc.src(a.w, w, kp), sc.bytes(kp));
+            for (; next < sc.nst; next += NP) {
+                const int slot = next % S;
+                if (!mbar_wait_abortable(&empty[slot], (uint32_t)(((next / S) - 1) & 1), a.err, flags, false)) {
+                    flags[0] = 1;
+                    break;
                 }
+                mbar_arrive_expect_tx(&full[slot], sc.bytes(next));
+                bulk_g2s(ring + (size_t)slot * p.slot, sc.src(a.w, next), sc.bytes(next), &full[slot], policy);
+                if (next + p.PF < sc.nst) bulk_prefetch_l2(sc.src(a.w, next + p.PF), sc.bytes(next + p.PF));
             }
+            // Never leave a copy in flight into the shared memory of an exiting CTA: each of this
+            // producer's slots has at most one outstanding copy, the last one issued into it.
+            for (int last = next - NP; last >= q && last >= next - S; last -= NP)
+                mbar_wait(&full[last % S], (uint32_t)((last / S) & 1), a.err);
         }
-    } else if (warp < CW) {
-        const int w = warp, ns = sc.nstages(w);
+    } else if (warp < NC) {
+        const int c = warp;
         unsigned long long best = 0ull;
-        float sum = 0.0f;
-        for (int k = 0; k < ns; ++k) {
-            const int slot = w * SPW + (k % SPW);
-            if (!mbar_wait(&full[slot], (uint32_t)((k / SPW) & 1), a.err)) {
-                if (lane == 0) *reinterpret_cast<volatile int *>(flags) = 1;
+        for (int s = c; s < sc.nst; s += NC) {
+            const int slot = s % S;
+            if (!__all_sync(FULL, mbar_wait_abortable(&full[slot], (uint32_t)((s / S) & 1), a.err, flags, false))) {
+                if (lane == 0) flags[0] = 1;
                 break;
             }
-            if (lane == 0) consumed[slot] += 1;
-            const int b = k % sc.nblk;
-            const int row = sc.tile_of(w, k) * p.T + lane;
+            const int b = s % sc.nblk;
+            const int row = (sc.t0 + s / sc.nblk) * p.T + lane;
             const bool live = lane < p.T && row < a.d;
-            if (b == 0) sum = 0.0f;
             const int wb = q8_blk_width(n, b);
+            float t[16] = {};
             if (live) {
                 const uint32_t seg = ring_s + (uint32_t)(slot * p.slot + lane * q8_blk_bytes(wb));
                 const uint32_t xqb = xq_s + 512u * b, xsb = xs_s + 64u * b;
-                if (wb == 512) sum = block_chain<true>(sum, seg, xqb, xsb, 512, lane);
-                else sum = block_chain<false>(sum, seg, xqb, xsb, wb, lane);
+                if (wb == 512) block_terms_full(t, seg, xqb, xsb, lane);
+                else block_terms_part(t, seg, xqb, xsb, wb, lane);
+                // Pin the terms here: without this the compiler may sink their arithmetic past the
+                // token wait below, onto the serial path that the hand-off is meant to keep short.
+                #pragma unroll
+                for (int g = 0; g < 16; ++g) asm volatile("" : "+f"(t[g]));
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
+            float sum = 0.0f;
+            if (s > 0) {  // the running sums of stage s-1
+                if (!__all_sync(FULL, token_wait(&tokflag[2 * c], s, a.err, flags))) {
+                    if (lane == 0) flags[0] = 1;
+                    break;
+                }
+                if (b > 0) sum = tokval[c * 32 + lane];
+            }
+            if (live) {
+                if (wb == 512) {
+                    #pragma unroll
+                    for (int g = 0; g < 16; ++g) sum = __fadd_rn(sum, t[g]);
+                } else {
+                    #pragma unroll
+                    for (int g = 0; g < 16; ++g)
+                        if (g < (wb >> 5)) sum = __fadd_rn(sum, t[g]);
+                }
+            }
             if (b == sc.nblk - 1) {  // the tile's rows are finished
                 if constexpr (EPI == EPI_SWIGLU) {
                     const float h3 = __shfl_down_sync(FULL, sum, 1);
@@ -302,6 +388,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const GemvArgs a, 
                     }
                 }
             }
+            if (s + 1 < sc.nst) {  // pass the running sums to the warp of stage s+1
+                const int cn = (c + 1) % NC;
+                tokval[cn * 32 + lane] = sum;
+                __threadfence_block();
+                __syncwarp();
+                if (lane == 0) *reinterpret_cast<volatile int *>(&tokflag[2 * cn]) = s + 1;
+            }
         }
         if constexpr (EPI == EPI_ARGMAX) {
             #pragma unroll
@@ -309,26 +402,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const GemvArgs a, 
                 const unsigned long long other = __shfl_xor_sync(FULL, best, o);
                 best = other > best ? other : best;
             }
-            if (lane == 0) wkey[w] = best;
+            if (lane == 0) wkey[c] = best;
         }
     }
     __syncthreads();
 
-    // Error path only: never leave a bulk copy in flight into shared memory of an exiting CTA.
-    if (tid == 0 && *reinterpret_cast<volatile int *>(flags)) {
-        for (int i = 0; i < CW * SPW; ++i) {
-            while (consumed[i] < issued[i]) {
-                if (!mbar_wait(&full[i], (uint32_t)(consumed[i] & 1), a.err)) break;
-                consumed[i] += 1;
-            }
-        }
-    }
-
     if constexpr (EPI == EPI_ARGMAX) {
         if (tid == 0) {
-            unsigned long long b = 0ull;
-            for (int w = 0; w < CW; ++w) b = wkey[w] > b ? wkey[w] : b;
-            a.amax_part[blockIdx.x] = b;
+            unsigned long long bb = 0ull;
+            for (int w = 0; w < NC; ++w) bb = wkey[w] > bb ? wkey[w] : bb;
+            a.amax_part[blockIdx.x] = bb;
             __threadfence();
             const unsigned ticket = atomicAdd(a.amax_count, 1u);
             flags[1] = (ticket == gridDim.x - 1);
@@ -336,12 +419,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const GemvArgs a, 
         __syncthreads();
         if (flags[1] && tid == 0) {
             __threadfence();
-            unsigned long long b = 0ull;
+            unsigned long long bb = 0ull;
             for (int i = 0; i < (int)gridDim.x; ++i) {
-                const unsigned long long k = __ldcg(a.amax_part + i);
-                b = k > b ? k : b;
+                const unsigned long long kk = __ldcg(a.amax_part + i);
+                bb = kk > bb ? kk : bb;
             }
-            int idx = (b == 0ull) ? 0 : argmax_idx(b);
+            int idx = (bb == 0ull) ? 0 : argmax_idx(bb);
             if (idx < 0 || idx >= a.d) idx = 0;
             const int pos = *a.pos;
             if (pos + 1 <= a.seq_len && pos + 1 >= *a.n_forced) a.tokens[pos + 1] = idx;
@@ -366,7 +449,7 @@ cudaError_t launch_t(const GemvArgs &a, const GemvPlan &p, cudaStream_t st, bool
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.grid);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(32 * kMinWarps);
     cfg.dynamicSmemBytes = p.smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -386,7 +469,12 @@ int gemv_tile_rows(int d, int epi, int num_sms) { return q8_tile_rows(d, num_sms
 bool gemv_supported(int n, int d, int epi) {
     if (n <= 0 || d <= 0 || n % 32) return false;
     if (epi == EPI_SWIGLU && (d & 1)) return false;
-    return gemv_x_bytes(n) + 36 * 1024 < kSmemBudget;  // the activation must fit beside one ring slot
+    return gemv_smem_tail(n) + 36 * 1024 < kSmemBudget;  // the activation must fit beside one ring slot
+}
+
+size_t gemv_smem_tail(int n) {
+    return gemv_x_bytes(n) + kMinWarps * 4 + 2 * kMaxSlots * 8 + kMaxConsumers * 8 + kMaxConsumers * 32 * 4 +
+           kMaxConsumers * 8 + 16;  // activation, red, full/empty, token flags, token sums, warp keys, flags
 }
 
 GemvPlan plan_gemv(int n, int d, int epi, int num_sms) {
@@ -395,23 +483,28 @@ GemvPlan plan_gemv(int n, int d, int epi, int num_sms) {
     p.ntiles = (d + p.T - 1) / p.T;
     p.grid = std::max(1, std::min(num_sms, p.ntiles));
     const int tiles_per_cta = (p.ntiles + p.grid - 1) / p.grid;
-    const int nblk = (n + 511) / 512;
-    p.CW = std::max(1, std::min(kMaxCW, tiles_per_cta));
+    const int stages = tiles_per_cta * ((n + 511) / 512);
     p.slot = (size_t)p.T * q8_blk_bytes(std::min(n, 512));
-    const size_t tail = gemv_x_bytes(n) + 32 + kMaxSlots * 16 + 8 + kMaxSlots * 8 + kMaxCW * 8 + 64;
-    const int stages_per_warp = ((tiles_per_cta + p.CW - 1) / p.CW) * nblk;
-    int spw = kMaxSPW;
-    while (spw > 1 && ((size_t)p.CW * spw * p.slot + tail > kSmemBudget || spw > stages_per_warp)) --spw;
-    p.SPW = spw;
-    p.PF = (int)(kPrefetchBytes / ((size_t)p.CW * p.slot));
-    p.xoff = (size_t)p.CW * spw * p.slot;
+    const size_t tail = gemv_smem_tail(n);
+    const size_t ring = kSmemBudget > tail ? kSmemBudget - tail : 0;
+    // Two producer threads, the deepest ring the budget allows (a multiple of 2), up to 4 consumer
+    // warps, and 3 stages of L2 prefetch beyond the ring: the best settings measured on B200 for the
+    // LLaMA shapes within the co-residency budget.
+    p.NP = 2;
+    p.S = std::max(1, std::min({kMaxSlots, (int)(ring / p.slot), stages}));
+    if (p.S >= 2) p.S -= p.S % p.NP;
+    else p.NP = 1;
+    p.NW = std::max(1, std::min({4, p.S, stages}));
+    p.PF = kPrefetchStages;
+    p.xoff = (size_t)p.S * p.slot;
     p.smem = p.xoff + tail;
     return p;
 }
 
 cudaError_t launch_gemv(const GemvArgs &a, const GemvPlan &p, cudaStream_t st, bool pdl) {
-    if (!gemv_supported(a.n, a.d, a.epi) || p.smem > 227 * 1024 || p.CW < 1 || p.CW > kMaxCW || p.SPW < 1 ||
-        p.SPW > kMaxSPW || p.T < 1 || p.T > 32)
+    if (!gemv_supported(a.n, a.d, a.epi) || p.smem > 227 * 1024 || p.NW < 1 || p.NW > kMaxConsumers || p.S < p.NW ||
+        p.NP < 1 || p.NW + p.NP > kMinWarps || p.S % p.NP ||
+        p.S > kMaxSlots || p.T < 1 || p.T > 32 || p.PF < 0 || p.smem < (size_t)p.S * p.slot + gemv_smem_tail(a.n))
         return cudaErrorInvalidValue;
 #define DK_GEMV_CASE(P, E) \
     if (a.pro == P && a.epi == E) return launch_t<P, E>(a, p, st, pdl);

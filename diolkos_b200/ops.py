@@ -84,6 +84,17 @@ def matmul_q(xq: torch.Tensor, xs: torch.Tensor, w_packed: torch.Tensor, n: int,
     return out
 
 
+def matmul_batch(x: torch.Tensor, ws: list, n: int, d: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """GEMVs of one activation against several packed matrices, back to back: out[i] = W_i * quant(x)."""
+    import ctypes
+
+    if out is None:
+        out = torch.empty((len(ws), d), dtype=torch.float32, device=x.device)
+    ptrs = (ctypes.c_void_p * len(ws))(*[_ptr(w) for w in ws])
+    check(lib().dk_matmul_q8_0_batch(_ptr(out), _ptr(x), ptrs, len(ws), n, d, stream_ptr()))
+    return out
+
+
 def rmsnorm(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     """rmsnorm (src/utils.c:59-76)."""
     o = torch.empty_like(x)

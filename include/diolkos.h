@@ -75,6 +75,12 @@ int dk_matmul_q8_0(float *out, const float *x, const uint8_t *w_packed, int n, i
 /* The same GEMV on an activation that is already quantised (xq int8[n], xs fp32[n/32]). */
 int dk_matmul_q8_0_q(float *out, const int8_t *xq, const float *xs, const uint8_t *w_packed, int n,
                      int d, void *stream);
+/* `count` GEMVs of the same activation x against count packed [d x n] matrices (the reference calls
+ * matmul once per matrix, e.g. wq, wk, wv on the same xb, src/transformer.c:83-85): out[i*d .. (i+1)*d)
+ * = W_i * quant(x).  Launched back to back; from the second GEMV on, each one starts streaming its
+ * weights while the previous one finishes, which is how the decode engine runs the kernel. */
+int dk_matmul_q8_0_batch(float *out, const float *x, const uint8_t *const *w_packed, int count, int n,
+                         int d, void *stream);
 /* rmsnorm (src/utils.c:59-76), device pointers; o may alias x. */
 int dk_rmsnorm(float *o, const float *x, const float *w, int n, void *stream);
 

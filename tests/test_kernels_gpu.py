@@ -275,3 +275,24 @@ def test_attention_decode_vs_fp64(torch_cuda, H, KVH, hs, seq, pos):
     np.testing.assert_allclose(out, ref, rtol=1e-5, atol=1e-5 * np.abs(ref).max())
     np.testing.assert_array_equal(dv[:, pos].cpu().numpy(), qkv[(H + KVH) * hs:].reshape(KVH, hs))
     assert not work[ops.attention_work_bytes(H, KVH, hs, seq) - 256:].any()  # counters back at zero
+
+
+def test_gemv_batch_equals_single(torch_cuda):
+    """dk_matmul_q8_0_batch (back-to-back GEMVs, the later ones started early) gives the same bits as
+    one dk_matmul_q8_0 call per matrix."""
+    from diolkos_b200 import ops
+
+    torch = torch_cuda
+    rng = np.random.default_rng(7)
+    n, d = 4096, 1000
+    ws = []
+    for _ in range(3):
+        q = rng.integers(-127, 128, n * d, dtype=np.int8)
+        s = (rng.random(n * d // 32, dtype=np.float32) * 0.001).astype(np.float32)
+        ws.append(ops.pack(_dev(torch, q), _dev(torch, s), n, d))
+    x = _dev(torch, rng.standard_normal(n).astype(np.float32))
+    batch = [ws[0], ws[1], ws[2], ws[1], ws[0]]
+    got = ops.matmul_batch(x, batch, n, d).cpu().numpy()
+    for i, w in enumerate(batch):
+        one = ops.matmul(x, w, n, d).cpu().numpy()
+        np.testing.assert_array_equal(got[i].view(np.uint32), one.view(np.uint32))
