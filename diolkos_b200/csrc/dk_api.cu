@@ -152,13 +152,16 @@ int dk_attention_decode(float *out, const float *qkv, const float *rope, void *k
         return set_error(DK_ERR_INVALID, "dk_attention_decode: bad kv_type %d", kv_type);
     if (!out || !qkv || !rope || !k_cache || !v_cache || !pos || !work)
         return set_error(DK_ERR_INVALID, "dk_attention_decode: null pointer");
+    if (reinterpret_cast<uintptr_t>(qkv) % 16 || reinterpret_cast<uintptr_t>(k_cache) % 16 ||
+        reinterpret_cast<uintptr_t>(v_cache) % 16)
+        return set_error(DK_ERR_INVALID, "dk_attention_decode: qkv, k_cache and v_cache must be 16-byte aligned");
     if (int r = check_aligned(work, 256, "work")) return r;
     AttnArgs a;
     a.qkv = qkv; a.rope = rope; a.k_cache = k_cache; a.v_cache = v_cache; a.out = out; a.pos = pos;
     a.n_heads = n_heads; a.n_kv_heads = n_kv_heads; a.head_size = head_size; a.seq_len = seq_len;
     a.kv_f32 = kv_type == DK_KV_F32;
     a.max_splits = attn_max_splits(seq_len, n_kv_heads, current_num_sms());
-    a.min_chunk = 64;
+    a.min_chunk = kAttnMinChunk;
     a.work = static_cast<float *>(work);
     a.count = reinterpret_cast<unsigned *>(static_cast<uint8_t *>(work) +
                                            attn_count_offset(n_heads, head_size, a.max_splits));

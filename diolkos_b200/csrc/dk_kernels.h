@@ -136,6 +136,8 @@ cudaError_t launch_embed(const uint8_t *emb_packed, int dim, int T, const int *t
                          cudaStream_t st, bool pdl);
 
 // ---------------- attention ------------------------------------------------------------------
+// Smallest run of positions one attention CTA takes (splits are never shorter).
+constexpr int kAttnMinChunk = 32;
 struct AttnArgs {
     const float *qkv = nullptr;  // [dim + 2*kv_dim]: q | k | v before RoPE
     const float *rope = nullptr; // [seq_len][head_size/2][2] (cos, sin)
@@ -147,7 +149,7 @@ struct AttnArgs {
     const int *pos = nullptr;
     int n_heads = 0, n_kv_heads = 0, head_size = 0, seq_len = 0;
     int kv_f32 = 0;
-    int max_splits = 1, min_chunk = 64;
+    int max_splits = 1, min_chunk = kAttnMinChunk;
     int *err = nullptr;
 };
 int attn_max_splits(int seq_len, int n_kv_heads, int num_sms);
@@ -156,7 +158,7 @@ size_t attn_smem_bytes(const AttnArgs &a);
 // at offset 0, then n_kv_heads arrival counters at attn_count_offset(); both 256-byte aligned.
 size_t attn_count_offset(int n_heads, int head_size, int max_splits);
 size_t attn_work_bytes(int n_heads, int n_kv_heads, int head_size, int max_splits);
-// Shape checks of launch_attention (head_size even and <= 128, n_heads a multiple of n_kv_heads
+// Shape checks of launch_attention (head_size a multiple of 4 and <= 128, n_heads a multiple of n_kv_heads
 // with at most 8 query heads per KV head).
 bool attn_supported(int n_heads, int n_kv_heads, int head_size);
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st, bool pdl);

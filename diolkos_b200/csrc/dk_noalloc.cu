@@ -58,6 +58,9 @@ extern "C" int dk_attention_decode_noalloc(float *out, const float *qkv, const f
         return set_error(DK_ERR_INVALID, "dk_attention_decode_noalloc: bad kv_type %d", kv_type);
     if (!out || !qkv || !rope || !k_cache || !v_cache || !pos)
         return set_error(DK_ERR_INVALID, "dk_attention_decode_noalloc: null pointer");
+    if (reinterpret_cast<uintptr_t>(qkv) % 16 || reinterpret_cast<uintptr_t>(k_cache) % 16 ||
+        reinterpret_cast<uintptr_t>(v_cache) % 16)
+        return set_error(DK_ERR_INVALID, "dk_attention_decode_noalloc: qkv, k_cache and v_cache must be 16-byte aligned");
     const int max_splits = attn_max_splits(seq_len, n_kv_heads, current_num_sms());
     const size_t work = attn_work_bytes(n_heads, n_kv_heads, head_size, max_splits);
     const size_t need = work + 256;  // + the error word
@@ -79,7 +82,7 @@ extern "C" int dk_attention_decode_noalloc(float *out, const float *qkv, const f
     a.n_heads = n_heads; a.n_kv_heads = n_kv_heads; a.head_size = head_size; a.seq_len = seq_len;
     a.kv_f32 = kv_type == DK_KV_F32;
     a.max_splits = max_splits;
-    a.min_chunk = 64;
+    a.min_chunk = kAttnMinChunk;
     a.work = reinterpret_cast<float *>(b);
     a.count = reinterpret_cast<unsigned *>(b + cnt_off);
     a.err = reinterpret_cast<int *>(b + work);

@@ -118,7 +118,7 @@ dk_model *dk_model_create(const int *cfg, int kv_type, int device, int tp_rank, 
     }
     const int dim = cfg[0], hidden = cfg[1], L = cfg[2], H = cfg[3], KVH = cfg[4], V = cfg[5], S = cfg[6];
     if (dim <= 0 || hidden <= 0 || L <= 0 || H <= 0 || KVH <= 0 || V <= 0 || S <= 0 || dim % H || H % KVH ||
-        dim % 32 || hidden % 32 || (dim / H) % 2 || dim / H > 128 || H / KVH > 8) {
+        dim % 32 || hidden % 32 || (dim / H) % 4 || dim / H > 128 || H / KVH > 8) {
         set_error(DK_ERR_INVALID, "dk_model_create: unsupported config dim=%d hidden=%d layers=%d heads=%d kv=%d",
                   dim, hidden, L, H, KVH);
         return nullptr;
@@ -368,7 +368,7 @@ static int enqueue_step(dk_model *m, cudaStream_t st) {
         at.v_cache = static_cast<uint8_t *>(m->vcache) + (size_t)l * m->kv_layer_elems * esz;
         at.out = m->xb; at.work = m->attn_work; at.count = m->attn_count; at.pos = m->pos;
         at.n_heads = m->n_heads; at.n_kv_heads = m->n_kv_heads; at.head_size = m->hs; at.seq_len = m->seq_len;
-        at.kv_f32 = m->kv_type == DK_KV_F32; at.max_splits = m->attn_splits; at.min_chunk = 64; at.err = m->err;
+        at.kv_f32 = m->kv_type == DK_KV_F32; at.max_splits = m->attn_splits; at.min_chunk = kAttnMinChunk; at.err = m->err;
         ++launches;
         if (int r = cuda_status(launch_attention(at, st, true), "attention")) return r;
         if (int r = gemv("wo gemv", m->p_wo, ly.wo, m->dim, m->dim, PRO_F32, EPI_ADD, m->xb, nullptr, m->x)) return r;
