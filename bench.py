@@ -36,6 +36,12 @@ PROMPT_LEN = 32
 GEN_LEN = 256
 SEED = 20260
 GEMV_SHAPES = [(4096, 4096), (11008, 4096), (4096, 11008), (32000, 4096)]  # [out x in]
+# The GEMVs of one 7B-shape decode step: (rows, cols, launches per step) -- fused q|k|v, wo, the
+# row-interleaved w1|w3, w2, and the classifier.
+DECODE_GEMVS = [(12288, 4096, 32), (4096, 4096, 32), (22016, 4096, 32), (4096, 11008, 32), (32000, 4096, 1)]
+# DRAM bytes / algorithmic bytes of one GEMV launch, from the ncu capture of every decode shape
+# summarised in profiles/gemv_q8_decode_shapes.txt (dram__bytes_read.sum + dram__bytes_write.sum).
+NCU_GEMV_TRAFFIC_RATIO = 1.003
 
 
 def parse():
@@ -235,16 +241,21 @@ class CpuReference:
 
 
 # ------------------------------------------------------------------ GEMV microbenchmark (config 2)
-def gemv_bench(reps: int = 64):
-    """The four GEMV shapes through dk_matmul_q8_0_batch: `reps` GEMVs back to back, rotating over
-    enough packed copies of the matrix that the working set is over 3x the L2, timed with CUDA
-    events on the launching stream (best of 3 batches)."""
+def gemv_alg_bytes(d: int, n: int) -> float:
+    """Algorithmic bytes of one [d x n] Q8_0 GEMV: weights + scales, the activation, the output."""
+    return d * n * 1.125 + n * 1.125 + d * 4
+
+
+def gemv_bench(reps: int = 64, shapes=None):
+    """GEMV shapes through dk_matmul_q8_0_batch: `reps` GEMVs back to back, rotating over enough
+    packed copies of the matrix that the working set is over 3x the L2, timed with CUDA events on
+    the launching stream (best of 3 batches)."""
     import torch
 
     from diolkos_b200 import ops
 
     out = {}
-    for d, n in GEMV_SHAPES:
+    for d, n in (shapes or GEMV_SHAPES):
         copies = max(2, int(3 * 126e6 // ops.packed_bytes(n, d)) + 1)
         g = torch.Generator(device="cuda").manual_seed(d * 31 + n)
         ws = []
@@ -266,7 +277,7 @@ def gemv_bench(reps: int = 64):
             e1.record()
             torch.cuda.synchronize()
             best = min(best, e0.elapsed_time(e1) * 1e3 / reps)
-        alg = d * n * 1.125 + n * 1.125 + d * 4
+        alg = gemv_alg_bytes(d, n)
         out[f"{d}x{n}"] = {"us": round(best, 2), "GBps": round(alg / best / 1e3, 1)}
         del ws, batch, y
         torch.cuda.empty_cache()
@@ -366,6 +377,12 @@ def run_decode(args):
     e2e = n_gen * len(e2e_times) / sum(e2e_times)
 
     gemv = gemv_bench()
+    # The dominant kernel: the GEMV, over the shapes and launch counts of one decode step.
+    mix = gemv_bench(shapes=[(d, n) for d, n, _ in DECODE_GEMVS])
+    mix_bytes = sum(c * gemv_alg_bytes(d, n) for d, n, c in DECODE_GEMVS)
+    mix_us = sum(c * mix[f"{d}x{n}"]["us"] for d, n, c in DECODE_GEMVS)
+    launches = sum(c for _, _, c in DECODE_GEMVS)
+    gemv_gbps = mix_bytes / mix_us / 1e3
     cpu = None
     if not args.no_cpu_baseline:
         try:
@@ -389,11 +406,20 @@ def run_decode(args):
                    "l2": "weights (7.4 GB) exceed L2; every token streams them from HBM"},
         "ms_per_token": round(ms_per_tok, 4),
         "gpu_launches": m.kernels_per_step * G * args.steps,
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(achieved / hbm, 4), "traffic": None,
-                     "what": f"whole decode step: weight + KV bytes per token ({bytes_tok / 1e9:.3f} GB) / "
-                             f"time per token; peak = {peak_kind} HBM copy bandwidth"},
+        "roofline": {"bound": "hbm", "achieved": round(gemv_gbps, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(gemv_gbps / hbm, 4),
+                     "traffic": (round(NCU_GEMV_TRAFFIC_RATIO * mix_bytes / launches)
+                                 if NCU_GEMV_TRAFFIC_RATIO else None),
+                     "kernel": "gemv_q8_kernel",
+                     "what": f"Q8_0 GEMV over one decode step's {launches} launches (shapes {DECODE_GEMVS}): "
+                             f"{mix_bytes / launches / 1e6:.2f} MB algorithmic bytes per launch / "
+                             f"{mix_us / launches:.2f} us average launch (CUDA events, back-to-back batches); "
+                             f"peak = {peak_kind} HBM copy bandwidth; traffic = DRAM bytes per launch"},
+        "step_roofline": {"achieved": round(achieved, 1), "frac": round(achieved / hbm, 4), "unit": "GB/s",
+                          "what": f"whole decode step: weight + KV bytes per token ({bytes_tok / 1e9:.3f} GB) / "
+                                  f"time per token"},
         "gemv": gemv,
+        "gemv_decode_shapes": mix,
         "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * P + 12,
                 "d2h_bytes_per_step": 4 * (P + G) + 4,
                 "how": "dk_model_generate (C ABI): host prompt -> host tokens, wall clock, prompt positions included"},
@@ -411,12 +437,14 @@ def run_gemv(args):
 
     torch.cuda.set_device(0)
     g = gemv_bench(reps=max(20, args.steps * 10))
+    mix = gemv_bench(reps=max(20, args.steps * 10), shapes=[(d, n) for d, n, _ in DECODE_GEMVS])
     hbm, kind = peaks()
     best = max(g.items(), key=lambda kv: kv[1]["GBps"])
     line = {"metric": "Q8_0 GEMV HBM GB/s", "value": best[1]["GBps"], "unit": "GB/s", "n_gpus": 1,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": "isolated Q8_0 GEMV, batch 1", "shapes": g}, "peak": hbm, "peak_kind": kind}
+            "config": {"workload": "isolated Q8_0 GEMV, batch 1", "shapes": g}, "decode_shapes": mix, "peak": hbm,
+            "peak_kind": kind}
     print(json.dumps(line), flush=True)
     return 0
 
