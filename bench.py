@@ -71,8 +71,8 @@ class ClockSampler:
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index  # an index, or a comma-separated list of indices
         self.proc = None
         self.path = None
 
@@ -134,13 +134,15 @@ def kv_bytes_read(cfg, pos0: int, pos1: int, elem: int) -> float:
     return 2.0 * tot * cfg.kv_dim * elem * cfg.n_layers
 
 
-def build_model(cfg, kv_f32: bool, seed: int):
+def build_model(cfg, kv_f32: bool, seed: int, rank: int = 0, world: int = 1, device: int = 0):
+    """The synthetic model on this GPU (this rank's shard of it under tensor parallelism): every rank
+    generates the same full weights on its GPU from the seed and the engine keeps its slices."""
     import torch
 
-    from diolkos_b200 import ops, synth
+    from diolkos_b200 import ops, synth, tp
     from diolkos_b200.model import Model, weight_id
 
-    m = Model(cfg, kv_f32=kv_f32)
+    m = Model(cfg, kv_f32=kv_f32, device=device, tp_rank=rank, tp_world=world)
     g = torch.Generator(device="cuda")
     for idx, (name, kind, shape) in enumerate(synth.tensor_specs(cfg)):
         which, layer = weight_id(name)
@@ -157,6 +159,8 @@ def build_model(cfg, kv_f32: bool, seed: int):
         torch.cuda.synchronize()
         m.set_weight_device(which, layer, q, s)
         del q, s
+    if world > 1:
+        tp.connect(m)
     m.finalize()
     return m
 
@@ -315,12 +319,36 @@ def run_reference(args):
 def run_decode(args):
     import torch
 
-    from diolkos_b200 import synth
+    from diolkos_b200 import synth, tp
 
     cfg = synth.LLAMA7B
     kv_f32 = args.kv == "f32"
-    torch.cuda.set_device(0)
-    m = build_model(cfg, kv_f32, SEED)
+    world = args.gpus
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        if int(os.environ.get("WORLD_SIZE", "1")) != world:
+            raise RuntimeError(f"--gpus {world} needs {world} ranks (torchrun --nproc-per-node {world})")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if dist is None:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    m = build_model(cfg, kv_f32, SEED, rank, world, local)
     stream = torch.cuda.ExternalStream(m.stream)
     prompt = synth.seeded_prompt(SEED, PROMPT_LEN, cfg.vocab_size)
     P, G = PROMPT_LEN, GEN_LEN
@@ -337,13 +365,16 @@ def run_decode(args):
     for _ in range(args.warmup):
         one_step()
     m.sync()
-    if m.device_error():
-        raise RuntimeError(f"device error word 0x{m.device_error():x} after warm-up")
+    err = int(max_over_ranks(float(m.device_error())))  # every rank takes the same exit
+    if err:
+        raise RuntimeError(f"device error word 0x{err:x} after warm-up")
 
-    sampler = ClockSampler(0)
-    sampler.start()
+    sampler = ClockSampler(",".join(str(i) for i in range(world)) if rank == 0 else local)
+    if rank == 0:
+        sampler.start()
     torch.cuda.synchronize()
     m.sync()
+    barrier()
     t_all0 = time.perf_counter()
     evs = []
     for _ in range(args.steps):
@@ -352,11 +383,13 @@ def run_decode(args):
         evs.append(e)
     m.sync()
     torch.cuda.synchronize()
+    barrier()
     wall = time.perf_counter() - t_all0
-    clocks = sampler.stop()
-    decode_ms = sum(a.elapsed_time(b) for a, b in evs)
-    if m.device_error():
-        raise RuntimeError(f"device error word 0x{m.device_error():x}")
+    clocks = sampler.stop() if rank == 0 else None
+    decode_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in evs))
+    err = int(max_over_ranks(float(m.device_error())))
+    if err:
+        raise RuntimeError(f"device error word 0x{err:x}")
     toks = m.get_tokens(P + G)
 
     value = G * args.steps / (decode_ms / 1e3)
@@ -370,21 +403,34 @@ def run_decode(args):
     e2e_times = []
     n_gen = 0
     for _ in range(max(1, args.steps)):
+        barrier()
         t0 = time.perf_counter()
         gen = m.generate(prompt, P - 1 + G)
-        e2e_times.append(time.perf_counter() - t0)
+        e2e_times.append(max_over_ranks(time.perf_counter() - t0))
         n_gen = len(gen)
     e2e = n_gen * len(e2e_times) / sum(e2e_times)
+    kernels_per_step = m.kernels_per_step
+    m.close()  # every rank leaves the exchange at the same point
+    barrier()
+    if dist is not None:
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
 
-    gemv = gemv_bench()
-    # The dominant kernel: the GEMV, over the shapes and launch counts of one decode step.
-    mix = gemv_bench(shapes=[(d, n) for d, n, _ in DECODE_GEMVS])
-    mix_bytes = sum(c * gemv_alg_bytes(d, n) for d, n, c in DECODE_GEMVS)
-    mix_us = sum(c * mix[f"{d}x{n}"]["us"] for d, n, c in DECODE_GEMVS)
-    launches = sum(c for _, _, c in DECODE_GEMVS)
+    # The dominant kernel: the GEMV, over this rank's shapes and launch counts of one decode step.
+    sh = tp.shard(cfg, rank, world)
+    ld, lkv, lh = sh.q_rows[1] - sh.q_rows[0], sh.kv_rows[1] - sh.kv_rows[0], sh.hidden_rows[1] - sh.hidden_rows[0]
+    lv = sh.vocab_rows[1] - sh.vocab_rows[0]
+    decode_gemvs = [(ld + 2 * lkv, cfg.dim, cfg.n_layers), (cfg.dim, ld, cfg.n_layers),
+                    (2 * lh, cfg.dim, cfg.n_layers), (cfg.dim, lh, cfg.n_layers), (lv, cfg.dim, 1)]
+    gemv = gemv_bench() if world == 1 else None
+    mix = gemv_bench(shapes=[(d, n) for d, n, _ in decode_gemvs])
+    mix_bytes = sum(c * gemv_alg_bytes(d, n) for d, n, c in decode_gemvs)
+    mix_us = sum(c * mix[f"{d}x{n}"]["us"] for d, n, c in decode_gemvs)
+    launches = sum(c for _, _, c in decode_gemvs)
     gemv_gbps = mix_bytes / mix_us / 1e3
     cpu = None
-    if not args.no_cpu_baseline:
+    if not args.no_cpu_baseline and world == 1:
         try:
             cb = CpuReference(cfg)
             cb.sample()
@@ -395,29 +441,34 @@ def run_decode(args):
                    "sample": f"not run: {ex}"}
 
     line = {
-        "metric": "Q8_0 decode tok/s batch 1", "value": round(value, 2), "unit": "tok/s", "n_gpus": 1,
+        "metric": "Q8_0 decode tok/s batch 1", "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(decode_ms / args.steps, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
         "data": "synthetic (seeded N(0,0.02) weights, seeded prompt)",
         "config": {"workload": "llama2-7b-shape q8_0 decode: 32-token prompt, then 256 greedy tokens timed",
                    "model": "llama2-7b-shape", "dim": cfg.dim, "hidden": cfg.hidden_dim, "layers": cfg.n_layers,
                    "heads": cfg.n_heads, "kv_heads": cfg.n_kv_heads, "vocab": cfg.vocab_size,
-                   "seq_len": cfg.seq_len, "kv_cache": args.kv, "global_batch": 1, "parallelism": "single GPU",
+                   "seq_len": cfg.seq_len, "kv_cache": args.kv, "global_batch": 1,
+                   "parallelism": "single GPU" if world == 1 else
+                   f"tp{world}: heads / w1,w3 rows / classifier rows per GPU, wo and w2 partial sums "
+                   f"exchanged inside the GEMVs over NVLink peer memory",
                    "l2": "weights (7.4 GB) exceed L2; every token streams them from HBM"},
         "ms_per_token": round(ms_per_tok, 4),
-        "gpu_launches": m.kernels_per_step * G * args.steps,
+        "gpu_launches": kernels_per_step * G * args.steps,
         "roofline": {"bound": "hbm", "achieved": round(gemv_gbps, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(gemv_gbps / hbm, 4),
                      "traffic": (round(NCU_GEMV_TRAFFIC_RATIO * mix_bytes / launches)
                                  if NCU_GEMV_TRAFFIC_RATIO else None),
                      "kernel": "gemv_q8_kernel",
-                     "what": f"Q8_0 GEMV over one decode step's {launches} launches (shapes {DECODE_GEMVS}): "
+                     "what": f"Q8_0 GEMV over one decode step's {launches} launches on rank 0 (shapes "
+                             f"{decode_gemvs}): "
                              f"{mix_bytes / launches / 1e6:.2f} MB algorithmic bytes per launch / "
                              f"{mix_us / launches:.2f} us average launch (CUDA events, back-to-back batches); "
                              f"peak = {peak_kind} HBM copy bandwidth; traffic = DRAM bytes per launch"},
-        "step_roofline": {"achieved": round(achieved, 1), "frac": round(achieved / hbm, 4), "unit": "GB/s",
+        "step_roofline": {"achieved": round(achieved, 1), "frac": round(achieved / (hbm * world), 4),
+                          "unit": "GB/s",
                           "what": f"whole decode step: weight + KV bytes per token ({bytes_tok / 1e9:.3f} GB) / "
-                                  f"time per token"},
+                                  f"time per token, against {world} x the HBM peak"},
         "gemv": gemv,
         "gemv_decode_shapes": mix,
         "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * P + 12,
@@ -453,9 +504,6 @@ def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
-    if args.gpus > 1:
-        print(json.dumps({"error": "tensor-parallel decode is not available in this build"}), flush=True)
-        return 1
     if args.workload == "gemv":
         return run_gemv(args)
     return run_decode(args)

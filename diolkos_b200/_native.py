@@ -15,6 +15,7 @@ DK_OK = 0
 DK_ERR_INVALID, DK_ERR_CUDA, DK_ERR_TIMEOUT, DK_ERR_NOMEM, DK_ERR_IO, DK_ERR_STATE, DK_ERR_COMM = (
     0x01, 0x02, 0x04, 0x08, 0x10, 0x20, 0x40)
 DK_KV_BF16, DK_KV_F32 = 0, 1
+DK_COMM_HANDLE_BYTES = 64
 (DK_W_EMB, DK_W_RMS_FINAL, DK_W_WCLS, DK_W_RMS_ATT, DK_W_WQ, DK_W_WK, DK_W_WV, DK_W_WO, DK_W_RMS_FFN,
  DK_W_W1, DK_W_W2, DK_W_W3) = range(12)
 
@@ -42,6 +43,8 @@ SIGNATURES = {
     "dk_model_destroy": (None, [_vp]),
     "dk_model_set_weight": (_i, [_vp, _i, _i, _vp, _vp]),
     "dk_model_set_weight_device": (_i, [_vp, _i, _i, _vp, _vp]),
+    "dk_model_comm_handle": (_i, [_vp, _vp]),
+    "dk_model_comm_connect": (_i, [_vp, _vp]),
     "dk_model_finalize": (_i, [_vp]),
     "dk_model_forward": (_i, [_vp, _i, _i, _vp]),
     "dk_model_generate": (_i, [_vp, _vp, _i, _i, _vp, C.POINTER(C.c_int)]),

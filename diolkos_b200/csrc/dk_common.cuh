@@ -93,6 +93,26 @@ __device__ __forceinline__ bool mbar_wait_abortable(uint64_t *bar, uint32_t pari
     }
 }
 
+// ---- cross-GPU signalling (tensor parallel, over NVLink peer memory) -----------------------------
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+// Bounded wait until the counter (written by other GPUs) reaches `target`.  A peer that never
+// arrives raises DK_ERR_COMM after DK_WAIT_LIMIT_CYCLES instead of hanging the kernel.
+__device__ __forceinline__ bool wait_counter(const unsigned long long *cnt, unsigned long long target, int *err) {
+    if (ld_acquire_sys(cnt) >= target) return true;
+    const long long t0 = clock64();
+    while (ld_acquire_sys(cnt) < target) {
+        if (clock64() - t0 > DK_WAIT_LIMIT_CYCLES) {
+            atomicOr(err, DK_ERR_COMM);
+            return false;
+        }
+    }
+    return true;
+}
+
 // ---- bulk copy engine (TMA, 1-D) --------------------------------------------------------------
 // L2 policy for streamed-once data (weights): evict first, so the KV cache and activations stay.
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {

@@ -14,6 +14,8 @@ enum GemvPro : int {
     PRO_F32 = 1,      // quantise fp32 x[n] (convert_f32_q8, src/tensor.c:199)
     PRO_RMS = 2,      // rmsnorm(x, norm_w) then quantise (src/utils.c:59 + src/tensor.c:199)
     PRO_EMB_RMS = 3,  // x = dequant(embedding row tokens[*pos]) (written back by CTA 0), then as PRO_RMS
+    PRO_RMS_REDUCE = 4,  // tensor parallel: wait for every rank's partial rows, x_out = x + sum over ranks
+                         // (rank order; written by CTA 0), then as PRO_RMS on x_out
 };
 // Epilogue: what happens to each finished row value.
 enum GemvEpi : int {
@@ -22,6 +24,8 @@ enum GemvEpi : int {
     EPI_SWIGLU = 2,  // rows (2i, 2i+1) = (w1_i, w3_i): out[i] = silu(v0) * v1 (src/transformer.c:212-222)
     EPI_ARGMAX = 3,  // out[row] = v, and the greedy token (src/sampler.c:6-17) is written to tokens[pos+1]
     EPI_NONE = 4,    // partial sums only (tensor-parallel split: the caller reduces)
+    EPI_PEER = 5,    // tensor parallel: store each row's partial sum into every rank's receive area
+                     // (over NVLink peer memory), then count the rows on every rank's counter
 };
 
 struct GemvArgs {
@@ -43,6 +47,27 @@ struct GemvArgs {
     const int *n_forced = nullptr;            // prompt length: tokens[0..n_forced) are forced
     int seq_len = 0;
     int *err = nullptr;                       // device error word
+    // ---- tensor-parallel exchange (tp_world > 1) ----
+    int tp_rank = 0, tp_world = 1;
+    // EPI_PEER: [tp_world] device pointers to each rank's receive area for this exchange point
+    // (float[tp_world][d], indexed by the source rank) and to each rank's counter for it.
+    float *const *peer_recv = nullptr;
+    unsigned long long *const *peer_cnt = nullptr;
+    // PRO_RMS_REDUCE: this rank's receive area (float[tp_world][n]) and counter; the wait ends when the
+    // counter reaches (epoch * red_period + red_index + 1) * tp_world * n.
+    const float *recv = nullptr;
+    const unsigned long long *cnt = nullptr;
+    int red_index = 0, red_period = 0;
+    const unsigned long long *epoch = nullptr;  // decode steps completed (advanced by the classifier)
+    float *x_out = nullptr;
+    // EPI_ARGMAX across ranks: each rank's key array (u64[tp_world]) and its counter; this rank's own.
+    unsigned long long *const *peer_amax = nullptr;
+    unsigned long long *const *peer_amax_cnt = nullptr;
+    const unsigned long long *amax_keys = nullptr;
+    const unsigned long long *amax_keys_cnt = nullptr;
+    unsigned long long *epoch_rw = nullptr;     // the classifier's writable view of epoch
+    int row_offset = 0;                         // global index of this rank's first classifier row
+    int vocab = 0;                              // rows of the whole classifier (0: d)
 };
 
 struct GemvPlan {
@@ -127,10 +152,12 @@ cudaError_t launch_quant_bf16(const uint16_t *x, size_t n, int8_t *q, float *s, 
 cudaError_t launch_quant_f32(const float *x, size_t n, int8_t *q, float *s, cudaStream_t st);
 cudaError_t launch_dequant(const int8_t *q, const float *s, size_t n, float *out, cudaStream_t st);
 cudaError_t launch_group_dots(const int8_t *xq, const int8_t *wq, int n, int d, int32_t *dots, cudaStream_t st);
-// Pack `rows` planar rows (int8 q[rows*n], fp32 s[rows*n/32]) into packed rows row0, row0+step, ...
-// of a matrix with tile height T (the destination must be zeroed beforehand: padding stays zero).
+// Pack `rows` planar rows into packed rows row0, row0+step, ... of an n-column matrix with tile
+// height T.  Source row i is columns [col0, col0+n) of a planar matrix with src_n columns: int8
+// q[i*src_n + col0 ..], fp32 s[i*src_n/32 + col0/32 ..] (col0 % 32 == 0).  The destination must be
+// zeroed beforehand (padding stays zero).
 cudaError_t launch_pack_rows(uint8_t *dst, int n, int T, const int8_t *q, const float *s, int rows, int row0,
-                             int step, cudaStream_t st);
+                             int step, cudaStream_t st, int src_n = 0, int col0 = 0);
 cudaError_t launch_rmsnorm(float *o, const float *x, const float *w, int n, cudaStream_t st);
 cudaError_t launch_embed(const uint8_t *emb_packed, int dim, int T, const int *tokens, const int *pos, float *x,
                          cudaStream_t st, bool pdl);

@@ -63,8 +63,9 @@ struct dk_model {
     // global config
     int dim, hidden, n_layers, n_heads, n_kv_heads, vocab, seq_len, kv_type, device, rank, world;
     int hs, kv_dim;
-    // this rank's shard sizes
-    int l_heads, l_kv_heads, l_hidden;
+    // this rank's shard: heads [rank*l_heads, ...), hidden rows [rank*l_hidden, ...), classifier rows
+    // [vocab_off, vocab_off + l_vocab); l_dim / l_kv_dim = its q / k columns of the attention
+    int l_heads, l_kv_heads, l_hidden, l_dim, l_kv_dim, l_vocab, vocab_off;
     int num_sms;
     cudaStream_t stream = nullptr;
     // weights
@@ -97,6 +98,16 @@ struct dk_model {
     cudaGraphExec_t exec = nullptr;
     int kernels_per_step = 0;
     bool finalized = false;
+    // tensor-parallel exchange area (world > 1): this rank's, exported over CUDA IPC, and the peers'
+    // mappings of theirs.  Layout: float recv[2][world][dim] | u64 cnt[2] | u64 keys[8] | u64 keys_cnt.
+    uint8_t *comm = nullptr;
+    size_t comm_bytes = 0, comm_ctl = 0;  // comm_ctl: offset of cnt[0]
+    std::vector<void *> peer_base;        // [world]; this rank's entry is `comm`
+    std::vector<bool> peer_opened;
+    void **d_ptrs = nullptr;              // device pointer tables (see comm_tables)
+    float *x2 = nullptr;                  // second residual buffer (the reduces ping-pong x <-> x2)
+    unsigned long long *epoch = nullptr;  // decode steps completed (the exchange counters' epoch)
+    bool connected = false;
 };
 
 static size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
@@ -123,8 +134,15 @@ dk_model *dk_model_create(const int *cfg, int kv_type, int device, int tp_rank, 
                   dim, hidden, L, H, KVH);
         return nullptr;
     }
-    if (tp_world != 1 || tp_rank != 0) {
-        set_error(DK_ERR_INVALID, "dk_model_create: this entry point builds single-GPU models (tp_world=1)");
+    if (tp_world < 1 || tp_world > 8 || tp_rank < 0 || tp_rank >= tp_world) {
+        set_error(DK_ERR_INVALID, "dk_model_create: tensor-parallel rank %d of %d (1 to 8 ranks)", tp_rank, tp_world);
+        return nullptr;
+    }
+    if (tp_world > 1 && (H % tp_world || KVH % tp_world || hidden % (32 * tp_world) || ((dim / H) * (H / tp_world)) % 32)) {
+        set_error(DK_ERR_INVALID,
+                  "dk_model_create: %d ranks need heads, kv heads divisible by the ranks, hidden/ranks and "
+                  "head_size*heads/ranks multiples of 32 (heads=%d kv=%d hidden=%d)",
+                  tp_world, H, KVH, hidden);
         return nullptr;
     }
     if (kv_type != DK_KV_BF16 && kv_type != DK_KV_F32) {
@@ -144,6 +162,18 @@ dk_model *dk_model_create(const int *cfg, int kv_type, int device, int tp_rank, 
     m->l_heads = H / tp_world;
     m->l_kv_heads = KVH / tp_world;
     m->l_hidden = hidden / tp_world;
+    m->l_dim = m->l_heads * m->hs;
+    m->l_kv_dim = m->l_kv_heads * m->hs;
+    {
+        const int per = (V + tp_world - 1) / tp_world;
+        m->vocab_off = tp_rank * per;
+        m->l_vocab = std::max(0, std::min(V - m->vocab_off, per));
+    }
+    if (m->l_vocab < 1) {
+        set_error(DK_ERR_INVALID, "dk_model_create: rank %d gets no classifier rows", tp_rank);
+        delete m;
+        return nullptr;
+    }
     cudaDeviceGetAttribute(&m->num_sms, cudaDevAttrMultiProcessorCount, device);
     m->layers.resize(L);
     m->have.assign((size_t)(L + 1) * DK_W_COUNT, 0);
@@ -155,16 +185,17 @@ dk_model *dk_model_create(const int *cfg, int kv_type, int device, int tp_rank, 
     };
     if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess) return fail("stream");
 
-    // ---- GEMV plans (they fix each matrix's tile height, hence its packed size)
-    const int qkv_rows = dim + 2 * m->kv_dim;
+    // ---- GEMV plans on this rank's shapes (they fix each matrix's tile height, hence its packed size)
+    const int qkv_rows = m->l_dim + 2 * m->l_kv_dim, lh = m->l_hidden;
     m->p_qkv = plan_gemv(dim, qkv_rows, EPI_STORE, m->num_sms);
-    m->p_wo = plan_gemv(dim, dim, EPI_ADD, m->num_sms);
-    m->p_w13 = plan_gemv(dim, 2 * hidden, EPI_SWIGLU, m->num_sms);
-    m->p_w2 = plan_gemv(hidden, dim, EPI_ADD, m->num_sms);
-    m->p_cls = plan_gemv(dim, V, EPI_ARGMAX, m->num_sms);
+    m->p_wo = plan_gemv(m->l_dim, dim, EPI_ADD, m->num_sms);
+    m->p_w13 = plan_gemv(dim, 2 * lh, EPI_SWIGLU, m->num_sms);
+    m->p_w2 = plan_gemv(lh, dim, EPI_ADD, m->num_sms);
+    m->p_cls = plan_gemv(dim, m->l_vocab, EPI_ARGMAX, m->num_sms);
     m->emb_T = gemv_tile_rows(V, EPI_STORE, m->num_sms);
-    if (!gemv_supported(dim, qkv_rows, EPI_STORE) || !gemv_supported(dim, 2 * hidden, EPI_SWIGLU) ||
-        !gemv_supported(hidden, dim, EPI_ADD) || !gemv_supported(dim, V, EPI_ARGMAX)) {
+    if (!gemv_supported(dim, qkv_rows, EPI_STORE) || !gemv_supported(dim, 2 * lh, EPI_SWIGLU) ||
+        !gemv_supported(lh, dim, EPI_ADD) || !gemv_supported(m->l_dim, dim, EPI_ADD) ||
+        !gemv_supported(dim, m->l_vocab, EPI_ARGMAX)) {
         set_error(DK_ERR_INVALID, "dk_model_create: matrix shapes exceed the GEMV's shared-memory budget");
         dk_model_destroy(m);
         return nullptr;
@@ -172,12 +203,12 @@ dk_model *dk_model_create(const int *cfg, int kv_type, int device, int tp_rank, 
 
     // ---- weights (zeroed: the pad rows of ragged last tiles and the pad bytes of segments stay 0)
     const size_t b_qkv = align256(q8_packed_bytes(dim, qkv_rows, m->p_qkv.T));
-    const size_t b_wo = align256(q8_packed_bytes(dim, dim, m->p_wo.T));
-    const size_t b_w13 = align256(q8_packed_bytes(dim, 2 * hidden, m->p_w13.T));
-    const size_t b_w2 = align256(q8_packed_bytes(hidden, dim, m->p_w2.T));
+    const size_t b_wo = align256(q8_packed_bytes(m->l_dim, dim, m->p_wo.T));
+    const size_t b_w13 = align256(q8_packed_bytes(dim, 2 * lh, m->p_w13.T));
+    const size_t b_w2 = align256(q8_packed_bytes(lh, dim, m->p_w2.T));
     const size_t b_norm = align256((size_t)dim * 4);
     const size_t b_emb = align256(q8_packed_bytes(dim, V, m->emb_T));
-    const size_t b_cls = align256(q8_packed_bytes(dim, V, m->p_cls.T));
+    const size_t b_cls = align256(q8_packed_bytes(dim, m->l_vocab, m->p_cls.T));
     const size_t per_layer = b_qkv + b_wo + b_w13 + b_w2 + 2 * b_norm;
     m->warena_bytes = per_layer * L + b_emb + b_cls + b_norm;
     if (cudaMalloc(&m->warena, m->warena_bytes) != cudaSuccess) return fail("weight memory");
@@ -198,26 +229,28 @@ dk_model *dk_model_create(const int *cfg, int kv_type, int device, int tp_rank, 
 
     // ---- KV cache
     const size_t esz = kv_type == DK_KV_F32 ? 4 : 2;
-    m->kv_layer_elems = (size_t)KVH * S * m->hs;
+    m->kv_layer_elems = (size_t)m->l_kv_heads * S * m->hs;
     if (cudaMalloc(&m->kcache, m->kv_layer_elems * L * esz) != cudaSuccess) return fail("key cache");
     if (cudaMalloc(&m->vcache, m->kv_layer_elems * L * esz) != cudaSuccess) return fail("value cache");
     cudaMemsetAsync(m->kcache, 0, m->kv_layer_elems * L * esz, m->stream);
     cudaMemsetAsync(m->vcache, 0, m->kv_layer_elems * L * esz, m->stream);
 
     // ---- activations and small state
-    m->attn_splits = attn_max_splits(S, KVH, m->num_sms);
+    m->attn_splits = attn_max_splits(S, m->l_kv_heads, m->num_sms);
     const size_t sz_x = align256((size_t)dim * 4), sz_qkv = align256((size_t)qkv_rows * 4);
-    const size_t sz_hb = align256((size_t)hidden * 4), sz_logits = align256((size_t)V * 4);
+    const size_t sz_hb = align256((size_t)lh * 4), sz_logits = align256((size_t)m->l_vocab * 4);
     const size_t sz_rope = align256((size_t)S * m->hs * 4);
-    const size_t sz_work = align256((size_t)H * m->attn_splits * (m->hs + 2) * 4);
-    const size_t sz_cnt = align256((size_t)KVH * 4);
+    const size_t sz_work = align256((size_t)m->l_heads * m->attn_splits * (m->hs + 2) * 4);
+    const size_t sz_cnt = align256((size_t)m->l_kv_heads * 4);
     const size_t sz_part = align256((size_t)kMaxGemvGrid * m->num_sms * 8);
     const size_t sz_tok = align256((size_t)(S + 1) * 4);
-    const size_t total = sz_x * 2 + sz_qkv + sz_hb + sz_logits + sz_rope + sz_work + sz_cnt + sz_part + 256 + sz_tok + 3 * 256;
+    const size_t total = sz_x * 3 + sz_qkv + sz_hb + sz_logits + sz_rope + sz_work + sz_cnt + sz_part + 256 + sz_tok +
+                         4 * 256;
     if (cudaMalloc(&m->aarena, total) != cudaSuccess) return fail("activation memory");
     cudaMemsetAsync(m->aarena, 0, total, m->stream);
     p = m->aarena;
     m->x = reinterpret_cast<float *>(p); p += sz_x;
+    m->x2 = reinterpret_cast<float *>(p); p += sz_x;
     m->xb = reinterpret_cast<float *>(p); p += sz_x;
     m->qkv = reinterpret_cast<float *>(p); p += sz_qkv;
     m->hb = reinterpret_cast<float *>(p); p += sz_hb;
@@ -231,6 +264,19 @@ dk_model *dk_model_create(const int *cfg, int kv_type, int device, int tp_rank, 
     m->pos = reinterpret_cast<int *>(p); p += 256;
     m->n_forced = reinterpret_cast<int *>(p); p += 256;
     m->err = reinterpret_cast<int *>(p); p += 256;
+    m->epoch = reinterpret_cast<unsigned long long *>(p); p += 256;
+
+    // ---- tensor-parallel exchange area (its own allocation: it is exported to the peers over IPC)
+    if (tp_world > 1) {
+        m->comm_ctl = align256((size_t)2 * tp_world * dim * 4);
+        m->comm_bytes = m->comm_ctl + 256;
+        if (cudaMalloc(&m->comm, m->comm_bytes) != cudaSuccess) return fail("exchange area");
+        if (cudaMemset(m->comm, 0, m->comm_bytes) != cudaSuccess) return fail("exchange area clear");
+        if (cudaMalloc(&m->d_ptrs, 6 * 8 * sizeof(void *)) != cudaSuccess) return fail("peer pointer tables");
+        m->peer_base.assign(tp_world, nullptr);
+        m->peer_opened.assign(tp_world, false);
+        m->peer_base[tp_rank] = m->comm;
+    }
 
     std::vector<float> rt;
     rope_table(rt, S, m->hs);
@@ -253,6 +299,10 @@ void dk_model_destroy(dk_model *m) {
     cudaFree(m->vcache);
     cudaFree(m->aarena);
     cudaFree(m->stage);
+    for (size_t q = 0; q < m->peer_base.size(); ++q)
+        if (m->peer_opened[q]) cudaIpcCloseMemHandle(m->peer_base[q]);
+    cudaFree(m->comm);
+    cudaFree(m->d_ptrs);
     if (m->h_small) cudaFreeHost(m->h_small);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
@@ -316,21 +366,35 @@ static int set_weight_impl(dk_model *m, int which, int layer, const void *q, con
             src_q = reinterpret_cast<const int8_t *>(m->stage);
             src_s = reinterpret_cast<const float *>(m->stage + align256(nq));
         }
+        // This rank's part of the full matrix: rows [r0, r0 + nrows) and columns [c0, c0 + ncols),
+        // packed into rows row0, row0 + step, ... of the local matrix.
         uint8_t *dst = nullptr;
-        int row0 = 0, step = 1, T = 32;
+        int row0 = 0, step = 1, T = 32, r0 = 0, nrows = rows, c0 = 0, ncols = cols;
+        const dk_layer *ly = per_layer ? &m->layers[layer] : nullptr;
         switch (which) {
         case DK_W_EMB: dst = m->emb; T = m->emb_T; break;
-        case DK_W_WCLS: dst = m->wcls; T = m->p_cls.T; break;
-        case DK_W_WQ: dst = m->layers[layer].wqkv; T = m->p_qkv.T; break;
-        case DK_W_WK: dst = m->layers[layer].wqkv; row0 = m->dim; T = m->p_qkv.T; break;
-        case DK_W_WV: dst = m->layers[layer].wqkv; row0 = m->dim + m->kv_dim; T = m->p_qkv.T; break;
-        case DK_W_WO: dst = m->layers[layer].wo; T = m->p_wo.T; break;
-        case DK_W_W1: dst = m->layers[layer].w13; row0 = 0; step = 2; T = m->p_w13.T; break;
-        case DK_W_W3: dst = m->layers[layer].w13; row0 = 1; step = 2; T = m->p_w13.T; break;
-        case DK_W_W2: dst = m->layers[layer].w2; T = m->p_w2.T; break;
+        case DK_W_WCLS: dst = m->wcls; T = m->p_cls.T; r0 = m->vocab_off; nrows = m->l_vocab; break;
+        case DK_W_WQ: dst = ly->wqkv; T = m->p_qkv.T; r0 = m->rank * m->l_dim; nrows = m->l_dim; break;
+        case DK_W_WK:
+            dst = ly->wqkv; row0 = m->l_dim; T = m->p_qkv.T; r0 = m->rank * m->l_kv_dim; nrows = m->l_kv_dim;
+            break;
+        case DK_W_WV:
+            dst = ly->wqkv; row0 = m->l_dim + m->l_kv_dim; T = m->p_qkv.T; r0 = m->rank * m->l_kv_dim;
+            nrows = m->l_kv_dim;
+            break;
+        case DK_W_WO: dst = ly->wo; T = m->p_wo.T; c0 = m->rank * m->l_dim; ncols = m->l_dim; break;
+        case DK_W_W1:
+            dst = ly->w13; row0 = 0; step = 2; T = m->p_w13.T; r0 = m->rank * m->l_hidden; nrows = m->l_hidden;
+            break;
+        case DK_W_W3:
+            dst = ly->w13; row0 = 1; step = 2; T = m->p_w13.T; r0 = m->rank * m->l_hidden; nrows = m->l_hidden;
+            break;
+        case DK_W_W2: dst = ly->w2; T = m->p_w2.T; c0 = m->rank * m->l_hidden; ncols = m->l_hidden; break;
         default: break;
         }
-        if (int r = cuda_status(launch_pack_rows(dst, cols, T, src_q, src_s, rows, row0, step, st), "pack rows"))
+        if (int r = cuda_status(launch_pack_rows(dst, ncols, T, src_q + (size_t)r0 * cols, src_s + (size_t)r0 * (cols / 32),
+                                                 nrows, row0, step, st, cols, c0),
+                                "pack rows"))
             return r;
         // The staging buffer is reused by the next call, and a caller may free its device source
         // buffers as soon as this returns: wait for the copy.
@@ -340,49 +404,109 @@ static int set_weight_impl(dk_model *m, int which, int layer, const void *q, con
     return DK_OK;
 }
 
+// Offsets inside a rank's exchange area and the device pointer tables built from the peers' mappings:
+// table t (8 entries, one per rank) at d_ptrs + 8*t: 0/1 receive areas of parity 0/1, 2/3 their
+// counters, 4 the argmax key arrays, 5 their counters.
+static size_t comm_recv_off(const dk_model *m, int par) { return (size_t)par * m->world * m->dim * 4; }
+static size_t comm_cnt_off(const dk_model *m, int par) { return m->comm_ctl + 8 * (size_t)par; }
+static size_t comm_keys_off(const dk_model *m) { return m->comm_ctl + 16; }
+static size_t comm_keys_cnt_off(const dk_model *m) { return m->comm_ctl + 16 + 64; }
+
 static int enqueue_step(dk_model *m, cudaStream_t st) {
     int launches = 0;
     // The first kernel of the step has no kernel predecessor inside the graph, so it is launched
     // without the programmatic-dependency attribute; every later kernel overlaps its weight
     // prefetch with the tail of the previous one.
-    auto gemv = [&](const char *what, const GemvPlan &p, const uint8_t *w, int n, int d, int pro, int epi,
-                    const float *x, const float *norm, float *out) -> int {
+    auto base_args = [&](const uint8_t *w, int n, int d, int pro, int epi, const float *x, const float *norm,
+                         float *out) {
         GemvArgs a;
         a.w = w; a.n = n; a.d = d; a.pro = pro; a.epi = epi; a.x = x; a.norm_w = norm; a.out = out;
-        a.emb = m->emb; a.emb_T = m->emb_T; a.tokens = m->tokens; a.pos = m->pos; a.n_forced = m->n_forced; a.seq_len = m->seq_len;
-        a.amax_part = m->amax_part; a.amax_count = m->amax_count; a.err = m->err;
+        a.emb = m->emb; a.emb_T = m->emb_T; a.tokens = m->tokens; a.pos = m->pos; a.n_forced = m->n_forced;
+        a.seq_len = m->seq_len; a.amax_part = m->amax_part; a.amax_count = m->amax_count; a.err = m->err;
+        a.tp_rank = m->rank; a.tp_world = m->world; a.epoch = m->epoch; a.epoch_rw = m->epoch;
+        a.row_offset = m->vocab_off; a.vocab = m->vocab;
+        return a;
+    };
+    auto launch = [&](const char *what, const GemvPlan &p, const GemvArgs &a) -> int {
         const bool pdl = launches > 0;
         ++launches;
         return cuda_status(launch_gemv(a, p, st, pdl), what);
     };
-    const int qkv_rows = m->dim + 2 * m->kv_dim;
+    const bool tp = m->world > 1;
+    void *const *tab = reinterpret_cast<void *const *>(m->d_ptrs);
+    // Tensor parallel: this rank's partial rows of wo / w2 go to every rank (EPI_PEER, exchange point
+    // parity 0 / 1); the next GEMV waits for all of them and adds them to x in rank order
+    // (PRO_RMS_REDUCE), writing the new residual to the other of the two x buffers.
+    auto peer_epi = [&](GemvArgs &a, int par) {
+        a.peer_recv = reinterpret_cast<float *const *>(tab + 8 * par);
+        a.peer_cnt = reinterpret_cast<unsigned long long *const *>(tab + 8 * (2 + par));
+    };
+    float *X[2] = {m->x, m->x2};
+    int cur = 0;
+    auto reduce_pro = [&](GemvArgs &a, int par, int index) {
+        a.x = X[cur];
+        a.x_out = X[1 - cur];
+        a.recv = reinterpret_cast<const float *>(m->comm + comm_recv_off(m, par));
+        a.cnt = reinterpret_cast<const unsigned long long *>(m->comm + comm_cnt_off(m, par));
+        a.red_index = index;
+        a.red_period = m->n_layers;
+        cur = 1 - cur;
+    };
+    const int qkv_rows = m->l_dim + 2 * m->l_kv_dim;
     const size_t esz = m->kv_type == DK_KV_F32 ? 4 : 2;
     for (int l = 0; l < m->n_layers; ++l) {
         const dk_layer &ly = m->layers[l];
-        if (int r = gemv("qkv gemv", m->p_qkv, ly.wqkv, m->dim, qkv_rows, l == 0 ? PRO_EMB_RMS : PRO_RMS,
-                         EPI_STORE, m->x, ly.rms_att, m->qkv))
-            return r;
+        {
+            GemvArgs a = base_args(ly.wqkv, m->dim, qkv_rows, l == 0 ? PRO_EMB_RMS : PRO_RMS, EPI_STORE, X[cur],
+                                   ly.rms_att, m->qkv);
+            if (tp && l > 0) {
+                a.pro = PRO_RMS_REDUCE;
+                reduce_pro(a, 1, l - 1);
+            }
+            if (int r = launch("qkv gemv", m->p_qkv, a)) return r;
+        }
         AttnArgs at;
         at.qkv = m->qkv; at.rope = m->rope;
         at.k_cache = static_cast<uint8_t *>(m->kcache) + (size_t)l * m->kv_layer_elems * esz;
         at.v_cache = static_cast<uint8_t *>(m->vcache) + (size_t)l * m->kv_layer_elems * esz;
         at.out = m->xb; at.work = m->attn_work; at.count = m->attn_count; at.pos = m->pos;
-        at.n_heads = m->n_heads; at.n_kv_heads = m->n_kv_heads; at.head_size = m->hs; at.seq_len = m->seq_len;
+        at.n_heads = m->l_heads; at.n_kv_heads = m->l_kv_heads; at.head_size = m->hs; at.seq_len = m->seq_len;
         at.kv_f32 = m->kv_type == DK_KV_F32; at.max_splits = m->attn_splits; at.min_chunk = kAttnMinChunk; at.err = m->err;
         ++launches;
         if (int r = cuda_status(launch_attention(at, st, true), "attention")) return r;
-        if (int r = gemv("wo gemv", m->p_wo, ly.wo, m->dim, m->dim, PRO_F32, EPI_ADD, m->xb, nullptr, m->x)) return r;
-        if (int r = gemv("w1/w3 gemv", m->p_w13, ly.w13, m->dim, 2 * m->hidden, PRO_RMS, EPI_SWIGLU, m->x,
-                         ly.rms_ffn, m->hb))
-            return r;
-        if (int r = gemv("w2 gemv", m->p_w2, ly.w2, m->hidden, m->dim, PRO_F32, EPI_ADD, m->hb, nullptr, m->x))
-            return r;
+        {
+            GemvArgs a = base_args(ly.wo, m->l_dim, m->dim, PRO_F32, tp ? EPI_PEER : EPI_ADD, m->xb, nullptr, X[cur]);
+            if (tp) peer_epi(a, 0);
+            if (int r = launch("wo gemv", m->p_wo, a)) return r;
+        }
+        {
+            GemvArgs a = base_args(ly.w13, m->dim, 2 * m->l_hidden, PRO_RMS, EPI_SWIGLU, X[cur], ly.rms_ffn, m->hb);
+            if (tp) {
+                a.pro = PRO_RMS_REDUCE;
+                reduce_pro(a, 0, l);
+            }
+            if (int r = launch("w1/w3 gemv", m->p_w13, a)) return r;
+        }
+        {
+            GemvArgs a = base_args(ly.w2, m->l_hidden, m->dim, PRO_F32, tp ? EPI_PEER : EPI_ADD, m->hb, nullptr, X[cur]);
+            if (tp) peer_epi(a, 1);
+            if (int r = launch("w2 gemv", m->p_w2, a)) return r;
+        }
     }
     if (m->p_cls.grid > kMaxGemvGrid * m->num_sms)
         return set_error(DK_ERR_INVALID, "classifier grid %d exceeds the argmax partials", m->p_cls.grid);
-    if (int r = gemv("classifier gemv", m->p_cls, m->wcls, m->dim, m->vocab, PRO_RMS, EPI_ARGMAX, m->x,
-                     m->rms_final, m->logits))
-        return r;
+    {
+        GemvArgs a = base_args(m->wcls, m->dim, m->l_vocab, PRO_RMS, EPI_ARGMAX, X[cur], m->rms_final, m->logits);
+        if (tp) {
+            a.pro = PRO_RMS_REDUCE;
+            reduce_pro(a, 1, m->n_layers - 1);
+            a.peer_amax = reinterpret_cast<unsigned long long *const *>(tab + 8 * 4);
+            a.peer_amax_cnt = reinterpret_cast<unsigned long long *const *>(tab + 8 * 5);
+            a.amax_keys = reinterpret_cast<const unsigned long long *>(m->comm + comm_keys_off(m));
+            a.amax_keys_cnt = reinterpret_cast<const unsigned long long *>(m->comm + comm_keys_cnt_off(m));
+        }
+        if (int r = launch("classifier gemv", m->p_cls, a)) return r;
+    }
     m->kernels_per_step = launches;
     return DK_OK;
 }
@@ -397,9 +521,56 @@ int dk_model_set_weight_device(dk_model *m, int which, int layer, const void *q,
     return set_weight_impl(m, which, layer, q, scale, true);
 }
 
+int dk_model_comm_handle(dk_model *m, void *handle) {
+    if (int r = need(m)) return r;
+    if (m->world < 2 || !m->comm) return set_error(DK_ERR_STATE, "dk_model_comm_handle: not a tensor-parallel model");
+    if (!handle) return set_error(DK_ERR_INVALID, "dk_model_comm_handle: null handle");
+    cudaIpcMemHandle_t h;
+    if (int r = cuda_status(cudaIpcGetMemHandle(&h, m->comm), "cudaIpcGetMemHandle")) return r;
+    static_assert(sizeof(h) == DK_COMM_HANDLE_BYTES, "IPC handle size");
+    memcpy(handle, &h, sizeof(h));
+    return DK_OK;
+}
+
+int dk_model_comm_connect(dk_model *m, const void *handles) {
+    if (int r = need(m)) return r;
+    if (m->world < 2 || !m->comm) return set_error(DK_ERR_STATE, "dk_model_comm_connect: not a tensor-parallel model");
+    if (m->connected) return set_error(DK_ERR_STATE, "dk_model_comm_connect: already connected");
+    if (!handles) return set_error(DK_ERR_INVALID, "dk_model_comm_connect: null handles");
+    for (int q = 0; q < m->world; ++q) {
+        if (q == m->rank) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, static_cast<const uint8_t *>(handles) + (size_t)q * DK_COMM_HANDLE_BYTES, sizeof(h));
+        void *ptr = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess)
+            return set_error(DK_ERR_COMM, "dk_model_comm_connect: opening rank %d's exchange area: %s", q,
+                             cudaGetErrorString(e));
+        m->peer_base[q] = ptr;
+        m->peer_opened[q] = true;
+    }
+    std::vector<void *> t(6 * 8, nullptr);
+    for (int q = 0; q < m->world; ++q) {
+        uint8_t *b = static_cast<uint8_t *>(m->peer_base[q]);
+        t[0 * 8 + q] = b + comm_recv_off(m, 0);
+        t[1 * 8 + q] = b + comm_recv_off(m, 1);
+        t[2 * 8 + q] = b + comm_cnt_off(m, 0);
+        t[3 * 8 + q] = b + comm_cnt_off(m, 1);
+        t[4 * 8 + q] = b + comm_keys_off(m);
+        t[5 * 8 + q] = b + comm_keys_cnt_off(m);
+    }
+    if (int r = cuda_status(cudaMemcpy(m->d_ptrs, t.data(), t.size() * sizeof(void *), cudaMemcpyHostToDevice),
+                            "peer table upload"))
+        return r;
+    m->connected = true;
+    return DK_OK;
+}
+
 int dk_model_finalize(dk_model *m) {
     if (int r = need(m)) return r;
     if (m->finalized) return DK_OK;
+    if (m->world > 1 && !m->connected)
+        return set_error(DK_ERR_STATE, "dk_model_finalize: connect the ranks first (dk_model_comm_connect)");
     for (int l = 0; l <= m->n_layers; ++l)
         for (int w = 0; w < DK_W_COUNT; ++w) {
             const bool per_layer = w >= DK_W_RMS_ATT;
@@ -487,12 +658,13 @@ int dk_model_kernels_per_step(dk_model *m) { return m ? m->kernels_per_step : 0;
 
 size_t dk_model_weight_bytes(dk_model *m) {
     if (!m) return 0;
-    // Bytes the GEMVs of one step stream (pad rows included): every layer's four matrices + lm_head.
-    const size_t per_layer = q8_packed_bytes(m->dim, m->dim + 2 * m->kv_dim, m->p_qkv.T) +
-                             q8_packed_bytes(m->dim, m->dim, m->p_wo.T) +
-                             q8_packed_bytes(m->dim, 2 * m->hidden, m->p_w13.T) +
-                             q8_packed_bytes(m->hidden, m->dim, m->p_w2.T);
-    return per_layer * m->n_layers + q8_packed_bytes(m->dim, m->vocab, m->p_cls.T);
+    // Bytes the GEMVs of one step stream on this rank (pad rows included): every layer's four
+    // matrices + the classifier rows.
+    const size_t per_layer = q8_packed_bytes(m->dim, m->l_dim + 2 * m->l_kv_dim, m->p_qkv.T) +
+                             q8_packed_bytes(m->l_dim, m->dim, m->p_wo.T) +
+                             q8_packed_bytes(m->dim, 2 * m->l_hidden, m->p_w13.T) +
+                             q8_packed_bytes(m->l_hidden, m->dim, m->p_w2.T);
+    return per_layer * m->n_layers + q8_packed_bytes(m->dim, m->l_vocab, m->p_cls.T);
 }
 
 int dk_model_forward(dk_model *m, int token, int pos, float *logits) {
@@ -510,7 +682,8 @@ int dk_model_forward(dk_model *m, int token, int pos, float *logits) {
         return set_error(DK_ERR_CUDA, "dk_model_forward: step upload failed");
     if (int r = cuda_status(cudaGraphLaunch(m->exec, st), "graph launch")) return r;
     if (logits) {
-        if (int r = cuda_status(cudaMemcpyAsync(logits, m->logits, (size_t)m->vocab * 4, cudaMemcpyDeviceToHost, st),
+        if (int r = cuda_status(cudaMemcpyAsync(logits + m->vocab_off, m->logits, (size_t)m->l_vocab * 4,
+                                                cudaMemcpyDeviceToHost, st),
                                 "logits readback"))
             return r;
     }

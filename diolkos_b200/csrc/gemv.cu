@@ -62,9 +62,35 @@ __device__ __forceinline__ void build_activation(const GemvArgs &a, int8_t *xq, 
     } else {
         int tok = 0;
         if constexpr (PRO == PRO_EMB_RMS) tok = a.tokens[*a.pos];
+        if constexpr (PRO == PRO_RMS_REDUCE) {
+            // Every rank's partial rows for this exchange point have landed in this rank's receive
+            // area once its counter reaches the target; then every thread reads them from L2.
+            if (tid == 0) {
+                const unsigned long long target =
+                    (*a.epoch * (unsigned long long)a.red_period + (unsigned long long)a.red_index + 1ull) *
+                    (unsigned long long)a.tp_world * (unsigned long long)n;
+                wait_counter(a.cnt, target, a.err);
+            }
+            __syncthreads();
+            __threadfence();
+        }
         auto load_group = [&](int g, float *f) {
             if constexpr (PRO == PRO_EMB_RMS) {
                 q8_packed_group(a.emb, n, a.emb_T, tok, g, f);  // embedding row dequant (src/transformer.c:69)
+            } else if constexpr (PRO == PRO_RMS_REDUCE) {
+                // x + (partial_0 + partial_1 + ...), ranks in order: the same bits on every rank.
+                const float4 *src = reinterpret_cast<const float4 *>(a.x + 32 * g);
+                #pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    float4 t = __ldcg(reinterpret_cast<const float4 *>(a.recv + 32 * g) + k);
+                    for (int q = 1; q < a.tp_world; ++q) {
+                        const float4 u = __ldcg(reinterpret_cast<const float4 *>(a.recv + (size_t)q * n + 32 * g) + k);
+                        t = make_float4(__fadd_rn(t.x, u.x), __fadd_rn(t.y, u.y), __fadd_rn(t.z, u.z), __fadd_rn(t.w, u.w));
+                    }
+                    const float4 x = src[k];
+                    f[4 * k] = __fadd_rn(x.x, t.x); f[4 * k + 1] = __fadd_rn(x.y, t.y);
+                    f[4 * k + 2] = __fadd_rn(x.z, t.z); f[4 * k + 3] = __fadd_rn(x.w, t.w);
+                }
             } else {
                 const float4 *src = reinterpret_cast<const float4 *>(a.x + 32 * g);
                 #pragma unroll
@@ -79,7 +105,7 @@ __device__ __forceinline__ void build_activation(const GemvArgs &a, int8_t *xq, 
         float f0[32];
         if (tid < ng) load_group(tid, f0);
         float r = 1.0f;
-        if constexpr (PRO == PRO_RMS || PRO == PRO_EMB_RMS) {
+        if constexpr (PRO == PRO_RMS || PRO == PRO_EMB_RMS || PRO == PRO_RMS_REDUCE) {
             float ss = 0.0f;
             for (int g = tid; g < ng; g += nthreads) {
                 float f[32];
@@ -89,9 +115,9 @@ __device__ __forceinline__ void build_activation(const GemvArgs &a, int8_t *xq, 
                 } else {
                     load_group(g, f);
                 }
-                if constexpr (PRO == PRO_EMB_RMS) {
-                    if (blockIdx.x == 0) {  // residual stream x
-                        float4 *dst = reinterpret_cast<float4 *>(const_cast<float *>(a.x) + 32 * g);
+                if constexpr (PRO == PRO_EMB_RMS || PRO == PRO_RMS_REDUCE) {
+                    if (blockIdx.x == 0) {  // residual stream x (the reduce writes a second buffer)
+                        float4 *dst = reinterpret_cast<float4 *>((PRO == PRO_RMS_REDUCE ? a.x_out : const_cast<float *>(a.x)) + 32 * g);
                         #pragma unroll
                         for (int k = 0; k < 8; ++k) dst[k] = make_float4(f[4 * k], f[4 * k + 1], f[4 * k + 2], f[4 * k + 3]);
                     }
@@ -117,7 +143,7 @@ __device__ __forceinline__ void build_activation(const GemvArgs &a, int8_t *xq, 
             } else {
                 load_group(g, f);
             }
-            if constexpr (PRO == PRO_RMS || PRO == PRO_EMB_RMS) {
+            if constexpr (PRO == PRO_RMS || PRO == PRO_EMB_RMS || PRO == PRO_RMS_REDUCE) {
                 // o = (w*x)*scale, the reference build's evaluation order (src/utils.c:73-75)
                 const float4 *wn = reinterpret_cast<const float4 *>(a.norm_w + 32 * g);
                 #pragma unroll
@@ -380,10 +406,17 @@ __global__ void __launch_bounds__(32 * kMinWarps, 2) gemv_q8_kernel(const GemvAr
                         a.out[row >> 1] = v;
                     }
                 } else if (live) {
-                    if constexpr (EPI == EPI_ADD) a.out[row] = __fadd_rn(a.out[row], sum);
-                    else a.out[row] = sum;
+                    if constexpr (EPI == EPI_ADD) {
+                        a.out[row] = __fadd_rn(a.out[row], sum);
+                    } else if constexpr (EPI == EPI_PEER) {
+                        // This rank's partial of row `row`, into every rank's receive area (peer stores
+                        // over NVLink; the local one for this rank).
+                        for (int q = 0; q < a.tp_world; ++q) a.peer_recv[q][(size_t)a.tp_rank * a.d + row] = sum;
+                    } else {
+                        a.out[row] = sum;
+                    }
                     if constexpr (EPI == EPI_ARGMAX) {
-                        const unsigned long long key = argmax_key(sum, row);
+                        const unsigned long long key = argmax_key(sum, row + a.row_offset);
                         best = key > best ? key : best;
                     }
                 }
@@ -407,6 +440,19 @@ __global__ void __launch_bounds__(32 * kMinWarps, 2) gemv_q8_kernel(const GemvAr
     }
     __syncthreads();
 
+    if constexpr (EPI == EPI_PEER) {
+        if (tid == 0) {
+            // Count this CTA's rows on every rank.  The barrier above orders every thread's peer stores
+            // before this thread's system-scope fence, which orders them before the counts: a rank
+            // that sees the count sees the rows.  (One fence per CTA: a fence in every thread costs
+            // several microseconds per exchange.)
+            const int lo = sc.t0 * p.T, hi = min(a.d, (sc.t0 + sc.nt) * p.T);
+            const unsigned long long rows = hi > lo ? (unsigned long long)(hi - lo) : 0ull;
+            __threadfence_system();
+            for (int q = 0; q < a.tp_world; ++q) atomicAdd_system(a.peer_cnt[q], rows);
+        }
+    }
+
     if constexpr (EPI == EPI_ARGMAX) {
         if (tid == 0) {
             unsigned long long bb = 0ull;
@@ -424,8 +470,23 @@ __global__ void __launch_bounds__(32 * kMinWarps, 2) gemv_q8_kernel(const GemvAr
                 const unsigned long long kk = __ldcg(a.amax_part + i);
                 bb = kk > bb ? kk : bb;
             }
+            if (a.tp_world > 1) {
+                // Exchange the ranks' best keys (global row indices), then every rank takes the same
+                // maximum.
+                for (int q = 0; q < a.tp_world; ++q) a.peer_amax[q][a.tp_rank] = bb;
+                __threadfence_system();
+                for (int q = 0; q < a.tp_world; ++q) atomicAdd_system(a.peer_amax_cnt[q], 1ull);
+                wait_counter(a.amax_keys_cnt, (*a.epoch + 1ull) * (unsigned long long)a.tp_world, a.err);
+                __threadfence();
+                for (int q = 0; q < a.tp_world; ++q) {
+                    const unsigned long long k = __ldcg(a.amax_keys + q);
+                    bb = k > bb ? k : bb;
+                }
+                *a.epoch_rw = *a.epoch + 1ull;
+            }
+            const int vocab = a.vocab > 0 ? a.vocab : a.d;
             int idx = (bb == 0ull) ? 0 : argmax_idx(bb);
-            if (idx < 0 || idx >= a.d) idx = 0;
+            if (idx < 0 || idx >= vocab) idx = 0;
             const int pos = *a.pos;
             if (pos + 1 <= a.seq_len && pos + 1 >= *a.n_forced) a.tokens[pos + 1] = idx;
             *a.pos = pos + 1;
@@ -516,6 +577,10 @@ cudaError_t launch_gemv(const GemvArgs &a, const GemvPlan &p, cudaStream_t st, b
     DK_GEMV_CASE(PRO_RMS, EPI_ARGMAX)
     DK_GEMV_CASE(PRO_EMB_RMS, EPI_STORE)
     DK_GEMV_CASE(PRO_F32, EPI_NONE)
+    DK_GEMV_CASE(PRO_F32, EPI_PEER)
+    DK_GEMV_CASE(PRO_RMS_REDUCE, EPI_STORE)
+    DK_GEMV_CASE(PRO_RMS_REDUCE, EPI_SWIGLU)
+    DK_GEMV_CASE(PRO_RMS_REDUCE, EPI_ARGMAX)
 #undef DK_GEMV_CASE
     return cudaErrorInvalidValue;
 }

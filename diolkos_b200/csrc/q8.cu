@@ -108,11 +108,11 @@ __global__ void group_dots_kernel(const int8_t *__restrict__ xq, const int8_t *_
 // swizzle of the row's index in its tile).  The destination is zeroed beforehand, so the pad bytes of
 // each segment and the rows of a ragged last tile stay zero.
 __global__ void pack_rows_kernel(uint8_t *__restrict__ dst, int n, int T, const int8_t *__restrict__ q,
-                                 const float *__restrict__ s, int row0, int step) {
+                                 const float *__restrict__ s, int row0, int step, int src_n, int col0) {
     const int i = blockIdx.x;  // source row
     const int drow = row0 + i * step, r = drow % T;
-    const int8_t *qrow = q + (size_t)i * n;
-    const float *srow = s + (size_t)i * (n / 32);
+    const int8_t *qrow = q + (size_t)i * src_n + col0;
+    const float *srow = s + (size_t)i * (src_n / 32) + col0 / 32;
     const int nblk = (n + 511) / 512;
     for (int b = 0; b < nblk; ++b) {
         const int wb = q8_blk_width(n, b);
@@ -192,10 +192,12 @@ cudaError_t launch_group_dots(const int8_t *xq, const int8_t *wq, int n, int d, 
 }
 
 cudaError_t launch_pack_rows(uint8_t *dst, int n, int T, const int8_t *q, const float *s, int rows, int row0,
-                             int step, cudaStream_t st) {
+                             int step, cudaStream_t st, int src_n, int col0) {
     if (rows <= 0) return cudaSuccess;
-    if (n <= 0 || n % 32 || T < 1 || T > 32) return cudaErrorInvalidValue;
-    pack_rows_kernel<<<rows, 128, 0, st>>>(dst, n, T, q, s, row0, step);
+    if (src_n == 0) src_n = n;
+    if (n <= 0 || n % 32 || T < 1 || T > 32 || src_n % 32 || col0 % 32 || col0 < 0 || col0 + n > src_n)
+        return cudaErrorInvalidValue;
+    pack_rows_kernel<<<rows, 128, 0, st>>>(dst, n, T, q, s, row0, step, src_n, col0);
     return cudaGetLastError();
 }
 

@@ -33,13 +33,29 @@ def weight_id(name: str) -> tuple[int, int]:
 class Model:
     """One model resident on one GPU; the whole decode step is a CUDA graph."""
 
-    def __init__(self, cfg: synth.Config, kv_f32: bool = False, device: int = 0):
+    def __init__(self, cfg: synth.Config, kv_f32: bool = False, device: int = 0, tp_rank: int = 0,
+                 tp_world: int = 1):
         self.cfg = cfg
+        self.tp_rank, self.tp_world = tp_rank, tp_world
         L = N.lib()
         arr = (C.c_int * 7)(*cfg.as_list())
-        self.h = L.dk_model_create(arr, N.DK_KV_F32 if kv_f32 else N.DK_KV_BF16, device, 0, 1)
+        self.h = L.dk_model_create(arr, N.DK_KV_F32 if kv_f32 else N.DK_KV_BF16, device, tp_rank, tp_world)
         if not self.h:
             raise N.DiolkosError(N.DK_ERR_INVALID, L.dk_last_error().decode())
+
+    def comm_handle(self) -> bytes:
+        """This rank's exchange-area IPC handle (tensor parallel)."""
+        buf = C.create_string_buffer(N.DK_COMM_HANDLE_BYTES)
+        N.check(N.lib().dk_model_comm_handle(self.h, buf))
+        return buf.raw
+
+    def comm_connect(self, handles: list) -> None:
+        """Map every rank's exchange area (handles in rank order, this rank's included)."""
+        blob = b"".join(handles)
+        if len(blob) != N.DK_COMM_HANDLE_BYTES * self.tp_world:
+            raise ValueError("one handle per rank expected")
+        buf = C.create_string_buffer(blob, len(blob))
+        N.check(N.lib().dk_model_comm_connect(self.h, buf))
 
     def set_weight(self, which: int, layer: int, q, s=None):
         """Host arrays: Q8_0 (int8 q, fp32 s) planar, or a fp32 vector."""
@@ -66,7 +82,9 @@ class Model:
         N.check(N.lib().dk_model_finalize(self.h))
 
     def forward(self, token: int, pos: int) -> np.ndarray:
-        logits = np.empty(self.cfg.vocab_size, np.float32)
+        """Logits of one step (tensor parallel: only this rank's classifier rows are filled, the rest
+        is NaN)."""
+        logits = np.full(self.cfg.vocab_size, np.nan, np.float32)
         N.check(N.lib().dk_model_forward(self.h, token, pos, logits.ctypes.data))
         return logits
 

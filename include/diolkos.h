@@ -145,8 +145,22 @@ enum dk_weight {
 
 /* cfg = {dim, hidden_dim, n_layers, n_heads, n_kv_heads, vocab_size, seq_len} (the reference's
  * Config, src/transformer.h:14-22).  Allocates all device memory of the model on `device`.
- * tp_rank / tp_world select this process's tensor-parallel shard (0 / 1 for one GPU). */
+ * tp_rank / tp_world select this process's tensor-parallel shard (0 / 1 for one GPU; up to 8 ranks,
+ * one process per GPU of one node), the split the reference's client/worker topology makes across
+ * machines (src/bin/client.c): attention heads and w1/w3 rows per rank, wo and w2 by columns (their
+ * partial outputs summed over the ranks), classifier rows per rank, embedding and norms on every
+ * rank.  heads, kv heads must divide by tp_world; hidden/tp_world and head_size*heads/tp_world must
+ * be multiples of 32. */
 dk_model *dk_model_create(const int *cfg, int kv_type, int device, int tp_rank, int tp_world);
+/* Tensor parallel only (tp_world > 1), before dk_model_finalize.  Each rank exports the CUDA IPC
+ * handle of its exchange area (DK_COMM_HANDLE_BYTES bytes), the ranks share them (any transport),
+ * and each rank connects to all of them: handles = tp_world handles in rank order.  The per-layer
+ * sums then travel inside the GEMVs over NVLink peer memory: no collective library is involved.
+ * All ranks must then run the same decode steps (forward / generate / enqueue_steps) in the same
+ * order; a rank that stops makes the others' waits time out with DK_ERR_COMM. */
+#define DK_COMM_HANDLE_BYTES 64
+int dk_model_comm_handle(dk_model *m, void *handle);
+int dk_model_comm_connect(dk_model *m, const void *handles);
 void dk_model_destroy(dk_model *m);
 /* Set one weight from HOST memory.  Q8_0 weights: q = int8[rows*cols], scale = fp32[rows*cols/32]
  * in the planar cache layout, full (unsharded) matrix; the engine keeps this rank's shard.
@@ -159,7 +173,8 @@ int dk_model_set_weight_device(dk_model *m, int which, int layer, const void *q,
 int dk_model_finalize(dk_model *m);
 
 /* One decode step (reference forward(transformer, token, pos)): writes vocab logits to the HOST
- * buffer `logits` (NULL: skip the copy). */
+ * buffer `logits` (NULL: skip the copy).  With tensor parallelism each rank writes only its own
+ * classifier rows (the slice of logits[vocab_size] it computes). */
 int dk_model_forward(dk_model *m, int token, int pos, float *logits);
 /* Greedy generation with the reference generate() rules (src/bin/localinfer.c:42-99): prompt
  * tokens are forced one position at a time, then argmax tokens (first index wins ties) are fed
