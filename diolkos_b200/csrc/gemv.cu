@@ -79,6 +79,7 @@ __device__ __forceinline__ void build_activation(const GemvArgs &a, int8_t *xq, 
                 q8_packed_group(a.emb, n, a.emb_T, tok, g, f);  // embedding row dequant (src/transformer.c:69)
             } else if constexpr (PRO == PRO_RMS_REDUCE) {
                 // x + (partial_0 + partial_1 + ...), ranks in order: the same bits on every rank.
+                // (L2 loads: this kernel skips the dependency wait.)
                 const float4 *src = reinterpret_cast<const float4 *>(a.x + 32 * g);
                 #pragma unroll
                 for (int k = 0; k < 8; ++k) {
@@ -87,7 +88,7 @@ __device__ __forceinline__ void build_activation(const GemvArgs &a, int8_t *xq, 
                         const float4 u = __ldcg(reinterpret_cast<const float4 *>(a.recv + (size_t)q * n + 32 * g) + k);
                         t = make_float4(__fadd_rn(t.x, u.x), __fadd_rn(t.y, u.y), __fadd_rn(t.z, u.z), __fadd_rn(t.w, u.w));
                     }
-                    const float4 x = src[k];
+                    const float4 x = __ldcg(src + k);
                     f[4 * k] = __fadd_rn(x.x, t.x); f[4 * k + 1] = __fadd_rn(x.y, t.y);
                     f[4 * k + 2] = __fadd_rn(x.z, t.z); f[4 * k + 3] = __fadd_rn(x.w, t.w);
                 }
@@ -172,6 +173,101 @@ __device__ __forceinline__ void build_activation(const GemvArgs &a, int8_t *xq, 
             xs[g] = sc;
         }
     }
+}
+
+// Fast prologue for the rmsnorm family when n == 16 * threads (e.g. dim 4096 on 256 threads): thread t
+// owns the 16 values [16t, 16t+16), half of group t/2, so every thread loads at once and one memory
+// round trip brings the whole activation in.  nw = this thread's 16 norm weights, loaded before the
+// dependency wait (weights are constant).  PRO_RMS_REDUCE adds the ranks' partials (rank order) and
+// CTA 0 stores the new residual; then rmsnorm, and the two threads of a group agree on its Q8_0 scale.
+template <int PRO>
+__device__ __forceinline__ void build_activation_half(const GemvArgs &a, int8_t *xq, float *xs, float *red,
+                                                      const float4 (&nw)[4]) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nwarps = blockDim.x >> 5;
+    const int n = a.n, e0 = 16 * tid;
+    float4 v[4];
+    #pragma unroll
+    for (int k = 0; k < 4; ++k) v[k] = __ldcg(reinterpret_cast<const float4 *>(a.x + e0) + k);
+    if constexpr (PRO == PRO_RMS_REDUCE) {
+        // Every rank's partial rows for this exchange point are in this rank's receive area once its
+        // counter reaches the target.
+        if (tid == 0) {
+            const unsigned long long target =
+                (*a.epoch * (unsigned long long)a.red_period + (unsigned long long)a.red_index + 1ull) *
+                (unsigned long long)a.tp_world * (unsigned long long)n;
+            wait_counter(a.cnt, target, a.err);
+        }
+        __syncthreads();
+        __threadfence();
+        // x + (partial_0 + partial_1 + ...), ranks in order: the same bits on every rank.  Two ranks'
+        // loads are in flight at a time.
+        float4 t[4];
+        #pragma unroll
+        for (int k = 0; k < 4; ++k) t[k] = __ldcg(reinterpret_cast<const float4 *>(a.recv + e0) + k);
+        for (int q = 1; q < a.tp_world; q += 2) {
+            float4 u[4], w[4];
+            const bool two = q + 1 < a.tp_world;
+            #pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                u[k] = __ldcg(reinterpret_cast<const float4 *>(a.recv + (size_t)q * n + e0) + k);
+                w[k] = two ? __ldcg(reinterpret_cast<const float4 *>(a.recv + (size_t)(q + 1) * n + e0) + k)
+                           : make_float4(0, 0, 0, 0);
+            }
+            #pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                t[k] = make_float4(__fadd_rn(t[k].x, u[k].x), __fadd_rn(t[k].y, u[k].y), __fadd_rn(t[k].z, u[k].z),
+                                   __fadd_rn(t[k].w, u[k].w));
+                if (two)
+                    t[k] = make_float4(__fadd_rn(t[k].x, w[k].x), __fadd_rn(t[k].y, w[k].y),
+                                       __fadd_rn(t[k].z, w[k].z), __fadd_rn(t[k].w, w[k].w));
+            }
+        }
+        #pragma unroll
+        for (int k = 0; k < 4; ++k)
+            v[k] = make_float4(__fadd_rn(v[k].x, t[k].x), __fadd_rn(v[k].y, t[k].y), __fadd_rn(v[k].z, t[k].z),
+                               __fadd_rn(v[k].w, t[k].w));
+        if (blockIdx.x == 0) {
+            #pragma unroll
+            for (int k = 0; k < 4; ++k) reinterpret_cast<float4 *>(a.x_out + e0)[k] = v[k];
+        }
+    }
+    float f[16];
+    #pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        f[4 * k] = v[k].x; f[4 * k + 1] = v[k].y; f[4 * k + 2] = v[k].z; f[4 * k + 3] = v[k].w;
+    }
+    float ss = 0.0f;
+    #pragma unroll
+    for (int k = 0; k < 16; ++k) ss = fmaf(f[k], f[k], ss);
+    ss = warp_sum(ss);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    float tot = 0.0f;
+    for (int w = 0; w < nwarps; ++w) tot += red[w];
+    // rmsnorm scale (src/utils.c:68-71): ss/n + 1e-5, then 1/sqrt; o = (w*x)*scale (:73-75)
+    float r = __fdiv_rn(tot, (float)n);
+    r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(r, 1e-5f)));
+    float amax = 0.0f;
+    #pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        f[4 * k] = __fmul_rn(__fmul_rn(nw[k].x, f[4 * k]), r);
+        f[4 * k + 1] = __fmul_rn(__fmul_rn(nw[k].y, f[4 * k + 1]), r);
+        f[4 * k + 2] = __fmul_rn(__fmul_rn(nw[k].z, f[4 * k + 2]), r);
+        f[4 * k + 3] = __fmul_rn(__fmul_rn(nw[k].w, f[4 * k + 3]), r);
+    }
+    #pragma unroll
+    for (int k = 0; k < 16; ++k) amax = fmaxf(amax, fabsf(f[k]));
+    amax = fmaxf(amax, __shfl_xor_sync(FULL, amax, 1));  // the group's other half
+    float sc, inv;
+    q8_scale(amax, sc, inv);
+    uint32_t wq[4];
+    #pragma unroll
+    for (int k = 0; k < 4; ++k)
+        wq[k] = (uint32_t)(uint8_t)q8_round(f[4 * k], inv) | ((uint32_t)(uint8_t)q8_round(f[4 * k + 1], inv) << 8) |
+                ((uint32_t)(uint8_t)q8_round(f[4 * k + 2], inv) << 16) |
+                ((uint32_t)(uint8_t)q8_round(f[4 * k + 3], inv) << 24);
+    reinterpret_cast<uint4 *>(xq + e0)[0] = make_uint4(wq[0], wq[1], wq[2], wq[3]);
+    if (!(tid & 1)) xs[tid >> 1] = sc;
 }
 
 // Data of 4 consecutive groups of one row: the 4 weight scales, the 4 activation scales, the 8
@@ -330,9 +426,27 @@ __global__ void __launch_bounds__(32 * kMinWarps, 2) gemv_q8_kernel(const GemvAr
         for (int s = S + q; s < min(S + p.PF, sc.nst); s += NP) bulk_prefetch_l2(sc.src(a.w, s), sc.bytes(s));
     }
 
-    pdl_wait();
+    // The rmsnorm family on n == 16 * threads takes the one-round-trip prologue; its norm weights are
+    // constant, so they are loaded before the dependency wait.
+    constexpr bool kRmsFamily = PRO == PRO_RMS || PRO == PRO_RMS_REDUCE;
+    const bool half = kRmsFamily && n == 16 * (int)blockDim.x;
+    float4 nw[4];
+    if (half) {
+        #pragma unroll
+        for (int k = 0; k < 4; ++k) nw[k] = __ldg(reinterpret_cast<const float4 *>(a.norm_w + 16 * tid) + k);
+    }
+    // A tensor-parallel reduce GEMV does not wait for the previous kernel: its new input (the ranks'
+    // partial rows) is announced by the exchange counter, and everything else it reads or overwrites
+    // was last written or read by kernels that an earlier kernel of the step already waited for.  So
+    // it starts on the partials as soon as the last rank's rows land, not when the producing kernel's
+    // last CTA has drained its fence and exited.
+    if constexpr (PRO != PRO_RMS_REDUCE) pdl_wait();
     pdl_trigger();
-    build_activation<PRO>(a, xq, xs, red);
+    if (half) {
+        if constexpr (kRmsFamily) build_activation_half<PRO>(a, xq, xs, red, nw);
+    } else {
+        build_activation<PRO>(a, xq, xs, red);
+    }
     __syncthreads();
 
     if (q >= 0 && q < NP) {

@@ -19,7 +19,12 @@ from diolkos_b200 import synth
 
 pytestmark = pytest.mark.gpu
 
-CFG = synth.Config(dim=512, hidden_dim=1024, n_layers=2, n_heads=8, n_kv_heads=2, vocab_size=2048, seq_len=256)
+CFGS = {
+    "small": synth.Config(dim=512, hidden_dim=1024, n_layers=2, n_heads=8, n_kv_heads=2, vocab_size=2048, seq_len=256),
+    # dim 4096 takes the GEMVs' one-round-trip reduce prologue (16 values per thread)
+    "dim4096": synth.Config(dim=4096, hidden_dim=1024, n_layers=2, n_heads=32, n_kv_heads=8, vocab_size=2048,
+                            seq_len=256),
+}
 SEED, STEPS = 77, 48
 
 
@@ -31,7 +36,8 @@ def _free_port() -> int:
     return port
 
 
-def _rank(rank, world, port, out_q):
+def _rank(rank, world, port, out_q, cfg_name):
+    CFG = CFGS[cfg_name]
     import torch.distributed as dist
 
     from diolkos_b200 import tp
@@ -59,7 +65,9 @@ def _rank(rank, world, port, out_q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tp2_matches_single_gpu():
+@pytest.mark.parametrize("cfg_name", sorted(CFGS))
+def test_tp2_matches_single_gpu(cfg_name):
+    CFG = CFGS[cfg_name]
     from diolkos_b200.model import Model
     from oracle import Port, load_port_weights
 
@@ -67,7 +75,7 @@ def test_tp2_matches_single_gpu():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, q, cfg_name)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
