@@ -25,6 +25,7 @@ SIGNATURES = {
     "dk_last_error": (C.c_char_p, []),
     "dk_device_count": (_i, []),
     "dk_quantize_bf16_q8_0": (_i, [_vp, _sz, _vp, _vp, _vp]),
+    "dk_quantize_f16_q8_0": (_i, [_vp, _sz, _vp, _vp, _vp]),
     "dk_quantize_f32_q8_0": (_i, [_vp, _sz, _vp, _vp, _vp]),
     "dk_dequantize_q8_0": (_i, [_vp, _vp, _sz, _vp, _vp]),
     "dk_q8_0_group_dots": (_i, [_vp, _vp, _i, _i, _vp, _vp]),
@@ -35,6 +36,8 @@ SIGNATURES = {
     "dk_matmul_q8_0": (_i, [_vp, _vp, _vp, _i, _i, _vp]),
     "dk_matmul_q8_0_q": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp]),
     "dk_matmul_q8_0_batch": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
+    "dk_sample": (_i, [_vp, _i, C.c_float, C.c_float, C.c_float, _vp, _vp, _vp]),
+    "dk_softmax": (_i, [_vp, _i, _vp]),
     "dk_rmsnorm": (_i, [_vp, _vp, _vp, _i, _vp]),
     "dk_attention_work_bytes": (_sz, [_i, _i, _i, _i]),
     "dk_attention_decode": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _vp, _vp]),

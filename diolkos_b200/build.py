@@ -62,7 +62,10 @@ def build(verbose: bool = True) -> str:
             _run([HOST_CC, *CC_FLAGS, "-c", src, "-o", obj])
         objs.append(obj)
     if _newer(LIB, objs):
-        _run([NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", LIB, *objs,
+        # -Bsymbolic: calls between the library's own functions (forward -> dk_model_forward, sample ->
+        # random_f32, ...) bind inside the library even where another loaded library exports the
+        # reference's function names.
+        _run([NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-Xlinker", "-Bsymbolic", "-o", LIB, *objs,
               "-lcudart_static", "-lrt", "-lpthread", "-ldl", "-lm"])
     # CLI binaries (reference bin/localinfer, bin/client, bin/benchmark counterparts)
     os.makedirs(BIN, exist_ok=True)

@@ -56,6 +56,14 @@ int dk_quantize_bf16_q8_0(const uint16_t *x, size_t n, int8_t *q, float *scale, 
     return cuda_status(launch_quant_bf16(x, n, q, scale, (cudaStream_t)stream), "dk_quantize_bf16_q8_0");
 }
 
+int dk_quantize_f16_q8_0(const uint16_t *x, size_t n, int8_t *q, float *scale, void *stream) {
+    if (n % 32) return set_error(DK_ERR_INVALID, "dk_quantize_f16_q8_0: n=%zu is not a multiple of 32", n);
+    if (!x || !q || !scale) return set_error(DK_ERR_INVALID, "dk_quantize_f16_q8_0: null pointer");
+    if (int r = check_aligned(x, 16, "x")) return r;
+    if (int r = check_aligned(q, 16, "q")) return r;
+    return cuda_status(launch_quant_f16(x, n, q, scale, (cudaStream_t)stream), "dk_quantize_f16_q8_0");
+}
+
 int dk_quantize_f32_q8_0(const float *x, size_t n, int8_t *q, float *scale, void *stream) {
     if (n % 32) return set_error(DK_ERR_INVALID, "dk_quantize_f32_q8_0: n=%zu is not a multiple of 32", n);
     if (!x || !q || !scale) return set_error(DK_ERR_INVALID, "dk_quantize_f32_q8_0: null pointer");

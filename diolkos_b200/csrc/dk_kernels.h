@@ -149,6 +149,7 @@ cudaError_t launch_gemv(const GemvArgs &a, const GemvPlan &p, cudaStream_t st, b
 
 // ---------------- Q8_0 conversions ----------------------------------------------------------
 cudaError_t launch_quant_bf16(const uint16_t *x, size_t n, int8_t *q, float *s, cudaStream_t st);
+cudaError_t launch_quant_f16(const uint16_t *x, size_t n, int8_t *q, float *s, cudaStream_t st);
 cudaError_t launch_quant_f32(const float *x, size_t n, int8_t *q, float *s, cudaStream_t st);
 cudaError_t launch_dequant(const int8_t *q, const float *s, size_t n, float *out, cudaStream_t st);
 cudaError_t launch_group_dots(const int8_t *xq, const int8_t *wq, int n, int d, int32_t *dots, cudaStream_t st);

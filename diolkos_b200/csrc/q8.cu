@@ -1,6 +1,7 @@
 // q8.cu -- Q8_0 conversions, packing and small helpers (sm_100a).
 //
-//  * quant_bf16: convert_bf16_q8_0 (reference src/tensor.c:312-344), the load-time weight quantiser.
+//  * quant_16bit: convert_bf16_q8_0 / convert_f16_q8_0 (reference src/tensor.c:312-344, :278-310),
+//    the load-time weight quantisers.
 //  * quant_f32:  convert_f32_q8_slice_into_offset (src/tensor.c:199-228), the activation quantiser.
 //  * dequant:    convert_q8_f32_slice_into_offset (src/tensor.c:245-265).
 //  * group_dots: the exact int32 per-group dots of matmul_Q8_0 (src/utils.c:122-127).
@@ -8,6 +9,8 @@
 //  * rmsnorm:    rmsnorm (src/utils.c:59-76) as a standalone kernel.
 //  * embed:      the embedding-row dequant that starts forward (src/transformer.c:69).
 // All of these are HBM-bound byte work: one thread per 32-element group, 16-byte loads and stores.
+#include <cuda_fp16.h>
+
 #include "dk_common.cuh"
 #include "dk_kernels.h"
 
@@ -51,8 +54,19 @@ __device__ __forceinline__ void quant_group(const float (&f)[32], int8_t *q, flo
     *s = sc;
 }
 
-__global__ void quant_bf16_kernel(const uint16_t *__restrict__ x, size_t ng, int8_t *__restrict__ q,
-                                  float *__restrict__ s) {
+// 16-bit source words to float, exactly: bf16 is the upper half of an fp32; IEEE half through the
+// hardware conversion (exact for every half value, subnormals included).
+struct Bf16Word {
+    __device__ float operator()(uint16_t b) const { return bf16_to_f32(b); }
+};
+struct F16Word {
+    __device__ float operator()(uint16_t h) const { return __half2float(__ushort_as_half(h)); }
+};
+
+template <typename Word>
+__global__ void quant_16bit_kernel(const uint16_t *__restrict__ x, size_t ng, int8_t *__restrict__ q,
+                                   float *__restrict__ s) {
+    const Word cvt;
     for (size_t g = blockIdx.x * (size_t)blockDim.x + threadIdx.x; g < ng; g += (size_t)gridDim.x * blockDim.x) {
         const uint4 *src = reinterpret_cast<const uint4 *>(x + g * 32);
         float f[32];
@@ -62,8 +76,8 @@ __global__ void quant_bf16_kernel(const uint16_t *__restrict__ x, size_t ng, int
             const uint32_t w[4] = {u.x, u.y, u.z, u.w};
             #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                f[8 * k + 2 * j] = bf16_to_f32((uint16_t)(w[j] & 0xFFFF));
-                f[8 * k + 2 * j + 1] = bf16_to_f32((uint16_t)(w[j] >> 16));
+                f[8 * k + 2 * j] = cvt((uint16_t)(w[j] & 0xFFFF));
+                f[8 * k + 2 * j + 1] = cvt((uint16_t)(w[j] >> 16));
             }
         }
         quant_group(f, q + g * 32, s + g);
@@ -167,7 +181,14 @@ __global__ void embed_kernel(const uint8_t *__restrict__ emb, int dim, int T, co
 cudaError_t launch_quant_bf16(const uint16_t *x, size_t n, int8_t *q, float *s, cudaStream_t st) {
     const size_t ng = n / 32;
     if (!ng) return cudaSuccess;
-    quant_bf16_kernel<<<grid_for(ng), kThreads, 0, st>>>(x, ng, q, s);
+    quant_16bit_kernel<Bf16Word><<<grid_for(ng), kThreads, 0, st>>>(x, ng, q, s);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quant_f16(const uint16_t *x, size_t n, int8_t *q, float *s, cudaStream_t st) {
+    const size_t ng = n / 32;
+    if (!ng) return cudaSuccess;
+    quant_16bit_kernel<F16Word><<<grid_for(ng), kThreads, 0, st>>>(x, ng, q, s);
     return cudaGetLastError();
 }
 

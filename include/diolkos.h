@@ -40,6 +40,8 @@ int dk_device_count(void);
  * pointers; n % 32 == 0.  Bit-exact with the reference build: scale = amax*(1/127),
  * q = rint(x * (1/scale)). */
 int dk_quantize_bf16_q8_0(const uint16_t *x, size_t n, int8_t *q, float *scale, void *stream);
+/* The same recipe on IEEE half weights: replaces convert_f16_q8_0 (src/tensor.c:278-310). */
+int dk_quantize_f16_q8_0(const uint16_t *x, size_t n, int8_t *q, float *scale, void *stream);
 /* Activation quantiser: replaces convert_f32_q8_slice_into_offset (src/tensor.c:199-228). */
 int dk_quantize_f32_q8_0(const float *x, size_t n, int8_t *q, float *scale, void *stream);
 /* Dequantiser: replaces convert_q8_f32_slice_into_offset (src/tensor.c:245-265). */
@@ -81,6 +83,16 @@ int dk_matmul_q8_0_q(float *out, const int8_t *xq, const float *xs, const uint8_
  * weights while the previous one finishes, which is how the decode engine runs the kernel. */
 int dk_matmul_q8_0_batch(float *out, const float *x, const uint8_t *const *w_packed, int count, int n,
                          int d, void *stream);
+/* Token sampling (reference sample(), src/sampler.c:108-131) on device logits[n]: temperature 0 is
+ * argmax (first index wins ties); otherwise softmax(logits / temperature), then with `coin` in
+ * [0, 1) multinomial sampling in index order (topp <= 0 or >= 1) or top-p sampling over the tokens
+ * sorted by decreasing probability.  Writes the token to the device int *out and, when probs is not
+ * NULL (temperature > 0), the probabilities to device probs[n] -- what the reference leaves in its
+ * logits buffer; probs may be the logits buffer itself.  One CTA; no scratch. */
+int dk_sample(const float *logits, int n, float temperature, float topp, float coin, float *probs, int *out,
+              void *stream);
+/* softmax_f32 (src/utils.c:39-57) in place on device x[n]. */
+int dk_softmax(float *x, int n, void *stream);
 /* rmsnorm (src/utils.c:59-76), device pointers; o may alias x. */
 int dk_rmsnorm(float *o, const float *x, const float *w, int n, void *stream);
 

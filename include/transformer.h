@@ -1,0 +1,63 @@
+/*
+ * transformer.h -- the reference's model API (src/transformer.h) served by the B200 engine.
+ *
+ * build_transformer_from_safetensors loads a HF LLaMA-2 directory exactly like the reference
+ * (config.json, *.safetensors, the Q8_0 cache under ./cache/<model>/), then moves the whole model to
+ * the current CUDA device (dk_model_* in diolkos.h).  forward() runs one decode step there as one
+ * CUDA graph and returns the logits in a HOST tensor, as the reference does.
+ */
+#ifndef DIOLKOS_TRANSFORMER_H
+#define DIOLKOS_TRANSFORMER_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "tensor.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct Model Model;
+struct dk_model;
+
+typedef struct {
+    int dim;        /* transformer dimension                              */
+    int hidden_dim; /* FFN dimension                                      */
+    int n_layers;
+    int n_heads;    /* query heads                                        */
+    int n_kv_heads; /* key/value heads (fewer than n_heads with GQA)      */
+    int vocab_size;
+    int seq_len;    /* maximum sequence length                            */
+} Config;
+
+/* The reference keeps every activation here; on the B200 they live on the device inside the engine,
+ * so only `logits` is set (host F32, vocab_size values, overwritten by each forward).  The other
+ * members stay NULL and exist for source compatibility. */
+typedef struct {
+    Tensor *x, *xb, *xb2, *hb, *hb2, *q, *att, *logits;
+    Tensor *key_cache, *value_cache;
+    Tensor *k, *v;
+} RunState;
+
+typedef struct Transformer {
+    Config config;
+    RunState state;
+    Model *safetensors;        /* the host weights as loaded (and cached) */
+    struct dk_model *engine;   /* the model on the GPU                    */
+} Transformer;
+
+/* Allocate the host-side state (the logits tensor) for a model of this shape. */
+void malloc_run_state(RunState *s, Config *p);
+/* Load `model_path` (a directory) and build the GPU model on the current CUDA device, with the
+ * reference's bf16 KV cache.  Exits with a message on failure, like the reference. */
+void build_transformer_from_safetensors(Transformer *t, const char *model_path);
+/* One decode step at `pos` with input `token`; returns the host logits (t->state.logits). */
+Tensor *forward(Transformer *transformer, int token, int pos);
+/* Release the GPU model and the host state (no counterpart in the reference, which never frees). */
+void free_transformer(Transformer *t);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
