@@ -10,13 +10,15 @@
 //      - top-p off (topp <= 0 or >= 1): the first index whose cumulative probability, in index order,
 //        exceeds the coin (sample_mult, src/sampler.c:19-30);
 //      - top-p (src/sampler.c:40-83): the reference keeps the candidates p >= (1-topp)/(n-1), sorts
-//        them by decreasing p, truncates after the first element where the running sum exceeds topp,
-//        and walks that list to r = coin * (the truncated sum).  Here both cut points are found
-//        without sorting: the truncation value v* is the largest u with sum(p >= u) > topp, and the
-//        sampled value w the largest u with sum over the truncated set of (p >= u) > r -- two
-//        bisections over the bit patterns of positive floats (their order is the value order).  The
-//        token is the lowest index holding w.  Sums run in a different order than the reference's
-//        sequential ones, so a coin landing within rounding of a boundary can pick the neighbour.
+//        them by decreasing p (equal p stay in index order: glibc's qsort is a stable merge sort),
+//        truncates after the first element where the running sum exceeds topp, and walks that list
+//        to r = coin * (the truncated sum).  Here both cut points are found without sorting: the
+//        truncation value v* is the largest u with sum(p >= u) > topp, the sampled value w the
+//        largest u with sum over the kept list of (p >= u) > r -- bisections over the bit patterns
+//        of positive floats (their order is the value order) -- and inside a group of equal
+//        values the position follows from the group's start sum, so the token is the k-th index
+//        holding that value.  Sums run in a different order than the reference's sequential ones,
+//        so a coin landing within rounding of a boundary can pick the neighbour.
 // Probabilities are recomputed from the logits on every pass (no scratch memory, any n).
 #include "dk_common.cuh"
 #include "dk_internal.h"
@@ -137,56 +139,119 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const float *log
             s_pick = pick;
         }
     } else {
-        // Top-p.  mass(u) = sum of the candidates' p with p >= u; bisection for the largest u
-        // (as a float bit pattern, 0 .. 1.0f) with mass(u) > limit.
+        // Top-p over the candidates p >= cutoff, in the reference's sorted order: decreasing p,
+        // equal p in increasing index (the order its stable qsort leaves them in).  With
+        // G(u) = sum of candidate p >= u, the running sum of that order passes through
+        // G(>v) + j*v for the j-th of the c_v candidates equal to v.
         const float cutoff = __fdiv_rn(__fsub_rn(1.0f, topp), (float)(n - 1));
-        auto mass = [&](float u, float floor_v) -> float {
+        auto mass = [&](float u) -> float {
             float m = 0.0f;
             for (int i = i0; i < i1; ++i) {
                 const float p = P(i);
-                if (p >= cutoff && p >= floor_v && p >= u) m = __fadd_rn(m, p);
+                if (p >= cutoff && p >= u) m = __fadd_rn(m, p);
             }
             return block_sum(m, shf);
         };
-        auto largest = [&](float limit, float floor_v, bool &found) -> float {
-            unsigned lo = 0u, hi = __float_as_uint(1.0f) + 1u;  // mass(lo) > limit ? ; mass(hi) == 0
-            found = mass(__uint_as_float(lo), floor_v) > limit;
+        auto count = [&](float v) -> int {
+            float c = 0.0f;
+            for (int i = i0; i < i1; ++i) {
+                const float p = P(i);
+                c += (p >= cutoff && p == v) ? 1.0f : 0.0f;
+            }
+            return (int)block_sum(c, shf);  // exact: counts stay far below 2^24
+        };
+        auto above = [](float v) { return __uint_as_float(__float_as_uint(v) + 1u); };
+        // The largest u >= lo (positive floats compare like their bit patterns) with G(u) > limit:
+        // always one of the candidate values.
+        auto largest = [&](float lo_v, float limit, bool &found) -> float {
+            unsigned lo = __float_as_uint(lo_v), hi = __float_as_uint(1.0f) + 1u;
+            found = mass(lo_v) > limit;
             if (!found) return 0.0f;
-            while (hi - lo > 1u) {  // invariant: mass(lo) > limit, mass(hi) <= limit
+            while (hi - lo > 1u) {  // invariant: G(lo) > limit, G(hi) <= limit
                 const unsigned mid = lo + (hi - lo) / 2u;
-                if (mass(__uint_as_float(mid), floor_v) > limit) lo = mid;
+                if (mass(__uint_as_float(mid)) > limit) lo = mid;
                 else hi = mid;
             }
             return __uint_as_float(lo);
         };
-        bool found = false;
-        // v*: the truncation value; without one (the candidates' sum does not exceed topp after
-        // rounding) every candidate stays, as in the reference.
-        const float vstar_raw = largest(topp, 0.0f, found);
-        const float vstar = found ? vstar_raw : 0.0f;
-        const float kept = mass(vstar, 0.0f);
-        const float r = __fmul_rn(coin, kept);
-        bool found_w = false;
-        float w = largest(r, vstar, found_w);
-        if (!found_w) {  // rounding: the reference returns the last kept element (the smallest p)
+        // Smallest j in [1, c] with g + j*v > limit (the first place the running sum passes it).
+        auto first_past = [](float g, float v, int c, float limit) -> int {
+            int j = (int)fminf(fmaxf(floorf(__fdiv_rn(__fsub_rn(limit, g), v)) + 1.0f, 1.0f), (float)c);
+            while (j > 1 && __fadd_rn(g, __fmul_rn((float)(j - 1), v)) > limit) --j;
+            while (j < c && !(__fadd_rn(g, __fmul_rn((float)j, v)) > limit)) ++j;
+            return j;
+        };
+        // The truncation: the element where the running sum first exceeds topp is the j*-th
+        // candidate equal to v*; the kept list ends there.  Without one (the candidates' sum does
+        // not exceed topp after rounding) every candidate is kept.
+        bool trunc = false;
+        const float vstar = largest(0.0f, topp, trunc);
+        float kept, last_v;
+        int jstar = 0, last_k;
+        if (trunc) {
+            const float g_gt = mass(above(vstar));
+            jstar = first_past(g_gt, vstar, count(vstar), topp);
+            kept = __fadd_rn(g_gt, __fmul_rn((float)jstar, vstar));
+            last_v = vstar;
+            last_k = jstar - 1;
+        } else {
+            kept = mass(0.0f);
             float mn = FLT_MAX;
             for (int i = i0; i < i1; ++i) {
                 const float p = P(i);
-                if (p >= cutoff && p >= vstar) mn = fminf(mn, p);
+                if (p >= cutoff) mn = fminf(mn, p);
             }
-            w = -block_max(-mn, shf);
+            last_v = -block_max(-mn, shf);
+            last_k = count(last_v) - 1;
         }
-        // The lowest index holding value w among the kept candidates.
-        unsigned long long best = 0ull;
+        // The sampled element: the first whose running sum exceeds r = coin * kept.
+        const float r = __fmul_rn(coin, kept);
+        bool hit = false;
+        float w = largest(trunc ? above(vstar) : 0.0f, r, hit);
+        if (!hit && trunc && r < kept) {  // r falls among the kept candidates equal to v*
+            w = vstar;
+            hit = true;
+        }
+        float pick_v = last_v;  // rounding: the reference returns the last kept element
+        int pick_k = last_k;
+        if (hit) {
+            const float g_gt = mass(above(w));
+            const int c = (trunc && w == vstar) ? jstar : count(w);
+            pick_v = w;
+            pick_k = first_past(g_gt, w, c, r) - 1;
+        }
+        // The pick_k-th (0-based, in index order) candidate equal to pick_v.
+        int c = 0;
         for (int i = i0; i < i1; ++i) {
             const float p = P(i);
-            if (p == w && p >= cutoff && p >= vstar) {
-                const unsigned long long k = 0xFFFFFFFFull - (unsigned long long)i;
-                best = k > best ? k : best;
+            c += (p >= cutoff && p == pick_v) ? 1 : 0;
+        }
+        __syncthreads();
+        scan[tid] = (float)c;
+        __syncthreads();
+        if (tid == 0) {
+            float run = 0.0f;
+            for (int t = 0; t < kSampleThreads; ++t) {
+                const float v = scan[t];
+                scan[t] = run;
+                run += v;
             }
         }
-        best = block_max_u64(best, shk);
-        if (tid == 0 && best) s_pick = (int)(0xFFFFFFFFu - (unsigned)best);
+        __syncthreads();
+        const int base = (int)scan[tid];
+        if (pick_k >= base && pick_k < base + c) {
+            int seen = base;
+            for (int i = i0; i < i1; ++i) {
+                const float p = P(i);
+                if (p >= cutoff && p == pick_v) {
+                    if (seen == pick_k) {
+                        s_pick = i;
+                        break;
+                    }
+                    ++seen;
+                }
+            }
+        }
     }
     // Every read of the logits is done before any probability is stored (probs may alias them).
     __syncthreads();

@@ -156,10 +156,14 @@ def test_sample_matches_reference_sampler(port, temperature, topp):
     L.build_sampler(C.byref(s), V, temperature, topp, 1234)
     state = 1234
     mism = 0
-    for it in range(60):
-        logits = (rng.standard_normal(V) * (1 + it % 5)).astype(np.float32)
+    for it in range(72):
+        heavy = it % 6 == 5  # few distinct values: tie groups of thousands of tokens
+        if heavy:
+            logits = np.round(rng.standard_normal(V) * 2).astype(np.float32)
+        else:
+            logits = (rng.standard_normal(V) * (1 + it % 5)).astype(np.float32)
         if it % 7 == 0:
-            logits[rng.integers(0, V, 5)] = logits.max()  # exact ties
+            logits[rng.integers(0, V, 5)] = logits.max()  # a small tie group at the top
         buf = logits.copy()
         coin = TP.random_f32(state)[0] if temperature > 0 else None
         tok = L.sample(C.byref(s), buf.ctypes.data_as(C.POINTER(C.c_float)))
@@ -171,18 +175,24 @@ def test_sample_matches_reference_sampler(port, temperature, topp):
             continue
         p = _probs(logits, temperature)
         np.testing.assert_allclose(buf, p, rtol=2e-5, atol=1e-9)
-        if tok != want:
-            # only a coin within float rounding of a cumulative-probability boundary (or a
-            # cumulative sum within rounding of topp) may pick the neighbouring token
-            mism += 1
-            if 0 < topp < 1:
-                kept = np.sort(p[p >= (1 - topp) / (V - 1)])[::-1]
-                cum = np.cumsum(kept)
-                last = int(np.argmax(cum > topp)) if (cum > topp).any() else len(cum) - 1
-                near = min(np.min(np.abs(cum - coin * cum[last])), np.min(np.abs(cum - topp)))
-            else:
-                near = np.min(np.abs(np.cumsum(p) - coin))
-            assert near < 1e-5, (it, tok, want, near)
+        if tok == want:
+            continue
+        if heavy and abs(tok - want) <= 64 and (buf[tok] == buf[want] or not 0 < topp < 1):
+            # thousands of equal small probabilities: the reference's float32 running sum drifts by
+            # ~1e-4 over the vocabulary, a few elements' worth, from the exact (or tree-summed)
+            # cumulative; top-p picks inside a tie group from the group's start sum
+            continue
+        # otherwise only a coin within float rounding of a cumulative-probability boundary (or a
+        # cumulative sum within rounding of topp) may pick the neighbouring token
+        mism += 1
+        if 0 < topp < 1:
+            kept = np.sort(p[p >= (1 - topp) / (V - 1)])[::-1]
+            cum = np.cumsum(kept)
+            last = int(np.argmax(cum > topp)) if (cum > topp).any() else len(cum) - 1
+            near = min(np.min(np.abs(cum - coin * cum[last])), np.min(np.abs(cum - topp)))
+        else:
+            near = np.min(np.abs(np.cumsum(p) - coin))
+        assert near < (1e-4 if heavy else 1e-5), (it, tok, want, near)
     assert mism <= 3
     L.free_sampler(C.byref(s))
 
