@@ -49,7 +49,7 @@ def _run(cmd: list[str]) -> None:
 def build(verbose: bool = True) -> str:
     os.makedirs(BUILD, exist_ok=True)
     headers = glob.glob(os.path.join(CSRC, "*.h")) + glob.glob(os.path.join(CSRC, "*.cuh")) + \
-        glob.glob(os.path.join(INCLUDE, "*.h"))
+        glob.glob(os.path.join(CSRC, "host", "*.h")) + glob.glob(os.path.join(INCLUDE, "*.h"))
     objs = []
     for src in sorted(glob.glob(os.path.join(CSRC, "*.cu"))):
         obj = os.path.join(BUILD, os.path.basename(src) + ".o")

@@ -179,7 +179,7 @@ int main(int argc, char **argv) {
 
     const size_t params = count_params(&transformer);
     fprintf(stderr, "Parameters: %zu (%.2f GB of weights read per token on the GPU)\n", params,
-            (double)dk_model_weight_bytes(transformer.engine) / 1e9);
+            (double)dk_model_weight_bytes(transformer_engine(&transformer)) / 1e9);
 
     if (strcmp(mode, "generate") == 0) {
         const float tok_s = generate(&transformer, &tokenizer, &sampler, prompt, steps);

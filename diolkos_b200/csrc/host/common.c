@@ -43,11 +43,18 @@ void *host_calloc(size_t n, size_t size) {
 }
 
 void *dev_reserve(dev_buf *b, size_t bytes) {
-    if (bytes <= b->bytes && b->ptr) return b->ptr;
-    if (b->ptr) host_check_cuda(cudaFree(b->ptr), "cudaFree");
+    int dev = 0;
+    host_check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+    if (b->ptr && b->device == dev && bytes <= b->bytes) return b->ptr;
+    if (b->ptr) {
+        if (b->device != dev) host_check_cuda(cudaSetDevice(b->device), "cudaSetDevice");
+        host_check_cuda(cudaFree(b->ptr), "cudaFree");
+        if (b->device != dev) host_check_cuda(cudaSetDevice(dev), "cudaSetDevice");
+    }
     b->ptr = NULL;
     b->bytes = 0;
     host_check_cuda(cudaMalloc(&b->ptr, bytes ? bytes : 16), "cudaMalloc (staging buffer)");
     b->bytes = bytes;
+    b->device = dev;
     return b->ptr;
 }

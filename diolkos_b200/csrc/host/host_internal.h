@@ -43,15 +43,25 @@ void *host_malloc(size_t n);
 void *host_calloc(size_t n, size_t size);
 
 /* ---- device staging -------------------------------------------------------------------------- */
-/* A growable device buffer owned by the caller's static state. */
+/* A growable device buffer owned by the caller's static state, on the device that was current when
+ * it was allocated. */
 typedef struct {
     void *ptr;
     size_t bytes;
+    int device;
 } dev_buf;
-/* Make b at least `bytes` long (contents are not kept); exits on failure. */
+/* Make b at least `bytes` long on the current device (contents are not kept; a buffer on another
+ * device is released and replaced); exits on failure. */
 void *dev_reserve(dev_buf *b, size_t bytes);
 
 /* Drop the GPU copy utils.c keeps of a matrix used with matmul() (called by tensor_destroy). */
 void utils_forget_tensor(const Tensor *t);
+
+/* load_safetensors allocates a Model inside this larger block, so that the GPU model built from it
+ * can be found from Transformer.safetensors while Transformer keeps the reference's layout. */
+struct Model;
+struct dk_model;
+struct dk_model **model_engine_slot(struct Model *m);
+struct Model *model_ext_alloc(void);
 
 #endif

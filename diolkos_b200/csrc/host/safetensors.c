@@ -201,6 +201,15 @@ static int process_file(const char *model_name, const char *path, Model *st) {
     return found;
 }
 
+typedef struct {
+    Model model;  /* first: a Model* to the block is a pointer to this member */
+    struct dk_model *engine;
+} model_ext;
+
+Model *model_ext_alloc(void) { return &((model_ext *)host_calloc(1, sizeof(model_ext)))->model; }
+
+struct dk_model **model_engine_slot(Model *m) { return &((model_ext *)m)->engine; }
+
 static int cmp_names(const void *a, const void *b) { return strcmp(*(char *const *)a, *(char *const *)b); }
 
 static int ends_with(const char *s, const char *suffix) {
@@ -234,7 +243,7 @@ Model *load_safetensors(const char *dir) {
         config->vocab_size <= 0 || config->hidden_dim <= 0 || config->seq_len <= 0 || config->dim % config->n_heads)
         die("Bad or incomplete config in %s%s", path, "");
 
-    Model *st = host_calloc(1, sizeof(Model));
+    Model *st = model_ext_alloc();
     st->config = config;
     st->huggingface_rope = true;
     st->layers = host_calloc((size_t)config->n_layers, sizeof(Layer));

@@ -21,18 +21,18 @@ void build_sampler(Sampler *s, int vocab_size, float temperature, float topp, un
     s->temperature = temperature;
     s->topp = topp;
     s->rng_state = rng_seed;
-    s->probindex = NULL;  /* no sort buffer is needed */
-    s->device_buf = NULL;
-    const size_t bytes = ((size_t)(vocab_size > 0 ? vocab_size : 1) * sizeof(float) + 15) / 16 * 16 + 16;
-    host_check_cuda(cudaMalloc(&s->device_buf, bytes), "build_sampler: cudaMalloc");
+    /* allocated like the reference's sort buffer; the GPU sampler does not use it */
+    s->probindex = host_malloc((size_t)(vocab_size > 0 ? vocab_size : 1) * sizeof(ProbIndex));
 }
 
 void free_sampler(Sampler *s) {
-    if (s->device_buf) cudaFree(s->device_buf);
-    s->device_buf = NULL;
     free(s->probindex);
     s->probindex = NULL;
 }
+
+/* Device logits + token, grown to the largest vocabulary seen (the Sampler keeps the reference's
+ * layout, so the buffer lives here; one per process like the reference's own scratch). */
+static dev_buf g_sample;
 
 unsigned int random_u32(unsigned long long *state) {
     /* xorshift* (Marsaglia's xorshift with a multiplicative output step), 64-bit state */
@@ -49,8 +49,9 @@ float random_f32(unsigned long long *state) { return (float)(random_u32(state) >
 int sample(Sampler *s, float *logits) {
     const int n = s->vocab_size;
     const size_t bytes = (size_t)n * sizeof(float);
-    float *d_logits = (float *)s->device_buf;
-    int *d_out = (int *)((char *)s->device_buf + (bytes + 15) / 16 * 16);
+    char *base = dev_reserve(&g_sample, (bytes + 15) / 16 * 16 + 16);
+    float *d_logits = (float *)base;
+    int *d_out = (int *)(base + (bytes + 15) / 16 * 16);
     host_check_cuda(cudaMemcpy(d_logits, logits, bytes, cudaMemcpyHostToDevice), "sample: copy logits");
     int next = 0;
     if (s->temperature == 0.0f) {

@@ -20,9 +20,35 @@
 #include "tensor.h"
 #include "transformer.h"
 
+/* The reference's RunState sizes (src/transformer.c:13-30).  Only logits is written on this path;
+ * the KV-cache tensors are descriptors of the bf16 cache the engine keeps in HBM (no host data). */
 void malloc_run_state(RunState *s, Config *p) {
+    const size_t kv_dim = (size_t)p->dim * (size_t)p->n_kv_heads / (size_t)p->n_heads;
     memset(s, 0, sizeof *s);
+    s->x = tensor_create((size_t)p->dim, F32);
+    s->xb = tensor_create((size_t)p->dim, F32);
+    s->xb2 = tensor_create((size_t)p->dim, F32);
+    s->hb = tensor_create((size_t)p->hidden_dim, F32);
+    s->hb2 = tensor_create((size_t)p->hidden_dim, F32);
+    s->q = tensor_create((size_t)p->dim, F32);
+    s->att = tensor_create((size_t)p->n_heads * (size_t)p->seq_len, F32);
     s->logits = tensor_create((size_t)p->vocab_size, F32);
+    Tensor *kv[2];
+    for (int i = 0; i < 2; ++i) {
+        kv[i] = host_calloc(1, sizeof(Tensor));
+        kv[i]->type = BF16;
+        kv[i]->dim = (size_t)p->n_layers * (size_t)p->seq_len * kv_dim;
+        kv[i]->vdim = 1;
+        kv[i]->hdim = kv[i]->dim;
+    }
+    s->key_cache = kv[0];
+    s->value_cache = kv[1];
+    s->k = tensor_create(kv_dim, F32);
+    s->v = tensor_create(kv_dim, F32);
+}
+
+struct dk_model *transformer_engine(Transformer *t) {
+    return t && t->safetensors ? *model_engine_slot(t->safetensors) : NULL;
 }
 
 static void set_q8(dk_model *m, int which, int layer, Tensor *t) {
@@ -51,24 +77,25 @@ void build_transformer_from_safetensors(Transformer *t, const char *model_path) 
     int device = 0;
     host_check_cuda(cudaGetDevice(&device), "cudaGetDevice");
     const int cfg[7] = {c->dim, c->hidden_dim, c->n_layers, c->n_heads, c->n_kv_heads, c->vocab_size, c->seq_len};
-    t->engine = dk_model_create(cfg, DK_KV_BF16, device, 0, 1);
-    if (!t->engine) host_check(DK_ERR_INVALID, "create the model");
-    set_q8(t->engine, DK_W_EMB, -1, st->token_embedding_table);
-    set_f32(t->engine, DK_W_RMS_FINAL, -1, st->rms_final_weight);
-    set_q8(t->engine, DK_W_WCLS, -1, st->wcls);
+    dk_model *g = dk_model_create(cfg, DK_KV_BF16, device, 0, 1);
+    if (!g) host_check(DK_ERR_INVALID, "create the model");
+    *model_engine_slot(st) = g;
+    set_q8(g, DK_W_EMB, -1, st->token_embedding_table);
+    set_f32(g, DK_W_RMS_FINAL, -1, st->rms_final_weight);
+    set_q8(g, DK_W_WCLS, -1, st->wcls);
     for (int l = 0; l < c->n_layers; ++l) {
         Layer *L = &st->layers[l];
-        set_f32(t->engine, DK_W_RMS_ATT, l, L->rms_att_weight);
-        set_q8(t->engine, DK_W_WQ, l, L->wq);
-        set_q8(t->engine, DK_W_WK, l, L->wk);
-        set_q8(t->engine, DK_W_WV, l, L->wv);
-        set_q8(t->engine, DK_W_WO, l, L->wo);
-        set_f32(t->engine, DK_W_RMS_FFN, l, L->rms_ffn_weight);
-        set_q8(t->engine, DK_W_W1, l, L->w1);
-        set_q8(t->engine, DK_W_W2, l, L->w2);
-        set_q8(t->engine, DK_W_W3, l, L->w3);
+        set_f32(g, DK_W_RMS_ATT, l, L->rms_att_weight);
+        set_q8(g, DK_W_WQ, l, L->wq);
+        set_q8(g, DK_W_WK, l, L->wk);
+        set_q8(g, DK_W_WV, l, L->wv);
+        set_q8(g, DK_W_WO, l, L->wo);
+        set_f32(g, DK_W_RMS_FFN, l, L->rms_ffn_weight);
+        set_q8(g, DK_W_W1, l, L->w1);
+        set_q8(g, DK_W_W2, l, L->w2);
+        set_q8(g, DK_W_W3, l, L->w3);
     }
-    host_check(dk_model_finalize(t->engine), "finalize the model");
+    host_check(dk_model_finalize(g), "finalize the model");
     fprintf(stderr,
             "Transformer config from safetensors: dim=%d, hidden_dim=%d, n_layers=%d, n_heads=%d, n_kv_heads=%d, "
             "vocab_size=%d, seq_len=%d\n",
@@ -76,13 +103,21 @@ void build_transformer_from_safetensors(Transformer *t, const char *model_path) 
 }
 
 Tensor *forward(Transformer *transformer, int token, int pos) {
-    host_check(dk_model_forward(transformer->engine, token, pos, data_f32(transformer->state.logits)), "forward");
+    dk_model *g = transformer_engine(transformer);
+    if (!g) host_check(DK_ERR_STATE, "forward: the transformer was not built");
+    host_check(dk_model_forward(g, token, pos, data_f32(transformer->state.logits)), "forward");
     return transformer->state.logits;
 }
 
 void free_transformer(Transformer *t) {
-    if (t->engine) dk_model_destroy(t->engine);
-    t->engine = NULL;
-    tensor_destroy(t->state.logits);
-    t->state.logits = NULL;
+    dk_model *g = transformer_engine(t);
+    if (g) dk_model_destroy(g);
+    if (t->safetensors) *model_engine_slot(t->safetensors) = NULL;
+    Tensor **all[] = {&t->state.x, &t->state.xb, &t->state.xb2, &t->state.hb, &t->state.hb2, &t->state.q,
+                      &t->state.att, &t->state.logits, &t->state.key_cache, &t->state.value_cache, &t->state.k,
+                      &t->state.v};
+    for (size_t i = 0; i < sizeof all / sizeof all[0]; ++i) {
+        tensor_destroy(*all[i]);
+        *all[i] = NULL;
+    }
 }

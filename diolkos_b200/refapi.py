@@ -1,9 +1,8 @@
 """ctypes mirror of the reference-compatible C API that libdiolkos.so exports (include/tensor.h,
 transformer.h, safetensors.h, utils.h, sampler.h, tokenizer.h).
 
-The structures have the reference's field order (src/tensor.h:18-28, src/transformer.h:14-51,
-src/safetensors.h:11-33, src/sampler.h:4-16, src/tokenizer.h:5-20), with the B200 additions only at
-the end of Transformer and Sampler.  These entry points keep the reference's failure behaviour: a
+The structures have the reference's layouts exactly (src/tensor.h:18-28, src/transformer.h:14-51,
+src/safetensors.h:11-33, src/sampler.h:4-16, src/tokenizer.h:5-20).  These entry points keep the reference's failure behaviour: a
 bad input prints a message and exits the process, so call them only with inputs that are known to
 be valid (or from a child process).
 """
@@ -58,7 +57,7 @@ class Model(C.Structure):
 
 
 class Transformer(C.Structure):
-    _fields_ = [("config", Config), ("state", RunState), ("safetensors", C.POINTER(Model)), ("engine", C.c_void_p)]
+    _fields_ = [("config", Config), ("state", RunState), ("safetensors", C.POINTER(Model))]
 
 
 class ProbIndex(C.Structure):
@@ -67,7 +66,7 @@ class ProbIndex(C.Structure):
 
 class Sampler(C.Structure):
     _fields_ = [("vocab_size", C.c_int), ("probindex", C.POINTER(ProbIndex)), ("temperature", C.c_float),
-                ("topp", C.c_float), ("rng_state", C.c_ulonglong), ("device_buf", C.c_void_p)]
+                ("topp", C.c_float), ("rng_state", C.c_ulonglong)]
 
 
 class TokenIndex(C.Structure):
@@ -104,6 +103,7 @@ _SIGS = {
     "build_transformer_from_safetensors": (None, [C.POINTER(Transformer), C.c_char_p]),
     "forward": (TensorP, [C.POINTER(Transformer), C.c_int, C.c_int]),
     "free_transformer": (None, [C.POINTER(Transformer)]),
+    "transformer_engine": (C.c_void_p, [C.POINTER(Transformer)]),
     "load_safetensors": (C.POINTER(Model), [C.c_char_p]),
     "build_sampler": (None, [C.POINTER(Sampler), C.c_int, C.c_float, C.c_float, C.c_ulonglong]),
     "free_sampler": (None, [C.POINTER(Sampler)]),

@@ -5,7 +5,8 @@
  * ties); otherwise softmax(logits / temperature) and either plain multinomial sampling (topp <= 0
  * or >= 1) or top-p (nucleus) sampling, with the reference's xorshift random stream on the host
  * giving the coin (so a seed reproduces the same coin sequence as the reference).  The arithmetic
- * runs in dk_sample (diolkos.h).
+ * runs in dk_sample (diolkos.h), on device buffers the library keeps per device (not re-entrant,
+ * like the reference's sampler and utils).
  */
 #ifndef DIOLKOS_SAMPLER_H
 #define DIOLKOS_SAMPLER_H
@@ -19,13 +20,14 @@ typedef struct {
     int index;
 } ProbIndex;
 
+/* Same layout as the reference's (callers allocate it).  probindex is allocated like the
+ * reference's but unused: the GPU needs no sort buffer. */
 typedef struct {
     int vocab_size;
-    ProbIndex *probindex;  /* unused here (the GPU needs no sort buffer); kept for compatibility */
+    ProbIndex *probindex;
     float temperature;
     float topp;
     unsigned long long rng_state;
-    void *device_buf;      /* logits and result on the device */
 } Sampler;
 
 void build_sampler(Sampler *sampler, int vocab_size, float temperature, float topp, unsigned long long rng_seed);

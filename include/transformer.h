@@ -19,7 +19,6 @@ extern "C" {
 #endif
 
 typedef struct Model Model;
-struct dk_model;
 
 typedef struct {
     int dim;        /* transformer dimension                              */
@@ -31,20 +30,22 @@ typedef struct {
     int seq_len;    /* maximum sequence length                            */
 } Config;
 
-/* The reference keeps every activation here; on the B200 they live on the device inside the engine,
- * so only `logits` is set (host F32, vocab_size values, overwritten by each forward).  The other
- * members stay NULL and exist for source compatibility. */
+/* The reference keeps every activation here.  On the B200 they live on the device inside the
+ * engine: `logits` (host F32, vocab_size values) is written by each forward; x .. att, k, v are host
+ * tensors of the reference's sizes that the GPU path does not write; key_cache / value_cache
+ * describe the size of the bf16 KV cache (held in HBM) and have no host data. */
 typedef struct {
     Tensor *x, *xb, *xb2, *hb, *hb2, *q, *att, *logits;
     Tensor *key_cache, *value_cache;
     Tensor *k, *v;
 } RunState;
 
+/* Same layout as the reference's, so callers may allocate it themselves (as localinfer does, on the
+ * stack): the GPU model is reached through `safetensors`, which this library allocates. */
 typedef struct Transformer {
     Config config;
     RunState state;
     Model *safetensors;        /* the host weights as loaded (and cached) */
-    struct dk_model *engine;   /* the model on the GPU                    */
 } Transformer;
 
 /* Allocate the host-side state (the logits tensor) for a model of this shape. */
@@ -54,7 +55,12 @@ void malloc_run_state(RunState *s, Config *p);
 void build_transformer_from_safetensors(Transformer *t, const char *model_path);
 /* One decode step at `pos` with input `token`; returns the host logits (t->state.logits). */
 Tensor *forward(Transformer *transformer, int token, int pos);
-/* Release the GPU model and the host state (no counterpart in the reference, which never frees). */
+/* The GPU model behind a built transformer (diolkos.h: dk_model_*), for callers that want the
+ * engine's own entry points (dk_model_generate, dk_model_weight_bytes, ...); NULL before
+ * build_transformer_from_safetensors. */
+struct dk_model *transformer_engine(Transformer *t);
+/* Release the GPU model and the host RunState tensors (no counterpart in the reference, which never
+ * frees); the host weights in t->safetensors stay. */
 void free_transformer(Transformer *t);
 
 #ifdef __cplusplus

@@ -260,3 +260,13 @@ def test_localinfer_greedy(tiny_dir, loaded, tiny_weights, tmp_path):
     out = r.stdout.split(b"Loaded ")[1].split(b"\n", 1)[1]
     assert out == text + b"\n", (out[:200], text[:200])
     assert b"achieved tok/s" in r.stderr
+    # The reference's own, unmodified src/bin/localinfer.c (+ transformer_info.c), compiled against
+    # include/ and linked with libdiolkos.so (oracle Makefile, target dropin), prints the same text.
+    dropin = os.path.join(ROOT, "oracle", "_ref", "dropin", "localinfer")
+    if not os.path.exists(dropin):
+        pytest.skip("oracle/_ref/dropin/localinfer not built here")
+    r2 = subprocess.run([dropin, d, "-t", "0", "-n", str(steps), "-i", prompt.decode(), "-z", tok_path],
+                        capture_output=True, cwd=root, timeout=300)
+    assert r2.returncode == 0, r2.stderr.decode()
+    assert r2.stdout.endswith(text + b"\n"), r2.stdout[-300:]
+    assert b"achieved tok/s" in r2.stderr
