@@ -59,6 +59,7 @@ SIGNATURES = {
     "dk_model_device_error": (_i, [_vp]),
     "dk_model_kernels_per_step": (_i, [_vp]),
     "dk_model_weight_bytes": (_sz, [_vp]),
+    "dk_model_trace": (_i, [_vp, _vp, _sz, _vp, _vp]),
 }
 
 _lib = None

@@ -29,7 +29,7 @@ NVCC_FLAGS = [
     "-lineinfo", "-O3", "-std=c++17", "--expt-relaxed-constexpr",
     "-Xcompiler", "-fPIC,-ffp-contract=off,-O2",
     "-ccbin", "g++",
-]
+] + os.environ.get("DIOLKOS_NVCC_EXTRA", "").split()  # e.g. -DDK_STEP_CHECKS for a self-checking build
 CC_FLAGS = ["-O2", "-fPIC", "-std=c11", "-D_GNU_SOURCE", "-ffp-contract=off", "-Wall", "-Wno-unused-function",
             f"-I{INCLUDE}", f"-I{CUDA_HOME}/include"]
 

@@ -191,4 +191,45 @@ size_t attn_work_bytes(int n_heads, int n_kv_heads, int head_size, int max_split
 bool attn_supported(int n_heads, int n_kv_heads, int head_size);
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st, bool pdl);
 
+// ---------------- persistent decode step ----------------------------------------------------------
+// The whole step as one cooperative kernel (step.cu): a list of ops that every CTA walks in order.
+constexpr int kStepProducers = 2;     // producer warps per CTA (one issuing thread each)
+constexpr int kStepMaxSlots = 16;     // ring slots
+constexpr int kStepMaxConsumers = 10; // GEMV consumer warps (at most the compute warps)
+constexpr int kStepMinChunk = 16;     // positions of the shortest attention split in the persistent step
+enum StepOpKind : int { OP_GEMV = 0, OP_ATTN = 1 };
+struct StepOp {
+    int kind = OP_GEMV;
+    GemvArgs g;             // OP_GEMV: matrix, prologue, epilogue (the standalone GEMV's arguments)
+    int T = 32, ntiles = 0; // OP_GEMV: the packed matrix's tile height and tile count
+    AttnArgs at;            // OP_ATTN
+    // Input dependency: wait until *wait_cnt >= (epoch + 1) * wait_units (nullptr: none; the
+    // tensor-parallel reduce prologue waits on its exchange counter itself).
+    const unsigned long long *wait_cnt = nullptr;
+    unsigned long long wait_units = 0;
+    // Completion: rows (SwiGLU: output pairs) or attention outputs finished are added here.
+    unsigned long long *done_cnt = nullptr;
+};
+struct StepArgs {
+    const StepOp *ops = nullptr;  // device array
+    int nops = 0;
+    int S = 2, NC = 1;            // ring slots, GEMV consumer warps
+    size_t slot = 0;              // bytes of one ring slot (>= the largest stage)
+    size_t xoff = 0;              // activation / attention scratch
+    size_t ctl_off = 0;           // control block
+    size_t smem = 0;              // dynamic shared memory
+    const unsigned long long *epoch = nullptr;  // decode steps completed
+    unsigned long long *epoch_rw = nullptr;     // advanced by the classifier's last CTA
+    const int *pos = nullptr;
+    int seq_len = 0;
+    int *err = nullptr;
+    unsigned long long *trace = nullptr;  // optional timeline [grid][nops][4] (globaltimer, ns)
+};
+size_t step_ctl_bytes();
+size_t step_attn_scratch_bytes(int n_heads, int n_kv_heads, int head_size);
+int step_attn_item_slots(int num_ctas);
+int step_threads();
+int step_max_ctas_per_sm(size_t smem);
+cudaError_t launch_step(const StepArgs &sa, int grid, cudaStream_t st);
+
 }  // namespace dk

@@ -12,6 +12,7 @@
 // graph; `pos` and the tokens live in device memory, so the same graph serves every position and
 // greedy decoding replays it back to back without the host in the loop.
 #include <cmath>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -108,6 +109,14 @@ struct dk_model {
     float *x2 = nullptr;                  // second residual buffer (the reduces ping-pong x <-> x2)
     unsigned long long *epoch = nullptr;  // decode steps completed (the exchange counters' epoch)
     bool connected = false;
+    // persistent decode step (step.cu): the op list on the device, its dependency counters and plan
+    bool use_step = true;                 // false: one kernel per GEMV / attention (DIOLKOS_STEP=kernels)
+    StepOp *d_ops = nullptr;
+    int n_ops = 0;
+    unsigned long long *step_cnt = nullptr;  // [n_layers][5]: qkv, attention, wo, w1|w3, w2
+    int step_splits = 1;                  // attention splits per KV head in the persistent step
+    StepArgs step;
+    unsigned long long *d_trace = nullptr;  // DIOLKOS_STEP_TRACE=1: the persistent step's timeline
 };
 
 static size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
@@ -237,15 +246,24 @@ dk_model *dk_model_create(const int *cfg, int kv_type, int device, int tp_rank, 
 
     // ---- activations and small state
     m->attn_splits = attn_max_splits(S, m->l_kv_heads, m->num_sms);
+    {
+        const char *mode = getenv("DIOLKOS_STEP");
+        m->use_step = !(mode && strcmp(mode, "kernels") == 0);
+    }
+    // the persistent step's attention: one (KV head, split) item per attention group of the grid
+    m->step_splits = std::max(1, std::min((step_attn_item_slots(m->num_sms) + m->l_kv_heads - 1) / m->l_kv_heads,
+                                          (S + kStepMinChunk - 1) / kStepMinChunk));
+    const int work_splits = std::max(m->attn_splits, m->step_splits);
     const size_t sz_x = align256((size_t)dim * 4), sz_qkv = align256((size_t)qkv_rows * 4);
     const size_t sz_hb = align256((size_t)lh * 4), sz_logits = align256((size_t)m->l_vocab * 4);
     const size_t sz_rope = align256((size_t)S * m->hs * 4);
-    const size_t sz_work = align256((size_t)m->l_heads * m->attn_splits * (m->hs + 2) * 4);
+    const size_t sz_work = align256((size_t)m->l_heads * work_splits * (m->hs + 2) * 4);
+    const size_t sz_stepcnt = align256((size_t)L * 5 * 8);
     const size_t sz_cnt = align256((size_t)m->l_kv_heads * 4);
     const size_t sz_part = align256((size_t)kMaxGemvGrid * m->num_sms * 8);
     const size_t sz_tok = align256((size_t)(S + 1) * 4);
     const size_t total = sz_x * 3 + sz_qkv + sz_hb + sz_logits + sz_rope + sz_work + sz_cnt + sz_part + 256 + sz_tok +
-                         4 * 256;
+                         4 * 256 + sz_stepcnt;
     if (cudaMalloc(&m->aarena, total) != cudaSuccess) return fail("activation memory");
     cudaMemsetAsync(m->aarena, 0, total, m->stream);
     p = m->aarena;
@@ -265,6 +283,7 @@ dk_model *dk_model_create(const int *cfg, int kv_type, int device, int tp_rank, 
     m->n_forced = reinterpret_cast<int *>(p); p += 256;
     m->err = reinterpret_cast<int *>(p); p += 256;
     m->epoch = reinterpret_cast<unsigned long long *>(p); p += 256;
+    m->step_cnt = reinterpret_cast<unsigned long long *>(p); p += sz_stepcnt;
 
     // ---- tensor-parallel exchange area (its own allocation: it is exported to the peers over IPC)
     if (tp_world > 1) {
@@ -303,6 +322,8 @@ void dk_model_destroy(dk_model *m) {
         if (m->peer_opened[q]) cudaIpcCloseMemHandle(m->peer_base[q]);
     cudaFree(m->comm);
     cudaFree(m->d_ptrs);
+    cudaFree(m->d_ops);
+    cudaFree(m->d_trace);
     if (m->h_small) cudaFreeHost(m->h_small);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
@@ -511,6 +532,169 @@ static int enqueue_step(dk_model *m, cudaStream_t st) {
     return DK_OK;
 }
 
+// The persistent step (step.cu): the step's op list -- per layer q|k|v GEMV, attention, wo GEMV, w1|w3
+// GEMV, w2 GEMV; then the classifier -- with the same arguments the per-kernel path gives each launch,
+// the dependency counters that replace the kernel boundaries, and the shared-memory plan.
+static int build_step(dk_model *m) {
+    const bool tp = m->world > 1;
+    void *const *tab = reinterpret_cast<void *const *>(m->d_ptrs);
+    std::vector<StepOp> ops;
+    auto cnt = [&](int l, int k) { return m->step_cnt + (size_t)l * 5 + k; };
+    auto gemv_op = [&](const uint8_t *w, int n, int d, int pro, int epi, const float *x, const float *norm, float *out,
+                       const GemvPlan &p) {
+        StepOp op;
+        op.kind = OP_GEMV;
+        GemvArgs &a = op.g;
+        a.w = w; a.n = n; a.d = d; a.pro = pro; a.epi = epi; a.x = x; a.norm_w = norm; a.out = out;
+        a.emb = m->emb; a.emb_T = m->emb_T; a.tokens = m->tokens; a.pos = m->pos; a.n_forced = m->n_forced;
+        a.seq_len = m->seq_len; a.amax_part = m->amax_part; a.amax_count = m->amax_count; a.err = m->err;
+        a.tp_rank = m->rank; a.tp_world = m->world; a.epoch = m->epoch; a.epoch_rw = m->epoch;
+        a.row_offset = m->vocab_off; a.vocab = m->vocab;
+        op.T = p.T;
+        op.ntiles = p.ntiles;
+        return op;
+    };
+    float *X[2] = {m->x, m->x2};
+    int cur = 0;
+    auto reduce_pro = [&](StepOp &op, int par, int index) {
+        GemvArgs &a = op.g;
+        a.pro = PRO_RMS_REDUCE;
+        a.x = X[cur];
+        a.x_out = X[1 - cur];
+        a.recv = reinterpret_cast<const float *>(m->comm + comm_recv_off(m, par));
+        a.cnt = reinterpret_cast<const unsigned long long *>(m->comm + comm_cnt_off(m, par));
+        a.red_index = index;
+        a.red_period = m->n_layers;
+        cur = 1 - cur;
+    };
+    auto peer_epi = [&](StepOp &op, int par) {
+        op.g.peer_recv = reinterpret_cast<float *const *>(tab + 8 * par);
+        op.g.peer_cnt = reinterpret_cast<unsigned long long *const *>(tab + 8 * (2 + par));
+    };
+    const int qkv_rows = m->l_dim + 2 * m->l_kv_dim;
+    const size_t esz = m->kv_type == DK_KV_F32 ? 4 : 2;
+    for (int l = 0; l < m->n_layers; ++l) {
+        const dk_layer &ly = m->layers[l];
+        StepOp q = gemv_op(ly.wqkv, m->dim, qkv_rows, l == 0 ? PRO_EMB_RMS : PRO_RMS, EPI_STORE, X[cur], ly.rms_att,
+                           m->qkv, m->p_qkv);
+        if (l > 0) {
+            if (tp) {
+                reduce_pro(q, 1, l - 1);
+            } else {
+                q.wait_cnt = cnt(l - 1, 4);
+                q.wait_units = (unsigned long long)m->dim;
+            }
+        }
+        q.done_cnt = cnt(l, 0);
+        ops.push_back(q);
+
+        StepOp at;
+        at.kind = OP_ATTN;
+        AttnArgs &t = at.at;
+        t.qkv = m->qkv; t.rope = m->rope;
+        t.k_cache = static_cast<uint8_t *>(m->kcache) + (size_t)l * m->kv_layer_elems * esz;
+        t.v_cache = static_cast<uint8_t *>(m->vcache) + (size_t)l * m->kv_layer_elems * esz;
+        t.out = m->xb; t.work = m->attn_work; t.count = m->attn_count; t.pos = m->pos;
+        t.n_heads = m->l_heads; t.n_kv_heads = m->l_kv_heads; t.head_size = m->hs; t.seq_len = m->seq_len;
+        t.kv_f32 = m->kv_type == DK_KV_F32; t.max_splits = m->step_splits; t.min_chunk = kStepMinChunk; t.err = m->err;
+        at.wait_cnt = cnt(l, 0);
+        at.wait_units = (unsigned long long)qkv_rows;
+        at.done_cnt = cnt(l, 1);
+        ops.push_back(at);
+
+        StepOp o = gemv_op(ly.wo, m->l_dim, m->dim, PRO_F32, tp ? EPI_PEER : EPI_ADD, m->xb, nullptr, X[cur], m->p_wo);
+        o.wait_cnt = cnt(l, 1);
+        o.wait_units = (unsigned long long)m->l_dim;
+        if (tp) peer_epi(o, 0);
+        else o.done_cnt = cnt(l, 2);
+        ops.push_back(o);
+
+        StepOp u = gemv_op(ly.w13, m->dim, 2 * m->l_hidden, PRO_RMS, EPI_SWIGLU, X[cur], ly.rms_ffn, m->hb, m->p_w13);
+        if (tp) {
+            reduce_pro(u, 0, l);
+        } else {
+            u.wait_cnt = cnt(l, 2);
+            u.wait_units = (unsigned long long)m->dim;
+        }
+        u.done_cnt = cnt(l, 3);
+        ops.push_back(u);
+
+        StepOp d = gemv_op(ly.w2, m->l_hidden, m->dim, PRO_F32, tp ? EPI_PEER : EPI_ADD, m->hb, nullptr, X[cur], m->p_w2);
+        d.wait_cnt = cnt(l, 3);
+        d.wait_units = (unsigned long long)m->l_hidden;
+        if (tp) peer_epi(d, 1);
+        else d.done_cnt = cnt(l, 4);
+        ops.push_back(d);
+    }
+    {
+        StepOp c = gemv_op(m->wcls, m->dim, m->l_vocab, PRO_RMS, EPI_ARGMAX, X[cur], m->rms_final, m->logits, m->p_cls);
+        if (tp) {
+            reduce_pro(c, 1, m->n_layers - 1);
+            c.g.peer_amax = reinterpret_cast<unsigned long long *const *>(tab + 8 * 4);
+            c.g.peer_amax_cnt = reinterpret_cast<unsigned long long *const *>(tab + 8 * 5);
+            c.g.amax_keys = reinterpret_cast<const unsigned long long *>(m->comm + comm_keys_off(m));
+            c.g.amax_keys_cnt = reinterpret_cast<const unsigned long long *>(m->comm + comm_keys_cnt_off(m));
+        } else {
+            c.wait_cnt = cnt(m->n_layers - 1, 4);
+            c.wait_units = (unsigned long long)m->dim;
+        }
+        ops.push_back(c);
+    }
+
+    // shared memory: the ring, the activation (or attention scratch), the control block
+    size_t slot = 0, act = step_attn_scratch_bytes(m->l_heads, m->l_kv_heads, m->hs);
+    for (const StepOp &op : ops)
+        if (op.kind == OP_GEMV) {
+            slot = std::max(slot, (size_t)op.T * q8_blk_bytes(std::min(op.g.n, 512)));
+            act = std::max(act, gemv_x_bytes(op.g.n));
+        }
+    StepArgs &sa = m->step;
+    sa.slot = (slot + 127) & ~(size_t)127;
+    sa.xoff = 0;  // set below
+    const size_t budget = 227 * 1024, tail = ((act + 127) & ~(size_t)127) + step_ctl_bytes();
+    int S = budget > tail ? (int)((budget - tail) / sa.slot) : 0;
+    S = std::min(S, kStepMaxSlots);
+    S -= S % kStepProducers;
+    if (S < 2 * kStepProducers)
+        return set_error(DK_ERR_INVALID, "persistent step: the activation (%zu bytes) leaves no room for the ring", act);
+    sa.S = S;
+    int nc = 4;  // measured best on B200 for the LLaMA shapes (more warps spin on the token flags)
+    if (const char *e = getenv("DIOLKOS_STEP_NC")) nc = atoi(e);
+    sa.NC = std::max(1, std::min(std::min(nc, S), kStepMaxConsumers));
+    sa.xoff = (size_t)S * sa.slot;
+    sa.ctl_off = sa.xoff + ((act + 127) & ~(size_t)127);
+    sa.smem = sa.ctl_off + step_ctl_bytes();
+    sa.epoch = m->epoch;
+    sa.epoch_rw = m->epoch;
+    sa.pos = m->pos;
+    sa.seq_len = m->seq_len;
+    sa.err = m->err;
+    m->n_ops = (int)ops.size();
+    if (cudaMalloc(&m->d_ops, ops.size() * sizeof(StepOp)) != cudaSuccess)
+        return set_error(DK_ERR_NOMEM, "persistent step: op list");
+    if (int r = cuda_status(cudaMemcpy(m->d_ops, ops.data(), ops.size() * sizeof(StepOp), cudaMemcpyHostToDevice),
+                            "persistent step: op upload"))
+        return r;
+    sa.ops = m->d_ops;
+    sa.nops = m->n_ops;
+    if (const char *e = getenv("DIOLKOS_STEP_TRACE"))
+        if (atoi(e) > 0) {
+            const size_t tb = (size_t)m->num_sms * m->n_ops * 4 * 8;
+            if (cudaMalloc(&m->d_trace, tb) != cudaSuccess || cudaMemset(m->d_trace, 0, tb) != cudaSuccess)
+                return set_error(DK_ERR_NOMEM, "persistent step: trace buffer");
+            sa.trace = m->d_trace;
+        }
+    const int per_sm = step_max_ctas_per_sm(sa.smem);
+    if (per_sm < 1)
+        return set_error(DK_ERR_INVALID, "persistent step: %zu bytes of shared memory per CTA do not fit an SM", sa.smem);
+    return DK_OK;
+}
+
+static int enqueue_step_persistent(dk_model *m, cudaStream_t st) {
+    m->kernels_per_step = 1;
+    return cuda_status(launch_step(m->step, m->num_sms, st), "persistent step");
+}
+
 extern "C" {
 
 int dk_model_set_weight(dk_model *m, int which, int layer, const void *q, const float *scale) {
@@ -583,10 +767,12 @@ int dk_model_finalize(dk_model *m) {
     cudaFree(m->stage);
     m->stage = nullptr;
     m->stage_bytes = 0;
+    if (m->use_step)
+        if (int r = build_step(m)) return r;
     // Capture one decode step.
     if (int r = cuda_status(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal), "begin capture"))
         return r;
-    const int rs = enqueue_step(m, m->stream);
+    const int rs = m->use_step ? enqueue_step_persistent(m, m->stream) : enqueue_step(m, m->stream);
     cudaGraph_t g = nullptr;
     cudaError_t e = cudaStreamEndCapture(m->stream, &g);
     if (rs) {
@@ -655,6 +841,16 @@ int dk_model_device_error(dk_model *m) {
 }
 
 int dk_model_kernels_per_step(dk_model *m) { return m ? m->kernels_per_step : 0; }
+
+int dk_model_trace(dk_model *m, unsigned long long *out, size_t n, int *grid, int *n_ops) {
+    if (int r = need(m)) return r;
+    if (grid) *grid = m->num_sms;
+    if (n_ops) *n_ops = m->n_ops;
+    if (!m->d_trace) return set_error(DK_ERR_STATE, "dk_model_trace: tracing is off (DIOLKOS_STEP_TRACE=1 at creation)");
+    const size_t total = (size_t)m->num_sms * m->n_ops * 4;
+    if (!out || n < total) return set_error(DK_ERR_INVALID, "dk_model_trace: need %zu entries", total);
+    return cuda_status(cudaMemcpy(out, m->d_trace, total * 8, cudaMemcpyDeviceToHost), "dk_model_trace");
+}
 
 size_t dk_model_weight_bytes(dk_model *m) {
     if (!m) return 0;

@@ -1,0 +1,890 @@
+// step.cu -- one whole decode step (reference forward, src/transformer.c:55-239, plus the greedy
+// sample_argmax of the generate loop) as ONE persistent kernel on sm_100a.
+//
+// Grid: one CTA per SM, launched cooperatively (all CTAs resident).  The step is a list of OPS built
+// on the host: per layer a q|k|v GEMV, attention, wo GEMV, w1|w3 GEMV and w2 GEMV, then the
+// classifier GEMV.  Every CTA walks the list in order.
+//
+//  * Two PRODUCER warps (one thread each) stream every GEMV stage this CTA owns -- in op order, ACROSS
+//    op boundaries -- through a ring of S shared-memory slots with the bulk-copy engine.  Weights never
+//    depend on activations, so while the CTA waits for an op's input (or runs attention) the ring keeps
+//    filling with the next matrix: the HBM stream does not stop between matrices the way it does
+//    between separate kernels.
+//  * Ten COMPUTE warps.  For a GEMV op: wait until the op's input is complete, build the Q8_0
+//    activation in shared memory (rmsnorm, embedding-row dequant or the tensor-parallel reduce fused
+//    in), then NC of them consume the stages exactly as the standalone GEMV does (gemv_core.cuh: the
+//    same bit-exact terms and in-order row sums), and the epilogue stores the rows.  For attention:
+//    five groups of two warps take (KV head, position split) items, flash-decoding style, and the last
+//    split of a head merges.
+//  * Dependencies between ops are COUNTERS in global memory, not grid barriers: an op adds the units
+//    it completed (rows, attention outputs) after a release fence, and a consumer op waits (bounded,
+//    acquire) until the counter reaches (epoch + 1) * units.  epoch = decode steps completed; the
+//    classifier's last CTA advances it, so counters never need resetting.  A CTA that owns no rows of
+//    an op neither reads its input nor counts, so every reader of a buffer has counted before anyone
+//    can overwrite it (the dataflow chain of the step orders all reuse).  The residual a prologue
+//    produces (embedding row, tensor-parallel sum) is stored by the CTA that owns the op's tile 0.
+//
+// Tensor parallel: wo / w2 store their partial rows into every rank's receive area (EPI_PEER) and the
+// next GEMV's prologue waits for all ranks' rows (PRO_RMS_REDUCE), exactly as the standalone kernels
+// do; only the waiting moved into the persistent kernel, where the weight stream hides it.
+//
+// Every wait is bounded (DK_WAIT_LIMIT_CYCLES): on a timeout the waiter records the error word and
+// raises the CTA's abort flag; all warps leave their loops at the next check, and the producers wait
+// for their copies in flight before the CTA exits.
+#include "dk_common.cuh"
+#include "dk_kernels.h"
+#include "gemv_core.cuh"
+
+#include <algorithm>
+#include <cstdio>
+
+namespace dk {
+namespace {
+
+constexpr int kStepWarps = 12;
+constexpr int kStepThreads = 32 * kStepWarps;
+constexpr int kComputeWarps = kStepWarps - kStepProducers;  // warps 0 .. 9
+constexpr int kComputeThreads = 32 * kComputeWarps;
+constexpr int kAttnGroupWarps = 2;
+constexpr int kAttnGroups = kComputeWarps / kAttnGroupWarps;  // 5
+constexpr int kAttnGroupThreads = 32 * kAttnGroupWarps;
+constexpr int kBatch = 8;          // positions an attention warp loads at once
+constexpr int kHeadsPerPass = 2;   // query heads of one KV head an attention warp holds at once
+constexpr int kBarCompute = 1;     // named barrier of the compute warps; 2 + g: attention group g
+static_assert(kComputeWarps % kAttnGroupWarps == 0, "attention groups");
+static_assert(2 + kAttnGroups <= 16, "named barriers");
+
+struct StepCtl {  // shared-memory control block
+    uint64_t full[kStepMaxSlots];    // ring slot holds its stage's weights
+    uint64_t empty[kStepMaxSlots];   // ring slot read by its consumer
+    unsigned long long wkey[kStepMaxConsumers];  // consumers' best greedy-token keys of the op
+    float red[kStepWarps];
+    float tokval[kStepMaxConsumers][32];  // running row sums handed to each consumer warp
+    int tokflag[kStepMaxConsumers];       // global index of the stage they are for
+    int abort;      // any wait gave up: every warp leaves
+    int last;       // this CTA took the classifier's last ticket
+    int grp_last[kAttnGroups];
+};
+
+// Self-checking build (-DDK_STEP_CHECKS): every global and shared access below whose index is not
+// trivially in range is tested first; a failed test records the site and value (first one only, with
+// a device printf), raises DK_ERR_INVALID and skips the access.  Off in normal builds.
+#ifdef DK_STEP_CHECKS
+__device__ __forceinline__ bool step_chk(bool ok, int *err, int site, long long v) {
+    if (!ok) {
+        if (atomicCAS(err + 1, 0, site) == 0)
+            printf("step check failed: site %d value %lld block %d thread %d\n", site, v, (int)blockIdx.x, (int)threadIdx.x);
+        atomicOr(err, DK_ERR_INVALID);
+    }
+    return ok;
+}
+#define DK_CHK(cond, err, site, v) step_chk((cond), (err), (site), (long long)(v))
+#else
+#define DK_CHK(cond, err, site, v) true
+#endif
+
+__device__ __forceinline__ unsigned long long globaltimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+// Optional timeline (StepArgs::trace): per CTA and op, [0] input ready, [1] activation built,
+// [2] op finished on this CTA, [3] the producers' last stage of the op issued.
+__device__ __forceinline__ void trace_mark(const StepArgs &sa, int op, int k) {
+    if (sa.trace) sa.trace[((size_t)blockIdx.x * sa.nops + op) * 4 + k] = globaltimer();
+}
+
+__device__ __forceinline__ void bar_compute() {
+    asm volatile("bar.sync %0, %1;" ::"n"(kBarCompute), "n"(kComputeThreads) : "memory");
+}
+__device__ __forceinline__ void bar_group(int g) {
+    asm volatile("bar.sync %0, %1;" ::"r"(2 + g), "n"(kAttnGroupThreads) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_gpu(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+// Bounded wait until a counter of this GPU reaches target.
+__device__ __forceinline__ bool wait_local(const unsigned long long *cnt, unsigned long long target, int *err) {
+    if (ld_acquire_gpu(cnt) >= target) return true;
+    const long long t0 = clock64();
+    while (ld_acquire_gpu(cnt) < target) {
+        if (clock64() - t0 > DK_WAIT_LIMIT_CYCLES) {
+            atomicOr(err, DK_ERR_TIMEOUT);
+            return false;
+        }
+    }
+    return true;
+}
+
+// The CTA's stages of a GEMV op: tile t0 + s / nblk, block s % nblk, for s < nst.
+__device__ __forceinline__ Sched op_sched(const StepOp &op) {
+    Sched sc;
+    sc.t0 = (int)((long long)blockIdx.x * op.ntiles / gridDim.x);
+    sc.nt = (int)((long long)(blockIdx.x + 1) * op.ntiles / gridDim.x) - sc.t0;
+    sc.nblk = (op.g.n + 511) >> 9;
+    sc.T = op.T;
+    sc.n = op.g.n;
+    sc.nst = sc.nt * sc.nblk;
+    sc.tile_bytes = (size_t)op.T * q8_row_bytes(op.g.n);
+    return sc;
+}
+
+// ---- activation prologue (compute threads) ------------------------------------------------------
+// 16 consecutive values of the op's input, half-group hg (values 16hg .. 16hg+15).
+__device__ __forceinline__ void load16(const GemvArgs &a, int tok, int hg, float (&f)[16]) {
+    const int n = a.n;
+    if (a.pro == PRO_EMB_RMS) {
+        if (!DK_CHK(tok >= 0 && tok < (a.vocab > 0 ? a.vocab : 1) && hg < (n >> 4), a.err, 10, tok)) {
+            #pragma unroll
+            for (int i = 0; i < 16; ++i) f[i] = 0.0f;
+            return;
+        }
+        // the embedding row's group g = hg/2, half hg&1 (src/transformer.c:69)
+        const int g = hg >> 1, b = g >> 4, wb = q8_blk_width(n, b), r = tok % a.emb_T, k = g & 15;
+        const uint8_t *seg = a.emb + q8_seg_off(n, a.emb_T, tok, b);
+        const uint4 c = __ldg(reinterpret_cast<const uint4 *>(seg + 16 * q8_swz_q(2 * k + (hg & 1), r, wb)));
+        const float s = __ldg(reinterpret_cast<const float *>(seg + wb + 16 * q8_swz_s(k >> 2, r, wb) + 4 * (k & 3)));
+        const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+        #pragma unroll
+        for (int i = 0; i < 16; ++i) f[i] = __fmul_rn((float)(int8_t)(w[i >> 2] >> (8 * (i & 3))), s);
+        return;
+    }
+    float4 v[4];
+    #pragma unroll
+    for (int k = 0; k < 4; ++k) v[k] = __ldcg(reinterpret_cast<const float4 *>(a.x + 16 * hg) + k);
+    if (a.pro == PRO_RMS_REDUCE) {
+        // x + (partial_0 + partial_1 + ...), ranks in order: the same bits on every rank
+        float4 t[4];
+        #pragma unroll
+        for (int k = 0; k < 4; ++k) t[k] = __ldcg(reinterpret_cast<const float4 *>(a.recv + 16 * hg) + k);
+        for (int q = 1; q < a.tp_world; ++q) {
+            #pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float4 u = __ldcg(reinterpret_cast<const float4 *>(a.recv + (size_t)q * n + 16 * hg) + k);
+                t[k] = make_float4(__fadd_rn(t[k].x, u.x), __fadd_rn(t[k].y, u.y), __fadd_rn(t[k].z, u.z),
+                                   __fadd_rn(t[k].w, u.w));
+            }
+        }
+        #pragma unroll
+        for (int k = 0; k < 4; ++k)
+            v[k] = make_float4(__fadd_rn(v[k].x, t[k].x), __fadd_rn(v[k].y, t[k].y), __fadd_rn(v[k].z, t[k].z),
+                               __fadd_rn(v[k].w, t[k].w));
+    }
+    #pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        f[4 * k] = v[k].x; f[4 * k + 1] = v[k].y; f[4 * k + 2] = v[k].z; f[4 * k + 3] = v[k].w;
+    }
+}
+
+// Quantise 16 values (one half of a group; the partner half is the neighbouring lane) into xq/xs.
+__device__ __forceinline__ void quant16(float (&f)[16], int hg, bool live, int8_t *xq, float *xs) {
+    float amax = 0.0f;
+    #pragma unroll
+    for (int k = 0; k < 16; ++k) amax = fmaxf(amax, fabsf(f[k]));
+    amax = fmaxf(amax, __shfl_xor_sync(FULL, amax, 1));  // the group's other half
+    float sc, inv;
+    q8_scale(amax, sc, inv);
+    if (!live) return;
+    uint32_t wq[4];
+    #pragma unroll
+    for (int k = 0; k < 4; ++k)
+        wq[k] = (uint32_t)(uint8_t)q8_round(f[4 * k], inv) | ((uint32_t)(uint8_t)q8_round(f[4 * k + 1], inv) << 8) |
+                ((uint32_t)(uint8_t)q8_round(f[4 * k + 2], inv) << 16) |
+                ((uint32_t)(uint8_t)q8_round(f[4 * k + 3], inv) << 24);
+    reinterpret_cast<uint4 *>(xq + 16 * hg)[0] = make_uint4(wq[0], wq[1], wq[2], wq[3]);
+    if (!(hg & 1)) xs[hg >> 1] = sc;
+}
+
+// Build the op's Q8_0 activation (xq int8[n], xs fp32[n/32]) with the compute threads.  Thread t
+// takes half-groups t, t + 320, ...; the rmsnorm family keeps up to two rounds in registers.
+// Returns false if a wait gave up.
+// writer: this CTA owns tile 0 of the op, so it stores the residual the prologue produces (the
+// embedding row, or x plus the ranks' partials): exactly one CTA of the grid does.
+// nw0: this thread's norm weights for round 0 (loaded before the input wait: they are constant).
+__device__ bool step_activation(const GemvArgs &a, int tok, int8_t *xq, float *xs, StepCtl &ctl, int tid,
+                                unsigned long long epoch, bool writer, const float4 (&nw0)[4]) {
+    const int n = a.n, nhg = n >> 4, warp = tid >> 5, lane = tid & 31;
+    if (a.pro == PRO_RMS_REDUCE) {
+        // every rank's partial rows for this exchange point have landed once the counter reaches this
+        if (tid == 0) {
+            const unsigned long long target =
+                (epoch * (unsigned long long)a.red_period + (unsigned long long)a.red_index + 1ull) *
+                (unsigned long long)a.tp_world * (unsigned long long)n;
+            if (!wait_counter(a.cnt, target, a.err)) ctl.abort = 1;
+        }
+        bar_compute();
+        if (*reinterpret_cast<volatile int *>(&ctl.abort)) return false;
+        __threadfence();
+    }
+    const bool rms = a.pro == PRO_RMS || a.pro == PRO_EMB_RMS || a.pro == PRO_RMS_REDUCE;
+    const bool write_x = (a.pro == PRO_EMB_RMS || a.pro == PRO_RMS_REDUCE) && writer;
+    float *xdst = a.pro == PRO_RMS_REDUCE ? a.x_out : const_cast<float *>(a.x);
+    const int rounds = (nhg + kComputeThreads - 1) / kComputeThreads;
+    if (rms && rounds <= 2) {
+        float f0[16], f1[16];
+        float ss = 0.0f;
+        #pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            float(&f)[16] = k == 0 ? f0 : f1;
+            const int hg = k * kComputeThreads + tid;
+            const bool live = k < rounds && hg < nhg;
+            if (live) {
+                load16(a, tok, hg, f);
+                if (write_x) {
+                    #pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        reinterpret_cast<float4 *>(xdst + 16 * hg)[j] =
+                            make_float4(f[4 * j], f[4 * j + 1], f[4 * j + 2], f[4 * j + 3]);
+                }
+                #pragma unroll
+                for (int j = 0; j < 16; ++j) ss = fmaf(f[j], f[j], ss);
+            } else {
+                #pragma unroll
+                for (int j = 0; j < 16; ++j) f[j] = 0.0f;
+            }
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) ctl.red[warp] = ss;
+        bar_compute();
+        float tot = 0.0f;
+        #pragma unroll
+        for (int w = 0; w < kComputeWarps; ++w) tot += ctl.red[w];
+        // rmsnorm (src/utils.c:68-75): 1/sqrt(ss/n + 1e-5), o = (w*x)*scale
+        float r = __fdiv_rn(tot, (float)n);
+        r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(r, 1e-5f)));
+        #pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            float(&f)[16] = k == 0 ? f0 : f1;
+            const int hg = k * kComputeThreads + tid;
+            if (k >= rounds) break;  // uniform
+            const bool live = hg < nhg;
+            if (live) {
+                #pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float4 w = k == 0 ? nw0[j] : __ldg(reinterpret_cast<const float4 *>(a.norm_w + 16 * hg) + j);
+                    f[4 * j] = __fmul_rn(__fmul_rn(w.x, f[4 * j]), r);
+                    f[4 * j + 1] = __fmul_rn(__fmul_rn(w.y, f[4 * j + 1]), r);
+                    f[4 * j + 2] = __fmul_rn(__fmul_rn(w.z, f[4 * j + 2]), r);
+                    f[4 * j + 3] = __fmul_rn(__fmul_rn(w.w, f[4 * j + 3]), r);
+                }
+            }
+            quant16(f, hg, live, xq, xs);
+        }
+        return true;
+    }
+    float r = 1.0f;
+    if (rms) {  // wide rmsnorm input: sum of squares first, values re-read below
+        float ss = 0.0f;
+        for (int hg = tid; hg < nhg; hg += kComputeThreads) {
+            float f[16];
+            load16(a, tok, hg, f);
+            if (write_x) {
+                #pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    reinterpret_cast<float4 *>(xdst + 16 * hg)[j] = make_float4(f[4 * j], f[4 * j + 1], f[4 * j + 2], f[4 * j + 3]);
+            }
+            #pragma unroll
+            for (int j = 0; j < 16; ++j) ss = fmaf(f[j], f[j], ss);
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) ctl.red[warp] = ss;
+        bar_compute();
+        float tot = 0.0f;
+        #pragma unroll
+        for (int w = 0; w < kComputeWarps; ++w) tot += ctl.red[w];
+        r = __fdiv_rn(tot, (float)n);
+        r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(r, 1e-5f)));
+    }
+    for (int base = 0; base < nhg; base += kComputeThreads) {  // uniform trip count: shuffles stay full-warp
+        const int hg = base + tid;
+        const bool live = hg < nhg;
+        float f[16];
+        if (live) {
+            load16(a, tok, hg, f);
+            if (rms) {
+                #pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float4 w = __ldg(reinterpret_cast<const float4 *>(a.norm_w + 16 * hg) + j);
+                    f[4 * j] = __fmul_rn(__fmul_rn(w.x, f[4 * j]), r);
+                    f[4 * j + 1] = __fmul_rn(__fmul_rn(w.y, f[4 * j + 1]), r);
+                    f[4 * j + 2] = __fmul_rn(__fmul_rn(w.z, f[4 * j + 2]), r);
+                    f[4 * j + 3] = __fmul_rn(__fmul_rn(w.w, f[4 * j + 3]), r);
+                }
+            }
+        } else {
+            #pragma unroll
+            for (int j = 0; j < 16; ++j) f[j] = 0.0f;
+        }
+        quant16(f, hg, live, xq, xs);
+    }
+    return true;
+}
+
+// ---- GEMV op: consumers ---------------------------------------------------------------------------
+// Consume this CTA's stages of the op (compute warp c < NC): the standalone GEMV's consumer loop
+// (gemv_core.cuh) with the ring position continuing from `gbase` (stages of earlier ops).  Stage s of
+// the op goes to warp s % NC; the rows' running sums travel from the warp of stage s to the warp of
+// stage s+1 (the TOKEN, flagged with the global stage index), so every row is summed in the
+// reference's group order while the terms of NC stages are computed at once.  Returns false on abort.
+__device__ bool gemv_consume(const StepOp &op, const Sched &sc, int gbase, int S, int NC, size_t slot_bytes,
+                             uint32_t ring_s, uint32_t xq_s, uint32_t xs_s, StepCtl &ctl, int c, int lane,
+                             unsigned long long &best) {
+    const GemvArgs &a = op.g;
+    const int n = a.n;
+    for (int s = c; s < sc.nst; s += NC) {
+        const int G = gbase + s, slot = G % S;
+        if (!__all_sync(FULL, mbar_wait_abortable(&ctl.full[slot], (uint32_t)((G / S) & 1), a.err, &ctl.abort, false))) {
+            if (lane == 0) ctl.abort = 1;
+            return false;
+        }
+        const int b = s % sc.nblk;
+        const int row = (sc.t0 + s / sc.nblk) * op.T + lane;
+        const bool live = lane < op.T && row < a.d;
+        const int wb = q8_blk_width(n, b);
+        float t[16] = {};
+        if (live && DK_CHK((size_t)slot * slot_bytes + (size_t)(lane + 1) * q8_blk_bytes(wb) <= (size_t)S * slot_bytes &&
+                               512 * b + wb <= n,
+                           a.err, 2, G)) {
+            const uint32_t seg = ring_s + (uint32_t)(slot * slot_bytes + lane * q8_blk_bytes(wb));
+            const uint32_t xqb = xq_s + 512u * b, xsb = xs_s + 64u * b;
+            if (wb == 512) block_terms_full(t, seg, xqb, xsb, lane);
+            else block_terms_part(t, seg, xqb, xsb, wb, lane);
+            // pinned here: otherwise the compiler may sink the term arithmetic past the token wait
+            #pragma unroll
+            for (int g = 0; g < 16; ++g) asm volatile("" : "+f"(t[g]));
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ctl.empty[slot]);
+        float sum = 0.0f;
+        if (s > 0) {  // the running sums of stage s-1
+            if (!__all_sync(FULL, token_wait(&ctl.tokflag[c], G, a.err, &ctl.abort))) {
+                if (lane == 0) ctl.abort = 1;
+                return false;
+            }
+            if (b > 0) sum = ctl.tokval[c][lane];
+        }
+        if (live) {
+            if (wb == 512) {
+                #pragma unroll
+                for (int g = 0; g < 16; ++g) sum = __fadd_rn(sum, t[g]);
+            } else {
+                #pragma unroll
+                for (int g = 0; g < 16; ++g)
+                    if (g < (wb >> 5)) sum = __fadd_rn(sum, t[g]);
+            }
+        }
+        if (b == sc.nblk - 1) {  // the tile's rows are finished
+            if (a.epi == EPI_SWIGLU) {
+                const float h3 = __shfl_down_sync(FULL, sum, 1);
+                if (live && !(lane & 1) && DK_CHK((row >> 1) < (a.d >> 1), a.err, 4, row)) {
+                    // val *= 1/(1+expf(-val)); val *= hb2 (src/transformer.c:214-220)
+                    float v = __fmul_rn(sum, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-sum))));
+                    a.out[row >> 1] = __fmul_rn(v, h3);
+                }
+            } else if (live) {
+                if (a.epi == EPI_ADD) {
+                    a.out[row] = __fadd_rn(__ldcg(a.out + row), sum);
+                } else if (a.epi == EPI_PEER) {
+                    for (int q = 0; q < a.tp_world; ++q) a.peer_recv[q][(size_t)a.tp_rank * a.d + row] = sum;
+                } else {
+                    a.out[row] = sum;
+                }
+                if (a.epi == EPI_ARGMAX) {
+                    const unsigned long long key = argmax_key(sum, row + a.row_offset);
+                    best = key > best ? key : best;
+                }
+            }
+        }
+        if (s + 1 < sc.nst) {  // hand the running sums to the warp of stage s+1
+            const int cn = (c + 1) % NC;
+            ctl.tokval[cn][lane] = sum;
+            __threadfence_block();
+            __syncwarp();
+            if (lane == 0) *reinterpret_cast<volatile int *>(&ctl.tokflag[cn]) = G + 1;
+        }
+    }
+    return true;
+}
+
+// ---- attention op ----------------------------------------------------------------------------------
+template <bool F32>
+__device__ __forceinline__ float4 load_kv4(const void *base, size_t idx) {
+    if constexpr (F32) {
+        return __ldcg(reinterpret_cast<const float4 *>(static_cast<const float *>(base) + idx));
+    } else {
+        const uint2 u = __ldcg(reinterpret_cast<const uint2 *>(static_cast<const uint16_t *>(base) + idx));
+        return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u), __uint_as_float(u.y << 16),
+                           __uint_as_float(u.y & 0xFFFF0000u));
+    }
+}
+template <bool F32>
+__device__ __forceinline__ void store_kv4(void *base, size_t idx, float4 v) {
+    if constexpr (F32) {
+        *reinterpret_cast<float4 *>(static_cast<float *>(base) + idx) = v;
+    } else {
+        const uint2 u = make_uint2((__float_as_uint(v.x) >> 16) | (__float_as_uint(v.y) & 0xFFFF0000u),
+                                   (__float_as_uint(v.z) >> 16) | (__float_as_uint(v.w) & 0xFFFF0000u));
+        *reinterpret_cast<uint2 *>(static_cast<uint16_t *>(base) + idx) = u;
+    }
+}
+template <bool F32>
+__device__ __forceinline__ float round_kv(float f) {
+    if constexpr (F32) return f;
+    else return __uint_as_float(__float_as_uint(f) & 0xFFFF0000u);
+}
+// RoPE (src/transformer.c:87-119, HF rotate-half) of dims d0..d0+3 of head vector v, as the reference's
+// compiled code evaluates it: a' = fma(a, c, -(b*s)), b' = fma(a, s, b*c).
+__device__ __forceinline__ float4 rope4(const float *v, const float *cs, int d0, int half) {
+    float r[4];
+    #pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const int d = d0 + e;
+        if (d < half) {
+            const float c = __ldg(cs + 2 * d), sn = __ldg(cs + 2 * d + 1);
+            r[e] = __fmaf_rn(__ldcg(v + d), c, -__fmul_rn(__ldcg(v + d + half), sn));
+        } else {
+            const int j = d - half;
+            const float c = __ldg(cs + 2 * j), sn = __ldg(cs + 2 * j + 1);
+            r[e] = __fmaf_rn(__ldcg(v + j), sn, __fmul_rn(__ldcg(v + d), c));
+        }
+    }
+    return make_float4(r[0], r[1], r[2], r[3]);
+}
+__device__ __forceinline__ float dot4(float4 a, float4 b) {
+    return __fmaf_rn(a.w, b.w, __fmaf_rn(a.z, b.z, __fmaf_rn(a.y, b.y, __fmul_rn(a.x, b.x))));
+}
+
+// K and V rows tb .. tb+kBatch-1 of this lane's 4 dims (row pos comes from registers: this step's k, v).
+template <bool F32>
+__device__ __forceinline__ void load_kv_batch(const AttnArgs &a, size_t head_base, int hs, int tb, int t1, int pos,
+                                              bool act, float4 kp, float4 vp, float4 (&kk)[kBatch],
+                                              float4 (&vv)[kBatch]) {
+    #pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+        const int t = tb + j;
+        if (t < t1 && act && t != pos) {
+            kk[j] = load_kv4<F32>(a.k_cache, head_base + (size_t)t * hs);
+            vv[j] = load_kv4<F32>(a.v_cache, head_base + (size_t)t * hs);
+        } else {
+            kk[j] = (t == pos) ? kp : make_float4(0, 0, 0, 0);
+            vv[j] = (t == pos) ? vp : make_float4(0, 0, 0, 0);
+        }
+    }
+}
+
+// One (KV head, split) item on attention group grp (kAttnGroupWarps warps): the arithmetic of the
+// standalone attention kernel (attention.cu), with the group's named barrier in place of the CTA's.
+// sm = the group's scratch [kAttnGroupWarps][kv_mul][hs + 4].  The output of a KV head's query heads
+// is complete when its last split has merged; that split counts them on done_cnt.
+template <bool F32>
+__device__ void attn_item(const AttnArgs &a, int pos, int kvh, int split, int nsplit, int chunk, int grp, int gt,
+                          float *sm, StepCtl &ctl, unsigned long long *done_cnt) {
+    const int lane = gt & 31, warp = gt >> 5;
+    const int hs = a.head_size, half = hs >> 1;
+    const int kv_mul = a.n_heads / a.n_kv_heads;
+    const int dim = a.n_heads * hs, kv_dim = a.n_kv_heads * hs;
+    const int t0 = split * chunk, t1 = min(pos + 1, t0 + chunk);
+    const int d0 = 4 * lane;
+    const bool act = d0 < hs;
+    const float *cs = a.rope + (size_t)pos * hs;
+    const size_t head_base = (size_t)kvh * a.seq_len * hs + d0;
+    if (!DK_CHK(kvh < a.n_kv_heads && split < a.max_splits && pos < a.seq_len && t0 <= pos && kv_mul <= 8 &&
+                    (size_t)(kvh + 1) * a.seq_len * hs <= (size_t)a.n_kv_heads * a.seq_len * hs,
+                a.err, 5, kvh * 1000 + split))
+        return;
+
+    float4 kp = make_float4(0, 0, 0, 0), vp = kp;
+    if (pos >= t0 && pos < t1 && act) {
+        const float4 kr = rope4(a.qkv + dim + (size_t)kvh * hs, cs, d0, half);
+        const float4 vr = __ldcg(reinterpret_cast<const float4 *>(a.qkv + dim + kv_dim + (size_t)kvh * hs + d0));
+        kp = make_float4(round_kv<F32>(kr.x), round_kv<F32>(kr.y), round_kv<F32>(kr.z), round_kv<F32>(kr.w));
+        vp = make_float4(round_kv<F32>(vr.x), round_kv<F32>(vr.y), round_kv<F32>(vr.z), round_kv<F32>(vr.w));
+        if (warp == 0) {
+            store_kv4<F32>(a.k_cache, head_base + (size_t)pos * hs, kr);
+            store_kv4<F32>(a.v_cache, head_base + (size_t)pos * hs, vr);
+        }
+    }
+    const float sq = __fsqrt_rn((float)hs);
+    const int SW = hs + 4;
+    // Query heads in passes of kHeadsPerPass (bounded registers; a pass re-reads the split's K/V).
+    for (int m0 = 0; m0 < kv_mul; m0 += kHeadsPerPass) {
+        float4 q[kHeadsPerPass];
+        float mx[kHeadsPerPass], l[kHeadsPerPass];
+        float4 acc[kHeadsPerPass];
+        #pragma unroll
+        for (int m = 0; m < kHeadsPerPass; ++m) {
+            q[m] = (m0 + m < kv_mul && act) ? rope4(a.qkv + (size_t)(kvh * kv_mul + m0 + m) * hs, cs, d0, half)
+                                            : make_float4(0, 0, 0, 0);
+            mx[m] = -INFINITY;
+            l[m] = 0.0f;
+            acc[m] = make_float4(0, 0, 0, 0);
+        }
+        for (int tb = t0 + warp * kBatch; tb < t1; tb += kAttnGroupWarps * kBatch) {
+            float4 kk[kBatch], vv[kBatch];
+            load_kv_batch<F32>(a, head_base, hs, tb, t1, pos, act, kp, vp, kk, vv);
+            #pragma unroll
+            for (int m = 0; m < kHeadsPerPass; ++m) {
+                if (m0 + m >= kv_mul) break;
+                float sc[kBatch];
+                float bmax = -INFINITY;
+                #pragma unroll
+                for (int j = 0; j < kBatch; ++j) {
+                    // score = q.k / sqrtf(head_size) (src/transformer.c:158-163)
+                    const float d = warp_sum(dot4(q[m], kk[j]));
+                    sc[j] = (tb + j < t1) ? __fdiv_rn(d, sq) : -INFINITY;
+                    bmax = fmaxf(bmax, sc[j]);
+                }
+                const float mnew = fmaxf(mx[m], bmax);
+                const float rescale = expf(mx[m] - mnew);
+                float lm = __fmul_rn(l[m], rescale);
+                float4 am = make_float4(__fmul_rn(acc[m].x, rescale), __fmul_rn(acc[m].y, rescale),
+                                        __fmul_rn(acc[m].z, rescale), __fmul_rn(acc[m].w, rescale));
+                #pragma unroll
+                for (int j = 0; j < kBatch; ++j) {
+                    const float pj = expf(sc[j] - mnew);
+                    lm = __fadd_rn(lm, pj);
+                    am.x = __fmaf_rn(pj, vv[j].x, am.x);
+                    am.y = __fmaf_rn(pj, vv[j].y, am.y);
+                    am.z = __fmaf_rn(pj, vv[j].z, am.z);
+                    am.w = __fmaf_rn(pj, vv[j].w, am.w);
+                }
+                mx[m] = mnew;
+                l[m] = lm;
+                acc[m] = am;
+            }
+        }
+        // the group's scratch per (warp, head): max, sum, 2 pad, hs accumulators
+        #pragma unroll
+        for (int m = 0; m < kHeadsPerPass; ++m) {
+            if (m0 + m >= kv_mul) break;
+            float *cw = sm + (size_t)(warp * kv_mul + m0 + m) * SW;
+            if (lane == 0) {
+                cw[0] = mx[m];
+                cw[1] = l[m];
+            }
+            if (act) *reinterpret_cast<float4 *>(cw + 4 + d0) = acc[m];
+        }
+    }
+    const int W = hs + 2;
+    bar_group(grp);
+    for (int m = 0; m < kv_mul; ++m) {
+        float M = -INFINITY;
+        for (int w = 0; w < kAttnGroupWarps; ++w) M = fmaxf(M, sm[(size_t)(w * kv_mul + m) * SW]);
+        float L = 0.0f;
+        for (int w = 0; w < kAttnGroupWarps; ++w) {
+            const float *cw = sm + (size_t)(w * kv_mul + m) * SW;
+            L = __fmaf_rn(cw[1], expf(cw[0] - M), L);
+        }
+        for (int e = gt; e < hs; e += kAttnGroupThreads) {
+            float o = 0.0f;
+            for (int w = 0; w < kAttnGroupWarps; ++w) {
+                const float *cw = sm + (size_t)(w * kv_mul + m) * SW;
+                o = __fmaf_rn(cw[4 + e], expf(cw[0] - M), o);
+            }
+            if (nsplit == 1) {
+                a.out[(size_t)(kvh * kv_mul + m) * hs + e] = __fdiv_rn(o, L);
+            } else {
+                a.work[((size_t)(kvh * kv_mul + m) * a.max_splits + split) * W + 2 + e] = o;
+            }
+        }
+        if (nsplit > 1 && gt == 0) {
+            float *w = a.work + ((size_t)(kvh * kv_mul + m) * a.max_splits + split) * W;
+            w[0] = M;
+            w[1] = L;
+        }
+    }
+    __threadfence();
+    bar_group(grp);  // the scratch is reused by the next item; every store above is fenced
+    if (nsplit > 1) {
+        if (gt == 0) {
+            const unsigned ticket = atomicAdd(a.count + kvh, 1u);
+            ctl.grp_last[grp] = ticket == (unsigned)nsplit - 1u;
+        }
+        bar_group(grp);
+        if (!ctl.grp_last[grp]) return;
+        __threadfence();
+        for (int m = 0; m < kv_mul; ++m) {
+            const float *wb = a.work + (size_t)(kvh * kv_mul + m) * a.max_splits * W;
+            float M = -INFINITY;
+            for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(wb + (size_t)s * W));
+            float L = 0.0f;
+            for (int s = 0; s < nsplit; ++s) L = __fmaf_rn(__ldcg(wb + (size_t)s * W + 1), expf(__ldcg(wb + (size_t)s * W) - M), L);
+            for (int e = gt; e < hs; e += kAttnGroupThreads) {
+                float o = 0.0f;
+                for (int s = 0; s < nsplit; ++s)
+                    o = __fmaf_rn(__ldcg(wb + (size_t)s * W + 2 + e), expf(__ldcg(wb + (size_t)s * W) - M), o);
+                a.out[(size_t)(kvh * kv_mul + m) * hs + e] = __fdiv_rn(o, L);
+            }
+        }
+        if (gt == 0) a.count[kvh] = 0u;
+        __threadfence();
+        bar_group(grp);
+    }
+    if (gt == 0) atomicAdd(done_cnt, (unsigned long long)kv_mul * hs);
+}
+
+__global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int S = sa.S, NC = sa.NC;
+    uint8_t *ring = smem;
+    uint8_t *act = smem + sa.xoff;
+    StepCtl &ctl = *reinterpret_cast<StepCtl *>(smem + sa.ctl_off);
+    const uint32_t ring_s = smem_u32(ring);
+
+    if (tid == 0) {
+        for (int i = 0; i < S; ++i) {
+            mbar_init(&ctl.full[i], 1);
+            mbar_init(&ctl.empty[i], 1);
+        }
+        for (int i = 0; i < kStepMaxConsumers; ++i) ctl.tokflag[i] = -1;
+        ctl.abort = 0;
+        ctl.last = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
+    const unsigned long long epoch = *sa.epoch;
+    const int pos = *sa.pos;
+    const bool pos_ok = pos >= 0 && pos < sa.seq_len;
+
+    if (warp >= kComputeWarps) {
+        // ---- producers: stream every GEMV stage of this CTA, op after op ----
+        const int q = warp - kComputeWarps;
+        if (lane != 0 || !pos_ok) return;
+        const uint64_t policy = l2_evict_first_policy();
+        int gbase = 0, issued_hi = -1;
+        bool ok = true;
+        for (int i = 0; i < sa.nops && ok; ++i) {
+            const StepOp &op = sa.ops[i];
+            if (op.kind == OP_ATTN) {
+                // The cache rows this CTA's attention items will read (positions < pos, written by earlier
+                // steps) go to L2 now, while the q|k|v GEMV still streams: attention then waits for L2,
+                // not behind the weight stream queued at HBM.
+                if (q == 0) {
+                    const AttnArgs &at = op.at;
+                    const int T = pos + 1;
+                    const int nsplit = min(at.max_splits, (T + at.min_chunk - 1) / at.min_chunk);
+                    const int chunk = (T + nsplit - 1) / nsplit;
+                    const size_t row = (size_t)at.head_size * (at.kv_f32 ? 4 : 2);
+                    for (int g = 0; g < kAttnGroups; ++g) {
+                        const int it = g * (int)gridDim.x + (int)blockIdx.x;
+                        if (it >= at.n_kv_heads * nsplit) break;
+                        const int kvh = it / nsplit, t0 = (it % nsplit) * chunk, t1 = min(pos, t0 + chunk);
+                        if (t1 <= t0) continue;
+                        const size_t off = ((size_t)kvh * at.seq_len + t0) * row;
+                        const uint32_t nb = (uint32_t)((size_t)(t1 - t0) * row);
+                        bulk_prefetch_l2(static_cast<const uint8_t *>(at.k_cache) + off, nb);
+                        bulk_prefetch_l2(static_cast<const uint8_t *>(at.v_cache) + off, nb);
+                    }
+                }
+                continue;
+            }
+            const Sched sc = op_sched(op);
+            // this producer's stages: global index G = gbase + s with G % NP == q
+            int s = (q - gbase % kStepProducers + kStepProducers) % kStepProducers;
+            for (; s < sc.nst; s += kStepProducers) {
+                const int G = gbase + s, slot = G % S;
+                if (G >= S && !mbar_wait_abortable(&ctl.empty[slot], (uint32_t)(((G / S) - 1) & 1), op.g.err, &ctl.abort, false)) {
+                    ctl.abort = 1;
+                    ok = false;
+                    break;
+                }
+                {
+                    const uint8_t *src = sc.src(op.g.w, s);
+                    const size_t packed = (size_t)op.ntiles * op.T * q8_row_bytes(op.g.n);
+                    const uint32_t nb = sc.bytes(s);
+                    if (!DK_CHK(src >= op.g.w && src + nb <= op.g.w + packed && !((uintptr_t)src & 15) && !(nb & 15) &&
+                                    nb <= sa.slot && slot < S,
+                                sa.err, 1, G)) {
+                        ctl.abort = 1;
+                        ok = false;
+                        break;
+                    }
+                }
+                mbar_arrive_expect_tx(&ctl.full[slot], sc.bytes(s));
+                bulk_g2s(ring + (size_t)slot * sa.slot, sc.src(op.g.w, s), sc.bytes(s), &ctl.full[slot], policy);
+                issued_hi = G;
+            }
+            if (q == 0) trace_mark(sa, i, 3);
+            gbase += sc.nst;
+        }
+        // Never leave a copy in flight into the shared memory of an exiting CTA: wait for the last copy
+        // issued into each of this producer's slots.
+        for (int G = issued_hi; G >= 0 && G > issued_hi - S; G -= kStepProducers)
+            mbar_wait(&ctl.full[G % S], (uint32_t)((G / S) & 1), sa.err);
+        return;
+    }
+
+    // ---- compute warps ----
+    if (!pos_ok) {
+        if (tid == 0 && blockIdx.x == 0) atomicOr(sa.err, DK_ERR_INVALID);
+        return;
+    }
+    int gbase = 0;
+    for (int i = 0; i < sa.nops; ++i) {
+        const StepOp &op = sa.ops[i];
+        if (op.kind == OP_GEMV) {
+            const GemvArgs &a = op.g;
+            const Sched sc = op_sched(op);
+            const bool mine = sc.nst > 0;
+            unsigned long long best = 0ull;
+            if (mine) {
+                float4 nw[4];
+                #pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    nw[j] = (a.norm_w && tid < (a.n >> 4)) ? __ldg(reinterpret_cast<const float4 *>(a.norm_w + 16 * tid) + j)
+                                                           : make_float4(0, 0, 0, 0);
+                if (op.wait_cnt && tid == 0 && !wait_local(op.wait_cnt, (epoch + 1ull) * op.wait_units, sa.err))
+                    ctl.abort = 1;
+                bar_compute();
+                if (*reinterpret_cast<volatile int *>(&ctl.abort)) break;
+                __threadfence();
+                if (tid == 0) trace_mark(sa, i, 0);
+                int8_t *xq = reinterpret_cast<int8_t *>(act);
+                float *xs = reinterpret_cast<float *>(act + ((a.n + 15) & ~15));
+                const int tok = a.pro == PRO_EMB_RMS ? __ldcg(a.tokens + pos) : 0;
+                const bool ok = step_activation(a, tok, xq, xs, ctl, tid, epoch, sc.t0 == 0, nw);
+                bar_compute();
+                if (!ok || *reinterpret_cast<volatile int *>(&ctl.abort)) break;
+                if (tid == 0) trace_mark(sa, i, 1);
+                if (warp < NC) {
+                    gemv_consume(op, sc, gbase, S, NC, sa.slot, ring_s, smem_u32(xq), smem_u32(xs), ctl, warp, lane, best);
+                    if (a.epi == EPI_ARGMAX) {
+                        #pragma unroll
+                        for (int o = 16; o > 0; o >>= 1) {
+                            const unsigned long long other = __shfl_xor_sync(FULL, best, o);
+                            best = other > best ? other : best;
+                        }
+                        if (lane == 0) ctl.wkey[warp] = best;
+                    }
+                }
+                bar_compute();  // every row stored, the activation no longer read
+                if (*reinterpret_cast<volatile int *>(&ctl.abort)) break;
+                if (tid == 0) {
+                    trace_mark(sa, i, 2);
+                    const int lo = sc.t0 * op.T, hi = min(a.d, (sc.t0 + sc.nt) * op.T);
+                    const unsigned long long rows = hi > lo ? (unsigned long long)(hi - lo) : 0ull;
+                    if (a.epi == EPI_PEER) {
+                        // count this CTA's rows on every rank: a rank that sees the count sees the rows
+                        __threadfence_system();
+                        for (int r = 0; r < a.tp_world; ++r) atomicAdd_system(a.peer_cnt[r], rows);
+                    } else if (op.done_cnt) {
+                        __threadfence();
+                        atomicAdd(op.done_cnt, a.epi == EPI_SWIGLU ? rows / 2 : rows);
+                    }
+                }
+            }
+            gbase += sc.nst;
+            if (a.epi == EPI_ARGMAX) {
+                // every CTA takes a ticket; the last one picks the token (src/sampler.c:6-17)
+                if (tid == 0) {
+                    unsigned long long bb = 0ull;
+                    if (mine)
+                        for (int w = 0; w < NC; ++w) bb = ctl.wkey[w] > bb ? ctl.wkey[w] : bb;
+                    a.amax_part[blockIdx.x] = bb;
+                    __threadfence();
+                    const unsigned ticket = atomicAdd(a.amax_count, 1u);
+                    ctl.last = ticket == gridDim.x - 1;
+                }
+                bar_compute();
+                if (ctl.last && tid == 0) {
+                    __threadfence();
+                    unsigned long long bb = 0ull;
+                    for (int c = 0; c < (int)gridDim.x; ++c) {
+                        const unsigned long long kk = __ldcg(a.amax_part + c);
+                        bb = kk > bb ? kk : bb;
+                    }
+                    if (a.tp_world > 1) {
+                        for (int r = 0; r < a.tp_world; ++r) a.peer_amax[r][a.tp_rank] = bb;
+                        __threadfence_system();
+                        for (int r = 0; r < a.tp_world; ++r) atomicAdd_system(a.peer_amax_cnt[r], 1ull);
+                        wait_counter(a.amax_keys_cnt, (epoch + 1ull) * (unsigned long long)a.tp_world, a.err);
+                        __threadfence();
+                        for (int r = 0; r < a.tp_world; ++r) {
+                            const unsigned long long k = __ldcg(a.amax_keys + r);
+                            bb = k > bb ? k : bb;
+                        }
+                    }
+                    const int vocab = a.vocab > 0 ? a.vocab : a.d;
+                    int idx = (bb == 0ull) ? 0 : argmax_idx(bb);
+                    if (idx < 0 || idx >= vocab) idx = 0;
+                    if (pos + 1 <= a.seq_len && pos + 1 >= *a.n_forced) a.tokens[pos + 1] = idx;
+                    *a.amax_count = 0u;
+                    __threadfence();
+                    *a.pos = pos + 1;
+                    *sa.epoch_rw = epoch + 1ull;
+                }
+            }
+        } else {  // OP_ATTN
+            const AttnArgs &at = op.at;
+            if (op.wait_cnt && tid == 0 && !wait_local(op.wait_cnt, (epoch + 1ull) * op.wait_units, sa.err)) ctl.abort = 1;
+            bar_compute();
+            if (*reinterpret_cast<volatile int *>(&ctl.abort)) break;
+            __threadfence();
+            if (tid == 0) trace_mark(sa, i, 0);
+            const int T = pos + 1;
+            const int nsplit = min(at.max_splits, (T + at.min_chunk - 1) / at.min_chunk);
+            const int chunk = (T + nsplit - 1) / nsplit;
+            const int items = at.n_kv_heads * nsplit;
+            const int grp = warp / kAttnGroupWarps, gt = tid - grp * kAttnGroupThreads;
+            const int kv_mul = at.n_heads / at.n_kv_heads;
+            float *sm = reinterpret_cast<float *>(act) + (size_t)grp * kAttnGroupWarps * kv_mul * (at.head_size + 4);
+            // item it runs on CTA it % grid: consecutive items (the splits of one head, then the next
+            // head) spread over all SMs, so every SM's share of the KV cache is loaded at once
+            for (int it = grp * (int)gridDim.x + (int)blockIdx.x; it < items; it += gridDim.x * kAttnGroups) {
+                const int kvh = it / nsplit, split = it % nsplit;
+                if (at.kv_f32) attn_item<true>(at, pos, kvh, split, nsplit, chunk, grp, gt, sm, ctl, op.done_cnt);
+                else attn_item<false>(at, pos, kvh, split, nsplit, chunk, grp, gt, sm, ctl, op.done_cnt);
+            }
+            bar_compute();  // the scratch (the activation area) is free again
+            if (tid == 0) trace_mark(sa, i, 2);
+        }
+    }
+}
+
+}  // namespace
+
+size_t step_ctl_bytes() { return (sizeof(StepCtl) + 127) & ~(size_t)127; }
+size_t step_attn_scratch_bytes(int n_heads, int n_kv_heads, int head_size) {
+    return sizeof(float) * (size_t)kAttnGroups * kAttnGroupWarps * (n_heads / n_kv_heads) * (head_size + 4);
+}
+int step_attn_item_slots(int num_ctas) { return num_ctas * kAttnGroups; }
+int step_threads() { return kStepThreads; }
+
+cudaError_t launch_step(const StepArgs &sa, int grid, cudaStream_t st) {
+    if (sa.S < 1 || sa.S > kStepMaxSlots || sa.S < kStepProducers || sa.S % kStepProducers || sa.NC < 1 ||
+        sa.NC > kStepMaxConsumers || sa.NC > kComputeWarps || sa.S < sa.NC || sa.smem > 227 * 1024 ||
+        sa.ctl_off + step_ctl_bytes() > sa.smem || sa.xoff < (size_t)sa.S * sa.slot || sa.ctl_off < sa.xoff)
+        return cudaErrorInvalidValue;
+    static int attr_bytes[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (attr_bytes[dev] < (int)sa.smem) {
+        cudaError_t e = cudaFuncSetAttribute(step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sa.smem);
+        if (e != cudaSuccess) return e;
+        attr_bytes[dev] = (int)sa.smem;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kStepThreads);
+    cfg.dynamicSmemBytes = sa.smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;  // all CTAs resident: the counter waits need it
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, step_kernel, sa);
+}
+
+int step_max_ctas_per_sm(size_t smem) {
+    int n = 0;
+    if (cudaFuncSetAttribute(step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, step_kernel, kStepThreads, smem) != cudaSuccess) return 0;
+    return n;
+}
+
+}  // namespace dk
