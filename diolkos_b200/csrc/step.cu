@@ -50,6 +50,8 @@ constexpr int kAttnGroups = kComputeWarps / kAttnGroupWarps;  // 5
 constexpr int kAttnGroupThreads = 32 * kAttnGroupWarps;
 constexpr int kBatch = 8;          // positions an attention warp loads at once
 constexpr int kHeadsPerPass = 2;   // query heads of one KV head an attention warp holds at once
+constexpr int kMergeChunk = 12;    // splits whose partials the merging group loads in one round trip
+constexpr int kMergeDims = 2;      // head dims per merging thread (head_size <= 128 on 64 threads)
 constexpr int kBarCompute = 1;     // named barrier of the compute warps; 2 + g: attention group g
 static_assert(kComputeWarps % kAttnGroupWarps == 0, "attention groups");
 static_assert(2 + kAttnGroups <= 16, "named barriers");
@@ -271,6 +273,27 @@ __device__ bool step_activation(const GemvArgs &a, int tok, int8_t *xq, float *x
                 }
             }
             quant16(f, hg, live, xq, xs);
+        }
+        return true;
+    }
+    if (!rms && rounds <= 3) {
+        // plain quantisation of up to three rounds: every load is issued before any is used
+        float f[3][16];
+        #pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            const int hg = k * kComputeThreads + tid;
+            if (k < rounds && hg < nhg) {
+                load16(a, tok, hg, f[k]);
+            } else {
+                #pragma unroll
+                for (int j = 0; j < 16; ++j) f[k][j] = 0.0f;
+            }
+        }
+        #pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            if (k >= rounds) break;  // uniform
+            const int hg = k * kComputeThreads + tid;
+            quant16(f[k], hg, hg < nhg, xq, xs);
         }
         return true;
     }
@@ -605,17 +628,47 @@ __device__ void attn_item(const AttnArgs &a, int pos, int kvh, int split, int ns
         bar_group(grp);
         if (!ctl.grp_last[grp]) return;
         __threadfence();
+        // Merge the splits: every split's (max, sum) and this thread's accumulators are loaded together
+        // (one round trip per kMergeChunk splits), folded with an online rescale.
         for (int m = 0; m < kv_mul; ++m) {
             const float *wb = a.work + (size_t)(kvh * kv_mul + m) * a.max_splits * W;
-            float M = -INFINITY;
-            for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(wb + (size_t)s * W));
-            float L = 0.0f;
-            for (int s = 0; s < nsplit; ++s) L = __fmaf_rn(__ldcg(wb + (size_t)s * W + 1), expf(__ldcg(wb + (size_t)s * W) - M), L);
-            for (int e = gt; e < hs; e += kAttnGroupThreads) {
-                float o = 0.0f;
-                for (int s = 0; s < nsplit; ++s)
-                    o = __fmaf_rn(__ldcg(wb + (size_t)s * W + 2 + e), expf(__ldcg(wb + (size_t)s * W) - M), o);
-                a.out[(size_t)(kvh * kv_mul + m) * hs + e] = __fdiv_rn(o, L);
+            float M = -INFINITY, L = 0.0f, o[kMergeDims];
+            #pragma unroll
+            for (int k = 0; k < kMergeDims; ++k) o[k] = 0.0f;
+            for (int s0 = 0; s0 < nsplit; s0 += kMergeChunk) {
+                float cm[kMergeChunk], cl[kMergeChunk], co[kMergeChunk][kMergeDims];
+                #pragma unroll
+                for (int j = 0; j < kMergeChunk; ++j) {
+                    const bool in = s0 + j < nsplit;
+                    const float *w = wb + (size_t)(s0 + j) * W;
+                    cm[j] = in ? __ldcg(w) : -INFINITY;
+                    cl[j] = in ? __ldcg(w + 1) : 0.0f;
+                    #pragma unroll
+                    for (int k = 0; k < kMergeDims; ++k) {
+                        const int e = gt + k * kAttnGroupThreads;
+                        co[j][k] = (in && e < hs) ? __ldcg(w + 2 + e) : 0.0f;
+                    }
+                }
+                float cmax = M;
+                #pragma unroll
+                for (int j = 0; j < kMergeChunk; ++j) cmax = fmaxf(cmax, cm[j]);
+                const float r = expf(M - cmax);  // 0 while M is -inf
+                L = __fmul_rn(L, r);
+                #pragma unroll
+                for (int k = 0; k < kMergeDims; ++k) o[k] = __fmul_rn(o[k], r);
+                #pragma unroll
+                for (int j = 0; j < kMergeChunk; ++j) {
+                    const float f = expf(cm[j] - cmax);  // 0 for the padding entries
+                    L = __fmaf_rn(cl[j], f, L);
+                    #pragma unroll
+                    for (int k = 0; k < kMergeDims; ++k) o[k] = __fmaf_rn(co[j][k], f, o[k]);
+                }
+                M = cmax;
+            }
+            #pragma unroll
+            for (int k = 0; k < kMergeDims; ++k) {
+                const int e = gt + k * kAttnGroupThreads;
+                if (e < hs) a.out[(size_t)(kvh * kv_mul + m) * hs + e] = __fdiv_rn(o[k], L);
             }
         }
         if (gt == 0) a.count[kvh] = 0u;
