@@ -223,7 +223,7 @@ struct StepArgs {
     const int *pos = nullptr;
     int seq_len = 0;
     int *err = nullptr;
-    unsigned long long *trace = nullptr;  // optional timeline [grid][nops][4] (globaltimer, ns)
+    unsigned long long *trace = nullptr;  // optional timeline [grid][nops][8] (globaltimer, ns)
 };
 size_t step_ctl_bytes();
 size_t step_attn_scratch_bytes(int n_heads, int n_kv_heads, int head_size);

@@ -679,7 +679,7 @@ static int build_step(dk_model *m) {
     sa.nops = m->n_ops;
     if (const char *e = getenv("DIOLKOS_STEP_TRACE"))
         if (atoi(e) > 0) {
-            const size_t tb = (size_t)m->num_sms * m->n_ops * 4 * 8;
+            const size_t tb = (size_t)m->num_sms * m->n_ops * 8 * 8;
             if (cudaMalloc(&m->d_trace, tb) != cudaSuccess || cudaMemset(m->d_trace, 0, tb) != cudaSuccess)
                 return set_error(DK_ERR_NOMEM, "persistent step: trace buffer");
             sa.trace = m->d_trace;
@@ -847,7 +847,7 @@ int dk_model_trace(dk_model *m, unsigned long long *out, size_t n, int *grid, in
     if (grid) *grid = m->num_sms;
     if (n_ops) *n_ops = m->n_ops;
     if (!m->d_trace) return set_error(DK_ERR_STATE, "dk_model_trace: tracing is off (DIOLKOS_STEP_TRACE=1 at creation)");
-    const size_t total = (size_t)m->num_sms * m->n_ops * 4;
+    const size_t total = (size_t)m->num_sms * m->n_ops * 8;
     if (!out || n < total) return set_error(DK_ERR_INVALID, "dk_model_trace: need %zu entries", total);
     return cuda_status(cudaMemcpy(out, m->d_trace, total * 8, cudaMemcpyDeviceToHost), "dk_model_trace");
 }

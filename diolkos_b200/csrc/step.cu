@@ -90,10 +90,12 @@ __device__ __forceinline__ unsigned long long globaltimer() {
     asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
     return t;
 }
-// Optional timeline (StepArgs::trace): per CTA and op, [0] input ready, [1] activation built,
-// [2] op finished on this CTA, [3] the producers' last stage of the op issued.
+// Optional timeline (StepArgs::trace): per CTA and op, [0] input ready (after the CTA barrier),
+// [1] activation built, [2] op finished on this CTA, [3] the producers' last stage of the op issued,
+// [4] the input counter seen by the polling thread.
+constexpr int kTraceSlots = 8;
 __device__ __forceinline__ void trace_mark(const StepArgs &sa, int op, int k) {
-    if (sa.trace) sa.trace[((size_t)blockIdx.x * sa.nops + op) * 4 + k] = globaltimer();
+    if (sa.trace) sa.trace[((size_t)blockIdx.x * sa.nops + op) * kTraceSlots + k] = globaltimer();
 }
 
 __device__ __forceinline__ void bar_compute() {
@@ -106,6 +108,11 @@ __device__ __forceinline__ unsigned long long ld_acquire_gpu(const unsigned long
     unsigned long long v;
     asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
+}
+// Add to a completion counter with release semantics: the calling thread's CTA barrier has ordered the
+// CTA's stores before it, and the release makes them visible to whoever acquires the new count.
+__device__ __forceinline__ void red_release_add(unsigned long long *p, unsigned long long v) {
+    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 // Bounded wait until a counter of this GPU reaches target.
 __device__ __forceinline__ bool wait_local(const unsigned long long *cnt, unsigned long long target, int *err) {
@@ -672,10 +679,9 @@ __device__ void attn_item(const AttnArgs &a, int pos, int kvh, int split, int ns
             }
         }
         if (gt == 0) a.count[kvh] = 0u;
-        __threadfence();
         bar_group(grp);
     }
-    if (gt == 0) atomicAdd(done_cnt, (unsigned long long)kv_mul * hs);
+    if (gt == 0) red_release_add(done_cnt, (unsigned long long)kv_mul * hs);
 }
 
 __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa) {
@@ -791,9 +797,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa
                                                            : make_float4(0, 0, 0, 0);
                 if (op.wait_cnt && tid == 0 && !wait_local(op.wait_cnt, (epoch + 1ull) * op.wait_units, sa.err))
                     ctl.abort = 1;
-                bar_compute();
+                if (tid == 0) trace_mark(sa, i, 4);
+                bar_compute();  // the polling thread's acquire, then this barrier, order every thread's reads
                 if (*reinterpret_cast<volatile int *>(&ctl.abort)) break;
-                __threadfence();
                 if (tid == 0) trace_mark(sa, i, 0);
                 int8_t *xq = reinterpret_cast<int8_t *>(act);
                 float *xs = reinterpret_cast<float *>(act + ((a.n + 15) & ~15));
@@ -824,8 +830,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa
                         __threadfence_system();
                         for (int r = 0; r < a.tp_world; ++r) atomicAdd_system(a.peer_cnt[r], rows);
                     } else if (op.done_cnt) {
-                        __threadfence();
-                        atomicAdd(op.done_cnt, a.epi == EPI_SWIGLU ? rows / 2 : rows);
+                        red_release_add(op.done_cnt, a.epi == EPI_SWIGLU ? rows / 2 : rows);
                     }
                 }
             }
@@ -873,9 +878,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa
         } else {  // OP_ATTN
             const AttnArgs &at = op.at;
             if (op.wait_cnt && tid == 0 && !wait_local(op.wait_cnt, (epoch + 1ull) * op.wait_units, sa.err)) ctl.abort = 1;
+            if (tid == 0) trace_mark(sa, i, 4);
             bar_compute();
             if (*reinterpret_cast<volatile int *>(&ctl.abort)) break;
-            __threadfence();
             if (tid == 0) trace_mark(sa, i, 0);
             const int T = pos + 1;
             const int nsplit = min(at.max_splits, (T + at.min_chunk - 1) / at.min_chunk);

@@ -208,9 +208,10 @@ int dk_model_device_error(dk_model *m);
 /* Number of kernels one decode step launches (for launch accounting). */
 int dk_model_kernels_per_step(dk_model *m);
 /* Diagnostics: the persistent step's timeline of the last decode step, when the model was created
- * with DIOLKOS_STEP_TRACE=1 in the environment: out[(cta * n_ops + op) * 4 + k] = GPU global timer (ns)
+ * with DIOLKOS_STEP_TRACE=1 in the environment: out[(cta * n_ops + op) * 8 + k] = GPU global timer (ns)
  * when, on that CTA, k = 0: the op's input was ready, 1: its activation was built, 2: it finished,
- * 3: the op's last weight stage was issued.  *grid and *n_ops give the dimensions. */
+ * 3: the op's last weight stage was issued, 4: the input counter was seen (0: not recorded).
+ * *grid and *n_ops give the dimensions. */
 int dk_model_trace(dk_model *m, unsigned long long *out, size_t n, int *grid, int *n_ops);
 /* Bytes of weights one decode step reads on this rank. */
 size_t dk_model_weight_bytes(dk_model *m);
