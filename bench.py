@@ -42,6 +42,9 @@ DECODE_GEMVS = [(12288, 4096, 32), (4096, 4096, 32), (22016, 4096, 32), (4096, 1
 # DRAM bytes / algorithmic bytes of one GEMV launch, from the ncu capture of every decode shape
 # summarised in profiles/gemv_q8_decode_shapes.txt (dram__bytes_read.sum + dram__bytes_write.sum).
 NCU_GEMV_TRAFFIC_RATIO = 1.003
+# DRAM bytes / algorithmic bytes of one persistent decode-step launch (step_kernel), from the ncu
+# capture summarised in profiles/step_kernel_7b.txt (full 7B shape, positions 40-43).
+NCU_STEP_TRAFFIC_RATIO = 1.001
 
 
 def parse():
@@ -53,6 +56,8 @@ def parse():
     ap.add_argument("--workload", choices=["decode", "gemv"], default="decode")
     ap.add_argument("--kv", choices=["f32", "bf16"], default="f32")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="truncate the 7B shape to this many layers (a small case of the same kernel, for profiling)")
     return ap.parse_args()
 
 
@@ -322,6 +327,8 @@ def run_decode(args):
     from diolkos_b200 import synth, tp
 
     cfg = synth.LLAMA7B
+    if args.layers > 0:
+        cfg = cfg.replace(n_layers=args.layers)
     kv_f32 = args.kv == "f32"
     world = args.gpus
     rank = int(os.environ.get("RANK", "0"))
@@ -398,6 +405,8 @@ def run_decode(args):
     bytes_tok = weight_bytes_per_token(cfg) + kv_bytes_read(cfg, P - 1, P - 1 + G, elem) / G
     hbm, peak_kind = peaks()
     achieved = bytes_tok / (ms_per_tok / 1e3) / 1e9
+    rank_bytes = bytes_tok / world  # every rank streams its shard of the weights and KV heads
+    step_gbps = rank_bytes / (ms_per_tok / 1e3) / 1e9
 
     # end to end through the public C-ABI generate entry point (host buffers)
     e2e_times = []
@@ -445,7 +454,8 @@ def run_decode(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(decode_ms / args.steps, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
         "data": "synthetic (seeded N(0,0.02) weights, seeded prompt)",
-        "config": {"workload": "llama2-7b-shape q8_0 decode: 32-token prompt, then 256 greedy tokens timed",
+        "config": {"workload": "llama2-7b-shape q8_0 decode: 32-token prompt, then 256 greedy tokens timed"
+                               + (f" ({cfg.n_layers} layers: profiling case)" if args.layers else ""),
                    "model": "llama2-7b-shape", "dim": cfg.dim, "hidden": cfg.hidden_dim, "layers": cfg.n_layers,
                    "heads": cfg.n_heads, "kv_heads": cfg.n_kv_heads, "vocab": cfg.vocab_size,
                    "seq_len": cfg.seq_len, "kv_cache": args.kv, "global_batch": 1,
@@ -455,7 +465,15 @@ def run_decode(args):
                    "l2": "weights (7.4 GB) exceed L2; every token streams them from HBM"},
         "ms_per_token": round(ms_per_tok, 4),
         "gpu_launches": kernels_per_step * G * args.steps,
-        "roofline": {"bound": "hbm", "achieved": round(gemv_gbps, 1), "peak": hbm, "unit": "GB/s",
+        "roofline": {"bound": "hbm", "achieved": round(step_gbps, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(step_gbps / hbm, 4),
+                     "traffic": (round(NCU_STEP_TRAFFIC_RATIO * rank_bytes) if NCU_STEP_TRAFFIC_RATIO else None),
+                     "kernel": "step_kernel",
+                     "what": f"the persistent decode step (one launch per token, {kernels_per_step} kernel per step): "
+                             f"this rank's weight + KV bytes per token ({rank_bytes / 1e9:.3f} GB) / time per token "
+                             f"(CUDA events around back-to-back steps); peak = {peak_kind} HBM copy bandwidth; "
+                             f"traffic = DRAM bytes per launch"},
+        "gemv_roofline": {"bound": "hbm", "achieved": round(gemv_gbps, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(gemv_gbps / hbm, 4),
                      "traffic": (round(NCU_GEMV_TRAFFIC_RATIO * mix_bytes / launches)
                                  if NCU_GEMV_TRAFFIC_RATIO else None),
