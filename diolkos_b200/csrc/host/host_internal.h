@@ -62,6 +62,7 @@ void utils_forget_tensor(const Tensor *t);
 struct Model;
 struct dk_model;
 struct dk_model **model_engine_slot(struct Model *m);
+int *model_tp_slot(struct Model *m);  /* {rank, world} of the engine */
 struct Model *model_ext_alloc(void);
 
 #endif

@@ -204,11 +204,14 @@ static int process_file(const char *model_name, const char *path, Model *st) {
 typedef struct {
     Model model;  /* first: a Model* to the block is a pointer to this member */
     struct dk_model *engine;
+    int tp[2];    /* tensor-parallel rank, world of the engine */
 } model_ext;
 
 Model *model_ext_alloc(void) { return &((model_ext *)host_calloc(1, sizeof(model_ext)))->model; }
 
 struct dk_model **model_engine_slot(Model *m) { return &((model_ext *)m)->engine; }
+
+int *model_tp_slot(Model *m) { return ((model_ext *)m)->tp; }
 
 static int cmp_names(const void *a, const void *b) { return strcmp(*(char *const *)a, *(char *const *)b); }
 

@@ -63,7 +63,20 @@ static void set_f32(dk_model *m, int which, int layer, Tensor *t) {
     host_check(dk_model_set_weight(m, which, layer, data_f32(t), NULL), "set weight");
 }
 
-void build_transformer_from_safetensors(Transformer *t, const char *model_path) {
+static void transformer_tp_shape(Transformer *t, int *rank, int *world) {
+    *rank = 0;
+    *world = 1;
+    if (t && t->safetensors) {
+        const int *tp = model_tp_slot(t->safetensors);
+        if (tp[1] > 0) {
+            *rank = tp[0];
+            *world = tp[1];
+        }
+    }
+}
+
+/* Load the model, size the state and create this rank's engine shard. */
+static dk_model *create_engine(Transformer *t, const char *model_path, int rank, int world, int device) {
     Model *st = load_safetensors(model_path);
     if (!st) {
         fprintf(stderr, "Failed to load safetensors model from %s\n", model_path);
@@ -72,14 +85,21 @@ void build_transformer_from_safetensors(Transformer *t, const char *model_path) 
     t->config = *st->config;
     t->safetensors = st;
     malloc_run_state(&t->state, &t->config);
-
     const Config *c = &t->config;
-    int device = 0;
-    host_check_cuda(cudaGetDevice(&device), "cudaGetDevice");
     const int cfg[7] = {c->dim, c->hidden_dim, c->n_layers, c->n_heads, c->n_kv_heads, c->vocab_size, c->seq_len};
-    dk_model *g = dk_model_create(cfg, DK_KV_BF16, device, 0, 1);
+    dk_model *g = dk_model_create(cfg, DK_KV_BF16, device, rank, world);
     if (!g) host_check(DK_ERR_INVALID, "create the model");
     *model_engine_slot(st) = g;
+    model_tp_slot(st)[0] = rank;
+    model_tp_slot(st)[1] = world;
+    return g;
+}
+
+/* Hand every weight to the engine (it keeps this rank's slices) and capture the step. */
+static void finish_engine(Transformer *t) {
+    Model *st = t->safetensors;
+    dk_model *g = *model_engine_slot(st);
+    const Config *c = &t->config;
     set_q8(g, DK_W_EMB, -1, st->token_embedding_table);
     set_f32(g, DK_W_RMS_FINAL, -1, st->rms_final_weight);
     set_q8(g, DK_W_WCLS, -1, st->wcls);
@@ -100,6 +120,41 @@ void build_transformer_from_safetensors(Transformer *t, const char *model_path) 
             "Transformer config from safetensors: dim=%d, hidden_dim=%d, n_layers=%d, n_heads=%d, n_kv_heads=%d, "
             "vocab_size=%d, seq_len=%d\n",
             c->dim, c->hidden_dim, c->n_layers, c->n_heads, c->n_kv_heads, c->vocab_size, c->seq_len);
+}
+
+void build_transformer_from_safetensors(Transformer *t, const char *model_path) {
+    int device = 0;
+    host_check_cuda(cudaGetDevice(&device), "cudaGetDevice");
+    create_engine(t, model_path, 0, 1, device);
+    finish_engine(t);
+}
+
+void build_transformer_tp(Transformer *t, const char *model_path, int rank, int world, int device, void *handle) {
+    if (world < 1 || rank < 0 || rank >= world) {
+        fprintf(stderr, "build_transformer_tp: rank %d of %d\n", rank, world);
+        exit(EXIT_FAILURE);
+    }
+    host_check_cuda(cudaSetDevice(device), "cudaSetDevice");
+    dk_model *g = create_engine(t, model_path, rank, world, device);
+    if (world > 1) host_check(dk_model_comm_handle(g, handle), "export the exchange area");
+}
+
+void build_transformer_tp_connect(Transformer *t, const void *handles) {
+    dk_model *g = transformer_engine(t);
+    if (!g) host_check(DK_ERR_STATE, "build_transformer_tp_connect: build_transformer_tp first");
+    int rank = 0, world = 1;
+    transformer_tp_shape(t, &rank, &world);
+    if (world > 1) host_check(dk_model_comm_connect(g, handles), "connect the ranks");
+    finish_engine(t);
+}
+
+void transformer_logit_rows(Transformer *t, int *begin, int *end) {
+    int rank = 0, world = 1;
+    transformer_tp_shape(t, &rank, &world);
+    const int V = t->config.vocab_size, per = (V + world - 1) / world;
+    const int b = rank * per, e = b + per < V ? b + per : V;
+    if (begin) *begin = b;
+    if (end) *end = e;
 }
 
 Tensor *forward(Transformer *transformer, int token, int pos) {

@@ -55,6 +55,18 @@ void malloc_run_state(RunState *s, Config *p);
 void build_transformer_from_safetensors(Transformer *t, const char *model_path);
 /* One decode step at `pos` with input `token`; returns the host logits (t->state.logits). */
 Tensor *forward(Transformer *transformer, int token, int pos);
+/* Tensor-parallel build: the reference's client/worker split (src/bin/client.c: heads and weight rows
+ * spread over workers), here over the GPUs of one box, one process per GPU.  Rank `rank` of `world`
+ * loads the model like build_transformer_from_safetensors and creates its shard on CUDA device
+ * `device`; `handle` receives DK_COMM_HANDLE_BYTES (diolkos.h) bytes to hand to every other rank (any
+ * transport).  build_transformer_tp_connect, given all ranks' handles in rank order, connects the
+ * ranks, uploads this rank's slices of the weights and captures the step.  Every rank must then run
+ * the same forward() calls in the same order; each fills only its own classifier rows of
+ * t->state.logits.  Exits with a message on failure. */
+void build_transformer_tp(Transformer *t, const char *model_path, int rank, int world, int device, void *handle);
+void build_transformer_tp_connect(Transformer *t, const void *handles);
+/* First and one-past-last vocabulary rows this rank's forward() writes ([0, vocab) with one rank). */
+void transformer_logit_rows(Transformer *t, int *begin, int *end);
 /* The GPU model behind a built transformer (diolkos.h: dk_model_*), for callers that want the
  * engine's own entry points (dk_model_generate, dk_model_weight_bytes, ...); NULL before
  * build_transformer_from_safetensors. */

@@ -270,3 +270,47 @@ def test_localinfer_greedy(tiny_dir, loaded, tiny_weights, tmp_path):
     assert r2.returncode == 0, r2.stderr.decode()
     assert r2.stdout.endswith(text + b"\n"), r2.stdout[-300:]
     assert b"achieved tok/s" in r2.stderr
+
+
+def _run_cli(exe, model_dir, tok_path, prompt, steps, cwd, extra=()):
+    r = subprocess.run([exe, model_dir, "-t", "0", "-n", str(steps), "-i", prompt, "-z", tok_path, *extra],
+                       capture_output=True, cwd=cwd, timeout=300)
+    assert r.returncode == 0, r.stderr.decode()[-2000:]
+    return r
+
+
+def test_client_cli_one_gpu(tiny_dir, loaded, tmp_path):
+    """bin/client (the reference client's flags, ranks = GPUs of this box) with one rank prints what
+    bin/localinfer prints."""
+    root, d = tiny_dir
+    tok_path = str(tmp_path / "tokenizer.bin")
+    synth.write_tokenizer(tok_path, synth.TINY.vocab_size)
+    bin_dir = os.path.join(ROOT, "diolkos_b200", "bin")
+    a = _run_cli(os.path.join(bin_dir, "localinfer"), d, tok_path, "abc de fgh", 40, root)
+    b = _run_cli(os.path.join(bin_dir, "client"), d, tok_path, "abc de fgh", 40, root, ("-g", "1"))
+    text = a.stdout.split(b"Loaded ")[1].split(b"\n", 1)[1]
+    assert b.stdout.endswith(text), (b.stdout[-200:], text[-200:])
+    assert b"achieved tok/s" in b.stderr
+
+
+def _gpus() -> int:
+    import torch
+
+    return torch.cuda.device_count()
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+def test_client_cli_two_gpus(tiny_dir, loaded, tmp_path):
+    """Two ranks (one process per GPU, the sums exchanged over NVLink) run the same generate loop; the
+    tensor-parallel sum order moves logits by ~1e-6 relative, so the greedy text agrees with one GPU's
+    except after a near-tie: the first pieces are compared."""
+    root, d = tiny_dir
+    tok_path = str(tmp_path / "tokenizer.bin")
+    synth.write_tokenizer(tok_path, synth.TINY.vocab_size)
+    exe = os.path.join(ROOT, "diolkos_b200", "bin", "client")
+    one = _run_cli(exe, d, tok_path, "abc de fgh", 24, root, ("-g", "1"))
+    two = _run_cli(exe, d, tok_path, "abc de fgh", 24, root, ("-g", "2"))
+    assert b"(2 GPUs)" in two.stderr
+    t1 = one.stdout.rstrip(b"\n").rsplit(b"Loaded", 1)[-1].split(b"\n", 1)[-1]
+    t2 = two.stdout.rstrip(b"\n").rsplit(b"Loaded", 1)[-1].split(b"\n", 1)[-1]
+    assert len(t2) > 0 and t1[:8] == t2[:8], (t1[:80], t2[:80])
