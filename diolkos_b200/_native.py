@@ -36,6 +36,7 @@ SIGNATURES = {
     "dk_matmul_q8_0": (_i, [_vp, _vp, _vp, _i, _i, _vp]),
     "dk_matmul_q8_0_q": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp]),
     "dk_matmul_q8_0_batch": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
+    "dk_matmul_q8_0_tokens": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "dk_sample": (_i, [_vp, _i, C.c_float, C.c_float, C.c_float, _vp, _vp, _vp]),
     "dk_softmax": (_i, [_vp, _i, _vp]),
     "dk_rmsnorm": (_i, [_vp, _vp, _vp, _i, _vp]),

@@ -178,6 +178,28 @@ int dk_attention_decode(float *out, const float *qkv, const float *rope, void *k
     return cuda_status(launch_attention(a, (cudaStream_t)stream, false), "dk_attention_decode");
 }
 
+int dk_matmul_q8_0_tokens(float *out, const int8_t *xq, const float *xs, const uint8_t *w_packed, int n, int d,
+                          int ntok, int accumulate, void *stream) {
+    if (!out || !xq || !xs || !w_packed) return set_error(DK_ERR_INVALID, "dk_matmul_q8_0_tokens: null pointer");
+    if (!gemm_supported(n, d, ntok, EPI_STORE))
+        return set_error(DK_ERR_INVALID, "dk_matmul_q8_0_tokens: unsupported shape n=%d d=%d tokens=%d", n, d, ntok);
+    if (int r = check_aligned(w_packed, 16, "w_packed")) return r;
+    if (int r = check_aligned(xq, 16, "xq")) return r;
+    GemmArgs g;
+    g.w = w_packed;
+    g.n = n;
+    g.d = d;
+    g.T = q8_tile_rows(d, current_num_sms(), 1);  // the tile height dk_q8_pack used
+    g.xq = xq;
+    g.xs = xs;
+    g.ntok = ntok;
+    g.epi = accumulate ? EPI_ADD : EPI_STORE;
+    g.out = out;
+    g.err = device_error_word();
+    if (!g.err) return set_error(DK_ERR_CUDA, "dk_matmul_q8_0_tokens: could not allocate the device error word");
+    return cuda_status(launch_gemm(g, (cudaStream_t)stream), "dk_matmul_q8_0_tokens");
+}
+
 int dk_matmul_q8_0_batch(float *out, const float *x, const uint8_t *const *w_packed, int count, int n, int d,
                          void *stream) {
     if (count < 0 || (count && !w_packed)) return set_error(DK_ERR_INVALID, "dk_matmul_q8_0_batch: bad count or list");

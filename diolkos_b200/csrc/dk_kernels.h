@@ -147,6 +147,20 @@ GemvPlan plan_gemv(int n, int d, int epi, int num_sms);
 bool gemv_supported(int n, int d, int epi);
 cudaError_t launch_gemv(const GemvArgs &a, const GemvPlan &p, cudaStream_t st, bool pdl);
 
+// ---------------- batched Q8_0 matmul on the tensor cores (prefill) --------------------------
+struct GemmArgs {
+    const uint8_t *w = nullptr;  // packed matrix (tile layout, tile height T)
+    int n = 0, d = 0, T = 32;
+    const int8_t *xq = nullptr;  // activations: int8 [ntok][n], fp32 scales [ntok][n/32]
+    const float *xs = nullptr;
+    int ntok = 0;
+    int epi = EPI_STORE;         // EPI_STORE: out[t][d]; EPI_ADD: out[t][d] +=; EPI_SWIGLU: out[t][d/2]
+    float *out = nullptr;
+    int *err = nullptr;
+};
+bool gemm_supported(int n, int d, int ntok, int epi);
+cudaError_t launch_gemm(const GemmArgs &g, cudaStream_t st);
+
 // ---------------- Q8_0 conversions ----------------------------------------------------------
 cudaError_t launch_quant_bf16(const uint16_t *x, size_t n, int8_t *q, float *s, cudaStream_t st);
 cudaError_t launch_quant_f16(const uint16_t *x, size_t n, int8_t *q, float *s, cudaStream_t st);
@@ -231,5 +245,15 @@ int step_attn_item_slots(int num_ctas);
 int step_threads();
 int step_max_ctas_per_sm(size_t smem);
 cudaError_t launch_step(const StepArgs &sa, int grid, cudaStream_t st);
+// Prompt prefill of positions pos0 .. pos0+ntok-1, with the decode step's own device code (step.cu):
+// the Q8_0 activation of every token (a.x: [ntok][n] rows; xq [ntok][n], xs [ntok][n/32] out), the
+// RoPE + KV-cache write of every position, and the attention of every position (qkv / out rows
+// `*_stride` floats apart; per-position split scratch work_stride floats and count_stride counters
+// apart).
+cudaError_t launch_prefill_act(const GemvArgs &a, int ntok, const int *tokens, int8_t *xq, float *xs, cudaStream_t st);
+cudaError_t launch_prefill_kv(const AttnArgs &a, int pos0, int ntok, size_t qkv_stride, cudaStream_t st);
+cudaError_t launch_prefill_attn(const AttnArgs &a, int pos0, int ntok, size_t qkv_stride, size_t out_stride,
+                                size_t work_stride, size_t count_stride, unsigned long long *sink, cudaStream_t st);
+long long prefill_attn_items(int pos0, int ntok, int n_kv_heads, int max_splits, int min_chunk);
 
 }  // namespace dk

@@ -140,6 +140,10 @@ __device__ __forceinline__ Sched op_sched(const StepOp &op) {
     return sc;
 }
 
+__device__ __forceinline__ size_t gemv_x_bytes_dev(int n) {
+    return (((size_t)n + 15) & ~(size_t)15) + (size_t)((n / 32 + 3) & ~3) * 4;
+}
+
 // ---- activation prologue (compute threads) ------------------------------------------------------
 // 16 consecutive values of the op's input, half-group hg (values 16hg .. 16hg+15).
 __device__ __forceinline__ void load16(const GemvArgs &a, int tok, int hg, float (&f)[16]) {
@@ -510,7 +514,8 @@ __device__ __forceinline__ void load_kv_batch(const AttnArgs &a, size_t head_bas
 // is complete when its last split has merged; that split counts them on done_cnt.
 template <bool F32>
 __device__ void attn_item(const AttnArgs &a, int pos, int kvh, int split, int nsplit, int chunk, int grp, int gt,
-                          float *sm, StepCtl &ctl, unsigned long long *done_cnt) {
+                          float *sm, StepCtl &ctl, unsigned long long *done_cnt, const StepArgs &sa, int opi) {
+    const bool mark = grp == 0 && gt == 0 && sa.trace;
     const int lane = gt & 31, warp = gt >> 5;
     const int hs = a.head_size, half = hs >> 1;
     const int kv_mul = a.n_heads / a.n_kv_heads;
@@ -551,6 +556,7 @@ __device__ void attn_item(const AttnArgs &a, int pos, int kvh, int split, int ns
             l[m] = 0.0f;
             acc[m] = make_float4(0, 0, 0, 0);
         }
+        if (mark && m0 == 0) trace_mark(sa, opi, 5);
         for (int tb = t0 + warp * kBatch; tb < t1; tb += kAttnGroupWarps * kBatch) {
             float4 kk[kBatch], vv[kBatch];
             load_kv_batch<F32>(a, head_base, hs, tb, t1, pos, act, kp, vp, kk, vv);
@@ -598,6 +604,7 @@ __device__ void attn_item(const AttnArgs &a, int pos, int kvh, int split, int ns
         }
     }
     const int W = hs + 2;
+    if (mark) trace_mark(sa, opi, 6);
     bar_group(grp);
     for (int m = 0; m < kv_mul; ++m) {
         float M = -INFINITY;
@@ -627,6 +634,7 @@ __device__ void attn_item(const AttnArgs &a, int pos, int kvh, int split, int ns
     }
     __threadfence();
     bar_group(grp);  // the scratch is reused by the next item; every store above is fenced
+    if (mark) trace_mark(sa, opi, 7);
     if (nsplit > 1) {
         if (gt == 0) {
             const unsigned ticket = atomicAdd(a.count + kvh, 1u);
@@ -893,8 +901,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa
             // head) spread over all SMs, so every SM's share of the KV cache is loaded at once
             for (int it = grp * (int)gridDim.x + (int)blockIdx.x; it < items; it += gridDim.x * kAttnGroups) {
                 const int kvh = it / nsplit, split = it % nsplit;
-                if (at.kv_f32) attn_item<true>(at, pos, kvh, split, nsplit, chunk, grp, gt, sm, ctl, op.done_cnt);
-                else attn_item<false>(at, pos, kvh, split, nsplit, chunk, grp, gt, sm, ctl, op.done_cnt);
+                if (at.kv_f32) attn_item<true>(at, pos, kvh, split, nsplit, chunk, grp, gt, sm, ctl, op.done_cnt, sa, i);
+                else attn_item<false>(at, pos, kvh, split, nsplit, chunk, grp, gt, sm, ctl, op.done_cnt, sa, i);
             }
             bar_compute();  // the scratch (the activation area) is free again
             if (tid == 0) trace_mark(sa, i, 2);
@@ -902,7 +910,135 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa
     }
 }
 
+// ---- prompt prefill: the step's own device code over a batch of prompt positions ----------------------
+// One CTA per token (the compute warps' layout: 320 threads): the token's Q8_0 activation exactly as the
+// decode step builds it (rmsnorm / embedding row / plain quantisation, same reduction order), written
+// to xq[t][n], xs[t][n/32] for the tensor-core matmul.  PRO_EMB_RMS also stores the embedding row as
+// the token's residual x[t].
+__global__ void __launch_bounds__(kComputeThreads) prefill_act_kernel(const GemvArgs a, int ntok, const int *tokens,
+                                                                      int8_t *xq_out, float *xs_out) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int t = blockIdx.x, tid = threadIdx.x;
+    if (t >= ntok) return;
+    const int n = a.n;
+    int8_t *xq = reinterpret_cast<int8_t *>(smem);
+    float *xs = reinterpret_cast<float *>(smem + ((n + 15) & ~15));
+    StepCtl &ctl = *reinterpret_cast<StepCtl *>(smem + gemv_x_bytes_dev(n));
+    if (tid == 0) ctl.abort = 0;
+    GemvArgs b = a;
+    b.x = a.x + (size_t)t * n;  // this token's input row (written back for PRO_EMB_RMS)
+    float4 nw[4];
+    #pragma unroll
+    for (int j = 0; j < 4; ++j)
+        nw[j] = (b.norm_w && tid < (n >> 4)) ? __ldg(reinterpret_cast<const float4 *>(b.norm_w + 16 * tid) + j)
+                                              : make_float4(0, 0, 0, 0);
+    bar_compute();
+    const int tok = a.pro == PRO_EMB_RMS ? __ldg(tokens + t) : 0;
+    step_activation(b, tok, xq, xs, ctl, tid, 0ull, true, nw);
+    bar_compute();
+    for (int i = tid; i < n / 16; i += kComputeThreads)
+        reinterpret_cast<uint4 *>(xq_out + (size_t)t * n)[i] = reinterpret_cast<const uint4 *>(xq)[i];
+    for (int g = tid; g < n / 32; g += kComputeThreads) xs_out[(size_t)t * (n / 32) + g] = xs[g];
+}
+
+// RoPE + KV-cache write of every prompt position (grid: tokens x KV heads, one warp): the rotated k and
+// the v of position t, rounded to the cache type, exactly as the decode step stores them.
+template <bool F32>
+__global__ void prefill_kv_kernel(const AttnArgs a, int pos0, int ntok, size_t qkv_stride) {
+    const int t = blockIdx.x, kvh = blockIdx.y, lane = threadIdx.x;
+    const int hs = a.head_size, half = hs >> 1, d0 = 4 * lane;
+    if (t >= ntok || kvh >= a.n_kv_heads || d0 >= hs || pos0 + t >= a.seq_len) return;
+    const int dim = a.n_heads * hs, kv_dim = a.n_kv_heads * hs;
+    const float *qkv = a.qkv + (size_t)t * qkv_stride;
+    const float *cs = a.rope + (size_t)(pos0 + t) * hs;
+    const float4 kr = rope4(qkv + dim + (size_t)kvh * hs, cs, d0, half);
+    const float4 vr = __ldcg(reinterpret_cast<const float4 *>(qkv + dim + kv_dim + (size_t)kvh * hs + d0));
+    const size_t at = (size_t)kvh * a.seq_len * hs + (size_t)(pos0 + t) * hs + d0;
+    store_kv4<F32>(a.k_cache, at, kr);
+    store_kv4<F32>(a.v_cache, at, vr);
+}
+
+// Attention of every prompt position at once: the decode step's (KV head, split) items of each query
+// position t, with t's own split count, partials and merge, so each output equals the decode step's
+// at position t.  Item i of the flattened list runs on attention group i % groups of CTA i / groups.
+// work / count hold per-position scratch (work_stride floats, count_stride counters per position).
+__global__ void __launch_bounds__(kComputeThreads, 1) prefill_attn_kernel(const AttnArgs a, int pos0, int ntok,
+                                                                          size_t qkv_stride,
+                                                                       size_t out_stride, size_t work_stride,
+                                                                       size_t count_stride,
+                                                                       unsigned long long *sink) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int grp = warp / kAttnGroupWarps, gt = tid - grp * kAttnGroupThreads;
+    const int kv_mul = a.n_heads / a.n_kv_heads;
+    StepCtl &ctl = *reinterpret_cast<StepCtl *>(smem);
+    float *sm = reinterpret_cast<float *>(smem + ((sizeof(StepCtl) + 127) & ~(size_t)127)) +
+                (size_t)grp * kAttnGroupWarps * kv_mul * (a.head_size + 4);
+    StepArgs none;  // no timeline
+    const long long item = (long long)blockIdx.x * kAttnGroups + grp;
+    // position t owns n_kv_heads * nsplit(t) items; walk to the position holding `item`
+    long long base = 0;
+    for (int t = 0; t < ntok; ++t) {
+        const int T = pos0 + t + 1;
+        const int nsplit = min(a.max_splits, (T + a.min_chunk - 1) / a.min_chunk);
+        const long long cnt = (long long)a.n_kv_heads * nsplit;
+        if (item < base + cnt) {
+            const int it = (int)(item - base), kvh = it / nsplit, split = it % nsplit;
+            const int chunk = (T + nsplit - 1) / nsplit;
+            AttnArgs b = a;
+            b.qkv = a.qkv + (size_t)t * qkv_stride;
+            b.out = a.out + (size_t)t * out_stride;
+            b.work = a.work + (size_t)t * work_stride;
+            b.count = a.count + (size_t)t * count_stride;
+            if (a.kv_f32) attn_item<true>(b, pos0 + t, kvh, split, nsplit, chunk, grp, gt, sm, ctl, sink, none, 0);
+            else attn_item<false>(b, pos0 + t, kvh, split, nsplit, chunk, grp, gt, sm, ctl, sink, none, 0);
+            return;
+        }
+        base += cnt;
+    }
+}
+
 }  // namespace
+
+long long prefill_attn_items(int pos0, int ntok, int n_kv_heads, int max_splits, int min_chunk) {
+    long long total = 0;
+    for (int t = 0; t < ntok; ++t)
+        total += (long long)n_kv_heads * std::min(max_splits, (pos0 + t + 1 + min_chunk - 1) / min_chunk);
+    return total;
+}
+
+cudaError_t launch_prefill_act(const GemvArgs &a, int ntok, const int *tokens, int8_t *xq, float *xs, cudaStream_t st) {
+    const size_t smem = gemv_x_bytes(a.n) + ((sizeof(StepCtl) + 127) & ~(size_t)127);
+    if (smem > 48 * 1024) {
+        const cudaError_t e = cudaFuncSetAttribute(prefill_act_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    prefill_act_kernel<<<ntok, kComputeThreads, smem, st>>>(a, ntok, tokens, xq, xs);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_prefill_kv(const AttnArgs &a, int pos0, int ntok, size_t qkv_stride, cudaStream_t st) {
+    dim3 grid(ntok, a.n_kv_heads);
+    if (a.kv_f32) prefill_kv_kernel<true><<<grid, 32, 0, st>>>(a, pos0, ntok, qkv_stride);
+    else prefill_kv_kernel<false><<<grid, 32, 0, st>>>(a, pos0, ntok, qkv_stride);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_prefill_attn(const AttnArgs &a, int pos0, int ntok, size_t qkv_stride, size_t out_stride,
+                                size_t work_stride, size_t count_stride, unsigned long long *sink, cudaStream_t st) {
+    if (pos0 < 0 || pos0 + ntok > a.seq_len) return cudaErrorInvalidValue;
+    const long long items = prefill_attn_items(pos0, ntok, a.n_kv_heads, a.max_splits, a.min_chunk);
+    const long long ctas = (items + kAttnGroups - 1) / kAttnGroups;
+    if (ctas < 1 || ctas > 0x7FFFFFFFLL) return cudaErrorInvalidValue;
+    const size_t smem = ((sizeof(StepCtl) + 127) & ~(size_t)127) + step_attn_scratch_bytes(a.n_heads, a.n_kv_heads, a.head_size);
+    if (smem > 48 * 1024) {
+        const cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    prefill_attn_kernel<<<(unsigned)ctas, kComputeThreads, smem, st>>>(a, pos0, ntok, qkv_stride, out_stride,
+                                                                        work_stride, count_stride, sink);
+    return cudaGetLastError();
+}
 
 size_t step_ctl_bytes() { return (sizeof(StepCtl) + 127) & ~(size_t)127; }
 size_t step_attn_scratch_bytes(int n_heads, int n_kv_heads, int head_size) {

@@ -84,6 +84,18 @@ def matmul_q(xq: torch.Tensor, xs: torch.Tensor, w_packed: torch.Tensor, n: int,
     return out
 
 
+def matmul_tokens(xq: torch.Tensor, xs: torch.Tensor, w_packed: torch.Tensor, n: int, d: int,
+                  out: torch.Tensor | None = None, accumulate: bool = False) -> torch.Tensor:
+    """dk_matmul_q8_0_tokens: the tensor-core matmul of ntok quantised activation rows (xq int8
+    [ntok, n], xs fp32 [ntok, n/32]) against a packed matrix; returns fp32 [ntok, d]."""
+    ntok = xq.shape[0]
+    if out is None:
+        out = torch.empty((ntok, d), dtype=torch.float32, device=xq.device)
+    check(lib().dk_matmul_q8_0_tokens(out.data_ptr(), xq.data_ptr(), xs.data_ptr(), w_packed.data_ptr(), n, d, ntok,
+                                      1 if accumulate else 0, stream_ptr()))
+    return out
+
+
 def matmul_batch(x: torch.Tensor, ws: list, n: int, d: int, out: torch.Tensor | None = None) -> torch.Tensor:
     """GEMVs of one activation against several packed matrices, back to back: out[i] = W_i * quant(x)."""
     import ctypes

@@ -83,6 +83,13 @@ int dk_matmul_q8_0_q(float *out, const int8_t *xq, const float *xs, const uint8_
  * weights while the previous one finishes, which is how the decode engine runs the kernel. */
 int dk_matmul_q8_0_batch(float *out, const float *x, const uint8_t *const *w_packed, int count, int n,
                          int d, void *stream);
+/* matmul_Q8_0 for a batch of `ntok` already-quantised activation vectors (prompt prefill; the
+ * reference calls matmul once per token): out[t*d + i] = W[i] . x_t (accumulate != 0: +=), from the
+ * same packed matrix as dk_matmul_q8_0.  xq int8[ntok][n] (16-byte aligned), xs fp32[ntok][n/32].
+ * The int32 group dots come from the tensor cores (tcgen05.mma kind::i8, one MMA per 32-value group);
+ * every output is bit-identical to dk_matmul_q8_0_q on that token. */
+int dk_matmul_q8_0_tokens(float *out, const int8_t *xq, const float *xs, const uint8_t *w_packed, int n, int d,
+                          int ntok, int accumulate, void *stream);
 /* Token sampling (reference sample(), src/sampler.c:108-131) on device logits[n]: temperature 0 is
  * argmax (first index wins ties); otherwise softmax(logits / temperature), then with `coin` in
  * [0, 1) multinomial sampling in index order (topp <= 0 or >= 1) or top-p sampling over the tokens

@@ -296,3 +296,36 @@ def test_gemv_batch_equals_single(torch_cuda):
     for i, w in enumerate(batch):
         one = ops.matmul(x, w, n, d).cpu().numpy()
         np.testing.assert_array_equal(got[i].view(np.uint32), one.view(np.uint32))
+
+
+@pytest.mark.parametrize("n,d,ntok", [(4096, 4096, 32), (4096, 4096, 5), (11008, 4096, 37), (288, 864, 70),
+                                      (4096, 300, 1), (8192, 1001, 33)])
+def test_tensor_core_matmul_tokens_bit_exact(torch_cuda, port, n, d, ntok):
+    """dk_matmul_q8_0_tokens (tcgen05 kind::i8, one MMA per 32-value group): every token's output row
+    equals the GEMV on that token bit for bit (and so the oracle's), for shapes that leave partial
+    M tiles, partial token tiles and a partial last 512-column block; and the accumulate form adds."""
+    from diolkos_b200 import ops
+
+    torch = torch_cuda
+    rng = np.random.default_rng(n + d + ntok)
+    wq = rng.integers(-127, 128, n * d, dtype=np.int8)
+    ws = (rng.random(n * d // 32, dtype=np.float32) * 0.001 + 1e-5).astype(np.float32)
+    w = ops.pack(_dev(torch, wq), _dev(torch, ws), n, d)
+    x = torch.from_numpy(rng.standard_normal((ntok, n)).astype(np.float32)).cuda()
+    xq = torch.empty((ntok, n), dtype=torch.int8, device="cuda")
+    xs = torch.empty((ntok, n // 32), dtype=torch.float32, device="cuda")
+    for t in range(ntok):
+        q, s = ops.quantize_f32(x[t].contiguous())
+        xq[t] = q
+        xs[t] = s
+    out = ops.matmul_tokens(xq, xs, w, n, d).cpu().numpy()
+    for t in range(ntok):
+        ref = ops.matmul_q(xq[t].contiguous(), xs[t].contiguous(), w, n, d).cpu().numpy()
+        np.testing.assert_array_equal(out[t].view(np.uint32), ref.view(np.uint32), err_msg=f"token {t}")
+    np.testing.assert_array_equal(
+        out[0].view(np.uint32),
+        port.matmul_q(xq[0].cpu().numpy(), xs[0].cpu().numpy(), wq, ws, n, d).view(np.uint32))
+    base = torch.from_numpy(rng.standard_normal((ntok, d)).astype(np.float32)).cuda()
+    acc = ops.matmul_tokens(xq, xs, w, n, d, out=base.clone(), accumulate=True).cpu().numpy()
+    want = (torch.from_numpy(out).cuda() + base).cpu().numpy()  # fp32 adds, round to nearest
+    np.testing.assert_array_equal(acc.view(np.uint32), want.view(np.uint32))
