@@ -54,6 +54,7 @@ SIGNATURES = {
     "dk_model_generate": (_i, [_vp, _vp, _i, _i, _vp, C.POINTER(C.c_int)]),
     "dk_model_set_tokens": (_i, [_vp, _vp, _i, _i]),
     "dk_model_enqueue_steps": (_i, [_vp, _i, _i]),
+    "dk_model_prefill": (_i, [_vp, _i, _i]),
     "dk_model_get_tokens": (_i, [_vp, _vp, _i]),
     "dk_model_sync": (_i, [_vp]),
     "dk_model_stream": (_vp, [_vp]),

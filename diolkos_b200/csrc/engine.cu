@@ -117,6 +117,14 @@ struct dk_model {
     int step_splits = 1;                  // attention splits per KV head in the persistent step
     StepArgs step;
     unsigned long long *d_trace = nullptr;  // DIOLKOS_STEP_TRACE=1: the persistent step's timeline
+    // prompt prefill (tensor-core matmuls over chunks of up to pchunk positions), allocated on first use
+    uint8_t *parena = nullptr;
+    int pchunk = 0;
+    float *px = nullptr, *pqkv = nullptr, *pxb = nullptr, *phb = nullptr, *pwork = nullptr, *pxs = nullptr;
+    int8_t *pxq = nullptr;
+    unsigned *pcount = nullptr;
+    unsigned long long *psink = nullptr;
+    size_t pwork_stride = 0, pcount_stride = 0;
 };
 
 static size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
@@ -324,6 +332,7 @@ void dk_model_destroy(dk_model *m) {
     cudaFree(m->d_ptrs);
     cudaFree(m->d_ops);
     cudaFree(m->d_trace);
+    cudaFree(m->parena);
     if (m->h_small) cudaFreeHost(m->h_small);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
@@ -889,6 +898,110 @@ int dk_model_forward(dk_model *m, int token, int pos, float *logits) {
     return DK_OK;
 }
 
+// Positions per prefill chunk: the tensor-core matmul's token tiles are 32 wide; 256 positions keep
+// the per-position attention scratch of a 7B-shape model near 100 MB.
+static constexpr int kPrefillChunk = 256;
+
+static bool prefill_available(const dk_model *m) { return m->world == 1 && m->use_step; }
+
+static int prefill_alloc(dk_model *m) {
+    if (m->parena) return DK_OK;
+    const int C = std::min(kPrefillChunk, m->seq_len);
+    const int qkv_rows = m->l_dim + 2 * m->l_kv_dim;
+    const int nmax = std::max(std::max(m->dim, m->l_dim), m->l_hidden);
+    m->pwork_stride = (size_t)m->l_heads * m->step_splits * (m->hs + 2);
+    m->pcount_stride = (size_t)m->l_kv_heads;
+    const size_t sz_x = align256((size_t)C * m->dim * 4), sz_qkv = align256((size_t)C * qkv_rows * 4);
+    const size_t sz_xb = align256((size_t)C * m->l_dim * 4), sz_hb = align256((size_t)C * m->l_hidden * 4);
+    const size_t sz_xq = align256((size_t)C * nmax), sz_xs = align256((size_t)C * (nmax / 32) * 4);
+    const size_t sz_work = align256((size_t)C * m->pwork_stride * 4), sz_cnt = align256((size_t)C * m->pcount_stride * 4);
+    const size_t total = sz_x + sz_qkv + sz_xb + sz_hb + sz_xq + sz_xs + sz_work + sz_cnt + 256;
+    if (cudaMalloc(&m->parena, total) != cudaSuccess) {
+        m->parena = nullptr;
+        return set_error(DK_ERR_NOMEM, "prefill: %zu bytes of scratch", total);
+    }
+    // the attention counters must start at zero (each position's merging split resets its own)
+    if (int r = cuda_status(cudaMemsetAsync(m->parena, 0, total, m->stream), "prefill scratch clear")) return r;
+    uint8_t *p = m->parena;
+    m->px = reinterpret_cast<float *>(p); p += sz_x;
+    m->pqkv = reinterpret_cast<float *>(p); p += sz_qkv;
+    m->pxb = reinterpret_cast<float *>(p); p += sz_xb;
+    m->phb = reinterpret_cast<float *>(p); p += sz_hb;
+    m->pxq = reinterpret_cast<int8_t *>(p); p += sz_xq;
+    m->pxs = reinterpret_cast<float *>(p); p += sz_xs;
+    m->pwork = reinterpret_cast<float *>(p); p += sz_work;
+    m->pcount = reinterpret_cast<unsigned *>(p); p += sz_cnt;
+    m->psink = reinterpret_cast<unsigned long long *>(p);
+    m->pchunk = C;
+    return DK_OK;
+}
+
+// One chunk of the prompt: positions pos0 .. pos0+n-1 through every layer.  The same arithmetic as the
+// decode step at each of those positions (the reference runs forward() once per prompt token,
+// src/transformer.c:61-232): Q8_0 activations from the step's own prologue code, the matmuls on the
+// tensor cores with the GEMV's summation order, RoPE / KV-cache writes and attention from the step's
+// attention items with the step's split plan -- so the cache entries are the decode step's, bit for
+// bit, and decoding continues from pos0+n as if every prompt token had been stepped.
+static int prefill_chunk(dk_model *m, int pos0, int n, cudaStream_t st) {
+    const int qkv_rows = m->l_dim + 2 * m->l_kv_dim;
+    const size_t esz = m->kv_type == DK_KV_F32 ? 4 : 2;
+    auto act = [&](int pro, const float *x, const float *norm, int cols) -> cudaError_t {
+        GemvArgs a;
+        a.n = cols; a.pro = pro; a.x = x; a.norm_w = norm; a.emb = m->emb; a.emb_T = m->emb_T;
+        a.vocab = m->vocab; a.err = m->err;
+        return launch_prefill_act(a, n, m->tokens + pos0, m->pxq, m->pxs, st);
+    };
+    auto mm = [&](const uint8_t *w, int cols, int rows, int T, int epi, float *out) -> cudaError_t {
+        GemmArgs g;
+        g.w = w; g.n = cols; g.d = rows; g.T = T; g.xq = m->pxq; g.xs = m->pxs; g.ntok = n; g.epi = epi;
+        g.out = out; g.err = m->err;
+        return launch_gemm(g, st);
+    };
+    for (int l = 0; l < m->n_layers; ++l) {
+        const dk_layer &ly = m->layers[l];
+        cudaError_t e = act(l == 0 ? PRO_EMB_RMS : PRO_RMS, m->px, ly.rms_att, m->dim);
+        if (!e) e = mm(ly.wqkv, m->dim, qkv_rows, m->p_qkv.T, EPI_STORE, m->pqkv);
+        AttnArgs t;
+        t.qkv = m->pqkv; t.rope = m->rope;
+        t.k_cache = static_cast<uint8_t *>(m->kcache) + (size_t)l * m->kv_layer_elems * esz;
+        t.v_cache = static_cast<uint8_t *>(m->vcache) + (size_t)l * m->kv_layer_elems * esz;
+        t.out = m->pxb; t.work = m->pwork; t.count = m->pcount; t.pos = m->pos;
+        t.n_heads = m->l_heads; t.n_kv_heads = m->l_kv_heads; t.head_size = m->hs; t.seq_len = m->seq_len;
+        t.kv_f32 = m->kv_type == DK_KV_F32; t.max_splits = m->step_splits; t.min_chunk = kStepMinChunk; t.err = m->err;
+        if (!e) e = launch_prefill_kv(t, pos0, n, (size_t)qkv_rows, st);
+        if (!e) e = launch_prefill_attn(t, pos0, n, (size_t)qkv_rows, (size_t)m->l_dim, m->pwork_stride, m->pcount_stride,
+                                        m->psink, st);
+        if (!e) e = act(PRO_F32, m->pxb, nullptr, m->l_dim);
+        if (!e) e = mm(ly.wo, m->l_dim, m->dim, m->p_wo.T, EPI_ADD, m->px);
+        if (!e) e = act(PRO_RMS, m->px, ly.rms_ffn, m->dim);
+        if (!e) e = mm(ly.w13, m->dim, 2 * m->l_hidden, m->p_w13.T, EPI_SWIGLU, m->phb);
+        if (!e) e = act(PRO_F32, m->phb, nullptr, m->l_hidden);
+        if (!e) e = mm(ly.w2, m->l_hidden, m->dim, m->p_w2.T, EPI_ADD, m->px);
+        if (e) return set_error(DK_ERR_CUDA, "prefill layer %d: %s", l, cudaGetErrorString(e));
+    }
+    return DK_OK;
+}
+
+// Enqueues the prefill of positions [pos0, pos0 + n) in chunks (no synchronisation).
+static int enqueue_prefill(dk_model *m, int pos0, int n) {
+    if (int r = prefill_alloc(m)) return r;
+    for (int c = 0; c < n; c += m->pchunk)
+        if (int r = prefill_chunk(m, pos0 + c, std::min(m->pchunk, n - c), m->stream)) return r;
+    return DK_OK;
+}
+
+int dk_model_prefill(dk_model *m, int pos0, int n_positions) {
+    if (int r = need(m)) return r;
+    if (!m->finalized) return set_error(DK_ERR_STATE, "dk_model_prefill: model not finalized");
+    if (!prefill_available(m))
+        return set_error(DK_ERR_STATE, "dk_model_prefill: needs a single-rank model on the persistent step");
+    if (pos0 < 0 || n_positions < 0 || pos0 + n_positions > m->seq_len)
+        return set_error(DK_ERR_INVALID, "dk_model_prefill: positions [%d, %d) exceed seq_len %d", pos0,
+                         pos0 + n_positions, m->seq_len);
+    if (n_positions == 0) return DK_OK;
+    return enqueue_prefill(m, pos0, n_positions);
+}
+
 int dk_model_generate(dk_model *m, const int *prompt, int n_prompt, int steps, int *out, int *n_out) {
     if (int r = need(m)) return r;
     if (!m->finalized) return set_error(DK_ERR_STATE, "dk_model_generate: model not finalized");
@@ -900,7 +1013,16 @@ int dk_model_generate(dk_model *m, const int *prompt, int n_prompt, int steps, i
             return set_error(DK_ERR_INVALID, "dk_model_generate: prompt token %d out of range", prompt[i]);
     const int nt = n_prompt < m->seq_len + 1 ? n_prompt : m->seq_len + 1;
     if (int r = dk_model_set_tokens(m, prompt, nt, n_prompt)) return r;
-    if (int r = dk_model_enqueue_steps(m, 0, steps)) return r;
+    // The prompt positions whose next token is forced (all but the last prompt token) go through the
+    // batched prefill; the decode steps continue from there.  DIOLKOS_PREFILL=0 steps them one by one.
+    int pre = 0;
+    if (prefill_available(m)) {
+        const char *e = getenv("DIOLKOS_PREFILL");
+        if (!(e && strcmp(e, "0") == 0)) pre = std::min(n_prompt - 1, steps);
+    }
+    if (pre > 0)
+        if (int r = enqueue_prefill(m, 0, pre)) return r;
+    if (int r = dk_model_enqueue_steps(m, pre, steps - pre)) return r;
     std::vector<int> toks((size_t)steps + 1);
     if (int r = dk_model_get_tokens(m, toks.data(), steps + 1)) return r;
     const int dev_err = dk_model_device_error(m);

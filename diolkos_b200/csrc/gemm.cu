@@ -98,7 +98,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q8_kernel(const GemmArgs
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5;
     const int n = g.n, d = g.d, T = g.T;
-    const int r0 = blockIdx.x * kGemmM, t0 = blockIdx.y * kGemmN;
+    const int t0 = blockIdx.x * kGemmN, r0 = blockIdx.y * kGemmM;
     const int row = r0 + tid;
     uint8_t *A = smem + kAOff, *B = smem + kBOff;
     float *ws_s = reinterpret_cast<float *>(smem + kWsOff), *xs_s = reinterpret_cast<float *>(smem + kXsOff);
@@ -224,7 +224,9 @@ cudaError_t launch_gemm(const GemmArgs &g, cudaStream_t st) {
         if (e != cudaSuccess) return e;
         attr_set[dev] = 1;
     }
-    dim3 grid((g.d + kGemmM - 1) / kGemmM, (g.ntok + kGemmN - 1) / kGemmN);
+    // token tiles along x: the CTAs of one row tile run side by side and share its weight reads in L2
+    dim3 grid((g.ntok + kGemmN - 1) / kGemmN, (g.d + kGemmM - 1) / kGemmM);
+    if (grid.y > 65535) return cudaErrorInvalidValue;
     gemm_q8_kernel<<<grid, kGemmThreads, kGemmSmemLaunch, st>>>(g);
     return cudaGetLastError();
 }

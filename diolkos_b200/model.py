@@ -102,6 +102,11 @@ class Model:
     def enqueue_steps(self, pos0: int, n_steps: int):
         N.check(N.lib().dk_model_enqueue_steps(self.h, pos0, n_steps))
 
+    def prefill(self, pos0: int, n_positions: int):
+        """Batched prefill of prompt positions [pos0, pos0 + n_positions) on the tensor cores (tokens
+        from set_tokens); fills their KV-cache entries, enqueued."""
+        N.check(N.lib().dk_model_prefill(self.h, pos0, n_positions))
+
     def get_tokens(self, n: int) -> np.ndarray:
         t = np.empty(n, np.int32)
         N.check(N.lib().dk_model_get_tokens(self.h, t.ctypes.data, n))

@@ -196,9 +196,12 @@ int dk_model_finalize(dk_model *m);
  * classifier rows (the slice of logits[vocab_size] it computes). */
 int dk_model_forward(dk_model *m, int token, int pos, float *logits);
 /* Greedy generation with the reference generate() rules (src/bin/localinfer.c:42-99): prompt
- * tokens are forced one position at a time, then argmax tokens (first index wins ties) are fed
- * back; stops after `steps` positions or when the sampled token is 1.  The whole loop runs on the
- * GPU; out receives the generated (non-forced) tokens, *n_out their count.  Host buffers. */
+ * tokens are forced, then argmax tokens (first index wins ties) are fed back; stops after `steps`
+ * positions or when the sampled token is 1.  The whole loop runs on the GPU: on a single-rank model
+ * the forced positions (all prompt tokens but the last) run as one batched prefill on the tensor
+ * cores, whose KV-cache entries equal the decode step's bit for bit; with tensor parallelism (or
+ * DIOLKOS_PREFILL=0) they are decode steps.  out receives the generated (non-forced) tokens, *n_out
+ * their count.  Host buffers. */
 int dk_model_generate(dk_model *m, const int *prompt, int n_prompt, int steps, int *out, int *n_out);
 
 /* Lower-level control used by benchmarks: enqueue decode steps for positions
@@ -206,6 +209,12 @@ int dk_model_generate(dk_model *m, const int *prompt, int n_prompt, int steps, i
  * and argmax results written back into it; nothing is synchronised. */
 int dk_model_set_tokens(dk_model *m, const int *tokens, int n_tokens, int n_forced);
 int dk_model_enqueue_steps(dk_model *m, int pos0, int n_steps);
+/* Prompt prefill: runs positions [pos0, pos0 + n_positions) through every layer at once for the
+ * tokens in the device token buffer, writing their KV-cache entries exactly as decode steps at those
+ * positions would (the reference forwards prompt tokens one by one, src/bin/localinfer.c:60-73);
+ * no logits.  Int8 tensor-core matmuls (tcgen05), chunks of up to 256 positions.  Single-rank models
+ * on the persistent decode step only (DK_ERR_STATE otherwise).  Enqueued, not synchronised. */
+int dk_model_prefill(dk_model *m, int pos0, int n_positions);
 int dk_model_get_tokens(dk_model *m, int *tokens, int n_tokens);
 int dk_model_sync(dk_model *m);
 /* The CUDA stream the engine launches on (cudaStream_t as void*). */

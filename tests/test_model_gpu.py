@@ -218,3 +218,57 @@ def test_dim4096_model_vs_oracle(port):
         top = np.sort(b)[-2:]
         if top[1] - top[0] > 0.03 * abs(top[1]):
             assert int(np.argmax(a)) == int(np.argmax(b)), pos
+
+
+def _logits_bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+@pytest.mark.parametrize(
+    "shape,kv_f32,P",
+    [
+        ("tiny", False, 8),
+        ("tiny", False, 200),
+        ("gqa", True, 300),   # two prefill chunks (256 + 43 positions), many attention splits
+        ("gqa", False, 300),
+        ("wide", True, 40),   # dim 4096: the one-round-trip rmsnorm prologue
+    ],
+)
+def test_prefill_equals_decode_steps(port, tiny_weights, shape, kv_f32, P):
+    """The batched prefill (tensor-core matmuls over the prompt positions) leaves the KV cache exactly
+    as decode steps at those positions do: the logits of the last prompt position, decoded after the
+    prefill, equal bit for bit those decoded after stepping every prompt position."""
+    from oracle import load_port_weights
+
+    if shape == "tiny":
+        cfg, by_name = synth.TINY, tiny_weights[1]
+    elif shape == "gqa":
+        cfg = synth.Config(dim=512, hidden_dim=1024, n_layers=2, n_heads=8, n_kv_heads=1, vocab_size=2048, seq_len=512)
+        by_name = load_port_weights(port, cfg, 77)[1]
+    else:
+        cfg = synth.Config(dim=4096, hidden_dim=1024, n_layers=1, n_heads=32, n_kv_heads=8, vocab_size=1000, seq_len=64)
+        by_name = load_port_weights(port, cfg, 91)[1]
+    m = _gpu_model(cfg, by_name, kv_f32=kv_f32)
+    prompt = np.random.default_rng(P).integers(3, cfg.vocab_size, P).astype(np.int32)
+    m.set_tokens(prompt, n_forced=P)
+    m.prefill(0, P - 1)
+    after_prefill = m.forward(int(prompt[P - 1]), P - 1)
+    for pos in range(P):  # the same positions as decode steps (they overwrite the cache entries)
+        stepped = m.forward(int(prompt[pos]), pos)
+    np.testing.assert_array_equal(_logits_bits(after_prefill), _logits_bits(stepped))
+
+
+def test_generate_with_prefill_equals_stepped_prompt(tiny_weights):
+    """dk_model_generate prefills the forced prompt positions; the generated tokens equal those of
+    the loop that steps every prompt position (DIOLKOS_PREFILL=0)."""
+    cfg, by_name = synth.TINY, tiny_weights[1]
+    m = _gpu_model(cfg, by_name)
+    prompt = synth.seeded_prompt(5, 40)
+    gen = m.generate(prompt, 120)
+    os.environ["DIOLKOS_PREFILL"] = "0"
+    try:
+        stepped = m.generate(prompt, 120)
+    finally:
+        del os.environ["DIOLKOS_PREFILL"]
+    assert len(gen) > 0
+    np.testing.assert_array_equal(gen, stepped)
