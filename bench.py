@@ -6,12 +6,14 @@
 Decode workload (N=1): LLaMA-2-7B shape (dim 4096, hidden 11008, 32 layers, 32 heads, 32 KV heads,
 vocab 32000, seq_len 4096), random-init weights N(0, 0.02) generated on the GPU from a seed, rounded
 to bf16 and quantised to Q8_0 by the library's load-time quantiser; fp32 KV cache.  One step = a
-seeded 32-token prompt forced position by position, then 256 greedy tokens (287 decode positions).
+seeded 32-token prompt whose 31 forced positions are prefilled in one batch on the tensor cores
+(dk_model_prefill; decode steps under tensor parallelism), then 256 greedy tokens.
 `value` = generated tokens per second of the 256-token decode phase, timed with CUDA events on the
 engine's stream, inputs resident in HBM; the weights (7.4 GB) are far larger than L2, so every token
 streams them from HBM.  `e2e` = the same tokens per second through the C-ABI generate entry point
-(dk_model_generate: host prompt in, host tokens out, copies included), wall clock, prompt positions
-included.
+(dk_model_generate: host prompt in, host tokens out, copies included), wall clock, prompt prefill
+included.  `prefill` = dk_model_prefill of a 2048-token prompt (positions/s, int8 TOPS of its
+matmuls); `prefill_gemm` = the tensor-core matmul alone on one layer's shapes at 256 positions.
 
 Reference arm (--impl reference): the reference's own CPU forward (its unmodified sources compiled
 with its own flags, oracle/_ref) on the host cores, on a bounded sample of the same workload: the
@@ -56,6 +58,7 @@ def parse():
     ap.add_argument("--workload", choices=["decode", "gemv"], default="decode")
     ap.add_argument("--kv", choices=["f32", "bf16"], default="f32")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the long-prompt prefill and GEMM measurements")
     ap.add_argument("--layers", type=int, default=0,
                     help="truncate the 7B shape to this many layers (a small case of the same kernel, for profiling)")
     return ap.parse_args()
@@ -293,6 +296,103 @@ def gemv_bench(reps: int = 64, shapes=None):
     return out
 
 
+PREFILL_LEN = 2048  # the long prompt of the tensor-parallel workload, prefilled on one GPU here
+GEMM_TOKENS = 256   # positions per prefill chunk (the engine's chunk)
+
+
+def gemm_ops(cfg, ntok: int) -> float:
+    """Int8 multiply-adds (x2) of the prefill matmuls over ntok positions: q|k|v, wo, w1|w3, w2."""
+    per_layer = cfg.dim * (cfg.dim + 2 * cfg.kv_dim) + cfg.dim * cfg.dim + 2 * cfg.hidden_dim * cfg.dim + cfg.dim * cfg.hidden_dim
+    return 2.0 * per_layer * cfg.n_layers * ntok
+
+
+def int8_peak():
+    """Dense int8 tensor peak: twice the measured bf16 cuBLAS burst (B200's int8 rate is 2x bf16)."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return 2.0 * float(json.load(f)["bf16_tflops"]), "2 x measured bf16 burst"
+    except Exception:
+        return 2.0 * 1590.0, "2 x fallback bf16"
+
+
+def prefill_bench(m, cfg, reps: int = 3):
+    """The batched prefill of a PREFILL_LEN-token seeded prompt (dk_model_prefill, positions
+    0..PREFILL_LEN-1, chunks of 256), CUDA events on the engine's stream, best of `reps`."""
+    import torch
+
+    from diolkos_b200 import synth
+
+    L = min(PREFILL_LEN, cfg.seq_len)
+    prompt = synth.seeded_prompt(SEED + 1, L, cfg.vocab_size)
+    stream = torch.cuda.ExternalStream(m.stream)
+    m.set_tokens(prompt, n_forced=L)
+    m.prefill(0, L)  # warm-up (allocates the chunk scratch)
+    m.sync()
+    best = float("inf")
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        m.prefill(0, L)
+        e1.record(stream)
+        m.sync()
+        best = min(best, e0.elapsed_time(e1))
+    if m.device_error():
+        raise RuntimeError("device error word after the prefill")
+    ops = gemm_ops(cfg, L)
+    return {"positions": L, "ms": round(best, 3), "tok_per_s": round(L / (best / 1e3), 1),
+            "int8_tops": round(ops / (best / 1e3) / 1e12, 1),
+            "what": "dk_model_prefill of a seeded prompt, all layers (matmuls, attention over the growing "
+                    "KV cache, activations), CUDA events; int8_tops = matmul multiply-adds x2 / time"}
+
+
+def gemm_bench(cfg, ntok: int = GEMM_TOKENS, reps: int = 8):
+    """The prefill matmul (dk_matmul_q8_0_tokens) on one layer's shapes at ntok positions: reps
+    launches back to back rotating over packed copies (working set > 3x L2), CUDA events, best of 3."""
+    import torch
+
+    from diolkos_b200 import ops
+
+    shapes = [(cfg.dim + 2 * cfg.kv_dim, cfg.dim), (cfg.dim, cfg.dim), (2 * cfg.hidden_dim, cfg.dim),
+              (cfg.dim, cfg.hidden_dim)]
+    out, tot_ops, tot_us = {}, 0.0, 0.0
+    for d, n in shapes:
+        copies = max(2, int(3 * 126e6 // ops.packed_bytes(n, d)) + 1)
+        g = torch.Generator(device="cuda").manual_seed(d * 17 + n)
+        ws = []
+        for _ in range(copies):
+            wf = (torch.randn(d * n, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+            q, s = ops.quantize_bf16(wf.view(torch.int16))
+            ws.append(ops.pack(q, s, n, d))
+            del wf, q, s
+        xf = torch.randn(ntok * n, generator=g, device="cuda").to(torch.bfloat16)
+        xq, xs = ops.quantize_bf16(xf.view(torch.int16))
+        xq, xs = xq.view(ntok, n), xs.view(ntok, n // 32)
+        y = torch.empty((ntok, d), device="cuda")
+        ops.matmul_tokens(xq, xs, ws[0], n, d, out=y)
+        torch.cuda.synchronize()
+        best = float("inf")
+        for _ in range(3):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(reps):
+                ops.matmul_tokens(xq, xs, ws[i % copies], n, d, out=y)
+            e1.record()
+            torch.cuda.synchronize()
+            best = min(best, e0.elapsed_time(e1) * 1e3 / reps)
+        o = 2.0 * d * n * ntok
+        tot_ops += o
+        tot_us += best
+        out[f"{d}x{n}"] = {"us": round(best, 2), "int8_tops": round(o / best / 1e6, 1)}
+        del ws, y, xq, xs
+        torch.cuda.empty_cache()
+    peak, kind = int8_peak()
+    ach = tot_ops / tot_us / 1e6
+    return {"tokens": ntok, "shapes": out, "achieved_tops": round(ach, 1), "peak_tops": round(peak, 1),
+            "frac": round(ach / peak, 4), "peak_kind": kind, "kernel": "gemm_q8_kernel",
+            "what": "one layer's four prefill matmuls at 256 positions (the engine's chunk), int8 multiply-adds x2 "
+                    "/ CUDA-event time per launch"}
+
+
 # ------------------------------------------------------------------ main arms
 def run_reference(args):
     from diolkos_b200 import synth
@@ -362,7 +462,12 @@ def run_decode(args):
 
     def one_step(record=None):
         m.set_tokens(prompt, n_forced=P)
-        m.enqueue_steps(0, P - 1)
+        if record:
+            record[2].record(stream)
+        if world == 1:
+            m.prefill(0, P - 1)  # the forced prompt positions on the tensor cores
+        else:
+            m.enqueue_steps(0, P - 1)
         if record:
             record[0].record(stream)
         m.enqueue_steps(P - 1, G)
@@ -385,7 +490,7 @@ def run_decode(args):
     t_all0 = time.perf_counter()
     evs = []
     for _ in range(args.steps):
-        e = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        e = tuple(torch.cuda.Event(enable_timing=True) for _ in range(3))
         one_step(e)
         evs.append(e)
     m.sync()
@@ -393,7 +498,8 @@ def run_decode(args):
     barrier()
     wall = time.perf_counter() - t_all0
     clocks = sampler.stop() if rank == 0 else None
-    decode_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in evs))
+    decode_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b, _ in evs))
+    prompt_ms = max_over_ranks(sum(c.elapsed_time(a) for a, _, c in evs)) / args.steps
     err = int(max_over_ranks(float(m.device_error())))
     if err:
         raise RuntimeError(f"device error word 0x{err:x}")
@@ -419,6 +525,7 @@ def run_decode(args):
         n_gen = len(gen)
     e2e = n_gen * len(e2e_times) / sum(e2e_times)
     kernels_per_step = m.kernels_per_step
+    long_prefill = prefill_bench(m, cfg) if world == 1 and not args.no_prefill else None
     m.close()  # every rank leaves the exchange at the same point
     barrier()
     if dist is not None:
@@ -433,6 +540,7 @@ def run_decode(args):
     decode_gemvs = [(ld + 2 * lkv, cfg.dim, cfg.n_layers), (cfg.dim, ld, cfg.n_layers),
                     (2 * lh, cfg.dim, cfg.n_layers), (cfg.dim, lh, cfg.n_layers), (lv, cfg.dim, 1)]
     gemv = gemv_bench() if world == 1 else None
+    gemm = gemm_bench(cfg) if world == 1 and not args.no_prefill else None
     mix = gemv_bench(shapes=[(d, n) for d, n, _ in decode_gemvs])
     mix_bytes = sum(c * gemv_alg_bytes(d, n) for d, n, c in decode_gemvs)
     mix_us = sum(c * mix[f"{d}x{n}"]["us"] for d, n, c in decode_gemvs)
@@ -464,7 +572,10 @@ def run_decode(args):
                    f"exchanged inside the GEMVs over NVLink peer memory",
                    "l2": "weights (7.4 GB) exceed L2; every token streams them from HBM"},
         "ms_per_token": round(ms_per_tok, 4),
-        "gpu_launches": kernels_per_step * G * args.steps,
+        # the prefill launches 10 kernels per layer and chunk (activation, matmul, KV write, attention,
+        # then activation + matmul for wo, w1|w3, w2), then one persistent step per token
+        "gpu_launches": (kernels_per_step * G + (10 * cfg.n_layers * (-(-(P - 1) // GEMM_TOKENS)) if world == 1 else
+                                                 kernels_per_step * (P - 1))) * args.steps,
         "roofline": {"bound": "hbm", "achieved": round(step_gbps, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(step_gbps / hbm, 4),
                      "traffic": (round(NCU_STEP_TRAFFIC_RATIO * rank_bytes) if NCU_STEP_TRAFFIC_RATIO else None),
@@ -489,9 +600,12 @@ def run_decode(args):
                                   f"time per token, against {world} x the HBM peak"},
         "gemv": gemv,
         "gemv_decode_shapes": mix,
+        "prompt_prefill_ms": round(prompt_ms, 3),
+        "prefill": long_prefill,
+        "prefill_gemm": gemm,
         "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * P + 12,
                 "d2h_bytes_per_step": 4 * (P + G) + 4,
-                "how": "dk_model_generate (C ABI): host prompt -> host tokens, wall clock, prompt positions included"},
+                "how": "dk_model_generate (C ABI): host prompt -> host tokens, wall clock, prompt prefill included"},
         "cpu_baseline": cpu,
         "clocks": clocks,
         "wall_s_timed_region": round(wall, 3),

@@ -63,8 +63,7 @@ struct AttnGeom {
 
 __device__ __forceinline__ AttnGeom attn_geom(int T, int split, int max_splits, int min_chunk) {
     AttnGeom g;
-    g.nsplit = min(max_splits, (T + min_chunk - 1) / min_chunk);
-    g.chunk = (T + g.nsplit - 1) / g.nsplit;
+    attn_split_plan(T, max_splits, min_chunk, g.nsplit, g.chunk);
     g.t0 = split * g.chunk;
     g.t1 = min(T, g.t0 + g.chunk);
     return g;

@@ -180,6 +180,16 @@ cudaError_t launch_embed(const uint8_t *emb_packed, int dim, int T, const int *t
 // ---------------- attention ------------------------------------------------------------------
 // Smallest run of positions one attention CTA takes (splits are never shorter).
 constexpr int kAttnMinChunk = 32;
+// Split plan of the attention over T positions (0 .. T-1): nsplit runs of `chunk` positions, the last one
+// shorter.  nsplit = min(max_splits, ceil(T / min_chunk)) rounds the chunk up; the split count then
+// follows from the chunk, so that no split is empty (T = 385 over at most 24 splits: chunk 17, 23 splits).
+__host__ __device__ inline void attn_split_plan(int T, int max_splits, int min_chunk, int &nsplit, int &chunk) {
+    int n = (T + min_chunk - 1) / min_chunk;
+    n = n < max_splits ? n : max_splits;
+    n = n < 1 ? 1 : n;
+    chunk = (T + n - 1) / n;
+    nsplit = (T + chunk - 1) / chunk;
+}
 struct AttnArgs {
     const float *qkv = nullptr;  // [dim + 2*kv_dim]: q | k | v before RoPE
     const float *rope = nullptr; // [seq_len][head_size/2][2] (cos, sin)
@@ -245,15 +255,26 @@ int step_attn_item_slots(int num_ctas);
 int step_threads();
 int step_max_ctas_per_sm(size_t smem);
 cudaError_t launch_step(const StepArgs &sa, int grid, cudaStream_t st);
-// Prompt prefill of positions pos0 .. pos0+ntok-1, with the decode step's own device code (step.cu):
-// the Q8_0 activation of every token (a.x: [ntok][n] rows; xq [ntok][n], xs [ntok][n/32] out), the
-// RoPE + KV-cache write of every position, and the attention of every position (qkv / out rows
-// `*_stride` floats apart; per-position split scratch work_stride floats and count_stride counters
-// apart).
+// Prompt prefill of positions pos0 .. pos0+ntok-1 with the decode step's arithmetic (step.cu): the
+// Q8_0 activation of every token (a.x: [ntok][n] rows; xq [ntok][n], xs [ntok][n/32] out), the RoPE +
+// KV-cache write of every position, and the attention of every position (qkv / out rows `*_stride`
+// floats apart; per-position split scratch work_stride floats and count_stride counters apart) with
+// the decode step's split plan, batch order and merges, K/V rows loaded once for a group of positions.
 cudaError_t launch_prefill_act(const GemvArgs &a, int ntok, const int *tokens, int8_t *xq, float *xs, cudaStream_t st);
 cudaError_t launch_prefill_kv(const AttnArgs &a, int pos0, int ntok, size_t qkv_stride, cudaStream_t st);
-cudaError_t launch_prefill_attn(const AttnArgs &a, int pos0, int ntok, size_t qkv_stride, size_t out_stride,
-                                size_t work_stride, size_t count_stride, unsigned long long *sink, cudaStream_t st);
-long long prefill_attn_items(int pos0, int ntok, int n_kv_heads, int max_splits, int min_chunk);
+// Prefill attention items: the prompt positions that share the decode step's split plan (split count and
+// chunk; any chunk when there is one split) go together, at most kPrefillRows (query, head) rows, and
+// one item = (group, KV head, split).
+constexpr int kPrefillRows = 16;
+struct PrefillGroup {
+    int first, count;   // positions first .. first+count-1
+    int nsplit, chunk;  // their split plan (one split: chunk = the last position + 1)
+    int item0;          // index of the group's first item
+};
+// Fills groups[0 .. n) (capacity ntok) for positions pos0 .. pos0+ntok-1; returns n, *items = total items.
+int prefill_attn_plan(const AttnArgs &a, int pos0, int ntok, PrefillGroup *groups, long long *items);
+cudaError_t launch_prefill_attn(const AttnArgs &a, int pos0, const PrefillGroup *d_groups, int ngroups,
+                                long long items, size_t qkv_stride, size_t out_stride, size_t work_stride,
+                                size_t count_stride, cudaStream_t st);
 
 }  // namespace dk

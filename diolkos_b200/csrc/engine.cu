@@ -123,7 +123,8 @@ struct dk_model {
     float *px = nullptr, *pqkv = nullptr, *pxb = nullptr, *phb = nullptr, *pwork = nullptr, *pxs = nullptr;
     int8_t *pxq = nullptr;
     unsigned *pcount = nullptr;
-    unsigned long long *psink = nullptr;
+    PrefillGroup *pgroups = nullptr;      // the attention's position groups of the current chunk
+    std::vector<PrefillGroup> h_groups;
     size_t pwork_stride = 0, pcount_stride = 0;
 };
 
@@ -915,7 +916,8 @@ static int prefill_alloc(dk_model *m) {
     const size_t sz_xb = align256((size_t)C * m->l_dim * 4), sz_hb = align256((size_t)C * m->l_hidden * 4);
     const size_t sz_xq = align256((size_t)C * nmax), sz_xs = align256((size_t)C * (nmax / 32) * 4);
     const size_t sz_work = align256((size_t)C * m->pwork_stride * 4), sz_cnt = align256((size_t)C * m->pcount_stride * 4);
-    const size_t total = sz_x + sz_qkv + sz_xb + sz_hb + sz_xq + sz_xs + sz_work + sz_cnt + 256;
+    const size_t sz_groups = align256((size_t)C * sizeof(PrefillGroup));
+    const size_t total = sz_x + sz_qkv + sz_xb + sz_hb + sz_xq + sz_xs + sz_work + sz_cnt + sz_groups;
     if (cudaMalloc(&m->parena, total) != cudaSuccess) {
         m->parena = nullptr;
         return set_error(DK_ERR_NOMEM, "prefill: %zu bytes of scratch", total);
@@ -931,7 +933,8 @@ static int prefill_alloc(dk_model *m) {
     m->pxs = reinterpret_cast<float *>(p); p += sz_xs;
     m->pwork = reinterpret_cast<float *>(p); p += sz_work;
     m->pcount = reinterpret_cast<unsigned *>(p); p += sz_cnt;
-    m->psink = reinterpret_cast<unsigned long long *>(p);
+    m->pgroups = reinterpret_cast<PrefillGroup *>(p);
+    m->h_groups.resize(C);
     m->pchunk = C;
     return DK_OK;
 }
@@ -957,20 +960,28 @@ static int prefill_chunk(dk_model *m, int pos0, int n, cudaStream_t st) {
         g.out = out; g.err = m->err;
         return launch_gemm(g, st);
     };
+    AttnArgs t;
+    t.qkv = m->pqkv; t.rope = m->rope;
+    t.out = m->pxb; t.work = m->pwork; t.count = m->pcount; t.pos = m->pos;
+    t.n_heads = m->l_heads; t.n_kv_heads = m->l_kv_heads; t.head_size = m->hs; t.seq_len = m->seq_len;
+    t.kv_f32 = m->kv_type == DK_KV_F32; t.max_splits = m->step_splits; t.min_chunk = kStepMinChunk; t.err = m->err;
+    // the attention's position groups (the same for every layer); pageable source: the copy is staged
+    // before the call returns, and stream order keeps it behind the previous chunk's kernels
+    long long items = 0;
+    const int ngroups = prefill_attn_plan(t, pos0, n, m->h_groups.data(), &items);
+    if (int r = cuda_status(cudaMemcpyAsync(m->pgroups, m->h_groups.data(), (size_t)ngroups * sizeof(PrefillGroup),
+                                            cudaMemcpyHostToDevice, st),
+                            "prefill: group table"))
+        return r;
     for (int l = 0; l < m->n_layers; ++l) {
         const dk_layer &ly = m->layers[l];
         cudaError_t e = act(l == 0 ? PRO_EMB_RMS : PRO_RMS, m->px, ly.rms_att, m->dim);
         if (!e) e = mm(ly.wqkv, m->dim, qkv_rows, m->p_qkv.T, EPI_STORE, m->pqkv);
-        AttnArgs t;
-        t.qkv = m->pqkv; t.rope = m->rope;
         t.k_cache = static_cast<uint8_t *>(m->kcache) + (size_t)l * m->kv_layer_elems * esz;
         t.v_cache = static_cast<uint8_t *>(m->vcache) + (size_t)l * m->kv_layer_elems * esz;
-        t.out = m->pxb; t.work = m->pwork; t.count = m->pcount; t.pos = m->pos;
-        t.n_heads = m->l_heads; t.n_kv_heads = m->l_kv_heads; t.head_size = m->hs; t.seq_len = m->seq_len;
-        t.kv_f32 = m->kv_type == DK_KV_F32; t.max_splits = m->step_splits; t.min_chunk = kStepMinChunk; t.err = m->err;
         if (!e) e = launch_prefill_kv(t, pos0, n, (size_t)qkv_rows, st);
-        if (!e) e = launch_prefill_attn(t, pos0, n, (size_t)qkv_rows, (size_t)m->l_dim, m->pwork_stride, m->pcount_stride,
-                                        m->psink, st);
+        if (!e) e = launch_prefill_attn(t, pos0, m->pgroups, ngroups, items, (size_t)qkv_rows, (size_t)m->l_dim,
+                                        m->pwork_stride, m->pcount_stride, st);
         if (!e) e = act(PRO_F32, m->pxb, nullptr, m->l_dim);
         if (!e) e = mm(ly.wo, m->l_dim, m->dim, m->p_wo.T, EPI_ADD, m->px);
         if (!e) e = act(PRO_RMS, m->px, ly.rms_ffn, m->dim);

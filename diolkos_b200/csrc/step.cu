@@ -732,8 +732,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa
                 if (q == 0) {
                     const AttnArgs &at = op.at;
                     const int T = pos + 1;
-                    const int nsplit = min(at.max_splits, (T + at.min_chunk - 1) / at.min_chunk);
-                    const int chunk = (T + nsplit - 1) / nsplit;
+                    int nsplit, chunk;
+                    attn_split_plan(T, at.max_splits, at.min_chunk, nsplit, chunk);
                     const size_t row = (size_t)at.head_size * (at.kv_f32 ? 4 : 2);
                     for (int g = 0; g < kAttnGroups; ++g) {
                         const int it = g * (int)gridDim.x + (int)blockIdx.x;
@@ -891,8 +891,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa
             if (*reinterpret_cast<volatile int *>(&ctl.abort)) break;
             if (tid == 0) trace_mark(sa, i, 0);
             const int T = pos + 1;
-            const int nsplit = min(at.max_splits, (T + at.min_chunk - 1) / at.min_chunk);
-            const int chunk = (T + nsplit - 1) / nsplit;
+            int nsplit, chunk;
+            attn_split_plan(T, at.max_splits, at.min_chunk, nsplit, chunk);
             const int items = at.n_kv_heads * nsplit;
             const int grp = warp / kAttnGroupWarps, gt = tid - grp * kAttnGroupThreads;
             const int kv_mul = at.n_heads / at.n_kv_heads;
@@ -958,53 +958,224 @@ __global__ void prefill_kv_kernel(const AttnArgs a, int pos0, int ntok, size_t q
     store_kv4<F32>(a.v_cache, at, vr);
 }
 
-// Attention of every prompt position at once: the decode step's (KV head, split) items of each query
-// position t, with t's own split count, partials and merge, so each output equals the decode step's
-// at position t.  Item i of the flattened list runs on attention group i % groups of CTA i / groups.
-// work / count hold per-position scratch (work_stride floats, count_stride counters per position).
-__global__ void __launch_bounds__(kComputeThreads, 1) prefill_attn_kernel(const AttnArgs a, int pos0, int ntok,
-                                                                          size_t qkv_stride,
-                                                                       size_t out_stride, size_t work_stride,
-                                                                       size_t count_stride,
-                                                                       unsigned long long *sink) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    const int tid = threadIdx.x, warp = tid >> 5;
-    const int grp = warp / kAttnGroupWarps, gt = tid - grp * kAttnGroupThreads;
+// Attention of the prompt positions of one group (positions that share the decode step's split plan)
+// for one (KV head, split): item = blockIdx.x, one attention group of kAttnGroupWarps warps.  Each K/V
+// batch is loaded once and used for every (position, query head) row of the group; each row keeps the
+// decode step's own arithmetic (attn_item): the same batches in the same order per warp, the same
+// masked tail, the warp merge, the split partials and the last split's merge -- so every output equals
+// the decode step's at that position, bit for bit.  The K/V rows of every position up to the group's
+// last are in the cache already (prefill_kv_kernel).  State per (warp, row) lives in shared memory:
+// [max, sum, -, -, acc[hs]].
+template <bool F32>
+__global__ void __launch_bounds__(kAttnGroupThreads) prefill_attn_kernel(const AttnArgs a, int pos0,
+                                                                         const PrefillGroup *groups, int ngroups,
+                                                                         size_t qkv_stride, size_t out_stride,
+                                                                         size_t work_stride, size_t count_stride) {
+    extern __shared__ __align__(16) float psm[];
+    __shared__ int last_split[kPrefillRows];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int hs = a.head_size, half = hs >> 1, d0 = 4 * lane;
+    const bool act = d0 < hs;
     const int kv_mul = a.n_heads / a.n_kv_heads;
-    StepCtl &ctl = *reinterpret_cast<StepCtl *>(smem);
-    float *sm = reinterpret_cast<float *>(smem + ((sizeof(StepCtl) + 127) & ~(size_t)127)) +
-                (size_t)grp * kAttnGroupWarps * kv_mul * (a.head_size + 4);
-    StepArgs none;  // no timeline
-    const long long item = (long long)blockIdx.x * kAttnGroups + grp;
-    // position t owns n_kv_heads * nsplit(t) items; walk to the position holding `item`
-    long long base = 0;
-    for (int t = 0; t < ntok; ++t) {
-        const int T = pos0 + t + 1;
-        const int nsplit = min(a.max_splits, (T + a.min_chunk - 1) / a.min_chunk);
-        const long long cnt = (long long)a.n_kv_heads * nsplit;
-        if (item < base + cnt) {
-            const int it = (int)(item - base), kvh = it / nsplit, split = it % nsplit;
-            const int chunk = (T + nsplit - 1) / nsplit;
-            AttnArgs b = a;
-            b.qkv = a.qkv + (size_t)t * qkv_stride;
-            b.out = a.out + (size_t)t * out_stride;
-            b.work = a.work + (size_t)t * work_stride;
-            b.count = a.count + (size_t)t * count_stride;
-            if (a.kv_f32) attn_item<true>(b, pos0 + t, kvh, split, nsplit, chunk, grp, gt, sm, ctl, sink, none, 0);
-            else attn_item<false>(b, pos0 + t, kvh, split, nsplit, chunk, grp, gt, sm, ctl, sink, none, 0);
-            return;
+    const long long item = blockIdx.x;
+    int lo = 0, hi = ngroups - 1;  // the group holding this item: the last with item0 <= item
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (groups[mid].item0 <= item) lo = mid;
+        else hi = mid - 1;
+    }
+    const PrefillGroup g = groups[lo];
+    const int it = (int)(item - g.item0), kvh = it / g.nsplit, split = it % g.nsplit;
+    const int rows = g.count * kv_mul;
+    if (kvh >= a.n_kv_heads || rows > kPrefillRows || g.first < pos0) return;
+    const int t0 = split * g.chunk, tmax = min(g.first + g.count, t0 + g.chunk);
+    const int SW = hs + 4, W = hs + 2;
+    float *qs = psm;                           // [kPrefillRows][hs]
+    float *stt = psm + (size_t)kPrefillRows * hs;  // [kAttnGroupWarps][kPrefillRows][SW]
+    for (int r = warp; r < rows; r += kAttnGroupWarps) {
+        const int q = r / kv_mul, m = r % kv_mul, pos = g.first + q;
+        if (act)
+            *reinterpret_cast<float4 *>(qs + (size_t)r * hs + d0) =
+                rope4(a.qkv + (size_t)(pos - pos0) * qkv_stride + (size_t)(kvh * kv_mul + m) * hs,
+                      a.rope + (size_t)pos * hs, d0, half);
+    }
+    for (int r = 0; r < rows; ++r) {
+        float *sw = stt + ((size_t)warp * kPrefillRows + r) * SW;
+        if (lane == 0) {
+            sw[0] = -INFINITY;
+            sw[1] = 0.0f;
         }
-        base += cnt;
+        if (act) *reinterpret_cast<float4 *>(sw + 4 + d0) = make_float4(0, 0, 0, 0);
+    }
+    __syncthreads();
+    const float sq = __fsqrt_rn((float)hs);
+    const size_t head_base = (size_t)kvh * a.seq_len * hs + d0;
+    for (int tb = t0 + warp * kBatch; tb < tmax; tb += kAttnGroupWarps * kBatch) {
+        float4 kk[kBatch], vv[kBatch];
+        #pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+            const int t = tb + j;
+            kk[j] = (t < tmax && act) ? load_kv4<F32>(a.k_cache, head_base + (size_t)t * hs) : make_float4(0, 0, 0, 0);
+            vv[j] = (t < tmax && act) ? load_kv4<F32>(a.v_cache, head_base + (size_t)t * hs) : make_float4(0, 0, 0, 0);
+        }
+        for (int r = 0; r < rows; ++r) {
+            const int t1 = min(g.first + r / kv_mul + 1, t0 + g.chunk);  // this row's end of the split
+            if (tb >= t1) continue;  // the decode step's warp has left its loop
+            float *sw = stt + ((size_t)warp * kPrefillRows + r) * SW;
+            const float4 qv = act ? *reinterpret_cast<const float4 *>(qs + (size_t)r * hs + d0) : make_float4(0, 0, 0, 0);
+            float4 am = act ? *reinterpret_cast<const float4 *>(sw + 4 + d0) : make_float4(0, 0, 0, 0);
+            const float mx = sw[0], l = sw[1];
+            // positions at or past t1 are the decode step's zero rows: score -inf, value 0
+            float sc[kBatch];
+            float bmax = -INFINITY;
+            #pragma unroll
+            for (int j = 0; j < kBatch; ++j) {
+                const float d = warp_sum(dot4(qv, kk[j]));
+                sc[j] = (tb + j < t1) ? __fdiv_rn(d, sq) : -INFINITY;
+                bmax = fmaxf(bmax, sc[j]);
+            }
+            const float mnew = fmaxf(mx, bmax);
+            const float rescale = expf(mx - mnew);
+            float lm = __fmul_rn(l, rescale);
+            am = make_float4(__fmul_rn(am.x, rescale), __fmul_rn(am.y, rescale), __fmul_rn(am.z, rescale),
+                             __fmul_rn(am.w, rescale));
+            #pragma unroll
+            for (int j = 0; j < kBatch; ++j) {
+                const float pj = expf(sc[j] - mnew);
+                const float4 v = (tb + j < t1) ? vv[j] : make_float4(0, 0, 0, 0);
+                lm = __fadd_rn(lm, pj);
+                am.x = __fmaf_rn(pj, v.x, am.x);
+                am.y = __fmaf_rn(pj, v.y, am.y);
+                am.z = __fmaf_rn(pj, v.z, am.z);
+                am.w = __fmaf_rn(pj, v.w, am.w);
+            }
+            __syncwarp();
+            if (lane == 0) {
+                sw[0] = mnew;
+                sw[1] = lm;
+            }
+            if (act) *reinterpret_cast<float4 *>(sw + 4 + d0) = am;
+            __syncwarp();
+        }
+    }
+    __syncthreads();
+    // the warps' merge, per row (attn_item's order), then the output or this split's partial
+    for (int r = 0; r < rows; ++r) {
+        const int q = r / kv_mul, m = r % kv_mul, pos = g.first + q;
+        const float *s0 = stt + (size_t)r * SW;
+        float M = -INFINITY;
+        for (int w = 0; w < kAttnGroupWarps; ++w) M = fmaxf(M, s0[(size_t)w * kPrefillRows * SW]);
+        float L = 0.0f;
+        for (int w = 0; w < kAttnGroupWarps; ++w) {
+            const float *cw = s0 + (size_t)w * kPrefillRows * SW;
+            L = __fmaf_rn(cw[1], expf(cw[0] - M), L);
+        }
+        const size_t hrow = (size_t)(kvh * kv_mul + m);
+        for (int e = tid; e < hs; e += kAttnGroupThreads) {
+            float o = 0.0f;
+            for (int w = 0; w < kAttnGroupWarps; ++w) {
+                const float *cw = s0 + (size_t)w * kPrefillRows * SW;
+                o = __fmaf_rn(cw[4 + e], expf(cw[0] - M), o);
+            }
+            if (g.nsplit == 1) a.out[(size_t)(pos - pos0) * out_stride + hrow * hs + e] = __fdiv_rn(o, L);
+            else a.work[(size_t)(pos - pos0) * work_stride + (hrow * a.max_splits + split) * W + 2 + e] = o;
+        }
+        if (g.nsplit > 1 && tid == 0) {
+            float *w = a.work + (size_t)(pos - pos0) * work_stride + (hrow * a.max_splits + split) * W;
+            w[0] = M;
+            w[1] = L;
+        }
+    }
+    if (g.nsplit == 1) return;
+    __threadfence();
+    __syncthreads();
+    if (tid < g.count) {
+        const unsigned ticket = atomicAdd(a.count + (size_t)(g.first + tid - pos0) * count_stride + kvh, 1u);
+        last_split[tid] = ticket == (unsigned)g.nsplit - 1u;
+    }
+    __syncthreads();
+    // the last split of a position merges its splits (attn_item's merge)
+    for (int q = 0; q < g.count; ++q) {
+        if (!last_split[q]) continue;
+        __threadfence();
+        const int pos = g.first + q;
+        const float *work = a.work + (size_t)(pos - pos0) * work_stride;
+        for (int m = 0; m < kv_mul; ++m) {
+            const float *wb = work + (size_t)(kvh * kv_mul + m) * a.max_splits * W;
+            float M = -INFINITY, L = 0.0f, o[kMergeDims];
+            #pragma unroll
+            for (int k = 0; k < kMergeDims; ++k) o[k] = 0.0f;
+            for (int s0 = 0; s0 < g.nsplit; s0 += kMergeChunk) {
+                float cm[kMergeChunk], cl[kMergeChunk], co[kMergeChunk][kMergeDims];
+                #pragma unroll
+                for (int j = 0; j < kMergeChunk; ++j) {
+                    const bool in = s0 + j < g.nsplit;
+                    const float *w = wb + (size_t)(s0 + j) * W;
+                    cm[j] = in ? __ldcg(w) : -INFINITY;
+                    cl[j] = in ? __ldcg(w + 1) : 0.0f;
+                    #pragma unroll
+                    for (int k = 0; k < kMergeDims; ++k) {
+                        const int e = tid + k * kAttnGroupThreads;
+                        co[j][k] = (in && e < hs) ? __ldcg(w + 2 + e) : 0.0f;
+                    }
+                }
+                float cmax = M;
+                #pragma unroll
+                for (int j = 0; j < kMergeChunk; ++j) cmax = fmaxf(cmax, cm[j]);
+                const float rr = expf(M - cmax);
+                L = __fmul_rn(L, rr);
+                #pragma unroll
+                for (int k = 0; k < kMergeDims; ++k) o[k] = __fmul_rn(o[k], rr);
+                #pragma unroll
+                for (int j = 0; j < kMergeChunk; ++j) {
+                    const float f = expf(cm[j] - cmax);
+                    L = __fmaf_rn(cl[j], f, L);
+                    #pragma unroll
+                    for (int k = 0; k < kMergeDims; ++k) o[k] = __fmaf_rn(co[j][k], f, o[k]);
+                }
+                M = cmax;
+            }
+            #pragma unroll
+            for (int k = 0; k < kMergeDims; ++k) {
+                const int e = tid + k * kAttnGroupThreads;
+                if (e < hs) a.out[(size_t)(pos - pos0) * out_stride + (size_t)(kvh * kv_mul + m) * hs + e] = __fdiv_rn(o[k], L);
+            }
+        }
+        if (tid == 0) a.count[(size_t)(pos - pos0) * count_stride + kvh] = 0u;
     }
 }
 
 }  // namespace
 
-long long prefill_attn_items(int pos0, int ntok, int n_kv_heads, int max_splits, int min_chunk) {
+int prefill_attn_plan(const AttnArgs &a, int pos0, int ntok, PrefillGroup *groups, long long *items) {
+    const int kv_mul = a.n_heads / a.n_kv_heads;
+    const int qmax = std::max(1, kPrefillRows / kv_mul);
+    int n = 0;
     long long total = 0;
-    for (int t = 0; t < ntok; ++t)
-        total += (long long)n_kv_heads * std::min(max_splits, (pos0 + t + 1 + min_chunk - 1) / min_chunk);
-    return total;
+    for (int t = 0; t < ntok; ++t) {
+        const int pos = pos0 + t, T = pos + 1;
+        int ns, ch;
+        attn_split_plan(T, a.max_splits, a.min_chunk, ns, ch);
+        if (n > 0) {
+            PrefillGroup &b = groups[n - 1];
+            // one split: the run is [0, T) whatever the chunk; more: the same chunk, the same split starts
+            if (b.count < qmax && b.nsplit == ns && (ns == 1 || b.chunk == ch)) {
+                ++b.count;
+                if (ns == 1) b.chunk = T;
+                continue;
+            }
+            total += (long long)a.n_kv_heads * b.nsplit;
+        }
+        groups[n].first = pos;
+        groups[n].count = 1;
+        groups[n].nsplit = ns;
+        groups[n].chunk = ch;
+        groups[n].item0 = (int)total;
+        ++n;
+    }
+    if (n > 0) total += (long long)a.n_kv_heads * groups[n - 1].nsplit;
+    if (items) *items = total;
+    return n;
 }
 
 cudaError_t launch_prefill_act(const GemvArgs &a, int ntok, const int *tokens, int8_t *xq, float *xs, cudaStream_t st) {
@@ -1024,19 +1195,27 @@ cudaError_t launch_prefill_kv(const AttnArgs &a, int pos0, int ntok, size_t qkv_
     return cudaGetLastError();
 }
 
-cudaError_t launch_prefill_attn(const AttnArgs &a, int pos0, int ntok, size_t qkv_stride, size_t out_stride,
-                                size_t work_stride, size_t count_stride, unsigned long long *sink, cudaStream_t st) {
-    if (pos0 < 0 || pos0 + ntok > a.seq_len) return cudaErrorInvalidValue;
-    const long long items = prefill_attn_items(pos0, ntok, a.n_kv_heads, a.max_splits, a.min_chunk);
-    const long long ctas = (items + kAttnGroups - 1) / kAttnGroups;
-    if (ctas < 1 || ctas > 0x7FFFFFFFLL) return cudaErrorInvalidValue;
-    const size_t smem = ((sizeof(StepCtl) + 127) & ~(size_t)127) + step_attn_scratch_bytes(a.n_heads, a.n_kv_heads, a.head_size);
-    if (smem > 48 * 1024) {
-        const cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
+cudaError_t launch_prefill_attn(const AttnArgs &a, int pos0, const PrefillGroup *d_groups, int ngroups,
+                                long long items, size_t qkv_stride, size_t out_stride, size_t work_stride,
+                                size_t count_stride, cudaStream_t st) {
+    if (ngroups < 1 || items < 1 || items > 0x7FFFFFFFLL || a.head_size > 128 || a.head_size % 4) return cudaErrorInvalidValue;
+    const size_t smem = sizeof(float) * ((size_t)kPrefillRows * a.head_size +
+                                         (size_t)kAttnGroupWarps * kPrefillRows * (a.head_size + 4));
+    if (a.kv_f32) {
+        if (smem > 48 * 1024) {
+            const cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+        }
+        prefill_attn_kernel<true><<<(unsigned)items, kAttnGroupThreads, smem, st>>>(a, pos0, d_groups, ngroups, qkv_stride,
+                                                                                   out_stride, work_stride, count_stride);
+    } else {
+        if (smem > 48 * 1024) {
+            const cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+        }
+        prefill_attn_kernel<false><<<(unsigned)items, kAttnGroupThreads, smem, st>>>(a, pos0, d_groups, ngroups, qkv_stride,
+                                                                                    out_stride, work_stride, count_stride);
     }
-    prefill_attn_kernel<<<(unsigned)ctas, kComputeThreads, smem, st>>>(a, pos0, ntok, qkv_stride, out_stride,
-                                                                        work_stride, count_stride, sink);
     return cudaGetLastError();
 }
 

@@ -220,6 +220,31 @@ def test_dim4096_model_vs_oracle(port):
             assert int(np.argmax(a)) == int(np.argmax(b)), pos
 
 
+# 32 KV heads of 32 dims: the decode attention's split count reaches its cap (ceil(5 * SMs / 32): 24 on
+# 148 SMs) at position 384, where a chunk rounded up can leave the last split without positions.
+CAPPED = synth.Config(dim=1024, hidden_dim=256, n_layers=1, n_heads=32, n_kv_heads=32, vocab_size=256, seq_len=600)
+
+
+def test_capped_split_plan_vs_oracle(port):
+    """Decode through the positions where the split count is capped (385 .. 529 had an empty last split
+    under a plan that fixed the count before the chunk): finite logits within the requantisation envelope
+    of the oracle at every position."""
+    from oracle import PortModel, load_port_weights
+
+    w, by_name = load_port_weights(port, CAPPED, 93)
+    m = _gpu_model(CAPPED, by_name, kv_f32=True)
+    pm = PortModel(port, CAPPED, w, kv_f32=True)
+    seq = np.random.default_rng(3).integers(3, CAPPED.vocab_size, 560)
+    worst = 0.0
+    for pos, tok in enumerate(seq):
+        a = m.forward(int(tok), pos)
+        b = pm.forward(int(tok), pos)
+        if pos >= 370:
+            assert np.isfinite(a).all(), pos
+            worst = max(worst, float(np.max(np.abs(a - b)) / np.max(np.abs(b))))
+    assert worst < 5e-2, worst
+
+
 def _logits_bits(a):
     return np.ascontiguousarray(a, np.float32).view(np.uint32)
 
@@ -232,6 +257,7 @@ def _logits_bits(a):
         ("gqa", True, 300),   # two prefill chunks (256 + 43 positions), many attention splits
         ("gqa", False, 300),
         ("wide", True, 40),   # dim 4096: the one-round-trip rmsnorm prologue
+        ("capped", False, 540),  # 32 KV heads: the split count is capped (24 on 148 SMs) from position 384
     ],
 )
 def test_prefill_equals_decode_steps(port, tiny_weights, shape, kv_f32, P):
@@ -245,6 +271,8 @@ def test_prefill_equals_decode_steps(port, tiny_weights, shape, kv_f32, P):
     elif shape == "gqa":
         cfg = synth.Config(dim=512, hidden_dim=1024, n_layers=2, n_heads=8, n_kv_heads=1, vocab_size=2048, seq_len=512)
         by_name = load_port_weights(port, cfg, 77)[1]
+    elif shape == "capped":
+        cfg, by_name = CAPPED, load_port_weights(port, CAPPED, 93)[1]
     else:
         cfg = synth.Config(dim=4096, hidden_dim=1024, n_layers=1, n_heads=32, n_kv_heads=8, vocab_size=1000, seq_len=64)
         by_name = load_port_weights(port, cfg, 91)[1]
