@@ -19,6 +19,11 @@
 // The epilogue then stores / adds (residual) / applies SwiGLU to the 32 sums.
 //
 // Every wait is bounded; a CTA that gives up still frees its TMEM.
+#include <cstdlib>
+#include <cstring>
+
+#include <cuda.h>  // CUtensorMap and its enums; the encoder is fetched from the driver at run time
+
 #include "dk_common.cuh"
 #include "dk_kernels.h"
 
@@ -207,10 +212,388 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q8_kernel(const GemmArgs
     if (warp == 0) tmem_dealloc(tmem, kTmemCols);
 }
 
+
+// ================================================================================================
+// The pipelined form (n a multiple of 128, packed tiles of 17..32 rows): TMA + warp specialisation.
+//
+// The packed layout already is the tensor cores' 128-byte-swizzled K-major layout, one 128-value
+// quarter of a block at a time: chunk c of tile row r sits at 16-byte position c ^ (r & 7) of its
+// quarter, which is where the SWIZZLE_128B pattern puts it when row r of the tile is row r (mod 8) of
+// an 8-row atom.  So TMA copies the packed bytes as they are (no swizzle of its own): per quarter, one
+// 4-D box [128 B][32 rows][1 block][4 tiles] lands as 128 rows x 128 B, tile j at rows 32j..32j+31 (rows
+// past the tile height T read as zeros); the matrix descriptor reads it with SWIZZLE_128B, SBO 1 KB,
+// advancing 32 B per group.  The activations are a plain 2-D int8 map swizzled by TMA the same way.
+//
+// CTA = 4 packed tiles (128 rows) x 64 tokens, 10 warps:
+//   warp 0   one thread issues the TMA copies of each 512-column block into a 2-stage ring;
+//   warp 1   allocates TMEM; one thread issues one MMA per group (K = 32, s32) into a ring of 8
+//            64-column TMEM accumulators and commits each to its mbarrier;
+//   warps 2-9 fold: warp w reads the lanes of tile w % 4 (row = lane) and 32 of the 64 token columns,
+//            and adds term = (float)dot * (ws * xs) to its running sums in group order, the GEMV's
+//            arithmetic.  (float)dot is exact: |dot| <= 32 * 128 * 128 < 2^22, so the bits of
+//            dot + 0x4B400000 are the float 1.5 * 2^23 + dot, and subtracting 1.5 * 2^23 is exact.
+// Every wait is bounded and gives up when another role has; TMEM is always freed.
+constexpr int kTcM = 128, kTcN = 64, kTcThreads = 320, kTcEpiWarps = 8, kTcTiles = 4, kTcTileRows = 32;
+constexpr uint32_t kTcSlots = 8, kTcSlotCols = 64, kTcTmemCols = kTcSlots * kTcSlotCols;
+// one stage: A [4 quarters][128 rows][128 B] | B [4 quarters][64 tokens][128 B] | weight scales [128 rows][64 B]
+// | activation scales [64 tokens][16] | the same transposed [16][64]
+constexpr size_t kStA = 0, kStB = 65536, kStWs = 98304, kStXs = 106496, kStXt = 110592, kStBytes = 114688;
+constexpr int kTcStages = 2;
+constexpr size_t kTcBarOff = kTcStages * kStBytes;
+constexpr size_t kTcSmem = kTcBarOff + 256 + 1024;  // barriers, then slack to align the base to 1 KB
+static_assert(kTcSmem <= 227 * 1024, "gemm stages");
+constexpr uint32_t kIdescTc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTcN >> 3) << 17) |
+                              ((uint32_t)(kTcM >> 4) << 24);
+
+struct GemmMaps {
+    CUtensorMap a[4];       // full blocks, quarter Q of the values: [128 B][T rows][blocks][tiles]
+    CUtensorMap s;          // full blocks, the scale chunks: [64 B][T][blocks][tiles]
+    CUtensorMap a_last[3];  // the last block when it is narrower (w % 128 == 0): [128 B][T][tiles]
+    CUtensorMap s_last;     // [w/8 B][T][tiles]
+    CUtensorMap x;          // activations int8 [ntok][n], box [128 B][64 tokens], 128-byte swizzle
+    CUtensorMap xs;         // activation scales fp32 [ntok][n/32], box [16][64]
+};
+struct GemmTmaParams {
+    GemmArgs g;
+    GemmMaps m;
+    int nfull;    // full 512-column blocks
+    int wb_last;  // width of the narrower last block (0: none)
+};
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int c0, int c1, uint64_t *bar) {
+    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+                 ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int c0, int c1, int c2, uint64_t *bar) {
+    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+                 ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, int c0, int c1, int c2, int c3,
+                                            uint64_t *bar) {
+    asm volatile("cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];"
+                 ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
+                   "r"(smem_u32(bar))
+                 : "memory");
+}
+// Matrix descriptor of a 128-byte-swizzled K-major operand: 8-row atoms of 128-byte rows, atoms 1 KB apart.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+    return (uint64_t)((addr >> 4) & 0x3FFFu) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
+           (2ull << 61);
+}
+__device__ __forceinline__ void mma_i8_tc(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(kIdescTc), "r"(0)
+        : "memory");
+}
+__device__ __forceinline__ void bar_epi() {  // the 8 fold warps
+    asm volatile("bar.sync 1, %0;" ::"n"(kTcEpiWarps * 32) : "memory");
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tma_kernel(const __grid_constant__ GemmTmaParams P) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    const GemmArgs &g = P.g;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int t0 = blockIdx.x * kTcN, tile0 = blockIdx.y * kTcTiles;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kTcBarOff);  // [2]
+    uint64_t *empty = full + kTcStages;                                 // [2]
+    uint64_t *tfull = empty + kTcStages;                                // [8]
+    uint64_t *tempty = tfull + kTcSlots;                                // [8]
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(tempty + kTcSlots);
+    int *abort = reinterpret_cast<int *>(tslot + 1);
+    const int nblk = P.nfull + (P.wb_last ? 1 : 0);
+
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tslot), kTcTmemCols);
+        tmem_relinquish();
+    }
+    if (tid == 0) {
+        for (int s = 0; s < kTcStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1 + kTcEpiWarps);
+        }
+        for (uint32_t k = 0; k < kTcSlots; ++k) {
+            mbar_init(&tfull[k], 1);
+            mbar_init(&tempty[k], kTcEpiWarps);
+        }
+        *abort = 0;
+        mbar_fence_init();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+
+    if (warp == 0) {
+        // ---- TMA producer
+        if (lane == 0) {
+            int issued[kTcStages] = {-1, -1};
+            for (int b = 0; b < nblk; ++b) {
+                const int s = b & 1;
+                if (b >= kTcStages && !mbar_wait_abortable(&empty[s], (uint32_t)(((b >> 1) - 1) & 1), g.err, abort, false)) {
+                    *abort = 1;
+                    break;
+                }
+                const bool part = b == P.nfull;
+                const int wb = part ? P.wb_last : 512, nq = wb >> 7;
+                uint8_t *st = smem + (size_t)s * kStBytes;
+                mbar_arrive_expect_tx(&full[s], (uint32_t)(nq * (16384 + 8192) + (wb / 8) * kTcM + 4096));
+                for (int q = 0; q < nq; ++q) {
+                    if (!part) tma_load_4d(st + kStA + q * 16384, &P.m.a[q], 0, 0, b, tile0, &full[s]);
+                    else tma_load_3d(st + kStA + q * 16384, &P.m.a_last[q], 0, 0, tile0, &full[s]);
+                    tma_load_2d(st + kStB + q * 8192, &P.m.x, 512 * b + 128 * q, t0, &full[s]);
+                }
+                if (!part) tma_load_4d(st + kStWs, &P.m.s, 0, 0, b, tile0, &full[s]);
+                else tma_load_3d(st + kStWs, &P.m.s_last, 0, 0, tile0, &full[s]);
+                tma_load_2d(st + kStXs, &P.m.xs, 16 * b, t0, &full[s]);
+                issued[s] = b;
+            }
+            // never leave with copies still landing in shared memory
+            for (int s = 0; s < kTcStages; ++s)
+                if (issued[s] >= 0) mbar_wait(&full[s], (uint32_t)((issued[s] >> 1) & 1), g.err);
+        }
+    } else if (warp == 1) {
+        // ---- MMA issuer
+        if (lane == 0) {
+            uint32_t gseq = 0;
+            int last_k = -1;
+            uint32_t last_par = 0;
+            bool ok = true;
+            for (int b = 0; b < nblk && ok; ++b) {
+                const int s = b & 1;
+                if (!mbar_wait_abortable(&full[s], (uint32_t)((b >> 1) & 1), g.err, abort, false)) {
+                    *abort = 1;
+                    break;
+                }
+                tc_fence_after();
+                const int ng = (b == P.nfull ? P.wb_last : 512) >> 5;
+                const uint32_t a0 = smem_u32(smem + (size_t)s * kStBytes + kStA);
+                const uint32_t b0 = smem_u32(smem + (size_t)s * kStBytes + kStB);
+                for (int q = 0; q < ng; ++q, ++gseq) {
+                    const uint32_t k = gseq & (kTcSlots - 1);
+                    if (gseq >= kTcSlots &&
+                        !mbar_wait_abortable(&tempty[k], ((gseq / kTcSlots) - 1) & 1, g.err, abort, true)) {
+                        *abort = 1;
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    mma_i8_tc(tmem + k * kTcSlotCols, sw128_desc(a0 + (q >> 2) * 16384 + (q & 3) * 32),
+                              sw128_desc(b0 + (q >> 2) * 8192 + (q & 3) * 32));
+                    mma_commit(smem_u32(&tfull[k]));
+                    last_k = (int)k;
+                    last_par = (gseq / kTcSlots) & 1;
+                }
+                if (ok) mma_commit(smem_u32(&empty[s]));
+            }
+            // the tensor cores are done with TMEM before it is freed
+            if (last_k >= 0) mbar_wait(&tfull[last_k], last_par, g.err);
+        }
+    } else {
+        // ---- fold warps
+        const int lq = warp & 3, h = (warp - 2) >> 2, et = tid - 64;
+        const int T = g.T, r = lane, row = (tile0 + lq) * T + r;
+        const int tok0 = t0 + 32 * h;
+        const bool any_tok = tok0 < g.ntok;
+        float sum[32];
+        #pragma unroll
+        for (int t = 0; t < 32; ++t) sum[t] = 0.0f;
+        uint32_t gseq = 0;
+        bool ok = true;
+        // every fold warp passes the per-block barrier once per block, whatever happened before
+        for (int b = 0; b < nblk; ++b) {
+            const int s = b & 1;
+            if (ok) {
+                const bool got = mbar_wait_abortable(&full[s], (uint32_t)((b >> 1) & 1), g.err, abort, false);
+                ok = __all_sync(FULL, got);
+                if (!ok) *abort = 1;
+            }
+            const uint8_t *st = smem + (size_t)s * kStBytes;
+            const int wb = b == P.nfull ? P.wb_last : 512, ng = wb >> 5;
+            // the activation scales transposed to [group][token] (4 per thread), then every fold warp
+            float *xt = reinterpret_cast<float *>(const_cast<uint8_t *>(st) + kStXt);
+            if (ok) {
+                const float *xsm = reinterpret_cast<const float *>(st + kStXs);
+                #pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int e = et + i * kTcEpiWarps * 32, tk = e >> 4, gg = e & 15;
+                    xt[gg * kTcN + tk] = xsm[e];
+                }
+            }
+            bar_epi();
+            if (__any_sync(FULL, *reinterpret_cast<volatile int *>(abort) != 0)) ok = false;
+            const uint8_t *wsr = st + kStWs + (size_t)(32 * lq + r) * (wb / 8);
+            for (int q = 0; q < ng && ok; ++q, ++gseq) {
+                const uint32_t k = gseq & (kTcSlots - 1);
+                const bool got = mbar_wait_abortable(&tfull[k], (gseq / kTcSlots) & 1, g.err, abort, true);
+                if (!__all_sync(FULL, got)) {
+                    *abort = 1;
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                int32_t dot[32];
+                if (any_tok) {
+                    tmem_ld32(tmem + ((uint32_t)(32 * lq) << 16) + k * kTcSlotCols + 32 * h, dot);
+                    tmem_wait_ld();
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[k]);  // the accumulator is in registers: free its columns
+                if (any_tok) {
+                    const float ws = *reinterpret_cast<const float *>(wsr + 16 * q8_swz_s(q >> 2, r, wb) + 4 * (q & 3));
+                    const float4 *xq4 = reinterpret_cast<const float4 *>(xt + q * kTcN + 32 * h);
+                    #pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const float4 x4 = xq4[i];
+                        const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
+                        #pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            const float f = __fsub_rn(__int_as_float(dot[4 * i + c] + 0x4B400000), 12582912.0f);
+                            sum[4 * i + c] = __fadd_rn(sum[4 * i + c], __fmul_rn(f, __fmul_rn(ws, xv[c])));
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            if (ok && lane == 0) mbar_arrive(&empty[s]);
+        }
+        // epilogue: this thread's row, 32 tokens
+        if (ok && any_tok) {
+            const bool live = r < T && row < g.d;
+            if (g.epi == EPI_SWIGLU) {
+                #pragma unroll
+                for (int t = 0; t < 32; ++t) {
+                    const float h3 = __shfl_down_sync(FULL, sum[t], 1);
+                    if (live && !(r & 1) && tok0 + t < g.ntok) {
+                        // val *= 1/(1+expf(-val)); val *= hb2 (src/transformer.c:214-220)
+                        const float v = __fmul_rn(sum[t], __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-sum[t]))));
+                        g.out[(size_t)(tok0 + t) * (g.d >> 1) + (row >> 1)] = __fmul_rn(v, h3);
+                    }
+                }
+            } else if (live) {
+                #pragma unroll
+                for (int t = 0; t < 32; ++t) {
+                    if (tok0 + t >= g.ntok) break;
+                    float *o = g.out + (size_t)(tok0 + t) * g.d + row;
+                    *o = g.epi == EPI_ADD ? __fadd_rn(*o, sum[t]) : sum[t];
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTcTmemCols);
+    }
+}
+
 }  // namespace
 
 bool gemm_supported(int n, int d, int ntok, int epi) {
     return n > 0 && n % 32 == 0 && d > 0 && ntok > 0 && (epi == EPI_STORE || epi == EPI_ADD || (epi == EPI_SWIGLU && d % 2 == 0));
+}
+
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+bool encode(CUtensorMap *m, CUtensorMapDataType type, int rank, const void *base, const cuuint64_t *dims,
+            const cuuint64_t *strides, const cuuint32_t *box, CUtensorMapSwizzle swz) {
+    const cuuint32_t es[5] = {1, 1, 1, 1, 1};
+    return encode_fn()(m, type, (cuuint32_t)rank, const_cast<void *>(base), dims, strides, box, es,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The tensor maps of the pipelined form; false when a shape or address does not fit it.
+bool make_maps(const GemmArgs &g, GemmTmaParams &P) {
+    const int n = g.n, T = g.T;
+    if (n % 128 || T <= 16 || T > kTcTileRows || !encode_fn()) return false;
+    if ((reinterpret_cast<uintptr_t>(g.w) | reinterpret_cast<uintptr_t>(g.xq) | reinterpret_cast<uintptr_t>(g.xs)) & 15)
+        return false;
+    const int ntiles = (g.d + T - 1) / T;
+    const uint64_t rowb = q8_row_bytes(n), tileb = (uint64_t)T * rowb;
+    P.g = g;
+    P.nfull = n / 512;
+    P.wb_last = n % 512;
+    const uint8_t *w = g.w;
+    if (P.nfull > 0) {
+        for (int q = 0; q < 4; ++q) {
+            const cuuint64_t dims[4] = {128, (cuuint64_t)T, (cuuint64_t)P.nfull, (cuuint64_t)ntiles};
+            const cuuint64_t str[3] = {576, (cuuint64_t)T * 576, tileb};
+            const cuuint32_t box[4] = {128, kTcTileRows, 1, kTcTiles};
+            if (!encode(&P.m.a[q], CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, w + 128 * q, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE))
+                return false;
+        }
+        const cuuint64_t dims[4] = {64, (cuuint64_t)T, (cuuint64_t)P.nfull, (cuuint64_t)ntiles};
+        const cuuint64_t str[3] = {576, (cuuint64_t)T * 576, tileb};
+        const cuuint32_t box[4] = {64, kTcTileRows, 1, kTcTiles};
+        if (!encode(&P.m.s, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, w + 512, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE))
+            return false;
+    }
+    if (P.wb_last) {
+        const int wb = P.wb_last;
+        const uint64_t blk = q8_blk_bytes(wb);
+        const uint8_t *base = w + (size_t)P.nfull * T * 576;
+        for (int q = 0; q < wb / 128; ++q) {
+            const cuuint64_t dims[3] = {128, (cuuint64_t)T, (cuuint64_t)ntiles};
+            const cuuint64_t str[2] = {blk, tileb};
+            const cuuint32_t box[3] = {128, kTcTileRows, kTcTiles};
+            if (!encode(&P.m.a_last[q], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, base + 128 * q, dims, str, box,
+                        CU_TENSOR_MAP_SWIZZLE_NONE))
+                return false;
+        }
+        const cuuint64_t dims[3] = {(cuuint64_t)(wb / 8), (cuuint64_t)T, (cuuint64_t)ntiles};
+        const cuuint64_t str[2] = {blk, tileb};
+        const cuuint32_t box[3] = {(cuuint32_t)(wb / 8), kTcTileRows, kTcTiles};
+        if (!encode(&P.m.s_last, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, base + wb, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE))
+            return false;
+    }
+    {
+        const cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)g.ntok};
+        const cuuint64_t str[1] = {(cuuint64_t)n};
+        const cuuint32_t box[2] = {128, kTcN};
+        if (!encode(&P.m.x, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, g.xq, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
+            return false;
+    }
+    {
+        const cuuint64_t dims[2] = {(cuuint64_t)(n / 32), (cuuint64_t)g.ntok};
+        const cuuint64_t str[1] = {(cuuint64_t)(n / 32) * 4};
+        const cuuint32_t box[2] = {16, kTcN};
+        if (!encode(&P.m.xs, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, g.xs, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE))
+            return false;
+    }
+    return true;
+}
+
+}  // namespace
+
+bool gemm_pipelined(const GemmArgs &g) {
+    GemmTmaParams P;
+    return gemm_supported(g.n, g.d, g.ntok, g.epi) && make_maps(g, P);
 }
 
 cudaError_t launch_gemm(const GemmArgs &g, cudaStream_t st) {
@@ -221,8 +604,22 @@ cudaError_t launch_gemm(const GemmArgs &g, cudaStream_t st) {
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     if (!attr_set[dev]) {
         cudaError_t e = cudaFuncSetAttribute(gemm_q8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmemLaunch);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(gemm_q8_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
         if (e != cudaSuccess) return e;
         attr_set[dev] = 1;
+    }
+    static const bool simple_only = [] {  // DIOLKOS_GEMM=simple: the simple form for every shape
+        const char *e = getenv("DIOLKOS_GEMM");
+        return e && strcmp(e, "simple") == 0;
+    }();
+    GemmTmaParams P;
+    if (!simple_only && make_maps(g, P)) {
+        const int ntiles = (g.d + g.T - 1) / g.T;
+        dim3 grid((g.ntok + kTcN - 1) / kTcN, (ntiles + kTcTiles - 1) / kTcTiles);
+        if (grid.y > 65535) return cudaErrorInvalidValue;
+        gemm_q8_tma_kernel<<<grid, kTcThreads, kTcSmem, st>>>(P);
+        return cudaGetLastError();
     }
     // token tiles along x: the CTAs of one row tile run side by side and share its weight reads in L2
     dim3 grid((g.ntok + kGemmN - 1) / kGemmN, (g.d + kGemmM - 1) / kGemmM);

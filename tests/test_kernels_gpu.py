@@ -298,8 +298,10 @@ def test_gemv_batch_equals_single(torch_cuda):
         np.testing.assert_array_equal(got[i].view(np.uint32), one.view(np.uint32))
 
 
+# Tile heights on 148 SMs: d 4096 / 12288 -> 28, d 4736 -> 32 (the pipelined TMA form, n % 128 == 0);
+# d 300 / 1001 -> 3 / 7 and n 288 -> the simple form.
 @pytest.mark.parametrize("n,d,ntok", [(4096, 4096, 32), (4096, 4096, 5), (11008, 4096, 37), (288, 864, 70),
-                                      (4096, 300, 1), (8192, 1001, 33)])
+                                      (4096, 300, 1), (8192, 1001, 33), (2048, 4736, 65), (4096, 12288, 130)])
 def test_tensor_core_matmul_tokens_bit_exact(torch_cuda, port, n, d, ntok):
     """dk_matmul_q8_0_tokens (tcgen05 kind::i8, one MMA per 32-value group): every token's output row
     equals the GEMV on that token bit for bit (and so the oracle's), for shapes that leave partial

@@ -258,6 +258,7 @@ def _logits_bits(a):
         ("gqa", False, 300),
         ("wide", True, 40),   # dim 4096: the one-round-trip rmsnorm prologue
         ("capped", False, 540),  # 32 KV heads: the split count is capped (24 on 148 SMs) from position 384
+        ("swiglu", True, 100),   # hidden 4096: w1|w3 (8192 rows) on the pipelined tensor-core matmul
     ],
 )
 def test_prefill_equals_decode_steps(port, tiny_weights, shape, kv_f32, P):
@@ -271,6 +272,9 @@ def test_prefill_equals_decode_steps(port, tiny_weights, shape, kv_f32, P):
     elif shape == "gqa":
         cfg = synth.Config(dim=512, hidden_dim=1024, n_layers=2, n_heads=8, n_kv_heads=1, vocab_size=2048, seq_len=512)
         by_name = load_port_weights(port, cfg, 77)[1]
+    elif shape == "swiglu":
+        cfg = synth.Config(dim=512, hidden_dim=4096, n_layers=1, n_heads=8, n_kv_heads=8, vocab_size=512, seq_len=128)
+        by_name = load_port_weights(port, cfg, 95)[1]
     elif shape == "capped":
         cfg, by_name = CAPPED, load_port_weights(port, CAPPED, 93)[1]
     else:
