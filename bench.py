@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Benchmark: batch-1 Q8_0 decode of a LLaMA-2-7B-shape model on B200, plus the Q8_0 GEMV shapes.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload decode|gemv]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload decode|gemv|gemm]
 
 Decode workload (N=1): LLaMA-2-7B shape (dim 4096, hidden 11008, 32 layers, 32 heads, 32 KV heads,
 vocab 32000, seq_len 4096), random-init weights N(0, 0.02) generated on the GPU from a seed, rounded
@@ -55,7 +55,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "gemv"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "gemv", "gemm"], default="decode")
     ap.add_argument("--kv", choices=["f32", "bf16"], default="f32")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the long-prompt prefill and GEMM measurements")
@@ -632,12 +632,30 @@ def run_gemv(args):
     return 0
 
 
+def run_gemm(args):
+    """The prefill matmul alone (dk_matmul_q8_0_tokens) on one 7B layer's shapes at 256 tokens."""
+    import torch
+
+    from diolkos_b200 import synth
+
+    torch.cuda.set_device(0)
+    g = gemm_bench(synth.LLAMA7B)
+    line = {"metric": "Q8_0 prefill matmul int8 TOPS", "value": g["achieved_tops"], "unit": "TOPS", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": "tensor-core Q8_0 matmul, 7B layer shapes, 256 tokens"}, "prefill_gemm": g}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
     if args.workload == "gemv":
         return run_gemv(args)
+    if args.workload == "gemm":
+        return run_gemm(args)
     return run_decode(args)
 
 

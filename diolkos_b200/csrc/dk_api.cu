@@ -178,6 +178,17 @@ int dk_attention_decode(float *out, const float *qkv, const float *rope, void *k
     return cuda_status(launch_attention(a, (cudaStream_t)stream, false), "dk_attention_decode");
 }
 
+int dk_gemm_trace(unsigned long long *out, size_t n, int *ctas, int *blocks) {
+    int c = 0, b = 0;
+    const unsigned long long *buf = gemm_trace_buffer(&c, &b);
+    if (ctas) *ctas = c;
+    if (blocks) *blocks = b;
+    if (!buf) return set_error(DK_ERR_STATE, "dk_gemm_trace: tracing is off (DIOLKOS_GEMM_TRACE=1 before the first launch)");
+    const size_t total = (size_t)c * b * kGemmTraceSlots;
+    if (!out || n < total) return set_error(DK_ERR_INVALID, "dk_gemm_trace: need %zu entries", total);
+    return cuda_status(cudaMemcpy(out, buf, total * 8, cudaMemcpyDeviceToHost), "dk_gemm_trace");
+}
+
 int dk_matmul_q8_0_tokens(float *out, const int8_t *xq, const float *xs, const uint8_t *w_packed, int n, int d,
                           int ntok, int accumulate, void *stream) {
     if (!out || !xq || !xs || !w_packed) return set_error(DK_ERR_INVALID, "dk_matmul_q8_0_tokens: null pointer");

@@ -157,9 +157,17 @@ struct GemmArgs {
     int epi = EPI_STORE;         // EPI_STORE: out[t][d]; EPI_ADD: out[t][d] +=; EPI_SWIGLU: out[t][d/2]
     float *out = nullptr;
     int *err = nullptr;
+    // Optional timeline of the pipelined form (%globaltimer, ns), [CTA][block][kGemmTraceSlots]: producer
+    // issued the block's copies, MMA thread saw them land, MMA thread issued its last group, fold warp 2
+    // saw them land, fold warp 2 finished the block.
+    unsigned long long *trace = nullptr;
+    int trace_ctas = 0, trace_blocks = 0;
 };
+constexpr int kGemmTraceSlots = 5;
 bool gemm_supported(int n, int d, int ntok, int epi);
 cudaError_t launch_gemm(const GemmArgs &g, cudaStream_t st);
+// The timeline buffer of the last traced launch (DIOLKOS_GEMM_TRACE=1), or nullptr.
+unsigned long long *gemm_trace_buffer(int *ctas, int *blocks);
 
 // ---------------- Q8_0 conversions ----------------------------------------------------------
 cudaError_t launch_quant_bf16(const uint16_t *x, size_t n, int8_t *q, float *s, cudaStream_t st);

@@ -224,16 +224,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q8_kernel(const GemmArgs
 // past the tile height T read as zeros); the matrix descriptor reads it with SWIZZLE_128B, SBO 1 KB,
 // advancing 32 B per group.  The activations are a plain 2-D int8 map swizzled by TMA the same way.
 //
-// CTA = 4 packed tiles (128 rows) x 64 tokens, 10 warps:
+// CTA = 4 packed tiles (128 rows) x 64 tokens, 18 warps:
 //   warp 0   one thread issues the TMA copies of each 512-column block into a 2-stage ring;
 //   warp 1   allocates TMEM; one thread issues one MMA per group (K = 32, s32) into a ring of 8
 //            64-column TMEM accumulators and commits each to its mbarrier;
-//   warps 2-9 fold: warp w reads the lanes of tile w % 4 (row = lane) and 32 of the 64 token columns,
-//            and adds term = (float)dot * (ws * xs) to its running sums in group order, the GEMV's
-//            arithmetic.  (float)dot is exact: |dot| <= 32 * 128 * 128 < 2^22, so the bits of
-//            dot + 0x4B400000 are the float 1.5 * 2^23 + dot, and subtracting 1.5 * 2^23 is exact.
+//   warps 2-17 fold: warp w reads the lanes of tile w % 4 (row = lane) and 16 of the 64 token columns
+//            (the next group's columns load while the current one folds; a block's groups are unrolled),
+//            refills the read columns with the bias below and hands them back, and adds term = (float)dot * (ws * xs) to its running sums in group order, the GEMV's
+//            arithmetic.  (float)dot is exact: the accumulators start at the bits 0x4B400000 and
+//            |dot| <= 32 * 128 * 128 < 2^22, so the s32 sum's bits are the float 1.5 * 2^23 + dot, and
+//            subtracting 1.5 * 2^23 is exact.
 // Every wait is bounded and gives up when another role has; TMEM is always freed.
-constexpr int kTcM = 128, kTcN = 64, kTcThreads = 320, kTcEpiWarps = 8, kTcTiles = 4, kTcTileRows = 32;
+constexpr int kTcM = 128, kTcN = 64, kTcThreads = 576, kTcEpiWarps = 16, kTcTiles = 4, kTcTileRows = 32;
 constexpr uint32_t kTcSlots = 8, kTcSlotCols = 64, kTcTmemCols = kTcSlots * kTcSlotCols;
 // one stage: A [4 quarters][128 rows][128 B] | B [4 quarters][64 tokens][128 B] | weight scales [128 rows][64 B]
 // | activation scales [64 tokens][16] | the same transposed [16][64]
@@ -287,10 +289,56 @@ __device__ __forceinline__ void mma_i8_tc(uint32_t d_tmem, uint64_t a_desc, uint
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
-        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(kIdescTc), "r"(0)
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(kIdescTc), "r"(1)
         : "memory");
 }
-__device__ __forceinline__ void bar_epi() {  // the 8 fold warps
+// 16 consecutive 32-bit TMEM columns of this thread's lane, and the wait that makes them usable (the
+// registers are operands of the wait, so no use of them is scheduled before it).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, int32_t (&v)[16]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+                 "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+                   "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+                 : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld16(int32_t (&v)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+                   "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15])
+                 :
+                 : "memory");
+}
+__device__ __forceinline__ void gemm_mark(const GemmArgs &g, int b, int k) {
+    const int cta = blockIdx.y * gridDim.x + blockIdx.x;
+    if (g.trace && cta < g.trace_ctas && b < g.trace_blocks) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        g.trace[((size_t)cta * g.trace_blocks + b) * kGemmTraceSlots + k] = t;
+    }
+}
+// 16 consecutive TMEM columns of this thread's lane set to v; the wait makes the store complete.
+__device__ __forceinline__ void tmem_st16_fill(uint32_t taddr, uint32_t v) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 "
+                 "[%0], {%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr), "r"(v)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// Fold one group into 16 running sums: term = (float)dot * (ws * xs[t]), added in group order.  The
+// accumulator columns hold the float 1.5 * 2^23 + dot.
+__device__ __forceinline__ void fold_group(float (&sum)[16], const int32_t (&d)[16], float ws, const float *xq) {
+    const float4 *xq4 = reinterpret_cast<const float4 *>(xq);
+    #pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float4 x4 = xq4[i];
+        const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
+        #pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const float f = __fsub_rn(__int_as_float(d[4 * i + c]), 12582912.0f);
+            sum[4 * i + c] = __fadd_rn(sum[4 * i + c], __fmul_rn(f, __fmul_rn(ws, xv[c])));
+        }
+    }
+}
+__device__ __forceinline__ void bar_epi() {  // the fold warps
     asm volatile("bar.sync 1, %0;" ::"n"(kTcEpiWarps * 32) : "memory");
 }
 
@@ -352,6 +400,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tma_kernel(const __grid
                 else tma_load_3d(st + kStWs, &P.m.s_last, 0, 0, tile0, &full[s]);
                 tma_load_2d(st + kStXs, &P.m.xs, 16 * b, t0, &full[s]);
                 issued[s] = b;
+                gemm_mark(g, b, 0);
             }
             // never leave with copies still landing in shared memory
             for (int s = 0; s < kTcStages; ++s)
@@ -371,13 +420,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tma_kernel(const __grid
                     break;
                 }
                 tc_fence_after();
+                gemm_mark(g, b, 1);
                 const int ng = (b == P.nfull ? P.wb_last : 512) >> 5;
                 const uint32_t a0 = smem_u32(smem + (size_t)s * kStBytes + kStA);
                 const uint32_t b0 = smem_u32(smem + (size_t)s * kStBytes + kStB);
                 for (int q = 0; q < ng; ++q, ++gseq) {
                     const uint32_t k = gseq & (kTcSlots - 1);
-                    if (gseq >= kTcSlots &&
-                        !mbar_wait_abortable(&tempty[k], ((gseq / kTcSlots) - 1) & 1, g.err, abort, true)) {
+                    // the slot holds the bias again (stored by the fold warps: first at the start, then
+                    // each time they have read it)
+                    if (!mbar_wait_abortable(&tempty[k], (gseq / kTcSlots) & 1, g.err, abort, false)) {
                         *abort = 1;
                         ok = false;
                         break;
@@ -390,21 +441,57 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tma_kernel(const __grid
                     last_par = (gseq / kTcSlots) & 1;
                 }
                 if (ok) mma_commit(smem_u32(&empty[s]));
+                gemm_mark(g, b, 2);
             }
             // the tensor cores are done with TMEM before it is freed
             if (last_k >= 0) mbar_wait(&tfull[last_k], last_par, g.err);
         }
     } else {
-        // ---- fold warps
+        // ---- fold warps: warp w reads the lanes of tile w % 4 and the 16 token columns 16 * ((w - 2) / 4) ..
+        // The accumulators start at the bias 0x4B400000 (the float 1.5 * 2^23): the MMA adds the s32 dot,
+        // so each column holds the float 1.5 * 2^23 + dot and (float)dot is one exact subtraction.
         const int lq = warp & 3, h = (warp - 2) >> 2, et = tid - 64;
         const int T = g.T, r = lane, row = (tile0 + lq) * T + r;
-        const int tok0 = t0 + 32 * h;
+        const int tok0 = t0 + 16 * h;
         const bool any_tok = tok0 < g.ntok;
-        float sum[32];
+        const uint32_t tbase = tmem + ((uint32_t)(32 * lq) << 16) + 16 * h;
+        constexpr uint32_t kBias = 0x4B400000u;
+        float sum[16];
         #pragma unroll
-        for (int t = 0; t < 32; ++t) sum[t] = 0.0f;
-        uint32_t gseq = 0;
+        for (int t = 0; t < 16; ++t) sum[t] = 0.0f;
         bool ok = true;
+        // A slot read into registers is refilled with the bias; it goes back to the MMA thread at the next
+        // release (or flush), once the store is known complete, so the store's latency is not waited on.
+        int pending = -1;
+        auto flush = [&]() {
+            if (pending < 0) return;
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[pending]);
+            pending = -1;
+        };
+        auto release = [&](uint32_t gq) {
+            flush();
+            tmem_st16_fill(tbase + (gq & (kTcSlots - 1)) * kTcSlotCols, kBias);
+            pending = (int)(gq & (kTcSlots - 1));
+        };
+        for (uint32_t k = 0; k < kTcSlots; ++k) release(k);  // first fill of every slot
+        flush();
+        // bounded wait for group gq's accumulator, the same outcome on every lane
+        auto wait_acc = [&](uint32_t gq) {
+            const bool got = mbar_wait_abortable(&tfull[gq & (kTcSlots - 1)], (gq / kTcSlots) & 1, g.err, abort, false);
+            if (!__all_sync(FULL, got)) {
+                *abort = 1;
+                ok = false;
+            }
+            if (ok) tc_fence_after();
+            return ok;
+        };
+        auto load_acc = [&](uint32_t gq, int32_t(&d)[16]) {
+            tmem_ld16(tbase + (gq & (kTcSlots - 1)) * kTcSlotCols, d);
+        };
+        uint32_t gseq = 0;
         // every fold warp passes the per-block barrier once per block, whatever happened before
         for (int b = 0; b < nblk; ++b) {
             const int s = b & 1;
@@ -413,62 +500,68 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tma_kernel(const __grid
                 ok = __all_sync(FULL, got);
                 if (!ok) *abort = 1;
             }
+            if (warp == 2 && lane == 0) gemm_mark(g, b, 3);
             const uint8_t *st = smem + (size_t)s * kStBytes;
             const int wb = b == P.nfull ? P.wb_last : 512, ng = wb >> 5;
-            // the activation scales transposed to [group][token] (4 per thread), then every fold warp
+            // the activation scales transposed to [group][token] (2 per thread), then every fold warp
             float *xt = reinterpret_cast<float *>(const_cast<uint8_t *>(st) + kStXt);
             if (ok) {
                 const float *xsm = reinterpret_cast<const float *>(st + kStXs);
                 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
+                for (int i = 0; i < 2; ++i) {
                     const int e = et + i * kTcEpiWarps * 32, tk = e >> 4, gg = e & 15;
                     xt[gg * kTcN + tk] = xsm[e];
                 }
             }
             bar_epi();
             if (__any_sync(FULL, *reinterpret_cast<volatile int *>(abort) != 0)) ok = false;
-            const uint8_t *wsr = st + kStWs + (size_t)(32 * lq + r) * (wb / 8);
-            for (int q = 0; q < ng && ok; ++q, ++gseq) {
-                const uint32_t k = gseq & (kTcSlots - 1);
-                const bool got = mbar_wait_abortable(&tfull[k], (gseq / kTcSlots) & 1, g.err, abort, true);
-                if (!__all_sync(FULL, got)) {
-                    *abort = 1;
-                    ok = false;
-                    break;
+            if (ok) {
+                // this row's weight scales: scale q at chunk q8_swz_s(q / 4), word q % 4
+                const uint8_t *wsr = st + kStWs + (size_t)(32 * lq + r) * (wb / 8);
+                const float *xth = xt + 16 * h;
+                auto scale = [&](int q) {
+                    return *reinterpret_cast<const float *>(wsr + 16 * q8_swz_s(q >> 2, r, wb) + 4 * (q & 3));
+                };
+                // group q+1's accumulator loads while group q folds (two register sets, groups in pairs)
+                int32_t da[16], db[16];
+                if (wait_acc(gseq)) {
+                    if (any_tok) {
+                        load_acc(gseq, da);
+                        tmem_wait_ld16(da);
+                    }
+                    release(gseq);
                 }
-                tc_fence_after();
-                int32_t dot[32];
-                if (any_tok) {
-                    tmem_ld32(tmem + ((uint32_t)(32 * lq) << 16) + k * kTcSlotCols + 32 * h, dot);
-                    tmem_wait_ld();
-                }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&tempty[k]);  // the accumulator is in registers: free its columns
-                if (any_tok) {
-                    const float ws = *reinterpret_cast<const float *>(wsr + 16 * q8_swz_s(q >> 2, r, wb) + 4 * (q & 3));
-                    const float4 *xq4 = reinterpret_cast<const float4 *>(xt + q * kTcN + 32 * h);
-                    #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const float4 x4 = xq4[i];
-                        const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
-                        #pragma unroll
-                        for (int c = 0; c < 4; ++c) {
-                            const float f = __fsub_rn(__int_as_float(dot[4 * i + c] + 0x4B400000), 12582912.0f);
-                            sum[4 * i + c] = __fadd_rn(sum[4 * i + c], __fmul_rn(f, __fmul_rn(ws, xv[c])));
-                        }
+                for (int q = 0; ok && q < ng; q += 2) {  // ng is a multiple of 4
+                    const uint32_t g1 = gseq + q + 1, g2 = gseq + q + 2;
+                    if (!wait_acc(g1)) break;
+                    if (any_tok) load_acc(g1, db);
+                    if (any_tok) fold_group(sum, da, scale(q), xth + q * kTcN);
+                    if (any_tok) tmem_wait_ld16(db);
+                    release(g1);
+                    const bool more = q + 2 < ng;
+                    if (more) {
+                        if (!wait_acc(g2)) break;
+                        if (any_tok) load_acc(g2, da);
+                    }
+                    if (any_tok) fold_group(sum, db, scale(q + 1), xth + (q + 1) * kTcN);
+                    if (more) {
+                        if (any_tok) tmem_wait_ld16(da);
+                        release(g2);
                     }
                 }
             }
+            gseq += ng;
             __syncwarp();
             if (ok && lane == 0) mbar_arrive(&empty[s]);
+            if (warp == 2 && lane == 0) gemm_mark(g, b, 4);
         }
-        // epilogue: this thread's row, 32 tokens
+        flush();
+        // epilogue: this thread's row, 16 tokens
         if (ok && any_tok) {
             const bool live = r < T && row < g.d;
             if (g.epi == EPI_SWIGLU) {
                 #pragma unroll
-                for (int t = 0; t < 32; ++t) {
+                for (int t = 0; t < 16; ++t) {
                     const float h3 = __shfl_down_sync(FULL, sum[t], 1);
                     if (live && !(r & 1) && tok0 + t < g.ntok) {
                         // val *= 1/(1+expf(-val)); val *= hb2 (src/transformer.c:214-220)
@@ -478,7 +571,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tma_kernel(const __grid
                 }
             } else if (live) {
                 #pragma unroll
-                for (int t = 0; t < 32; ++t) {
+                for (int t = 0; t < 16; ++t) {
                     if (tok0 + t >= g.ntok) break;
                     float *o = g.out + (size_t)(tok0 + t) * g.d + row;
                     *o = g.epi == EPI_ADD ? __fadd_rn(*o, sum[t]) : sum[t];
@@ -591,6 +684,16 @@ bool make_maps(const GemmArgs &g, GemmTmaParams &P) {
 
 }  // namespace
 
+// DIOLKOS_GEMM_TRACE=1: the pipelined form records the first 148 CTAs' first 32 blocks (dk_gemm_trace).
+static unsigned long long *g_trace = nullptr;
+static constexpr int kTraceCtas = 148, kTraceBlocks = 32;
+
+unsigned long long *gemm_trace_buffer(int *ctas, int *blocks) {
+    *ctas = kTraceCtas;
+    *blocks = kTraceBlocks;
+    return g_trace;
+}
+
 bool gemm_pipelined(const GemmArgs &g) {
     GemmTmaParams P;
     return gemm_supported(g.n, g.d, g.ntok, g.epi) && make_maps(g, P);
@@ -613,8 +716,20 @@ cudaError_t launch_gemm(const GemmArgs &g, cudaStream_t st) {
         const char *e = getenv("DIOLKOS_GEMM");
         return e && strcmp(e, "simple") == 0;
     }();
+    static const bool tracing = [] {
+        const char *e = getenv("DIOLKOS_GEMM_TRACE");
+        return e && atoi(e) > 0;
+    }();
     GemmTmaParams P;
     if (!simple_only && make_maps(g, P)) {
+        if (tracing) {
+            if (!g_trace &&
+                cudaMalloc(&g_trace, sizeof(unsigned long long) * kTraceCtas * kTraceBlocks * kGemmTraceSlots) != cudaSuccess)
+                return cudaErrorMemoryAllocation;
+            P.g.trace = g_trace;
+            P.g.trace_ctas = kTraceCtas;
+            P.g.trace_blocks = kTraceBlocks;
+        }
         const int ntiles = (g.d + g.T - 1) / g.T;
         dim3 grid((g.ntok + kTcN - 1) / kTcN, (ntiles + kTcTiles - 1) / kTcTiles);
         if (grid.y > 65535) return cudaErrorInvalidValue;

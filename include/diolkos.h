@@ -229,6 +229,12 @@ int dk_model_kernels_per_step(dk_model *m);
  * 3: the op's last weight stage was issued, 4: the input counter was seen (0: not recorded).
  * *grid and *n_ops give the dimensions. */
 int dk_model_trace(dk_model *m, unsigned long long *out, size_t n, int *grid, int *n_ops);
+/* Diagnostics: the timeline of the last pipelined tensor-core matmul launched on this device while
+ * DIOLKOS_GEMM_TRACE=1 was set at the first launch: out[(cta * blocks + b) * 5 + k] = GPU global timer
+ * (ns) when, for 512-column block b of that CTA, k = 0: its copies were issued, 1: the MMA thread saw
+ * them land, 2: its last MMA was issued, 3: fold warp 2 saw them land, 4: fold warp 2 finished it
+ * (0: not recorded).  *ctas and *blocks give the dimensions (the first 148 CTAs, 32 blocks). */
+int dk_gemm_trace(unsigned long long *out, size_t n, int *ctas, int *blocks);
 /* Bytes of weights one decode step reads on this rank. */
 size_t dk_model_weight_bytes(dk_model *m);
 
