@@ -958,6 +958,12 @@ __global__ void prefill_kv_kernel(const AttnArgs a, int pos0, int ntok, size_t q
     store_kv4<F32>(a.v_cache, at, vr);
 }
 
+// Rows (query head of one position) whose batch scores one warp takes at once: 4 rows x kBatch positions
+// = one (row, position) per lane.
+constexpr int kPreRowChunk = 4;
+static_assert(kPreRowChunk * kBatch == 32, "one score per lane");
+constexpr int kPrePartStride = 36;  // floats per (row, position) block of lane partials: 16-byte reads without conflicts
+
 // Attention of the prompt positions of one group (positions that share the decode step's split plan)
 // for one (KV head, split): item = blockIdx.x, one attention group of kAttnGroupWarps warps.  Each K/V
 // batch is loaded once and used for every (position, query head) row of the group; each row keeps the
@@ -966,6 +972,14 @@ __global__ void prefill_kv_kernel(const AttnArgs a, int pos0, int ntok, size_t q
 // the decode step's at that position, bit for bit.  The K/V rows of every position up to the group's
 // last are in the cache already (prefill_kv_kernel).  State per (warp, row) lives in shared memory:
 // [max, sum, -, -, acc[hs]].
+// Per K/V batch a warp works on 4 rows at a time in three steps, so that each score's scalar work is
+// done once instead of on all 32 lanes:
+//   (a) lanes over head dims: each lane's 4-dim partial dot of every (row, position) -> shared memory;
+//   (b) one lane per (row, position): the 32 partials summed in warp_sum's butterfly order (at step o,
+//       v[l] = v[l] + v[l + o]: the value every lane of warp_sum ends with), the division by sqrt(hs),
+//       the batch max over the row's 8 lanes, the rescale and exp, and the running sum in position order
+//       through shuffles;
+//   (c) lanes over head dims: acc = acc * rescale, then acc = fma(p_j, v_j, acc) in position order.
 template <bool F32>
 __global__ void __launch_bounds__(kAttnGroupThreads) prefill_attn_kernel(const AttnArgs a, int pos0,
                                                                          const PrefillGroup *groups, int ngroups,
@@ -1010,6 +1024,11 @@ __global__ void __launch_bounds__(kAttnGroupThreads) prefill_attn_kernel(const A
     __syncthreads();
     const float sq = __fsqrt_rn((float)hs);
     const size_t head_base = (size_t)kvh * a.seq_len * hs + d0;
+    float *part = psm + (size_t)kPrefillRows * hs + (size_t)kAttnGroupWarps * kPrefillRows * SW +
+                  (size_t)warp * kPreRowChunk * kBatch * kPrePartStride;  // this warp's [32][36] partials
+    float *pjs = psm + (size_t)kPrefillRows * hs + (size_t)kAttnGroupWarps * kPrefillRows * SW +
+                 (size_t)kAttnGroupWarps * kPreRowChunk * kBatch * kPrePartStride + (size_t)warp * 40;  // [4][8], [4]
+    auto row_end = [&](int r) { return min(g.first + r / kv_mul + 1, t0 + g.chunk); };
     for (int tb = t0 + warp * kBatch; tb < tmax; tb += kAttnGroupWarps * kBatch) {
         float4 kk[kBatch], vv[kBatch];
         #pragma unroll
@@ -1018,43 +1037,84 @@ __global__ void __launch_bounds__(kAttnGroupThreads) prefill_attn_kernel(const A
             kk[j] = (t < tmax && act) ? load_kv4<F32>(a.k_cache, head_base + (size_t)t * hs) : make_float4(0, 0, 0, 0);
             vv[j] = (t < tmax && act) ? load_kv4<F32>(a.v_cache, head_base + (size_t)t * hs) : make_float4(0, 0, 0, 0);
         }
-        for (int r = 0; r < rows; ++r) {
-            const int t1 = min(g.first + r / kv_mul + 1, t0 + g.chunk);  // this row's end of the split
-            if (tb >= t1) continue;  // the decode step's warp has left its loop
-            float *sw = stt + ((size_t)warp * kPrefillRows + r) * SW;
-            const float4 qv = act ? *reinterpret_cast<const float4 *>(qs + (size_t)r * hs + d0) : make_float4(0, 0, 0, 0);
-            float4 am = act ? *reinterpret_cast<const float4 *>(sw + 4 + d0) : make_float4(0, 0, 0, 0);
-            const float mx = sw[0], l = sw[1];
-            // positions at or past t1 are the decode step's zero rows: score -inf, value 0
-            float sc[kBatch];
-            float bmax = -INFINITY;
-            #pragma unroll
-            for (int j = 0; j < kBatch; ++j) {
-                const float d = warp_sum(dot4(qv, kk[j]));
-                sc[j] = (tb + j < t1) ? __fdiv_rn(d, sq) : -INFINITY;
-                bmax = fmaxf(bmax, sc[j]);
-            }
-            const float mnew = fmaxf(mx, bmax);
-            const float rescale = expf(mx - mnew);
-            float lm = __fmul_rn(l, rescale);
-            am = make_float4(__fmul_rn(am.x, rescale), __fmul_rn(am.y, rescale), __fmul_rn(am.z, rescale),
-                             __fmul_rn(am.w, rescale));
-            #pragma unroll
-            for (int j = 0; j < kBatch; ++j) {
-                const float pj = expf(sc[j] - mnew);
-                const float4 v = (tb + j < t1) ? vv[j] : make_float4(0, 0, 0, 0);
-                lm = __fadd_rn(lm, pj);
-                am.x = __fmaf_rn(pj, v.x, am.x);
-                am.y = __fmaf_rn(pj, v.y, am.y);
-                am.z = __fmaf_rn(pj, v.z, am.z);
-                am.w = __fmaf_rn(pj, v.w, am.w);
+        for (int rc = 0; rc < rows; rc += kPreRowChunk) {
+            const int nr = min(kPreRowChunk, rows - rc);
+            // (a) partial dots: part[rr * 8 + j][lane]
+            for (int rr = 0; rr < nr; ++rr) {
+                if (tb >= row_end(rc + rr)) continue;  // the decode step's warp has left its loop for this row
+                const float4 qv =
+                    act ? *reinterpret_cast<const float4 *>(qs + (size_t)(rc + rr) * hs + d0) : make_float4(0, 0, 0, 0);
+                #pragma unroll
+                for (int j = 0; j < kBatch; ++j) part[(rr * kBatch + j) * kPrePartStride + lane] = dot4(qv, kk[j]);
             }
             __syncwarp();
-            if (lane == 0) {
-                sw[0] = mnew;
-                sw[1] = lm;
+            // (b) lane = rr * 8 + j
+            {
+                const int rr = lane >> 3, j = lane & 7, r = rc + rr;
+                const int t1 = rr < nr ? row_end(r) : 0;
+                const bool live = rr < nr && tb < t1;  // the same on the row's 8 lanes
+                float v[32];
+                const float4 *pv = reinterpret_cast<const float4 *>(part + lane * kPrePartStride);
+                #pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float4 f = pv[i];
+                    v[4 * i] = f.x;
+                    v[4 * i + 1] = f.y;
+                    v[4 * i + 2] = f.z;
+                    v[4 * i + 3] = f.w;
+                }
+                #pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    #pragma unroll
+                    for (int l = 0; l < o; ++l) v[l] = __fadd_rn(v[l], v[l + o]);
+                }
+                // score = q.k / sqrtf(head_size) (src/transformer.c:158-163)
+                const float sc = (live && tb + j < t1) ? __fdiv_rn(v[0], sq) : -INFINITY;
+                float bmax = sc;
+                bmax = fmaxf(bmax, __shfl_xor_sync(FULL, bmax, 4));
+                bmax = fmaxf(bmax, __shfl_xor_sync(FULL, bmax, 2));
+                bmax = fmaxf(bmax, __shfl_xor_sync(FULL, bmax, 1));
+                float *sw = stt + ((size_t)warp * kPrefillRows + (live ? r : 0)) * SW;
+                const float mx = live ? sw[0] : 0.0f, l = live ? sw[1] : 0.0f;
+                const float mnew = fmaxf(mx, bmax);
+                const float rescale = expf(mx - mnew);
+                const float pj = expf(sc - mnew);
+                float lm = __fmul_rn(l, rescale);
+                #pragma unroll
+                for (int jj = 0; jj < kBatch; ++jj) lm = __fadd_rn(lm, __shfl_sync(FULL, pj, (lane & ~7) + jj));
+                __syncwarp();
+                if (live) {
+                    pjs[rr * kBatch + j] = pj;
+                    if (j == 0) {
+                        pjs[kPreRowChunk * kBatch + rr] = rescale;
+                        sw[0] = mnew;
+                        sw[1] = lm;
+                    }
+                }
             }
-            if (act) *reinterpret_cast<float4 *>(sw + 4 + d0) = am;
+            __syncwarp();
+            // (c) acc = acc * rescale, then fma(p_j, v_j, acc); positions at or past t1 are zero rows
+            for (int rr = 0; rr < nr; ++rr) {
+                const int r = rc + rr, t1 = row_end(r);
+                if (tb >= t1) continue;
+                float *sw = stt + ((size_t)warp * kPrefillRows + r) * SW;
+                if (act) {
+                    const float rescale = pjs[kPreRowChunk * kBatch + rr];
+                    float4 am = *reinterpret_cast<const float4 *>(sw + 4 + d0);
+                    am = make_float4(__fmul_rn(am.x, rescale), __fmul_rn(am.y, rescale), __fmul_rn(am.z, rescale),
+                                     __fmul_rn(am.w, rescale));
+                    #pragma unroll
+                    for (int j = 0; j < kBatch; ++j) {
+                        const float pj = pjs[rr * kBatch + j];
+                        const float4 vj = (tb + j < t1) ? vv[j] : make_float4(0, 0, 0, 0);
+                        am.x = __fmaf_rn(pj, vj.x, am.x);
+                        am.y = __fmaf_rn(pj, vj.y, am.y);
+                        am.z = __fmaf_rn(pj, vj.z, am.z);
+                        am.w = __fmaf_rn(pj, vj.w, am.w);
+                    }
+                    *reinterpret_cast<float4 *>(sw + 4 + d0) = am;
+                }
+            }
             __syncwarp();
         }
     }
@@ -1200,7 +1260,9 @@ cudaError_t launch_prefill_attn(const AttnArgs &a, int pos0, const PrefillGroup 
                                 size_t count_stride, cudaStream_t st) {
     if (ngroups < 1 || items < 1 || items > 0x7FFFFFFFLL || a.head_size > 128 || a.head_size % 4) return cudaErrorInvalidValue;
     const size_t smem = sizeof(float) * ((size_t)kPrefillRows * a.head_size +
-                                         (size_t)kAttnGroupWarps * kPrefillRows * (a.head_size + 4));
+                                         (size_t)kAttnGroupWarps * kPrefillRows * (a.head_size + 4) +
+                                         (size_t)kAttnGroupWarps * kPreRowChunk * kBatch * kPrePartStride +
+                                         (size_t)kAttnGroupWarps * 40);
     if (a.kv_f32) {
         if (smem > 48 * 1024) {
             const cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
