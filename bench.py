@@ -36,6 +36,14 @@ sys.path.insert(0, ROOT)
 
 PROMPT_LEN = 32
 GEN_LEN = 256
+
+
+def _models():
+    from diolkos_b200 import synth
+
+    # name -> (shape, prompt positions, greedy tokens timed, label)
+    return {"7b": (synth.LLAMA7B, PROMPT_LEN, GEN_LEN, "llama2-7b-shape"),
+            "70b": (synth.LLAMA70B, 512, 128, "llama2-70b-shape")}
 SEED = 20260
 GEMV_SHAPES = [(4096, 4096), (11008, 4096), (4096, 11008), (32000, 4096)]  # [out x in]
 # The GEMVs of one 7B-shape decode step: (rows, cols, launches per step) -- fused q|k|v, wo, the
@@ -57,6 +65,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["decode", "gemv", "gemm"], default="decode")
     ap.add_argument("--kv", choices=["f32", "bf16"], default="f32")
+    ap.add_argument("--model", choices=["7b", "70b"], default="7b",
+                    help="7b: the headline workload; 70b: the 70B-shape GQA model, 512-token prompt, 128 tokens")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the long-prompt prefill and GEMM measurements")
     ap.add_argument("--layers", type=int, default=0,
@@ -426,7 +436,7 @@ def run_decode(args):
 
     from diolkos_b200 import synth, tp
 
-    cfg = synth.LLAMA7B
+    cfg, P, G, model_name = _models()[args.model]
     if args.layers > 0:
         cfg = cfg.replace(n_layers=args.layers)
     kv_f32 = args.kv == "f32"
@@ -457,8 +467,7 @@ def run_decode(args):
 
     m = build_model(cfg, kv_f32, SEED, rank, world, local)
     stream = torch.cuda.ExternalStream(m.stream)
-    prompt = synth.seeded_prompt(SEED, PROMPT_LEN, cfg.vocab_size)
-    P, G = PROMPT_LEN, GEN_LEN
+    prompt = synth.seeded_prompt(SEED, P, cfg.vocab_size)
 
     def one_step(record=None):
         m.set_tokens(prompt, n_forced=P)
@@ -547,7 +556,7 @@ def run_decode(args):
     launches = sum(c for _, _, c in decode_gemvs)
     gemv_gbps = mix_bytes / mix_us / 1e3
     cpu = None
-    if not args.no_cpu_baseline and world == 1:
+    if not args.no_cpu_baseline and world == 1 and args.model == "7b":
         try:
             cb = CpuReference(cfg)
             cb.sample()
@@ -562,15 +571,16 @@ def run_decode(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(decode_ms / args.steps, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
         "data": "synthetic (seeded N(0,0.02) weights, seeded prompt)",
-        "config": {"workload": "llama2-7b-shape q8_0 decode: 32-token prompt, then 256 greedy tokens timed"
+        "config": {"workload": f"{model_name} q8_0 decode: {P}-token prompt, then {G} greedy tokens timed"
                                + (f" ({cfg.n_layers} layers: profiling case)" if args.layers else ""),
-                   "model": "llama2-7b-shape", "dim": cfg.dim, "hidden": cfg.hidden_dim, "layers": cfg.n_layers,
+                   "model": model_name, "dim": cfg.dim, "hidden": cfg.hidden_dim, "layers": cfg.n_layers,
                    "heads": cfg.n_heads, "kv_heads": cfg.n_kv_heads, "vocab": cfg.vocab_size,
                    "seq_len": cfg.seq_len, "kv_cache": args.kv, "global_batch": 1,
                    "parallelism": "single GPU" if world == 1 else
                    f"tp{world}: heads / w1,w3 rows / classifier rows per GPU, wo and w2 partial sums "
                    f"exchanged inside the GEMVs over NVLink peer memory",
-                   "l2": "weights (7.4 GB) exceed L2; every token streams them from HBM"},
+                   "l2": f"weights ({weight_bytes_per_token(cfg) / 1e9:.1f} GB) exceed L2; every token streams them "
+                         f"from HBM"},
         "ms_per_token": round(ms_per_tok, 4),
         # the prefill launches 10 kernels per layer and chunk (activation, matmul, KV write, attention,
         # then activation + matmul for wo, w1|w3, w2), then one persistent step per token

@@ -304,3 +304,55 @@ def test_generate_with_prefill_equals_stepped_prompt(tiny_weights):
         del os.environ["DIOLKOS_PREFILL"]
     assert len(gen) > 0
     np.testing.assert_array_equal(gen, stepped)
+
+
+def _device_model(cfg, seed, kv_f32=True):
+    """A seeded random model built on the GPU (bf16 N(0, 0.02) weights quantised by the library)."""
+    import torch
+
+    from diolkos_b200 import ops
+    from diolkos_b200.model import Model, weight_id
+
+    m = Model(cfg, kv_f32=kv_f32)
+    g = torch.Generator(device="cuda")
+    for idx, (name, kind, shape) in enumerate(synth.tensor_specs(cfg)):
+        which, layer = weight_id(name)
+        n = int(np.prod(shape))
+        if kind == "norm":
+            m.set_weight_device(which, layer, torch.ones(n, device="cuda", dtype=torch.float32))
+            continue
+        g.manual_seed(seed * 1000003 + idx)
+        w = (torch.randn(n, generator=g, device="cuda", dtype=torch.float32) * 0.02).to(torch.bfloat16)
+        q, s = ops.quantize_bf16(w.view(torch.int16))
+        m.set_weight_device(which, layer, q, s)
+    m.finalize()
+    return m
+
+
+def test_70b_shape_layer_prefill_and_decode():
+    """One layer of the 70B shape (dim 8192, hidden 28672, 64 heads over 8 KV heads): the wide
+    activation prologue, 28672-column matmuls on the tensor cores and 8 query heads per KV head in the
+    prefill attention.  The prefill leaves the KV cache stepped decode leaves (bit-exact logits
+    after it), logits are finite, and generate equals the argmax over forward."""
+    cfg = synth.LLAMA70B.replace(n_layers=1, seq_len=256)
+    m = _device_model(cfg, 70)
+    P = 150
+    prompt = np.random.default_rng(70).integers(3, cfg.vocab_size, P).astype(np.int32)
+    m.set_tokens(prompt, n_forced=P)
+    m.prefill(0, P - 1)
+    after_prefill = m.forward(int(prompt[P - 1]), P - 1)
+    assert np.isfinite(after_prefill).all()
+    for pos in range(P):
+        stepped = m.forward(int(prompt[pos]), pos)
+    np.testing.assert_array_equal(_logits_bits(after_prefill), _logits_bits(stepped))
+    gen = m.generate(prompt[:8], 24)
+    tok, out = int(prompt[0]), []
+    for pos in range(24):
+        lg = m.forward(tok, pos)
+        nxt = int(prompt[pos + 1]) if pos < 7 else int(np.argmax(lg))
+        if pos >= 7:
+            out.append(nxt)
+        if nxt == 1:
+            break
+        tok = nxt
+    np.testing.assert_array_equal(gen, np.array(out, np.int32))
