@@ -66,7 +66,11 @@ class Model:
                                              s.ctypes.data if s is not None else None))
 
     def set_weight_device(self, which: int, layer: int, q, s=None):
-        """Device tensors (torch): Q8_0 planar (int8, fp32) or a fp32 vector."""
+        """Device tensors (torch): Q8_0 planar (int8, fp32) or a fp32 vector.  The engine copies on its
+        own stream, so the torch stream that produced the tensors is synchronised first."""
+        import torch
+
+        torch.cuda.current_stream(q.device).synchronize()
         N.check(N.lib().dk_model_set_weight_device(self.h, which, layer, q.data_ptr(),
                                                     s.data_ptr() if s is not None else None))
 

@@ -186,7 +186,9 @@ void dk_model_destroy(dk_model *m);
  * F32 weights: q = float[n], scale = NULL.  layer = -1 for the non-layer weights. */
 int dk_model_set_weight(dk_model *m, int which, int layer, const void *q, const float *scale);
 /* Same, with the planar Q8_0 (or F32) data in DEVICE memory of the model's GPU.  Both calls return
- * once the data has been copied: the caller may free or reuse its buffers afterwards. */
+ * once the data has been copied: the caller may free or reuse its buffers afterwards.  The copy runs
+ * on the model's own (non-blocking) stream, so the work that produced the data must be complete
+ * before the call (e.g. synchronise the stream that wrote it). */
 int dk_model_set_weight_device(dk_model *m, int which, int layer, const void *q, const float *scale);
 /* Check that every weight is present and capture the per-token CUDA graph. */
 int dk_model_finalize(dk_model *m);
