@@ -5,6 +5,8 @@
 
 #include "dk_internal.h"
 
+#include <vector>
+
 namespace dk {
 
 static thread_local char g_err[512] = "";
@@ -176,6 +178,36 @@ int dk_attention_decode(float *out, const float *qkv, const float *rope, void *k
     a.err = device_error_word();
     if (!a.err) return set_error(DK_ERR_CUDA, "dk_attention_decode: could not allocate the device error word");
     return cuda_status(launch_attention(a, (cudaStream_t)stream, false), "dk_attention_decode");
+}
+
+int dk_attn_split_plan(int T, int max_splits, int min_chunk, int *nsplit, int *chunk) {
+    if (T < 1 || max_splits < 1 || min_chunk < 1 || !nsplit || !chunk)
+        return set_error(DK_ERR_INVALID, "dk_attn_split_plan: bad arguments");
+    attn_split_plan(T, max_splits, min_chunk, *nsplit, *chunk);
+    return DK_OK;
+}
+
+int dk_prefill_attn_plan(int n_heads, int n_kv_heads, int max_splits, int min_chunk, int pos0, int ntok,
+                         int *groups_out, long long *items) {
+    if (n_heads < 1 || n_kv_heads < 1 || n_heads % n_kv_heads || max_splits < 1 || min_chunk < 1 || pos0 < 0 ||
+        ntok < 1 || !groups_out)
+        return -set_error(DK_ERR_INVALID, "dk_prefill_attn_plan: bad arguments");
+    AttnArgs a;
+    a.n_heads = n_heads;
+    a.n_kv_heads = n_kv_heads;
+    a.max_splits = max_splits;
+    a.min_chunk = min_chunk;
+    std::vector<PrefillGroup> g((size_t)ntok);
+    const int n = prefill_attn_plan(a, pos0, ntok, g.data(), items);
+    for (int i = 0; i < n; ++i) {
+        int *o = groups_out + 5 * (size_t)i;
+        o[0] = g[i].first;
+        o[1] = g[i].count;
+        o[2] = g[i].nsplit;
+        o[3] = g[i].chunk;
+        o[4] = g[i].item0;
+    }
+    return n;
 }
 
 int dk_gemm_trace(unsigned long long *out, size_t n, int *ctas, int *blocks) {

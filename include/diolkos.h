@@ -83,8 +83,8 @@ int dk_matmul_q8_0_q(float *out, const int8_t *xq, const float *xs, const uint8_
  * weights while the previous one finishes, which is how the decode engine runs the kernel. */
 int dk_matmul_q8_0_batch(float *out, const float *x, const uint8_t *const *w_packed, int count, int n,
                          int d, void *stream);
-/* matmul_Q8_0 for a batch of `ntok` already-quantised activation vectors (prompt prefill; the
- * reference calls matmul once per token): out[t*d + i] = W[i] . x_t (accumulate != 0: +=), from the
+/* matmul_Q8_0 (src/utils.c:106-138) for a batch of `ntok` already-quantised activation vectors
+ * (prompt prefill; the reference calls matmul once per token): out[t*d + i] = W[i] . x_t (accumulate != 0: +=), from the
  * same packed matrix as dk_matmul_q8_0.  xq int8[ntok][n] (16-byte aligned), xs fp32[ntok][n/32].
  * The int32 group dots come from the tensor cores (tcgen05.mma kind::i8, one MMA per 32-value group);
  * every output is bit-identical to dk_matmul_q8_0_q on that token. */
@@ -237,6 +237,14 @@ int dk_model_trace(dk_model *m, unsigned long long *out, size_t n, int *grid, in
  * them land, 2: its last MMA was issued, 3: fold warp 2 saw them land, 4: fold warp 2 finished it
  * (0: not recorded).  *ctas and *blocks give the dimensions (the first 148 CTAs, 32 blocks). */
 int dk_gemm_trace(unsigned long long *out, size_t n, int *ctas, int *blocks);
+/* Diagnostics (host only, no GPU): the attention's split plan over T positions (the count of splits and
+ * their length; the decode step's attention, src/transformer.c:149-193, split for the GPU), and the
+ * prefill attention's position groups for positions pos0 .. pos0+ntok-1: groups_out receives 5 ints
+ * per group (first position, count, split count, chunk, first item index), capacity ntok groups;
+ * returns the group count and *items the total (group, KV head, split) items. */
+int dk_attn_split_plan(int T, int max_splits, int min_chunk, int *nsplit, int *chunk);
+int dk_prefill_attn_plan(int n_heads, int n_kv_heads, int max_splits, int min_chunk, int pos0, int ntok,
+                         int *groups_out, long long *items);
 /* Bytes of weights one decode step reads on this rank. */
 size_t dk_model_weight_bytes(dk_model *m);
 
