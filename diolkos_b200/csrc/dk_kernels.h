@@ -273,7 +273,7 @@ cudaError_t launch_prefill_kv(const AttnArgs &a, int pos0, int ntok, size_t qkv_
 // Prefill attention items: the prompt positions that share the decode step's split plan (split count and
 // chunk; any chunk when there is one split) go together, at most kPrefillRows (query, head) rows, and
 // one item = (group, KV head, split).
-constexpr int kPrefillRows = 16;
+constexpr int kPrefillRows = 8;
 struct PrefillGroup {
     int first, count;   // positions first .. first+count-1
     int nsplit, chunk;  // their split plan (one split: chunk = the last position + 1)

@@ -981,7 +981,7 @@ constexpr int kPrePartStride = 36;  // floats per (row, position) block of lane 
 //       through shuffles;
 //   (c) lanes over head dims: acc = acc * rescale, then acc = fma(p_j, v_j, acc) in position order.
 template <bool F32>
-__global__ void __launch_bounds__(kAttnGroupThreads) prefill_attn_kernel(const AttnArgs a, int pos0,
+__global__ void __launch_bounds__(kAttnGroupThreads, 8) prefill_attn_kernel(const AttnArgs a, int pos0,
                                                                          const PrefillGroup *groups, int ngroups,
                                                                          size_t qkv_stride, size_t out_stride,
                                                                          size_t work_stride, size_t count_stride) {
