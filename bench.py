@@ -398,7 +398,7 @@ def gemm_bench(cfg, ntok: int = GEMM_TOKENS, reps: int = 8):
     peak, kind = int8_peak()
     ach = tot_ops / tot_us / 1e6
     return {"tokens": ntok, "shapes": out, "achieved_tops": round(ach, 1), "peak_tops": round(peak, 1),
-            "frac": round(ach / peak, 4), "peak_kind": kind, "kernel": "gemm_q8_kernel",
+            "frac": round(ach / peak, 4), "peak_kind": kind, "kernel": "gemm_q8_tma_kernel",
             "what": "one layer's four prefill matmuls at 256 positions (the engine's chunk), int8 multiply-adds x2 "
                     "/ CUDA-event time per launch"}
 

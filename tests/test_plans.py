@@ -53,7 +53,7 @@ def prefill_plan(n_heads, n_kv_heads, max_splits, pos0, ntok):
 def test_prefill_groups_cover_each_item_once_with_the_decode_plan(n_heads, n_kv_heads, max_splits, pos0, ntok):
     g, items = prefill_plan(n_heads, n_kv_heads, max_splits, pos0, ntok)
     kv_mul = n_heads // n_kv_heads
-    rows_max = 16
+    rows_max = 8  # kPrefillRows
     seen = set()
     expect_item0 = 0
     for first, count, nsplit, chunk, item0 in g:
