@@ -7,7 +7,7 @@ Decode workload (N=1): LLaMA-2-7B shape (dim 4096, hidden 11008, 32 layers, 32 h
 vocab 32000, seq_len 4096), random-init weights N(0, 0.02) generated on the GPU from a seed, rounded
 to bf16 and quantised to Q8_0 by the library's load-time quantiser; fp32 KV cache.  One step = a
 seeded 32-token prompt whose 31 forced positions are prefilled in one batch on the tensor cores
-(dk_model_prefill; decode steps under tensor parallelism), then 256 greedy tokens.
+(dk_model_prefill, on every rank under tensor parallelism), then 256 greedy tokens.
 `value` = generated tokens per second of the 256-token decode phase, timed with CUDA events on the
 engine's stream, inputs resident in HBM; the weights (7.4 GB) are far larger than L2, so every token
 streams them from HBM.  `e2e` = the same tokens per second through the C-ABI generate entry point
@@ -473,10 +473,7 @@ def run_decode(args):
         m.set_tokens(prompt, n_forced=P)
         if record:
             record[2].record(stream)
-        if world == 1:
-            m.prefill(0, P - 1)  # the forced prompt positions on the tensor cores
-        else:
-            m.enqueue_steps(0, P - 1)
+        m.prefill(0, P - 1)  # the forced prompt positions on the tensor cores
         if record:
             record[0].record(stream)
         m.enqueue_steps(P - 1, G)
@@ -582,10 +579,11 @@ def run_decode(args):
                    "l2": f"weights ({weight_bytes_per_token(cfg) / 1e9:.1f} GB) exceed L2; every token streams them "
                          f"from HBM"},
         "ms_per_token": round(ms_per_tok, 4),
-        # the prefill launches 10 kernels per layer and chunk (activation, matmul, KV write, attention,
-        # then activation + matmul for wo, w1|w3, w2), then one persistent step per token
-        "gpu_launches": (kernels_per_step * G + (10 * cfg.n_layers * (-(-(P - 1) // GEMM_TOKENS)) if world == 1 else
-                                                 kernels_per_step * (P - 1))) * args.steps,
+        # the prefill launches per chunk 10 kernels per layer (activation, matmul, KV write, attention, then
+        # activation + matmul for wo, w1|w3, w2; tensor parallel: + scatter, signal, wait, reduce after wo
+        # and after w2) and 3 for the last layer (its K/V rows); then one persistent step per token
+        "gpu_launches": (kernels_per_step * G + ((cfg.n_layers - 1) * (10 + (8 if world > 1 else 0)) + 3) *
+                         (-(-(P - 1) // GEMM_TOKENS))) * args.steps,
         "roofline": {"bound": "hbm", "achieved": round(step_gbps, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(step_gbps / hbm, 4),
                      "traffic": (round(NCU_STEP_TRAFFIC_RATIO * rank_bytes) if NCU_STEP_TRAFFIC_RATIO else None),

@@ -279,6 +279,15 @@ struct PrefillGroup {
     int nsplit, chunk;  // their split plan (one split: chunk = the last position + 1)
     int item0;          // index of the group's first item
 };
+// Tensor-parallel prefill exchange (wo / w2 partial sums of a chunk, over NVLink peer memory):
+// scatter: dst[q] + off receives this rank's nf partial floats, for every rank q (system fence after);
+// signal:  every rank's counter cnt[q] + 1 (after the scatter, in stream order);
+// wait:    until *cnt >= target (bounded; DK_ERR_COMM in *err when a rank never arrives);
+// reduce:  x[i] = x[i] + (recv[0][i] + recv[1][i] + ...), ranks in order, recv[q] = recv + q * stride.
+cudaError_t launch_prefill_scatter(const float *src, float *const *dst, int world, size_t off, size_t nf, cudaStream_t st);
+cudaError_t launch_prefill_signal(unsigned long long *const *cnt, int world, cudaStream_t st);
+cudaError_t launch_prefill_wait(const unsigned long long *cnt, unsigned long long target, int *err, cudaStream_t st);
+cudaError_t launch_prefill_reduce(float *x, const float *recv, size_t stride, int world, size_t nf, cudaStream_t st);
 // Fills groups[0 .. n) (capacity ntok) for positions pos0 .. pos0+ntok-1; returns n, *items = total items.
 int prefill_attn_plan(const AttnArgs &a, int pos0, int ntok, PrefillGroup *groups, long long *items);
 cudaError_t launch_prefill_attn(const AttnArgs &a, int pos0, const PrefillGroup *d_groups, int ngroups,

@@ -124,11 +124,17 @@ struct dk_model {
     int8_t *pxq = nullptr;
     unsigned *pcount = nullptr;
     PrefillGroup *pgroups = nullptr;      // the attention's position groups of the current chunk
+    float *ppart = nullptr;               // tensor parallel: this rank's wo / w2 partial rows [chunk][dim]
+    size_t comm_pre = 0;                  // offset of the prefill receive areas in `comm`
+    unsigned long long pex[2] = {0, 0};   // prefill exchanges done per parity (counter targets)
     std::vector<PrefillGroup> h_groups;
     size_t pwork_stride = 0, pcount_stride = 0;
 };
 
 static size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+// Positions per prefill chunk: the tensor-core matmul's token tiles are 32 wide; 256 positions keep
+// the per-position attention scratch of a 7B-shape model near 100 MB.
+static constexpr int kPrefillChunk = 256;
 // Capacity of the per-CTA argmax partials, in CTAs per SM (plan_gemv never launches more).
 static constexpr int kMaxGemvGrid = 4;
 
@@ -297,10 +303,12 @@ dk_model *dk_model_create(const int *cfg, int kv_type, int device, int tp_rank, 
     // ---- tensor-parallel exchange area (its own allocation: it is exported to the peers over IPC)
     if (tp_world > 1) {
         m->comm_ctl = align256((size_t)2 * tp_world * dim * 4);
-        m->comm_bytes = m->comm_ctl + 256;
+        // then the prefill's two receive areas, [rank][chunk position][dim] floats each
+        m->comm_pre = m->comm_ctl + 256;
+        m->comm_bytes = m->comm_pre + 2 * align256((size_t)tp_world * std::min(kPrefillChunk, S) * dim * 4);
         if (cudaMalloc(&m->comm, m->comm_bytes) != cudaSuccess) return fail("exchange area");
         if (cudaMemset(m->comm, 0, m->comm_bytes) != cudaSuccess) return fail("exchange area clear");
-        if (cudaMalloc(&m->d_ptrs, 6 * 8 * sizeof(void *)) != cudaSuccess) return fail("peer pointer tables");
+        if (cudaMalloc(&m->d_ptrs, 10 * 8 * sizeof(void *)) != cudaSuccess) return fail("peer pointer tables");
         m->peer_base.assign(tp_world, nullptr);
         m->peer_opened.assign(tp_world, false);
         m->peer_base[tp_rank] = m->comm;
@@ -442,6 +450,10 @@ static size_t comm_recv_off(const dk_model *m, int par) { return (size_t)par * m
 static size_t comm_cnt_off(const dk_model *m, int par) { return m->comm_ctl + 8 * (size_t)par; }
 static size_t comm_keys_off(const dk_model *m) { return m->comm_ctl + 16; }
 static size_t comm_keys_cnt_off(const dk_model *m) { return m->comm_ctl + 16 + 64; }
+static size_t comm_pcnt_off(const dk_model *m, int par) { return m->comm_ctl + 128 + 8 * (size_t)par; }
+static size_t comm_pre_off(const dk_model *m, int par) {
+    return m->comm_pre + (size_t)par * align256((size_t)m->world * std::min(kPrefillChunk, m->seq_len) * m->dim * 4);
+}
 
 static int enqueue_step(dk_model *m, cudaStream_t st) {
     int launches = 0;
@@ -743,7 +755,7 @@ int dk_model_comm_connect(dk_model *m, const void *handles) {
         m->peer_base[q] = ptr;
         m->peer_opened[q] = true;
     }
-    std::vector<void *> t(6 * 8, nullptr);
+    std::vector<void *> t(10 * 8, nullptr);
     for (int q = 0; q < m->world; ++q) {
         uint8_t *b = static_cast<uint8_t *>(m->peer_base[q]);
         t[0 * 8 + q] = b + comm_recv_off(m, 0);
@@ -752,6 +764,10 @@ int dk_model_comm_connect(dk_model *m, const void *handles) {
         t[3 * 8 + q] = b + comm_cnt_off(m, 1);
         t[4 * 8 + q] = b + comm_keys_off(m);
         t[5 * 8 + q] = b + comm_keys_cnt_off(m);
+        t[6 * 8 + q] = b + comm_pre_off(m, 0);  // prefill receive areas and counters
+        t[7 * 8 + q] = b + comm_pre_off(m, 1);
+        t[8 * 8 + q] = b + comm_pcnt_off(m, 0);
+        t[9 * 8 + q] = b + comm_pcnt_off(m, 1);
     }
     if (int r = cuda_status(cudaMemcpy(m->d_ptrs, t.data(), t.size() * sizeof(void *), cudaMemcpyHostToDevice),
                             "peer table upload"))
@@ -899,11 +915,7 @@ int dk_model_forward(dk_model *m, int token, int pos, float *logits) {
     return DK_OK;
 }
 
-// Positions per prefill chunk: the tensor-core matmul's token tiles are 32 wide; 256 positions keep
-// the per-position attention scratch of a 7B-shape model near 100 MB.
-static constexpr int kPrefillChunk = 256;
-
-static bool prefill_available(const dk_model *m) { return m->world == 1 && m->use_step; }
+static bool prefill_available(const dk_model *m) { return m->use_step && (m->world == 1 || m->connected); }
 
 static int prefill_alloc(dk_model *m) {
     if (m->parena) return DK_OK;
@@ -917,7 +929,8 @@ static int prefill_alloc(dk_model *m) {
     const size_t sz_xq = align256((size_t)C * nmax), sz_xs = align256((size_t)C * (nmax / 32) * 4);
     const size_t sz_work = align256((size_t)C * m->pwork_stride * 4), sz_cnt = align256((size_t)C * m->pcount_stride * 4);
     const size_t sz_groups = align256((size_t)C * sizeof(PrefillGroup));
-    const size_t total = sz_x + sz_qkv + sz_xb + sz_hb + sz_xq + sz_xs + sz_work + sz_cnt + sz_groups;
+    const size_t sz_ppart = m->world > 1 ? align256((size_t)C * m->dim * 4) : 0;
+    const size_t total = sz_x + sz_qkv + sz_xb + sz_hb + sz_xq + sz_xs + sz_work + sz_cnt + sz_groups + sz_ppart;
     if (cudaMalloc(&m->parena, total) != cudaSuccess) {
         m->parena = nullptr;
         return set_error(DK_ERR_NOMEM, "prefill: %zu bytes of scratch", total);
@@ -933,7 +946,8 @@ static int prefill_alloc(dk_model *m) {
     m->pxs = reinterpret_cast<float *>(p); p += sz_xs;
     m->pwork = reinterpret_cast<float *>(p); p += sz_work;
     m->pcount = reinterpret_cast<unsigned *>(p); p += sz_cnt;
-    m->pgroups = reinterpret_cast<PrefillGroup *>(p);
+    m->pgroups = reinterpret_cast<PrefillGroup *>(p); p += sz_groups;
+    m->ppart = sz_ppart ? reinterpret_cast<float *>(p) : nullptr;
     m->h_groups.resize(C);
     m->pchunk = C;
     return DK_OK;
@@ -953,6 +967,23 @@ static int prefill_chunk(dk_model *m, int pos0, int n, cudaStream_t st) {
         a.n = cols; a.pro = pro; a.x = x; a.norm_w = norm; a.emb = m->emb; a.emb_T = m->emb_T;
         a.vocab = m->vocab; a.err = m->err;
         return launch_prefill_act(a, n, m->tokens + pos0, m->pxq, m->pxs, st);
+    };
+    // Tensor parallel: the wo / w2 partial rows (this rank's columns) go to every rank; once all ranks'
+    // rows are in, x += (partial_0 + partial_1 + ...) in rank order -- the decode step's reduce.
+    const bool tp = m->world > 1;
+    const int C = m->pchunk;
+    auto exchange = [&](int par) -> cudaError_t {
+        const size_t nf = (size_t)n * m->dim;
+        cudaError_t e = launch_prefill_scatter(m->ppart, reinterpret_cast<float *const *>(m->d_ptrs + 8 * (6 + par)),
+                                               m->world, (size_t)m->rank * C * m->dim, nf, st);
+        if (!e) e = launch_prefill_signal(reinterpret_cast<unsigned long long *const *>(m->d_ptrs + 8 * (8 + par)),
+                                          m->world, st);
+        m->pex[par] += 1;
+        if (!e) e = launch_prefill_wait(reinterpret_cast<const unsigned long long *>(m->comm + comm_pcnt_off(m, par)),
+                                        m->pex[par] * (unsigned long long)m->world, m->err, st);
+        if (!e) e = launch_prefill_reduce(m->px, reinterpret_cast<const float *>(m->comm + comm_pre_off(m, par)),
+                                          (size_t)C * m->dim, m->world, nf, st);
+        return e;
     };
     auto mm = [&](const uint8_t *w, int cols, int rows, int T, int epi, float *out) -> cudaError_t {
         GemmArgs g;
@@ -980,14 +1011,21 @@ static int prefill_chunk(dk_model *m, int pos0, int n, cudaStream_t st) {
         t.k_cache = static_cast<uint8_t *>(m->kcache) + (size_t)l * m->kv_layer_elems * esz;
         t.v_cache = static_cast<uint8_t *>(m->vcache) + (size_t)l * m->kv_layer_elems * esz;
         if (!e) e = launch_prefill_kv(t, pos0, n, (size_t)qkv_rows, st);
+        // The last layer's attention and MLP feed only these positions' logits, which nothing reads: the
+        // decode step recomputes the last prompt position.  Its K/V rows are all that is kept.
+        if (!e && l == m->n_layers - 1) break;
         if (!e) e = launch_prefill_attn(t, pos0, m->pgroups, ngroups, items, (size_t)qkv_rows, (size_t)m->l_dim,
                                         m->pwork_stride, m->pcount_stride, st);
         if (!e) e = act(PRO_F32, m->pxb, nullptr, m->l_dim);
-        if (!e) e = mm(ly.wo, m->l_dim, m->dim, m->p_wo.T, EPI_ADD, m->px);
+        if (!e) e = tp ? mm(ly.wo, m->l_dim, m->dim, m->p_wo.T, EPI_STORE, m->ppart)
+                       : mm(ly.wo, m->l_dim, m->dim, m->p_wo.T, EPI_ADD, m->px);
+        if (!e && tp) e = exchange(0);
         if (!e) e = act(PRO_RMS, m->px, ly.rms_ffn, m->dim);
         if (!e) e = mm(ly.w13, m->dim, 2 * m->l_hidden, m->p_w13.T, EPI_SWIGLU, m->phb);
         if (!e) e = act(PRO_F32, m->phb, nullptr, m->l_hidden);
-        if (!e) e = mm(ly.w2, m->l_hidden, m->dim, m->p_w2.T, EPI_ADD, m->px);
+        if (!e) e = tp ? mm(ly.w2, m->l_hidden, m->dim, m->p_w2.T, EPI_STORE, m->ppart)
+                       : mm(ly.w2, m->l_hidden, m->dim, m->p_w2.T, EPI_ADD, m->px);
+        if (!e && tp) e = exchange(1);
         if (e) return set_error(DK_ERR_CUDA, "prefill layer %d: %s", l, cudaGetErrorString(e));
     }
     return DK_OK;
@@ -1005,7 +1043,7 @@ int dk_model_prefill(dk_model *m, int pos0, int n_positions) {
     if (int r = need(m)) return r;
     if (!m->finalized) return set_error(DK_ERR_STATE, "dk_model_prefill: model not finalized");
     if (!prefill_available(m))
-        return set_error(DK_ERR_STATE, "dk_model_prefill: needs a single-rank model on the persistent step");
+        return set_error(DK_ERR_STATE, "dk_model_prefill: needs the persistent step (and connected ranks)");
     if (pos0 < 0 || n_positions < 0 || pos0 + n_positions > m->seq_len)
         return set_error(DK_ERR_INVALID, "dk_model_prefill: positions [%d, %d) exceed seq_len %d", pos0,
                          pos0 + n_positions, m->seq_len);

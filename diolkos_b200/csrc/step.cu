@@ -1207,6 +1207,66 @@ __global__ void __launch_bounds__(kAttnGroupThreads, 8) prefill_attn_kernel(cons
 
 }  // namespace
 
+namespace {
+
+// ---- tensor-parallel prefill exchange ----------------------------------------------------------------
+// The partial rows of wo / w2 (this rank's columns), stored to every rank's receive area with plain
+// peer stores, then a system-scope fence so that a rank that sees the counter sees the rows.
+__global__ void prefill_scatter_kernel(const float4 *src, float *const *dst, int world, size_t off, size_t n4) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+        const float4 v = __ldcg(src + i);
+        for (int q = 0; q < world; ++q) reinterpret_cast<float4 *>(dst[q] + off)[i] = v;
+    }
+    __threadfence_system();
+}
+__global__ void prefill_signal_kernel(unsigned long long *const *cnt, int world) {
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        for (int q = 0; q < world; ++q) atomicAdd_system(cnt[q], 1ull);
+    }
+}
+__global__ void prefill_wait_kernel(const unsigned long long *cnt, unsigned long long target, int *err) {
+    if (threadIdx.x == 0 && !wait_counter(cnt, target, err)) atomicOr(err, DK_ERR_COMM);
+}
+// x + (partial_0 + partial_1 + ...), ranks in order: the decode step's reduce prologue, element by element.
+__global__ void prefill_reduce_kernel(float4 *x, const float4 *recv, size_t stride4, int world, size_t n4) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+        float4 t = __ldcg(recv + i);
+        for (int q = 1; q < world; ++q) {
+            const float4 u = __ldcg(recv + (size_t)q * stride4 + i);
+            t = make_float4(__fadd_rn(t.x, u.x), __fadd_rn(t.y, u.y), __fadd_rn(t.z, u.z), __fadd_rn(t.w, u.w));
+        }
+        const float4 v = x[i];
+        x[i] = make_float4(__fadd_rn(v.x, t.x), __fadd_rn(v.y, t.y), __fadd_rn(v.z, t.z), __fadd_rn(v.w, t.w));
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_prefill_scatter(const float *src, float *const *dst, int world, size_t off, size_t nf, cudaStream_t st) {
+    if (nf % 4 || off % 4 || world < 1 || world > 8) return cudaErrorInvalidValue;
+    const size_t n4 = nf / 4;
+    const unsigned blocks = (unsigned)std::min<size_t>((n4 + 255) / 256, 4096);
+    prefill_scatter_kernel<<<blocks ? blocks : 1, 256, 0, st>>>(reinterpret_cast<const float4 *>(src), dst, world, off, n4);
+    return cudaGetLastError();
+}
+cudaError_t launch_prefill_signal(unsigned long long *const *cnt, int world, cudaStream_t st) {
+    prefill_signal_kernel<<<1, 32, 0, st>>>(cnt, world);
+    return cudaGetLastError();
+}
+cudaError_t launch_prefill_wait(const unsigned long long *cnt, unsigned long long target, int *err, cudaStream_t st) {
+    prefill_wait_kernel<<<1, 32, 0, st>>>(cnt, target, err);
+    return cudaGetLastError();
+}
+cudaError_t launch_prefill_reduce(float *x, const float *recv, size_t stride, int world, size_t nf, cudaStream_t st) {
+    if (nf % 4 || stride % 4) return cudaErrorInvalidValue;
+    const size_t n4 = nf / 4;
+    const unsigned blocks = (unsigned)std::min<size_t>((n4 + 255) / 256, 4096);
+    prefill_reduce_kernel<<<blocks ? blocks : 1, 256, 0, st>>>(reinterpret_cast<float4 *>(x),
+                                                               reinterpret_cast<const float4 *>(recv), stride / 4, world, n4);
+    return cudaGetLastError();
+}
+
 int prefill_attn_plan(const AttnArgs &a, int pos0, int ntok, PrefillGroup *groups, long long *items) {
     const int kv_mul = a.n_heads / a.n_kv_heads;
     const int qmax = std::max(1, kPrefillRows / kv_mul);

@@ -199,10 +199,10 @@ int dk_model_finalize(dk_model *m);
 int dk_model_forward(dk_model *m, int token, int pos, float *logits);
 /* Greedy generation with the reference generate() rules (src/bin/localinfer.c:42-99): prompt
  * tokens are forced, then argmax tokens (first index wins ties) are fed back; stops after `steps`
- * positions or when the sampled token is 1.  The whole loop runs on the GPU: on a single-rank model
- * the forced positions (all prompt tokens but the last) run as one batched prefill on the tensor
- * cores, whose KV-cache entries equal the decode step's bit for bit; with tensor parallelism (or
- * DIOLKOS_PREFILL=0) they are decode steps.  out receives the generated (non-forced) tokens, *n_out
+ * positions or when the sampled token is 1.  The whole loop runs on the GPU: the forced positions
+ * (all prompt tokens but the last) run as one batched prefill on the tensor cores, whose KV-cache
+ * entries equal the decode step's bit for bit (tensor parallel too: call it on every rank);
+ * DIOLKOS_PREFILL=0 steps them instead.  out receives the generated (non-forced) tokens, *n_out
  * their count.  Host buffers. */
 int dk_model_generate(dk_model *m, const int *prompt, int n_prompt, int steps, int *out, int *n_out);
 
@@ -214,8 +214,11 @@ int dk_model_enqueue_steps(dk_model *m, int pos0, int n_steps);
 /* Prompt prefill: runs positions [pos0, pos0 + n_positions) through every layer at once for the
  * tokens in the device token buffer, writing their KV-cache entries exactly as decode steps at those
  * positions would (the reference forwards prompt tokens one by one, src/bin/localinfer.c:60-73);
- * no logits.  Int8 tensor-core matmuls (tcgen05), chunks of up to 256 positions.  Single-rank models
- * on the persistent decode step only (DK_ERR_STATE otherwise).  Enqueued, not synchronised. */
+ * no logits.  Int8 tensor-core matmuls (tcgen05), chunks of up to 256 positions.  Tensor parallel:
+ * every rank makes the same call; the wo / w2 partial sums cross NVLink once per layer each and are
+ * summed in rank order like the decode step's (a rank that never arrives makes the others' waits end
+ * with DK_ERR_COMM).  Needs the persistent decode step (DK_ERR_STATE otherwise).  Enqueued, not
+ * synchronised. */
 int dk_model_prefill(dk_model *m, int pos0, int n_positions);
 int dk_model_get_tokens(dk_model *m, int *tokens, int n_tokens);
 int dk_model_sync(dk_model *m);

@@ -222,7 +222,7 @@ def test_dim4096_model_vs_oracle(port):
 
 # 32 KV heads of 32 dims: the decode attention's split count reaches its cap (ceil(5 * SMs / 32): 24 on
 # 148 SMs) at position 384, where a chunk rounded up can leave the last split without positions.
-CAPPED = synth.Config(dim=1024, hidden_dim=256, n_layers=1, n_heads=32, n_kv_heads=32, vocab_size=256, seq_len=600)
+CAPPED = synth.Config(dim=1024, hidden_dim=256, n_layers=2, n_heads=32, n_kv_heads=32, vocab_size=256, seq_len=600)
 
 
 def test_capped_split_plan_vs_oracle(port):
@@ -263,7 +263,8 @@ def _logits_bits(a):
 )
 def test_prefill_equals_decode_steps(port, tiny_weights, shape, kv_f32, P):
     """The batched prefill (tensor-core matmuls over the prompt positions) leaves the KV cache exactly
-    as decode steps at those positions do: the logits of the last prompt position, decoded after the
+    as decode steps at those positions do (every model here has 2 layers or more: the prefill stops
+    after the last layer's K/V rows, so only earlier layers run attention and the MLP): the logits of the last prompt position, decoded after the
     prefill, equal bit for bit those decoded after stepping every prompt position."""
     from oracle import load_port_weights
 
@@ -273,12 +274,12 @@ def test_prefill_equals_decode_steps(port, tiny_weights, shape, kv_f32, P):
         cfg = synth.Config(dim=512, hidden_dim=1024, n_layers=2, n_heads=8, n_kv_heads=1, vocab_size=2048, seq_len=512)
         by_name = load_port_weights(port, cfg, 77)[1]
     elif shape == "swiglu":
-        cfg = synth.Config(dim=512, hidden_dim=4096, n_layers=1, n_heads=8, n_kv_heads=8, vocab_size=512, seq_len=128)
+        cfg = synth.Config(dim=512, hidden_dim=4096, n_layers=2, n_heads=8, n_kv_heads=8, vocab_size=512, seq_len=128)
         by_name = load_port_weights(port, cfg, 95)[1]
     elif shape == "capped":
         cfg, by_name = CAPPED, load_port_weights(port, CAPPED, 93)[1]
     else:
-        cfg = synth.Config(dim=4096, hidden_dim=1024, n_layers=1, n_heads=32, n_kv_heads=8, vocab_size=1000, seq_len=64)
+        cfg = synth.Config(dim=4096, hidden_dim=1024, n_layers=2, n_heads=32, n_kv_heads=8, vocab_size=1000, seq_len=64)
         by_name = load_port_weights(port, cfg, 91)[1]
     m = _gpu_model(cfg, by_name, kv_f32=kv_f32)
     prompt = np.random.default_rng(P).integers(3, cfg.vocab_size, P).astype(np.int32)
@@ -330,11 +331,11 @@ def _device_model(cfg, seed, kv_f32=True):
 
 
 def test_70b_shape_layer_prefill_and_decode():
-    """One layer of the 70B shape (dim 8192, hidden 28672, 64 heads over 8 KV heads): the wide
+    """Two layers of the 70B shape (dim 8192, hidden 28672, 64 heads over 8 KV heads): the wide
     activation prologue, 28672-column matmuls on the tensor cores and 8 query heads per KV head in the
     prefill attention.  The prefill leaves the KV cache stepped decode leaves (bit-exact logits
     after it), logits are finite, and generate equals the argmax over forward."""
-    cfg = synth.LLAMA70B.replace(n_layers=1, seq_len=256)
+    cfg = synth.LLAMA70B.replace(n_layers=2, seq_len=256)
     m = _device_model(cfg, 70)
     P = 150
     prompt = np.random.default_rng(70).integers(3, cfg.vocab_size, P).astype(np.int32)

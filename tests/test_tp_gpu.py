@@ -114,3 +114,69 @@ def test_tp2_matches_single_gpu(cfg_name):
     n = min(len(ref_toks), len(res[0][1]))
     first_div = next((i for i in range(n) if ref_toks[i] != res[0][1][i]), n)
     assert first_div >= min(bound, n), (first_div, bound, ref_toks[:16], res[0][1][:16])
+
+
+def _rank_prefill(rank, world, port, out_q, cfg_name):
+    CFG = CFGS[cfg_name]
+    import torch.distributed as dist
+
+    from diolkos_b200 import tp
+    from diolkos_b200.model import Model
+    from oracle import Port, load_port_weights
+
+    torch.cuda.set_device(rank)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        _, by_name = load_port_weights(Port(), CFG, SEED)
+        m = Model(CFG, kv_f32=True, device=rank, tp_rank=rank, tp_world=world)
+        m.load_named(by_name)
+        tp.connect(m)
+        m.finalize()
+        P = 40
+        prompt = synth.seeded_prompt(5, P, CFG.vocab_size)
+        m.set_tokens(prompt, n_forced=P)
+        m.prefill(0, P - 1)
+        after = m.forward(int(prompt[P - 1]), P - 1)
+        for pos in range(P):
+            stepped = m.forward(int(prompt[pos]), pos)
+        gen = m.generate(prompt[:12], STEPS)
+        os.environ["DIOLKOS_PREFILL"] = "0"
+        gen_stepped = m.generate(prompt[:12], STEPS)
+        del os.environ["DIOLKOS_PREFILL"]
+        err = m.device_error()
+        m.close()
+        out_q.put((rank, after, stepped, gen, gen_stepped, err))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("cfg_name", sorted(CFGS))
+def test_tp2_prefill_equals_stepped_decode(cfg_name):
+    """Tensor-parallel prefill: the wo / w2 partial rows of a chunk cross NVLink and are summed in rank
+    order, as the decode step sums them; so the KV cache after a prefill is the one stepped decode leaves
+    on every rank (bit-exact logits of this rank's classifier rows after it), and generate gives the same
+    tokens with and without the prefill."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_prefill, args=(r, world, port, q, cfg_name)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r, after, stepped, gen, gen_stepped, err = q.get(timeout=300)
+        res[r] = (after, stepped, gen, gen_stepped, err)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r, (after, stepped, gen, gen_stepped, err) in res.items():
+        assert err == 0, (r, err)
+        rows = ~np.isnan(stepped)  # this rank's classifier rows
+        assert rows.any()
+        np.testing.assert_array_equal(after[rows].view(np.uint32), stepped[rows].view(np.uint32))
+        assert len(gen) > 0
+        np.testing.assert_array_equal(gen, gen_stepped)
