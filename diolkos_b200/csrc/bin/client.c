@@ -113,8 +113,23 @@ static int run_rank(int rank, int world, Shared *sh, const char *model_dir, cons
     barrier(sh, world);
 
     long start = 0;
-    int token = prompt_tokens[0], pos = 0, next;
-    while (pos < steps) {
+    int token = prompt_tokens[0], pos = 0, next = 0, pos_start = 0, stop = 0;
+    /* the forced prompt positions as one prefill on every rank (pieces printed as the loop prints them) */
+    const int pre = n_prompt - 1 < steps ? n_prompt - 1 : steps;
+    if (pre > 0 && transformer_prefill(&t, prompt_tokens, pre) == 0) {
+        while (pos < pre) {
+            next = prompt_tokens[pos + 1];
+            pos++;
+            if (next == 1) {
+                stop = 1;
+                break;
+            }
+            if (rank == 0) safe_printf(decode(&tok, token, next));
+            token = next;
+        }
+        if (rank == 0) fflush(stdout);
+    }
+    while (!stop && pos < steps) {
         Tensor *logits = forward(&t, token, pos);
         if (pos < n_prompt - 1) {
             next = prompt_tokens[pos + 1];
@@ -140,14 +155,17 @@ static int run_rank(int rank, int world, Shared *sh, const char *model_dir, cons
             fflush(stdout);
         }
         token = next;
-        if (start == 0) start = time_in_ms();
+        if (start == 0) {
+            start = time_in_ms();
+            pos_start = pos;
+        }
     }
     if (rank == 0) {
         printf("\n");
-        if (pos > 1) {
+        if (start && pos > pos_start) {
             const long end = time_in_ms();
-            fprintf(stderr, "achieved tok/s: %.2f (%d GPUs)\n", (double)(pos - 1) * 1000.0 / (double)(end > start ? end - start : 1),
-                    world);
+            fprintf(stderr, "achieved tok/s: %.2f (%d GPUs)\n",
+                    (double)(pos - pos_start) * 1000.0 / (double)(end > start ? end - start : 1), world);
         }
     }
     barrier(sh, world);  /* nobody leaves the exchange while another rank still steps */

@@ -50,8 +50,25 @@ static float generate(Transformer *tf, Tokenizer *tok, Sampler *sampler, const c
         exit(EXIT_FAILURE);
     }
     long start = 0;
-    int token = prompt_tokens[0], pos = 0, next;
-    while (pos < steps) {
+    int token = prompt_tokens[0], pos = 0, next = 0, pos_start = 0, stop = 0;
+    /* The forced prompt positions (all but the last prompt token) run as one prefill on the GPU, which
+     * leaves the KV cache as forward() at each of them would; their pieces print as the loop prints
+     * them.  If the engine cannot prefill, the loop forwards them one by one. */
+    const int pre = n_prompt - 1 < steps ? n_prompt - 1 : steps;
+    if (pre > 0 && transformer_prefill(tf, prompt_tokens, pre) == 0) {
+        while (pos < pre) {
+            next = prompt_tokens[pos + 1];
+            pos++;
+            if (next == 1) {
+                stop = 1;
+                break;
+            }
+            safe_printf(decode(tok, token, next));
+            token = next;
+        }
+        fflush(stdout);
+    }
+    while (!stop && pos < steps) {
         Tensor *logits = forward(tf, token, pos);
         next = pos < n_prompt - 1 ? prompt_tokens[pos + 1] : sample(sampler, data_f32(logits));
         pos++;
@@ -59,13 +76,16 @@ static float generate(Transformer *tf, Tokenizer *tok, Sampler *sampler, const c
         safe_printf(decode(tok, token, next));
         fflush(stdout);
         token = next;
-        if (start == 0) start = time_in_ms();
+        if (start == 0) {
+            start = time_in_ms();
+            pos_start = pos;
+        }
     }
     printf("\n");
     float tok_s = 0.0f;
-    if (pos > 1) {
+    if (start && pos > pos_start) {  /* the positions forwarded after the first timed one */
         const long end = time_in_ms();
-        tok_s = (float)(pos - 1) * 1000.0f / (float)(end > start ? end - start : 1);
+        tok_s = (float)(pos - pos_start) * 1000.0f / (float)(end > start ? end - start : 1);
         fprintf(stderr, "achieved tok/s: %.2f\n", tok_s);
     }
     free(prompt_tokens);

@@ -164,6 +164,18 @@ Tensor *forward(Transformer *transformer, int token, int pos) {
     return transformer->state.logits;
 }
 
+int transformer_prefill(Transformer *t, const int *tokens, int n) {
+    dk_model *g = transformer_engine(t);
+    if (!g) return DK_ERR_STATE;
+    if (n <= 0) return DK_OK;
+    int r = dk_model_set_tokens(g, tokens, n, n);
+    if (!r) r = dk_model_prefill(g, 0, n);
+    if (!r) r = dk_model_sync(g);
+    if (!r) r = dk_model_device_error(g);
+    if (r) fprintf(stderr, "transformer_prefill: %s (code 0x%x)\n", dk_last_error(), r);
+    return r;
+}
+
 void free_transformer(Transformer *t) {
     dk_model *g = transformer_engine(t);
     if (g) dk_model_destroy(g);

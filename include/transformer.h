@@ -71,6 +71,12 @@ void transformer_logit_rows(Transformer *t, int *begin, int *end);
  * engine's own entry points (dk_model_generate, dk_model_weight_bytes, ...); NULL before
  * build_transformer_from_safetensors. */
 struct dk_model *transformer_engine(Transformer *t);
+/* The forward() calls of positions 0 .. n-1 with tokens[0 .. n-1], batched (no counterpart in the
+ * reference, whose generate loop forwards prompt tokens one by one, src/bin/localinfer.c:60-73): one
+ * prefill on the GPU's tensor cores that leaves the KV cache exactly as those forward() calls would;
+ * no logits.  forward(tokens[n], n) continues from there.  Tensor parallel: every rank calls it.
+ * Returns 0, or the DK_ERR_* code (with the message on stderr) when the engine cannot prefill. */
+int transformer_prefill(Transformer *t, const int *tokens, int n);
 /* Release the GPU model and the host RunState tensors (no counterpart in the reference, which never
  * frees); the host weights in t->safetensors stay. */
 void free_transformer(Transformer *t);
