@@ -229,9 +229,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q8_kernel(const GemmArgs
 //   warp 1   allocates TMEM; one thread issues one MMA per group (K = 32, s32) into a ring of 8
 //            64-column TMEM accumulators and commits each to its mbarrier;
 //   warps 2-17 fold: warp w reads the lanes of tile w % 4 (row = lane) and 16 of the 64 token columns
-//            (the next group's columns load while the current one folds; a block's groups are unrolled),
-//            refills the read columns with the bias below and hands them back, and adds term = (float)dot * (ws * xs) to its running sums in group order, the GEMV's
-//            arithmetic.  (float)dot is exact: the accumulators start at the bits 0x4B400000 and
+//            (the next group's columns load while the current one folds), refills the read columns
+//            with the bias below and hands them back, and adds term = (float)dot * (ws * xs) to its
+//            running sums in group order, the GEMV's arithmetic.
+//            (float)dot is exact: the accumulators start at the bits 0x4B400000 and
 //            |dot| <= 32 * 128 * 128 < 2^22, so the s32 sum's bits are the float 1.5 * 2^23 + dot, and
 //            subtracting 1.5 * 2^23 is exact.
 // Every wait is bounded and gives up when another role has; TMEM is always freed.
