@@ -480,6 +480,9 @@ def run_decode(args):
         if record:
             record[1].record(stream)
 
+    # the ranks start together: the prefill's and the decode step's cross-rank waits are bounded
+    torch.cuda.synchronize()
+    barrier()
     for _ in range(args.warmup):
         one_step()
     m.sync()
