@@ -127,7 +127,9 @@ struct dk_model {
     float *ppart = nullptr;               // tensor parallel: this rank's wo / w2 partial rows [chunk][dim]
     size_t comm_pre = 0;                  // offset of the prefill receive areas in `comm`
     unsigned long long pex[2] = {0, 0};   // prefill exchanges done per parity (counter targets)
-    std::vector<PrefillGroup> h_groups;
+    PrefillGroup *h_groups = nullptr;     // pinned: one slot of pchunk groups per chunk of the sequence
+    int pslots = 0;
+    std::vector<cudaEvent_t> pslot_done;  // recorded after each slot's upload: rewrite only after it
     size_t pwork_stride = 0, pcount_stride = 0;
 };
 
@@ -342,6 +344,9 @@ void dk_model_destroy(dk_model *m) {
     cudaFree(m->d_ops);
     cudaFree(m->d_trace);
     cudaFree(m->parena);
+    if (m->h_groups) cudaFreeHost(m->h_groups);
+    for (cudaEvent_t e : m->pslot_done)
+        if (e) cudaEventDestroy(e);
     if (m->h_small) cudaFreeHost(m->h_small);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
@@ -918,7 +923,15 @@ int dk_model_forward(dk_model *m, int token, int pos, float *logits) {
 static bool prefill_available(const dk_model *m) { return m->use_step && (m->world == 1 || m->connected); }
 
 static int prefill_alloc(dk_model *m) {
-    if (m->parena) return DK_OK;
+    if (m->pchunk) return DK_OK;  // set last, once everything below succeeded
+    // a previous attempt that failed part-way: start over
+    cudaFree(m->parena);
+    m->parena = nullptr;
+    if (m->h_groups) cudaFreeHost(m->h_groups);
+    m->h_groups = nullptr;
+    for (cudaEvent_t e : m->pslot_done)
+        if (e) cudaEventDestroy(e);
+    m->pslot_done.clear();
     const int C = std::min(kPrefillChunk, m->seq_len);
     const int qkv_rows = m->l_dim + 2 * m->l_kv_dim;
     const int nmax = std::max(std::max(m->dim, m->l_dim), m->l_hidden);
@@ -948,7 +961,15 @@ static int prefill_alloc(dk_model *m) {
     m->pcount = reinterpret_cast<unsigned *>(p); p += sz_cnt;
     m->pgroups = reinterpret_cast<PrefillGroup *>(p); p += sz_groups;
     m->ppart = sz_ppart ? reinterpret_cast<float *>(p) : nullptr;
-    m->h_groups.resize(C);
+    // the group tables go up from pinned memory (a pageable source may synchronise the stream)
+    m->pslots = (m->seq_len + C - 1) / C;
+    if (cudaMallocHost(&m->h_groups, (size_t)m->pslots * C * sizeof(PrefillGroup)) != cudaSuccess) {
+        m->h_groups = nullptr;
+        return set_error(DK_ERR_NOMEM, "prefill: pinned group tables");
+    }
+    m->pslot_done.assign(m->pslots, nullptr);
+    for (auto &e : m->pslot_done)
+        if (int r = cuda_status(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "prefill: slot event")) return r;
     m->pchunk = C;
     return DK_OK;
 }
@@ -996,14 +1017,19 @@ static int prefill_chunk(dk_model *m, int pos0, int n, cudaStream_t st) {
     t.out = m->pxb; t.work = m->pwork; t.count = m->pcount; t.pos = m->pos;
     t.n_heads = m->l_heads; t.n_kv_heads = m->l_kv_heads; t.head_size = m->hs; t.seq_len = m->seq_len;
     t.kv_f32 = m->kv_type == DK_KV_F32; t.max_splits = m->step_splits; t.min_chunk = kStepMinChunk; t.err = m->err;
-    // the attention's position groups (the same for every layer); pageable source: the copy is staged
-    // before the call returns, and stream order keeps it behind the previous chunk's kernels
+    // the attention's position groups (the same for every layer), planned into this chunk's pinned slot
+    // once that slot's previous upload is done; stream order keeps the upload behind the previous
+    // chunk's kernels
+    const int slot = (pos0 / C) % m->pslots;
+    PrefillGroup *hg = m->h_groups + (size_t)slot * C;
+    if (int r = cuda_status(cudaEventSynchronize(m->pslot_done[slot]), "prefill: group slot")) return r;
     long long items = 0;
-    const int ngroups = prefill_attn_plan(t, pos0, n, m->h_groups.data(), &items);
-    if (int r = cuda_status(cudaMemcpyAsync(m->pgroups, m->h_groups.data(), (size_t)ngroups * sizeof(PrefillGroup),
+    const int ngroups = prefill_attn_plan(t, pos0, n, hg, &items);
+    if (int r = cuda_status(cudaMemcpyAsync(m->pgroups, hg, (size_t)ngroups * sizeof(PrefillGroup),
                                             cudaMemcpyHostToDevice, st),
                             "prefill: group table"))
         return r;
+    if (int r = cuda_status(cudaEventRecord(m->pslot_done[slot], st), "prefill: group slot")) return r;
     for (int l = 0; l < m->n_layers; ++l) {
         const dk_layer &ly = m->layers[l];
         cudaError_t e = act(l == 0 ? PRO_EMB_RMS : PRO_RMS, m->px, ly.rms_att, m->dim);
