@@ -421,7 +421,8 @@ def run_reference(args):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 / v, 2),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
         "data": "synthetic (seeded N(0,0.02) weights, seeded prompt)",
-        "config": {"workload": "llama2-7b-shape q8_0 decode, 32-token prompt + 256 greedy tokens",
+        "config": {"workload": f"llama2-7b-shape q8_0 decode: {PROMPT_LEN}-token prompt, then {GEN_LEN} greedy "
+                               f"tokens timed",
                    "model": "llama2-7b-shape", "kv_cache": "bf16 (the reference's)"},
         "cpu_baseline": {"value": round(v, 3), "unit": "tok/s", "cores": cpu.cores, "kind": cpu.kind,
                          "sample": cpu.describe()},
