@@ -65,6 +65,10 @@ SIGNATURES = {
     "dk_model_kernels_per_step": (_i, [_vp]),
     "dk_model_weight_bytes": (_sz, [_vp]),
     "dk_model_trace": (_i, [_vp, _vp, _sz, _vp, _vp]),
+    "dk_model_dump_enable": (_i, [_vp, _i]),
+    "dk_model_dump_read": (_i, [_vp, _vp, _vp, _vp]),
+    "dk_model_kv_write": (_i, [_vp, _i, _i, _i, _vp, _vp, _i]),
+    "dk_model_kv_read": (_i, [_vp, _i, _i, _i, _vp, _vp]),
 }
 
 _lib = None

@@ -68,6 +68,12 @@ struct GemvArgs {
     unsigned long long *epoch_rw = nullptr;     // the classifier's writable view of epoch
     int row_offset = 0;                         // global index of this rank's first classifier row
     int vocab = 0;                              // rows of the whole classifier (0: d)
+    // Diagnostics (persistent step only; nullptr: off): the CTA that owns tile 0 copies the op's fp32
+    // input vector (n floats; the residual written by the prologue where it writes one) and the Q8_0
+    // activation it built (n int8, n/32 scales) here, for per-layer parity checks.
+    float *dump_in = nullptr;
+    int8_t *dump_q = nullptr;
+    float *dump_s = nullptr;
 };
 
 struct GemvPlan {

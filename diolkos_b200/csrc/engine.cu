@@ -117,6 +117,9 @@ struct dk_model {
     int step_splits = 1;                  // attention splits per KV head in the persistent step
     StepArgs step;
     unsigned long long *d_trace = nullptr;  // DIOLKOS_STEP_TRACE=1: the persistent step's timeline
+    std::vector<StepOp> h_ops;            // the op list as uploaded (diagnostics rewrite it)
+    uint8_t *dump = nullptr;              // dk_model_dump_enable: per GEMV op input | int8 | scales
+    std::vector<int> dump_ops;            // indices of the GEMV ops, step order
     // prompt prefill (tensor-core matmuls over chunks of up to pchunk positions), allocated on first use
     uint8_t *parena = nullptr;
     int pchunk = 0;
@@ -127,6 +130,7 @@ struct dk_model {
     float *ppart = nullptr;               // tensor parallel: this rank's wo / w2 partial rows [chunk][dim]
     size_t comm_pre = 0;                  // offset of the prefill receive areas in `comm`
     unsigned long long pex[2] = {0, 0};   // prefill exchanges done per parity (counter targets)
+    bool prefill_broken = false;          // a tensor-parallel prefill exchange failed: prefill refused
     PrefillGroup *h_groups = nullptr;     // pinned: one slot of pchunk groups per chunk of the sequence
     int pslots = 0;
     std::vector<cudaEvent_t> pslot_done;  // recorded after each slot's upload: rewrite only after it
@@ -343,6 +347,7 @@ void dk_model_destroy(dk_model *m) {
     cudaFree(m->d_ptrs);
     cudaFree(m->d_ops);
     cudaFree(m->d_trace);
+    cudaFree(m->dump);
     cudaFree(m->parena);
     if (m->h_groups) cudaFreeHost(m->h_groups);
     for (cudaEvent_t e : m->pslot_done)
@@ -697,6 +702,10 @@ static int build_step(dk_model *m) {
     sa.seq_len = m->seq_len;
     sa.err = m->err;
     m->n_ops = (int)ops.size();
+    m->h_ops = ops;
+    m->dump_ops.clear();
+    for (int i = 0; i < (int)ops.size(); ++i)
+        if (ops[i].kind == OP_GEMV) m->dump_ops.push_back(i);
     if (cudaMalloc(&m->d_ops, ops.size() * sizeof(StepOp)) != cudaSuccess)
         return set_error(DK_ERR_NOMEM, "persistent step: op list");
     if (int r = cuda_status(cudaMemcpy(m->d_ops, ops.data(), ops.size() * sizeof(StepOp), cudaMemcpyHostToDevice),
@@ -883,6 +892,127 @@ int dk_model_trace(dk_model *m, unsigned long long *out, size_t n, int *grid, in
     return cuda_status(cudaMemcpy(out, m->d_trace, total * 8, cudaMemcpyDeviceToHost), "dk_model_trace");
 }
 
+// Diagnostics layout: GEMV op k (step order) with n_k input columns occupies, at 256-byte aligned
+// offsets, n_k floats of input, n_k int8 values and n_k/32 float scales.
+static size_t dump_layout(const dk_model *m, std::vector<size_t> *off) {
+    size_t o = 0;
+    for (int i : m->dump_ops) {
+        const size_t n = (size_t)m->h_ops[i].g.n;
+        if (off) off->push_back(o);
+        o += align256(4 * n) + align256(n) + align256(n / 8);
+    }
+    return o;
+}
+
+int dk_model_dump_enable(dk_model *m, int on) {
+    if (int r = need(m)) return r;
+    if (!m->finalized || !m->use_step)
+        return set_error(DK_ERR_STATE, "dk_model_dump_enable: needs a finalized model on the persistent step");
+    if (int r = cuda_status(cudaStreamSynchronize(m->stream), "dk_model_dump_enable: sync")) return r;
+    std::vector<size_t> off;
+    const size_t bytes = dump_layout(m, &off);
+    if (on && !m->dump) {
+        if (cudaMalloc(&m->dump, bytes) != cudaSuccess) return set_error(DK_ERR_NOMEM, "dk_model_dump_enable");
+        if (int r = cuda_status(cudaMemset(m->dump, 0, bytes), "dk_model_dump_enable: clear")) return r;
+    }
+    std::vector<StepOp> ops = m->h_ops;
+    for (size_t k = 0; k < m->dump_ops.size(); ++k) {
+        GemvArgs &a = ops[m->dump_ops[k]].g;
+        const size_t n = (size_t)a.n;
+        a.dump_in = on ? reinterpret_cast<float *>(m->dump + off[k]) : nullptr;
+        a.dump_q = on ? reinterpret_cast<int8_t *>(m->dump + off[k] + align256(4 * n)) : nullptr;
+        a.dump_s = on ? reinterpret_cast<float *>(m->dump + off[k] + align256(4 * n) + align256(n)) : nullptr;
+    }
+    // The captured graph reads the op list from this device array at every launch.
+    return cuda_status(cudaMemcpy(m->d_ops, ops.data(), ops.size() * sizeof(StepOp), cudaMemcpyHostToDevice),
+                       "dk_model_dump_enable: op upload");
+}
+
+int dk_model_dump_read(dk_model *m, float *in, int8_t *q, float *s) {
+    if (int r = need(m)) return r;
+    if (!m->dump) return set_error(DK_ERR_STATE, "dk_model_dump_read: dumps are off (dk_model_dump_enable)");
+    std::vector<size_t> off;
+    const size_t bytes = dump_layout(m, &off);
+    std::vector<uint8_t> h(bytes);
+    if (int r = cuda_status(cudaStreamSynchronize(m->stream), "dk_model_dump_read: sync")) return r;
+    if (int r = cuda_status(cudaMemcpy(h.data(), m->dump, bytes, cudaMemcpyDeviceToHost), "dk_model_dump_read")) return r;
+    size_t e = 0;
+    for (size_t k = 0; k < m->dump_ops.size(); ++k) {
+        const size_t n = (size_t)m->h_ops[m->dump_ops[k]].g.n;
+        if (in) memcpy(in + e, h.data() + off[k], 4 * n);
+        if (q) memcpy(q + e, h.data() + off[k] + align256(4 * n), n);
+        if (s) memcpy(s + e / 32, h.data() + off[k] + align256(4 * n) + align256(n), n / 8);
+        e += n;
+    }
+    return DK_OK;
+}
+
+int dk_model_kv_write(dk_model *m, int layer, int pos0, int n_pos, const void *k, const void *v, int src_type) {
+    if (int r = need(m)) return r;
+    if (layer < 0 || layer >= m->n_layers || pos0 < 0 || n_pos < 0 || pos0 + n_pos > m->seq_len || !k || !v ||
+        (src_type != DK_KV_BF16 && src_type != DK_KV_F32))
+        return set_error(DK_ERR_INVALID, "dk_model_kv_write: bad arguments");
+    if (n_pos == 0) return DK_OK;
+    if (int r = cuda_status(cudaStreamSynchronize(m->stream), "dk_model_kv_write: sync")) return r;
+    const size_t esz = m->kv_type == DK_KV_F32 ? 4 : 2;
+    const int hs = m->hs, kvd = m->kv_dim;
+    // this rank's KV heads, [head][position][hs] in the cache's element type
+    std::vector<uint8_t> buf((size_t)m->l_kv_heads * n_pos * hs * esz);
+    for (int w = 0; w < 2; ++w) {
+        const void *src = w == 0 ? k : v;
+        for (int h = 0; h < m->l_kv_heads; ++h) {
+            const int hg = m->rank * m->l_kv_heads + h;
+            for (int p = 0; p < n_pos; ++p)
+                for (int d = 0; d < hs; ++d) {
+                    const size_t from = (size_t)p * kvd + (size_t)hg * hs + d;
+                    uint32_t u;  // the value's fp32 bits
+                    if (src_type == DK_KV_BF16) u = (uint32_t)static_cast<const uint16_t *>(src)[from] << 16;
+                    else memcpy(&u, static_cast<const float *>(src) + from, 4);
+                    const size_t at = ((size_t)h * n_pos + p) * hs + d;
+                    if (esz == 2) reinterpret_cast<uint16_t *>(buf.data())[at] = (uint16_t)(u >> 16);  // truncation
+                    else memcpy(buf.data() + 4 * at, &u, 4);
+                }
+        }
+        uint8_t *base = static_cast<uint8_t *>(w == 0 ? m->kcache : m->vcache) + (size_t)layer * m->kv_layer_elems * esz;
+        for (int h = 0; h < m->l_kv_heads; ++h)
+            if (int r = cuda_status(cudaMemcpyAsync(base + ((size_t)h * m->seq_len + pos0) * hs * esz,
+                                                    buf.data() + (size_t)h * n_pos * hs * esz, (size_t)n_pos * hs * esz,
+                                                    cudaMemcpyHostToDevice, m->stream),
+                                    "dk_model_kv_write"))
+                return r;
+        // stream order puts the rows before the next step; the host buffer must outlive the copies
+        if (int r = cuda_status(cudaStreamSynchronize(m->stream), "dk_model_kv_write: sync")) return r;
+    }
+    return DK_OK;
+}
+
+int dk_model_kv_read(dk_model *m, int layer, int pos0, int n_pos, void *k, void *v) {
+    if (int r = need(m)) return r;
+    if (layer < 0 || layer >= m->n_layers || pos0 < 0 || n_pos < 0 || pos0 + n_pos > m->seq_len || !k || !v)
+        return set_error(DK_ERR_INVALID, "dk_model_kv_read: bad arguments");
+    if (n_pos == 0) return DK_OK;
+    const size_t esz = m->kv_type == DK_KV_F32 ? 4 : 2;
+    const int hs = m->hs, lkvd = m->l_kv_heads * hs;
+    std::vector<uint8_t> buf((size_t)m->l_kv_heads * n_pos * hs * esz);
+    for (int w = 0; w < 2; ++w) {
+        const uint8_t *base =
+            static_cast<const uint8_t *>(w == 0 ? m->kcache : m->vcache) + (size_t)layer * m->kv_layer_elems * esz;
+        for (int h = 0; h < m->l_kv_heads; ++h)
+            if (int r = cuda_status(cudaMemcpyAsync(buf.data() + (size_t)h * n_pos * hs * esz,
+                                                    base + ((size_t)h * m->seq_len + pos0) * hs * esz,
+                                                    (size_t)n_pos * hs * esz, cudaMemcpyDeviceToHost, m->stream),
+                                    "dk_model_kv_read"))
+                return r;
+        if (int r = cuda_status(cudaStreamSynchronize(m->stream), "dk_model_kv_read: sync")) return r;
+        uint8_t *dst = static_cast<uint8_t *>(w == 0 ? k : v);
+        for (int h = 0; h < m->l_kv_heads; ++h)
+            for (int p = 0; p < n_pos; ++p)
+                memcpy(dst + ((size_t)p * lkvd + (size_t)h * hs) * esz, buf.data() + ((size_t)h * n_pos + p) * hs * esz,
+                       (size_t)hs * esz);
+    }
+    return DK_OK;
+}
+
 size_t dk_model_weight_bytes(dk_model *m) {
     if (!m) return 0;
     // Bytes the GEMVs of one step stream on this rank (pad rows included): every layer's four
@@ -920,7 +1050,9 @@ int dk_model_forward(dk_model *m, int token, int pos, float *logits) {
     return DK_OK;
 }
 
-static bool prefill_available(const dk_model *m) { return m->use_step && (m->world == 1 || m->connected); }
+static bool prefill_available(const dk_model *m) {
+    return m->use_step && (m->world == 1 || (m->connected && !m->prefill_broken));
+}
 
 static int prefill_alloc(dk_model *m) {
     if (m->pchunk) return DK_OK;  // set last, once everything below succeeded
@@ -999,11 +1131,15 @@ static int prefill_chunk(dk_model *m, int pos0, int n, cudaStream_t st) {
                                                m->world, (size_t)m->rank * C * m->dim, nf, st);
         if (!e) e = launch_prefill_signal(reinterpret_cast<unsigned long long *const *>(m->d_ptrs + 8 * (8 + par)),
                                           m->world, st);
-        m->pex[par] += 1;
+        // The counter target counts only exchanges whose signal was enqueued: every peer counts the same ones.
+        if (!e) m->pex[par] += 1;
         if (!e) e = launch_prefill_wait(reinterpret_cast<const unsigned long long *>(m->comm + comm_pcnt_off(m, par)),
                                         m->pex[par] * (unsigned long long)m->world, m->err, st);
         if (!e) e = launch_prefill_reduce(m->px, reinterpret_cast<const float *>(m->comm + comm_pre_off(m, par)),
                                           (size_t)C * m->dim, m->world, nf, st);
+        // After a failed exchange this rank's count may no longer match its peers': later prefills would wait
+        // for a wrong target, so tensor-parallel prefill is refused from here on.
+        if (e) m->prefill_broken = true;
         return e;
     };
     auto mm = [&](const uint8_t *w, int cols, int rows, int T, int epi, float *out) -> cudaError_t {
@@ -1069,7 +1205,7 @@ int dk_model_prefill(dk_model *m, int pos0, int n_positions) {
     if (int r = need(m)) return r;
     if (!m->finalized) return set_error(DK_ERR_STATE, "dk_model_prefill: model not finalized");
     if (!prefill_available(m))
-        return set_error(DK_ERR_STATE, "dk_model_prefill: needs the persistent step (and connected ranks)");
+        return set_error(DK_ERR_STATE, "dk_model_prefill: needs the persistent step (and connected ranks whose prefill exchanges never failed)");
     if (pos0 < 0 || n_positions < 0 || pos0 + n_positions > m->seq_len)
         return set_error(DK_ERR_INVALID, "dk_model_prefill: positions [%d, %d) exceed seq_len %d", pos0,
                          pos0 + n_positions, m->seq_len);

@@ -816,6 +816,14 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa
                 bar_compute();
                 if (!ok || *reinterpret_cast<volatile int *>(&ctl.abort)) break;
                 if (tid == 0) trace_mark(sa, i, 1);
+                if (a.dump_q && sc.t0 == 0) {  // diagnostics: the op's input and activation, one CTA
+                    const float *src = a.pro == PRO_RMS_REDUCE ? a.x_out : a.x;
+                    for (int j = tid; j < (a.n >> 2); j += kComputeThreads)
+                        reinterpret_cast<float4 *>(a.dump_in)[j] = __ldcg(reinterpret_cast<const float4 *>(src) + j);
+                    for (int j = tid; j < (a.n >> 4); j += kComputeThreads)
+                        reinterpret_cast<uint4 *>(a.dump_q)[j] = reinterpret_cast<const uint4 *>(xq)[j];
+                    for (int j = tid; j < (a.n >> 5); j += kComputeThreads) a.dump_s[j] = xs[j];
+                }
                 if (warp < NC) {
                     gemv_consume(op, sc, gbase, S, NC, sa.slot, ring_s, smem_u32(xq), smem_u32(xs), ctl, warp, lane, best);
                     if (a.epi == EPI_ARGMAX) {

@@ -36,6 +36,7 @@ class Model:
     def __init__(self, cfg: synth.Config, kv_f32: bool = False, device: int = 0, tp_rank: int = 0,
                  tp_world: int = 1):
         self.cfg = cfg
+        self.kv_f32 = kv_f32
         self.tp_rank, self.tp_world = tp_rank, tp_world
         L = N.lib()
         arr = (C.c_int * 7)(*cfg.as_list())
@@ -125,6 +126,51 @@ class Model:
 
     def device_error(self) -> int:
         return N.lib().dk_model_device_error(self.h)
+
+    def dump_enable(self, on: bool = True) -> None:
+        """Record every later decode step's per-op inputs and Q8_0 activations (dk_model_dump_enable)."""
+        N.check(N.lib().dk_model_dump_enable(self.h, int(on)))
+
+    def kv_write(self, layer: int, pos0: int, k, v) -> None:
+        """Overwrite KV rows pos0.. of one layer with rows in the reference's layout ([n][kv_dim]):
+        uint16 arrays are bf16 bits, float32 arrays fp32 values."""
+        k = np.ascontiguousarray(k)
+        v = np.ascontiguousarray(v)
+        if k.dtype == np.uint16:
+            t = N.DK_KV_BF16
+        elif k.dtype == np.float32:
+            t = N.DK_KV_F32
+        else:
+            raise TypeError("KV rows must be uint16 (bf16 bits) or float32")
+        kv_dim = self.cfg.n_kv_heads * (self.cfg.dim // self.cfg.n_heads)
+        N.check(N.lib().dk_model_kv_write(self.h, layer, pos0, k.size // kv_dim, k.ctypes.data, v.ctypes.data, t))
+
+    def kv_read(self, layer: int, pos0: int, n: int = 1):
+        """This rank's KV rows pos0 .. pos0+n-1 of one layer ([n][kv_dim]; uint16 bf16 bits, or float32
+        for an fp32 cache)."""
+        kv_dim = (self.cfg.n_kv_heads // self.tp_world) * (self.cfg.dim // self.cfg.n_heads)
+        dt = np.float32 if self.kv_f32 else np.uint16
+        k, v = np.empty((n, kv_dim), dt), np.empty((n, kv_dim), dt)
+        N.check(N.lib().dk_model_kv_read(self.h, layer, pos0, n, k.ctypes.data, v.ctypes.data))
+        return k, v
+
+    def dump_read(self):
+        """The last step's record: per layer [q|k|v input, wo input, w1|w3 input, w2 input], then the
+        classifier's; each (fp32 input, int8 values, fp32 scales).  Under tensor parallelism the wo and
+        w2 inputs are this rank's slices (its heads' attention output, its SwiGLU rows)."""
+        c = self.cfg
+        W = self.tp_world
+        sizes = [c.dim, c.dim // W, c.dim, c.hidden_dim // W] * c.n_layers + [c.dim]
+        tot = sum(sizes)
+        ain = np.empty(tot, np.float32)
+        aq = np.empty(tot, np.int8)
+        asc = np.empty(tot // 32, np.float32)
+        N.check(N.lib().dk_model_dump_read(self.h, ain.ctypes.data, aq.ctypes.data, asc.ctypes.data))
+        out, off = [], 0
+        for n in sizes:
+            out.append((ain[off:off + n], aq[off:off + n], asc[off // 32:(off + n) // 32]))
+            off += n
+        return out
 
     @property
     def kernels_per_step(self) -> int:

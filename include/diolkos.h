@@ -217,8 +217,10 @@ int dk_model_enqueue_steps(dk_model *m, int pos0, int n_steps);
  * no logits.  Int8 tensor-core matmuls (tcgen05), chunks of up to 256 positions.  Tensor parallel:
  * every rank makes the same call; the wo / w2 partial sums cross NVLink once per layer each and are
  * summed in rank order like the decode step's (a rank that never arrives makes the others' waits end
- * with DK_ERR_COMM).  Needs the persistent decode step (DK_ERR_STATE otherwise).  Enqueued, not
- * synchronised. */
+ * with DK_ERR_COMM).  Needs the persistent decode step (DK_ERR_STATE otherwise).  After an exchange
+ * of a tensor-parallel prefill failed to enqueue, the ranks' exchange counts may disagree, so that
+ * model refuses further prefills (DK_ERR_STATE) and dk_model_generate steps its prompt instead.
+ * Enqueued, not synchronised. */
 int dk_model_prefill(dk_model *m, int pos0, int n_positions);
 int dk_model_get_tokens(dk_model *m, int *tokens, int n_tokens);
 int dk_model_sync(dk_model *m);
@@ -228,6 +230,25 @@ void *dk_model_stream(dk_model *m);
 int dk_model_device_error(dk_model *m);
 /* Number of kernels one decode step launches (for launch accounting). */
 int dk_model_kernels_per_step(dk_model *m);
+/* Diagnostics for per-layer parity checks (persistent step only).  dk_model_dump_enable(m, 1) makes
+ * every later decode step record, for each GEMV of the step in order -- per layer q|k|v, wo, w1|w3,
+ * w2, then the classifier -- its fp32 input vector (the residual stream for the rmsnorm prologues, the
+ * attention output for wo, the SwiGLU output for w2; n floats) and the Q8_0 activation it multiplied
+ * (n int8 values, n/32 fp32 scales): the checkpoints of the reference's forward() at its rmsnorm and
+ * matmul calls (src/transformer.c:76-237).  dk_model_dump_read copies the last step's record into
+ * host buffers holding the ops' n summed (in, q) and that sum / 32 (s); NULL skips one.  Costs one
+ * branch per op when off; (0) turns it off again. */
+int dk_model_dump_enable(dk_model *m, int on);
+int dk_model_dump_read(dk_model *m, float *in, int8_t *q, float *s);
+/* Diagnostics: overwrite the KV-cache rows of positions [pos0, pos0 + n_pos) of one layer with host
+ * rows in the reference's cache layout (src/transformer.c:25-26, :145-146: [n_pos][kv_dim], all KV
+ * heads; a tensor-parallel rank takes its own heads) of src_type DK_KV_BF16 (bf16 bits) or DK_KV_F32,
+ * converted to the cache's type as the decode step stores it (bf16 truncates, bf16 -> fp32 is exact).
+ * Lets a test give the engine an oracle's own history before a step.  Synchronous. */
+int dk_model_kv_write(dk_model *m, int layer, int pos0, int n_pos, const void *k, const void *v, int src_type);
+/* Diagnostics: this rank's KV-cache rows of positions [pos0, pos0 + n_pos) of one layer, in the
+ * reference's layout ([n_pos][this rank's KV heads * hs]) and the cache's element type.  Synchronous. */
+int dk_model_kv_read(dk_model *m, int layer, int pos0, int n_pos, void *k, void *v);
 /* Diagnostics: the persistent step's timeline of the last decode step, when the model was created
  * with DIOLKOS_STEP_TRACE=1 in the environment: out[(cta * n_ops + op) * 8 + k] = GPU global timer (ns)
  * when, on that CTA, k = 0: the op's input was ready, 1: its activation was built, 2: it finished,

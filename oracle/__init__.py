@@ -53,6 +53,9 @@ class Port:
         L.port_model_set.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
         L.port_forward.argtypes = [C.c_void_p, C.c_int, C.c_int, _f32p, C.c_void_p]
         L.port_generate.argtypes = [C.c_void_p, _i32p, C.c_int, C.c_int, _i32p]
+        L.port_forward_dump.argtypes = [C.c_void_p, C.c_int, C.c_int, _f32p, _f32p, _f32p, _i8p, _f32p]
+        L.port_kv_rows.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
+        L.port_kv_write.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
         L.port_generate.restype = C.c_int
 
     def quant_bf16(self, x_bits: np.ndarray):
@@ -123,7 +126,7 @@ class PortModel:
     """A whole model in the restatement; holds references to the weight arrays it registers."""
 
     def __init__(self, port: Port, cfg, weights: dict, kv_f32: bool = False):
-        self.port, self.cfg = port, cfg
+        self.port, self.cfg, self.kv_f32 = port, cfg, kv_f32
         self._keep = []
         self.h = port.lib.port_model_create(np.array(cfg.as_list(), np.int32), int(kv_f32))
         for (which, layer), w in weights.items():
@@ -149,6 +152,38 @@ class PortModel:
         n = self.port.lib.port_generate(self.h, p, p.size, steps, out)
         return out[:n].copy()
 
+    def forward_dump(self, token, pos):
+        """forward with per-layer checkpoints, the layout of RefModel.forward_dump."""
+        c = self.cfg
+        sizes = [c.dim, c.dim, c.dim, c.hidden_dim] * c.n_layers + [c.dim]
+        tot = sum(sizes)
+        logits = np.empty(c.vocab_size, np.float32)
+        xres = np.empty((2 * c.n_layers + 1, c.dim), np.float32)
+        ain, aq, asc = np.empty(tot, np.float32), np.empty(tot, np.int8), np.empty(tot // 32, np.float32)
+        self.port.lib.port_forward_dump(self.h, token, pos, logits, xres, ain, aq, asc)
+        acts, off = [], 0
+        for n in sizes:
+            acts.append((ain[off:off + n], aq[off:off + n], asc[off // 32:(off + n) // 32]))
+            off += n
+        return logits, xres, acts
+
+    def kv_write(self, layer, pos0, k, v):
+        """Overwrite KV-cache rows pos0.. of one layer ([n][kv_dim] of the cache's element type)."""
+        k = np.ascontiguousarray(k)
+        v = np.ascontiguousarray(v)
+        kv_dim = self.cfg.dim * self.cfg.n_kv_heads // self.cfg.n_heads
+        self.port.lib.port_kv_write(self.h, layer, pos0, k.size // kv_dim, k.ctypes.data, v.ctypes.data)
+
+    def kv_rows(self, layer, pos0, n):
+        """KV-cache rows of positions pos0 .. pos0+n-1 ([n][kv_dim]): uint16 bf16 bits, or float32 for an
+        fp32 cache."""
+        c = self.cfg
+        kv_dim = c.dim * c.n_kv_heads // c.n_heads
+        dt = np.float32 if self.kv_f32 else np.uint16
+        k, v = np.empty((n, kv_dim), dt), np.empty((n, kv_dim), dt)
+        self.port.lib.port_kv_rows(self.h, layer, pos0, n, k.ctypes.data, v.ctypes.data)
+        return k, v
+
     def __del__(self):
         try:
             self.port.lib.port_model_destroy(self.h)
@@ -156,15 +191,17 @@ class PortModel:
             pass
 
 
-def ref_path(variant: str = "auto") -> str | None:
+def ref_path(variant: str = "auto", hooked: bool = False) -> str | None:
     """Path of the compiled reference library, or None when it was not built here.
 
     "auto" prefers the portable (-march=x86-64-v3) build: its arithmetic is the same on every
     AVX2+FMA host, whereas -march=native lets the compiler pick a host-dependent vector shape that
-    changes the order of the GEMV's fp32 sums."""
+    changes the order of the GEMV's fp32 sums.  hooked: the build whose forward() records per-layer
+    checkpoints (ref_hooks.c; portable only)."""
     order = ["portable", "native"] if variant == "auto" else [variant]
+    name = "liboracle_ref_hooked.so" if hooked else "liboracle_ref.so"
     for v in order:
-        p = os.path.join(REF_DIR, v, "liboracle_ref.so")
+        p = os.path.join(REF_DIR, v, name)
         if os.path.exists(p):
             return p
     return None
@@ -173,17 +210,20 @@ def ref_path(variant: str = "auto") -> str | None:
 class Ref:
     """The unmodified reference C code (oracle/_ref), driven through ref_driver.c."""
 
-    def __init__(self, variant: str = "auto"):
-        p = ref_path(variant)
+    def __init__(self, variant: str = "auto", hooked: bool = False):
+        p = ref_path(variant, hooked)
         if p is None:
             raise FileNotFoundError("oracle/_ref is not built (needs the reference source tree)")
-        self.path = p
+        self.path, self.hooked = p, hooked
         L = self.lib = C.CDLL(p)
+        if hooked:
+            L.oref_forward_dump.argtypes = [C.c_void_p, C.c_int, C.c_int, _f32p, _f32p, _f32p, _i8p, _f32p, _i32p]
         L.oref_load.argtypes = [C.c_char_p, C.c_char_p]
         L.oref_load.restype = C.c_void_p
         L.oref_config.argtypes = [C.c_void_p, _i32p]
         L.oref_forward.argtypes = [C.c_void_p, C.c_int, C.c_int, _f32p]
         L.oref_state_x.argtypes = [C.c_void_p, _f32p]
+        L.oref_kv_rows.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, _u16p, _u16p]
         L.oref_generate.argtypes = [C.c_void_p, _i32p, C.c_int, C.c_int, _i32p, C.POINTER(C.c_double)]
         L.oref_generate.restype = C.c_int
         L.oref_quant_f32.argtypes = [_f32p, C.c_size_t, _i8p, _f32p]
@@ -267,6 +307,40 @@ class RefModel:
         tps = C.c_double(0.0)
         n = self.ref.lib.oref_generate(self.h, p, p.size, steps, out, C.byref(tps))
         return out[:n].copy(), tps.value
+
+    def kv_rows(self, layer, pos0, n):
+        """The reference's bf16 KV-cache rows (uint16 bits) of positions pos0 .. pos0+n-1: (k, v), [n][kv_dim]."""
+        kv_dim = self.cfg[0] * self.cfg[4] // self.cfg[3]
+        k = np.empty((n, kv_dim), np.uint16)
+        v = np.empty((n, kv_dim), np.uint16)
+        self.ref.lib.oref_kv_rows(self.h, layer, pos0, n, k, v)
+        return k, v
+
+    def forward_dump(self, token, pos):
+        """forward() with per-layer checkpoints (hooked build only).  Returns (logits, xres, acts):
+        xres[2L+1][dim] = the residual stream before each rmsnorm (the embedding row, then x after every
+        residual add); acts = per layer [attention-norm input activation, attention output, FFN-norm
+        output, SwiGLU output] then the classifier's: each (fp32 input, int8 Q8_0 values, fp32 scales)
+        exactly as matmul_Q8_0 quantised it."""
+        if not self.ref.hooked:
+            raise RuntimeError("forward_dump needs Ref(hooked=True)")
+        dim, hidden, L, vocab = self.cfg[0], self.cfg[1], self.cfg[2], self.cfg[5]
+        sizes = [dim, dim, dim, hidden] * L + [dim]
+        tot = sum(sizes)
+        logits = np.empty(vocab, np.float32)
+        xres = np.empty((2 * L + 1, dim), np.float32)
+        ain = np.empty(tot, np.float32)
+        aq = np.empty(tot, np.int8)
+        asc = np.empty(tot // 32, np.float32)
+        counts = np.zeros(2, np.int32)
+        self.ref.lib.oref_forward_dump(self.h, token, pos, logits, xres, ain, aq, asc, counts)
+        if counts[0] != 2 * L + 1 or counts[1] != 7 * L + 1:
+            raise RuntimeError(f"hooked forward made {counts[0]} rmsnorm / {counts[1]} matmul calls")
+        acts, off = [], 0
+        for n in sizes:
+            acts.append((ain[off:off + n], aq[off:off + n], asc[off // 32:(off + n) // 32]))
+            off += n
+        return logits, xres, acts
 
 
 def load_port_weights(port: Port, cfg, seed: int):

@@ -259,7 +259,27 @@ struct PortModel {
     /* run state (src/transformer.c:13-30) */
     float *x, *xb, *xb2, *hb, *hb2, *q, *k, *v, *att, *logits;
     void *key_cache, *value_cache; /* [layer][seq][kv_dim], bf16 or f32 */
+    /* checkpoint recorder of port_forward_dump (NULL: off): the same checkpoints as the hooked
+     * reference build (oracle/ref_hooks.c) */
+    float *rec_x, *rec_in, *rec_s;
+    int8_t *rec_q;
+    int rec_nx;
+    size_t rec_off;
 };
+
+/* Checkpoints (test infrastructure): the input of every rmsnorm (the residual stream), and the fp32
+ * input plus Q8_0 form of the activation each distinct matmul input is quantised to. */
+static void rec_x(PortModel *m, const float *x) {
+    if (!m->rec_x) return;
+    memcpy(m->rec_x + (size_t)m->rec_nx * m->dim, x, (size_t)m->dim * sizeof(float));
+    m->rec_nx++;
+}
+static void rec_act(PortModel *m, const float *in, int n) {
+    if (!m->rec_x) return;
+    memcpy(m->rec_in + m->rec_off, in, (size_t)n * sizeof(float));
+    port_quant_f32(in, (size_t)n, m->rec_q + m->rec_off, m->rec_s + m->rec_off / 32);
+    m->rec_off += (size_t)n;
+}
 
 PortModel *port_model_create(const int *cfg, int kv_f32) {
     PortModel *m = calloc(1, sizeof(PortModel));
@@ -333,7 +353,9 @@ void port_forward(PortModel *m, int token, int pos, float *logits, float *xdump)
 
     for (int l = 0; l < m->n_layers; l++) {
         const PortLayer *L = &m->layers[l];
+        rec_x(m, x);
         port_rmsnorm(m->xb, x, L->rms_att, dim);                               /* :77 */
+        rec_act(m, m->xb, dim);
         const size_t loff = (size_t)l * m->seq_len * kv_dim;                   /* :80 */
         port_matmul(m->q, m->xb, L->wq.q, L->wq.s, dim, dim);                  /* :83-85 */
         port_matmul(m->k, m->xb, L->wk.q, L->wk.s, dim, kv_dim);
@@ -386,10 +408,13 @@ void port_forward(PortModel *m, int token, int pos, float *logits, float *xdump)
             }
         }
 
+        rec_act(m, m->xb, dim);
         port_matmul(m->xb2, m->xb, L->wo.q, L->wo.s, dim, dim);               /* :196 */
         for (int i = 0; i < dim; i++) x[i] = x[i] + m->xb2[i];                 /* :199-201 */
 
+        rec_x(m, x);
         port_rmsnorm(m->xb, x, L->rms_ffn, dim);                               /* :204 */
+        rec_act(m, m->xb, dim);
         port_matmul(m->hb, m->xb, L->w1.q, L->w1.s, dim, hidden);             /* :208 */
         port_matmul(m->hb2, m->xb, L->w3.q, L->w3.s, dim, hidden);            /* :209 */
         for (int i = 0; i < hidden; i++) {                                     /* :212-222 */
@@ -398,13 +423,16 @@ void port_forward(PortModel *m, int token, int pos, float *logits, float *xdump)
             val = val * m->hb2[i];
             m->hb[i] = val;
         }
+        rec_act(m, m->hb, hidden);
         port_matmul(m->xb, m->hb, L->w2.q, L->w2.s, hidden, dim);             /* :225 */
         for (int i = 0; i < dim; i++) x[i] = x[i] + m->xb[i];                  /* :228-230 */
 
         if (xdump) memcpy(xdump + (size_t)l * dim, x, (size_t)dim * sizeof(float));
     }
 
+    rec_x(m, x);
     port_rmsnorm(x, x, m->rms_final, dim);                                     /* :234 */
+    rec_act(m, x, dim);
     port_matmul(m->logits, x, m->wcls.q, m->wcls.s, dim, m->vocab);            /* :237 */
     memcpy(logits, m->logits, (size_t)m->vocab * sizeof(float));
     free(cs);
@@ -430,4 +458,33 @@ int port_generate(PortModel *m, const int *prompt, int n_prompt, int steps, int 
     }
     free(logits);
     return n_out;
+}
+
+/* port_forward with the checkpoints recorded (same layout as oref_forward_dump in ref_hooks.c):
+ * xres [2L+1][dim]; per layer the activations of wq, wo, w1, w2 and then wcls's, concatenated in
+ * ain / aq (n each) and as (n/32 each). */
+void port_forward_dump(PortModel *m, int token, int pos, float *logits, float *xres, float *ain, int8_t *aq,
+                       float *as) {
+    m->rec_x = xres; m->rec_in = ain; m->rec_q = aq; m->rec_s = as;
+    m->rec_nx = 0; m->rec_off = 0;
+    port_forward(m, token, pos, logits, NULL);
+    m->rec_x = NULL; m->rec_in = NULL; m->rec_q = NULL; m->rec_s = NULL;
+}
+
+/* KV-cache rows [pos0, pos0+n) of one layer in the cache's own element type ([n][kv_dim]). */
+void port_kv_rows(const PortModel *m, int layer, int pos0, int n, void *k, void *v) {
+    const size_t kv_dim = (size_t)m->dim * m->n_kv_heads / m->n_heads;
+    const size_t esz = m->kv_f32 ? 4 : 2;
+    const size_t off = ((size_t)layer * m->seq_len + pos0) * kv_dim * esz;
+    memcpy(k, (const uint8_t *)m->key_cache + off, kv_dim * (size_t)n * esz);
+    memcpy(v, (const uint8_t *)m->value_cache + off, kv_dim * (size_t)n * esz);
+}
+
+/* Overwrite KV-cache rows [pos0, pos0+n) of one layer with rows of the cache's element type. */
+void port_kv_write(PortModel *m, int layer, int pos0, int n, const void *k, const void *v) {
+    const size_t kv_dim = (size_t)m->dim * m->n_kv_heads / m->n_heads;
+    const size_t esz = m->kv_f32 ? 4 : 2;
+    const size_t off = ((size_t)layer * m->seq_len + pos0) * kv_dim * esz;
+    memcpy((uint8_t *)m->key_cache + off, k, kv_dim * (size_t)n * esz);
+    memcpy((uint8_t *)m->value_cache + off, v, kv_dim * (size_t)n * esz);
 }

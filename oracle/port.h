@@ -68,6 +68,16 @@ void port_model_set(PortModel *m, int which, int layer, const void *data, const 
 /* One decode step; writes logits[vocab]; if xdump != NULL, writes the residual stream after each
  * layer to xdump[l*dim .. (l+1)*dim). */
 void port_forward(PortModel *m, int token, int pos, float *logits, float *xdump);
+/* port_forward recording per-layer checkpoints: xres[2L+1][dim] = the input of every rmsnorm (the
+ * residual stream; src/transformer.c:76, :204, :234); per layer the fp32 input and Q8_0 form of the
+ * activations of wq (:83), wo (:196), w1 (:208), w2 (:225), then of wcls (:237), concatenated in
+ * ain / aq and as. */
+void port_forward_dump(PortModel *m, int token, int pos, float *logits, float *xres, float *ain, int8_t *aq,
+                       float *as);
+/* KV-cache rows [pos0, pos0+n) of one layer, [n][kv_dim] in the cache's element type. */
+void port_kv_rows(const PortModel *m, int layer, int pos0, int n, void *k, void *v);
+/* Overwrite KV-cache rows [pos0, pos0+n) of one layer with rows of the cache's element type. */
+void port_kv_write(PortModel *m, int layer, int pos0, int n, const void *k, const void *v);
 /* Greedy generate loop (src/bin/localinfer.c:42-99) on token ids; returns #generated tokens. */
 int port_generate(PortModel *m, const int *prompt, int n_prompt, int steps, int *out);
 

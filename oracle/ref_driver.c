@@ -79,6 +79,17 @@ void oref_state_x(void *hp, float *out) {
     memcpy(out, h->t.state.x->data, sizeof(float) * (size_t)h->t.config.dim);
 }
 
+/* The bf16 KV-cache rows of positions [pos0, pos0 + n) of one layer (RunState key_cache /
+ * value_cache, [layer][pos][kv_dim], transformer.c:25-26, written at :145-146). */
+void oref_kv_rows(void *hp, int layer, int pos0, int n, uint16_t *k, uint16_t *v) {
+    ORef *h = hp;
+    const Config *c = &h->t.config;
+    const size_t kv_dim = (size_t)c->dim * c->n_kv_heads / c->n_heads;
+    const size_t off = ((size_t)layer * c->seq_len + pos0) * kv_dim;
+    memcpy(k, (uint16_t *)h->t.state.key_cache->data + off, sizeof(uint16_t) * kv_dim * (size_t)n);
+    memcpy(v, (uint16_t *)h->t.state.value_cache->data + off, sizeof(uint16_t) * kv_dim * (size_t)n);
+}
+
 static double now_s(void) {
     struct timespec ts;
     clock_gettime(CLOCK_MONOTONIC, &ts);

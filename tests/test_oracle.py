@@ -175,3 +175,43 @@ def test_reference_native_build(ref):
     for pos in range(6):
         la, lb = ma.forward(int(prompt[pos]), pos), mb.forward(int(prompt[pos]), pos)
         assert np.max(np.abs(la - lb)) / np.max(np.abs(lb)) < 5e-2
+
+
+def test_hooked_reference_checkpoints(ref):
+    """The hooked reference build (oracle/ref_hooks.c: the unmodified transformer.c with its rmsnorm /
+    matmul calls routed through recording hooks) computes exactly what the plain build computes --
+    logits and KV rows bit-identical over several positions -- and its checkpoints are the reference's
+    own values: each recorded activation is rmsnorm(recorded residual) for the norm prologues and
+    the reference quantiser's output of the recorded input, bit for bit."""
+    from oracle import Ref, ref_path
+
+    if ref_path("portable", hooked=True) is None:
+        pytest.skip("the hooked reference build is not present")
+    hk = Ref("portable", hooked=True)
+    plain = Ref("portable")
+    cfg = synth.TINY
+    tmp = tempfile.mkdtemp()
+    md = os.path.join(tmp, "tiny")
+    synth.write_model(md, cfg, G.TINY_SEED)
+    mh, mp = hk.load(md, tmp), plain.load(md, tmp)
+    prompt = synth.seeded_prompt(7, 8)
+    w_att = np.ones(cfg.dim, np.float32)  # the synthetic models' norm weights are 1.0
+    L = cfg.n_layers
+    for pos in range(6):
+        tok = int(prompt[pos])
+        lh, xres, acts = mh.forward_dump(tok, pos)
+        lp = mp.forward(tok, pos)
+        np.testing.assert_array_equal(lh.view(np.uint32), lp.view(np.uint32))
+        assert xres.shape == (2 * L + 1, cfg.dim) and len(acts) == 4 * L + 1
+        for l in range(L):
+            for k, xi in ((0, 2 * l), (2, 2 * l + 1)):
+                np.testing.assert_array_equal(acts[4 * l + k][0].view(np.uint32),
+                                              plain.rmsnorm(xres[xi], w_att).view(np.uint32))
+        np.testing.assert_array_equal(acts[4 * L][0].view(np.uint32), plain.rmsnorm(xres[2 * L], w_att).view(np.uint32))
+        for ain, aq, asc in acts:
+            q, s = plain.quant_f32(ain)
+            np.testing.assert_array_equal(aq, q)
+            np.testing.assert_array_equal(asc.view(np.uint32), s.view(np.uint32))
+    for l in (0, L - 1):
+        for a, b in zip(mh.kv_rows(l, 0, 6), mp.kv_rows(l, 0, 6)):
+            np.testing.assert_array_equal(a, b)
