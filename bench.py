@@ -31,6 +31,8 @@ import sys
 import tempfile
 import time
 
+import numpy as np
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
@@ -69,6 +71,8 @@ def parse():
                     help="7b: the headline workload; 70b: the 70B-shape GQA model, 512-token prompt, 128 tokens")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the long-prompt prefill and GEMM measurements")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the long-context (2048-token prompt) and 70B-shape measurements")
     ap.add_argument("--layers", type=int, default=0,
                     help="truncate the 7B shape to this many layers (a small case of the same kernel, for profiling)")
     return ap.parse_args()
@@ -184,82 +188,148 @@ def build_model(cfg, kv_f32: bool, seed: int, rank: int = 0, world: int = 1, dev
 
 
 # ------------------------------------------------------------------ CPU baseline: the reference
-def _write_cpu_model(dirpath, cfg, seed, port, layers_from=None):
-    """Q8_0 cache files + header-only safetensors for the reference loader (quantised with the
-    oracle's load-time quantiser, bit-exact with the reference's)."""
+def physical_cores() -> int:
+    """Physical cores of this host (the reference's OpenMP loops run one thread per core)."""
+    try:
+        import psutil
+
+        n = psutil.cpu_count(logical=False)
+        if n:
+            return int(n)
+    except Exception:
+        pass
+    return os.cpu_count() or 1
+
+
+def host_weights(cfg, seed: int, device: int = 0):
+    """The seeded weights of build_model, tensor by tensor, brought to the host: (name, kind, value) with
+    value = (int8 q, fp32 s) planar Q8_0 or an fp32 vector.  Generated on the GPU from the same seeds and
+    quantised by the library's quantiser, which is bit-exact with the reference loader's
+    (convert_bf16_q8_0), so both arms run the same model."""
+    import torch
+
+    from diolkos_b200 import ops, synth
+
+    g = torch.Generator(device=f"cuda:{device}")
+    for idx, (name, kind, shape) in enumerate(synth.tensor_specs(cfg)):
+        n = 1
+        for d in shape:
+            n *= d
+        if kind == "norm":
+            yield name, kind, np.ones(n, np.float32)
+            continue
+        g.manual_seed(seed * 1000003 + idx)
+        with torch.cuda.device(device):
+            w = (torch.randn(n, generator=g, device=f"cuda:{device}", dtype=torch.float32) * 0.02).to(torch.bfloat16)
+            q, sc = ops.quantize_bf16(w.view(torch.int16))
+            torch.cuda.synchronize()
+            yield name, kind, (q.cpu().numpy(), sc.cpu().numpy())
+            del w, q, sc
+
+
+def write_reference_model(root: str, cfg, seed: int, name: str = "llama7b") -> str:
+    """The model directory the reference loads: config.json, a header-only safetensors and the Q8_0 / F32
+    cache files its loader reads instead of quantising (src/safetensors.c:57-114), written from
+    host_weights.  Returns the model directory (its cache sits in root/cache/<name>)."""
     from diolkos_b200 import synth
 
-    name = os.path.basename(dirpath)
-    synth.write_model(dirpath, cfg, seed, header_only=True)
-    cache = os.path.join(os.path.dirname(dirpath), "cache", name)
-    os.makedirs(cache, exist_ok=True)
-    for idx, (tname, kind, shape) in enumerate(synth.tensor_specs(cfg)):
-        if layers_from is not None:
-            src_f = os.path.join(layers_from, f"{tname}-{'Q8_0' if kind == 'q8' else 'F32'}.tensor")
-            dst_f = os.path.join(cache, os.path.basename(src_f))
-            if os.path.exists(src_f):
-                os.symlink(src_f, dst_f)
-                continue
-        bits = synth.gen_tensor(seed, idx, kind, shape)
+    md = os.path.join(root, name)
+    synth.write_model(md, cfg, seed, header_only=True)
+    cache = os.path.join(root, "cache", name)
+    for tname, kind, val in host_weights(cfg, seed):
         if kind == "q8":
-            q, s = port.quant_bf16(bits)
-            synth.write_q8_cache(cache, tname, q, s)
+            synth.write_q8_cache(cache, tname, val[0], val[1])
         else:
-            synth.write_f32_cache(cache, tname, synth.bf16_bits_to_f32(bits))
-    return cache
+            synth.write_f32_cache(cache, tname, val)
+    return md
 
 
 class CpuReference:
-    """Bounded sample of the 7B decode on the reference's CPU path (oracle/_ref, all host cores)."""
+    """The reference's own generate loop on the host cores: its unmodified sources compiled with its own
+    flags (oracle/_ref, -march=native build) driven through ref_driver.c (oref_generate: the loop of
+    src/bin/localinfer.c:42-99 on token ids), loading the decode workload's model -- the same weights as
+    the GPU arm -- from Q8_0 cache files, all physical cores.  Where the reference build is absent, the
+    restatement (oracle/port.c) runs the same loop."""
 
-    def __init__(self, cfg, positions: int = 12):
-        os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
-        from oracle import Port, Ref, ref_path
+    def __init__(self, cfg, seed: int = None):
+        seed = SEED if seed is None else seed
+        from oracle import Ref, ref_path
 
-        self.kind = "reference" if ref_path() else "port"
-        self.variant = "native" if ref_path("native") else "portable"
-        self.cores = int(os.environ["OMP_NUM_THREADS"])
+        self.cfg = cfg
+        self.want = physical_cores()
         self.tmp = tempfile.mkdtemp(prefix="dk_cpu_")
-        port = Port()
-        c3 = cfg.replace(n_layers=3)
-        c1 = cfg.replace(n_layers=1)
-        d3 = os.path.join(self.tmp, "llama7b_l3")
-        d1 = os.path.join(self.tmp, "llama7b_l1")
-        cache3 = _write_cpu_model(d3, c3, SEED, port)
-        _write_cpu_model(d1, c1, SEED, port, layers_from=cache3)
-        self.positions = positions
-        from diolkos_b200 import synth
-
-        self.prompt = synth.seeded_prompt(SEED, PROMPT_LEN)
+        self.kind = "reference" if ref_path("native") or ref_path() else "port"
         if self.kind == "reference":
-            ref = Ref(self.variant)  # the reference's own flags (-march=native) for timing
-            self.m1 = ref.load(d1, self.tmp)
-            self.m3 = ref.load(d3, self.tmp)
-        else:  # the restatement, when the reference build is not present
-            from oracle import PortModel, load_port_weights
+            self.variant = "native" if ref_path("native") else "portable"
+            ref = Ref(self.variant)
+            self.cores = ref.threads(self.want)  # overrides a launcher's OMP_NUM_THREADS=1
+            md = write_reference_model(self.tmp, cfg, seed)
+            self.m = ref.load(md, self.tmp)
+        else:
+            from oracle import Port, PortModel
 
-            self.m1 = PortModel(port, c1, load_port_weights(port, c1, SEED)[0])
-            self.m3 = PortModel(port, c3, load_port_weights(port, c3, SEED)[0])
-        self.n_layers = cfg.n_layers
+            os.environ["OMP_NUM_THREADS"] = str(self.want)
+            self.variant = "port"
+            self.cores = self.want
+            port = Port()
+            w = {}
+            from diolkos_b200.model import weight_id
 
-    def _tok_time(self, m) -> float:
-        toks = list(self.prompt[: self.positions])
+            for tname, kind, val in host_weights(cfg, seed):
+                w[(_port_key(weight_id(tname)[0]), weight_id(tname)[1])] = val
+            self.m = PortModel(port, cfg, w)
+
+    def generate(self, prompt, steps):
+        """(generated tokens, seconds of the positions that produced them, top-2 logits per token)."""
+        if self.kind == "reference":
+            return self.m.generate_timed(prompt, steps)
+        n_prompt = len(prompt)
         t0 = time.perf_counter()
-        for pos, tok in enumerate(toks):
-            m.forward(int(tok), pos)
-        return (time.perf_counter() - t0) / len(toks)
+        self.m.generate(prompt, n_prompt - 1)  # the forced positions alone
+        t1 = time.perf_counter()
+        toks = self.m.generate(prompt, steps)
+        t2 = time.perf_counter()
+        return toks, (t2 - t1) - (t1 - t0), None
 
-    def sample(self) -> float:
-        """Extrapolated decode tokens/s of the 32-layer model."""
-        t1 = self._tok_time(self.m1)
-        t3 = self._tok_time(self.m3)
-        per_layer = (t3 - t1) / 2.0
-        t32 = t1 + (self.n_layers - 1) * per_layer
-        return 1.0 / t32
+    def warm(self, prompt):
+        """Page the weights in: a few positions of the loop."""
+        self.generate(prompt, min(len(prompt), 4))
 
-    def describe(self) -> str:
-        return (f"7B-shape model with 1 and 3 layers (Q8_0, bf16 KV as in the reference), {self.positions} "
-                f"positions each; per-token time extrapolated linearly to {self.n_layers} layers")
+    def describe(self, P, G) -> str:
+        return (f"{'oracle/_ref (the reference built with its own flags, -march=' + self.variant + ')' if self.kind == 'reference' else 'oracle/port.c restatement'}: "
+                f"its generate loop over the {self.cfg.n_layers}-layer model with the GPU arm's weights, {P}-token "
+                f"prompt forced one position at a time, then {G} greedy tokens; tok/s = generated tokens / wall "
+                f"time of the positions that produced them; bf16 KV (the reference's); {self.cores} OpenMP threads "
+                f"({self.want} physical cores)")
+
+
+def _port_key(which: int) -> int:
+    import oracle
+    from diolkos_b200 import _native as N
+
+    return {N.DK_W_EMB: oracle.PW_EMB, N.DK_W_RMS_FINAL: oracle.PW_RMS_FINAL, N.DK_W_WCLS: oracle.PW_WCLS,
+            N.DK_W_RMS_ATT: oracle.PW_RMS_ATT, N.DK_W_WQ: oracle.PW_WQ, N.DK_W_WK: oracle.PW_WK,
+            N.DK_W_WV: oracle.PW_WV, N.DK_W_WO: oracle.PW_WO, N.DK_W_RMS_FFN: oracle.PW_RMS_FFN,
+            N.DK_W_W1: oracle.PW_W1, N.DK_W_W2: oracle.PW_W2, N.DK_W_W3: oracle.PW_W3}[which]
+
+
+# The reference's greedy stream of the decode workload (tests/golden/make_llama7b_stream.py: oracle/_ref
+# portable build, the GPU arm's weights): the check for runs that do not run the reference themselves.
+STREAM_FIXTURE = os.path.join(ROOT, "tests", "golden", "llama7b_greedy.json")
+
+
+def token_check(gpu_toks, ref_toks, ref_top2, source: str) -> dict:
+    """Greedy tokens of the GPU arm against a reference stream: identical count, first divergence and the
+    reference's top-2 logit gap there (relative to the top logit; a near-tie when small)."""
+    gpu_toks = [int(t) for t in gpu_toks]
+    ref_toks = [int(t) for t in ref_toks]
+    n = min(len(gpu_toks), len(ref_toks))
+    first = next((i for i in range(n) if gpu_toks[i] != ref_toks[i]), None)
+    out = {"identical": n if first is None else first, "of": n, "first_divergence": first, "vs": source}
+    if first is not None and ref_top2 is not None and first < len(ref_top2):
+        a, b = float(ref_top2[first][0]), float(ref_top2[first][1])
+        out["ref_top2_gap_at_divergence"] = round((a - b) / abs(a), 7) if a else None
+    return out
 
 
 # ------------------------------------------------------------------ GEMV microbenchmark (config 2)
@@ -404,32 +474,78 @@ def gemm_bench(cfg, ntok: int = GEMM_TOKENS, reps: int = 8):
 
 
 # ------------------------------------------------------------------ main arms
+def workload_config(cfg, model_name, P, G, kv: str, world: int, layers_note: str = "") -> dict:
+    """The `config` object both arms print for the decode workload."""
+    return {"workload": f"{model_name} q8_0 decode: {P}-token prompt, then {G} greedy tokens timed" + layers_note,
+            "model": model_name, "dim": cfg.dim, "hidden": cfg.hidden_dim, "layers": cfg.n_layers,
+            "heads": cfg.n_heads, "kv_heads": cfg.n_kv_heads, "vocab": cfg.vocab_size, "seq_len": cfg.seq_len,
+            "kv_cache": kv, "global_batch": 1,
+            "parallelism": "single GPU" if world == 1 else
+            f"tp{world}: heads / w1,w3 rows / classifier rows per GPU, wo and w2 partial sums exchanged inside "
+            f"the GEMVs over NVLink peer memory",
+            "l2": f"weights ({weight_bytes_per_token(cfg) / 1e9:.1f} GB) exceed L2; every token streams them from HBM"}
+
+
+# Wall-clock budget of the reference arm's timed steps: each step is the whole workload (tens of seconds on a
+# CPU); steps past the budget are not run, and the line says how many ran.
+REFERENCE_BUDGET_S = 150.0
+
+
 def run_reference(args):
+    """The reference arm: the reference's own generate loop (CpuReference) over the decode workload, each
+    timed step one full run of it (32-token prompt forced one position at a time, 256 greedy tokens)."""
     from diolkos_b200 import synth
 
-    cfg = synth.LLAMA7B
+    cfg, P, G, model_name = _models()["7b"]
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
+    import torch
+
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))  # only to generate the seeded weights
     cpu = CpuReference(cfg)
+    prompt = synth.seeded_prompt(SEED, P, cfg.vocab_size)
     for _ in range(args.warmup):
-        cpu.sample()
-    vals = [cpu.sample() for _ in range(args.steps)]
-    v = statistics.mean(vals)
+        cpu.warm(prompt)
+    n_tok, secs, runs = 0, 0.0, 0
+    toks = None
+    t_start = time.perf_counter()
+    for _ in range(args.steps):
+        toks, gs, _ = cpu.generate(prompt, P - 1 + G)
+        n_tok += len(toks)
+        secs += gs
+        runs += 1
+        if time.perf_counter() - t_start > REFERENCE_BUDGET_S:
+            break
+    v = n_tok / secs
+    kv = "bf16 (the reference's)"
     line = {
         "impl": "reference", "metric": "Q8_0 decode tok/s batch 1", "value": round(v, 3), "unit": "tok/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 / v, 2),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
-        "data": "synthetic (seeded N(0,0.02) weights, seeded prompt)",
-        "config": {"workload": f"llama2-7b-shape q8_0 decode: {PROMPT_LEN}-token prompt, then {GEN_LEN} greedy "
-                               f"tokens timed",
-                   "model": "llama2-7b-shape", "kv_cache": "bf16 (the reference's)"},
+        "n_gpus": args.gpus, "steps": args.steps, "steps_run": runs, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * secs / runs, 2), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded N(0,0.02) weights, seeded prompt)",
+        "config": workload_config(cfg, model_name, P, G, kv, args.gpus),
         "cpu_baseline": {"value": round(v, 3), "unit": "tok/s", "cores": cpu.cores, "kind": cpu.kind,
-                         "sample": cpu.describe()},
+                         "sample": cpu.describe(P, G) + f"; {runs} full run(s) of the workload"},
         "e2e": {"value": round(v, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "tokens_sample": [int(t) for t in toks[:8]],
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+LONG_PROMPT = 2048  # config 4: the long prompt, prefilled on the tensor cores, then GEN_LEN decode tokens
+
+
+def decode_roofline(cfg, P, G, ms_per_tok, world, kv_f32) -> dict:
+    """Weight + KV bytes per token over the decode positions P-1 .. P-2+G, per rank, against the HBM peak."""
+    elem = 4 if kv_f32 else 2
+    bytes_tok = weight_bytes_per_token(cfg) + kv_bytes_read(cfg, P - 1, P - 1 + G, elem) / G
+    hbm, kind = peaks()
+    rank_gbps = bytes_tok / world / (ms_per_tok / 1e3) / 1e9
+    return {"bound": "hbm", "achieved": round(rank_gbps, 1), "peak": hbm, "unit": "GB/s",
+            "frac": round(rank_gbps / hbm, 4), "bytes_per_token_per_rank": round(bytes_tok / world),
+            "what": f"weight + KV bytes per token per rank / time per token; peak = {kind} HBM copy bandwidth"}
 
 
 def run_decode(args):
@@ -453,7 +569,7 @@ def run_decode(args):
 
         if int(os.environ.get("WORLD_SIZE", "1")) != world:
             raise RuntimeError(f"--gpus {world} needs {world} ranks (torchrun --nproc-per-node {world})")
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
 
     def barrier():
         if dist is not None:
@@ -466,32 +582,60 @@ def run_decode(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    def check_err(m, what):
+        err = int(max_over_ranks(float(m.device_error())))  # every rank takes the same exit
+        if err:
+            raise RuntimeError(f"device error word 0x{err:x} {what}")
+
     m = build_model(cfg, kv_f32, SEED, rank, world, local)
     stream = torch.cuda.ExternalStream(m.stream)
     prompt = synth.seeded_prompt(SEED, P, cfg.vocab_size)
 
-    def one_step(record=None):
-        m.set_tokens(prompt, n_forced=P)
+    def one_step(mm, pr, g, record=None):
+        mm.set_tokens(pr, n_forced=len(pr))
         if record:
-            record[2].record(stream)
-        m.prefill(0, P - 1)  # the forced prompt positions on the tensor cores
+            record[2].record(stream_of[id(mm)])
+        mm.prefill(0, len(pr) - 1)  # the forced prompt positions on the tensor cores
         if record:
-            record[0].record(stream)
-        m.enqueue_steps(P - 1, G)
+            record[0].record(stream_of[id(mm)])
+        mm.enqueue_steps(len(pr) - 1, g)
         if record:
-            record[1].record(stream)
+            record[1].record(stream_of[id(mm)])
 
+    stream_of = {id(m): stream}
+
+    def timed_decode(mm, pr, g, steps, warmup):
+        """warm-up, then `steps` timed runs of prefill + g greedy tokens: (decode ms, prompt ms per run)."""
+        torch.cuda.synchronize()
+        barrier()
+        for _ in range(warmup):
+            one_step(mm, pr, g)
+        mm.sync()
+        check_err(mm, "after warm-up")
+        torch.cuda.synchronize()
+        barrier()
+        evs = []
+        for _ in range(steps):
+            e = tuple(torch.cuda.Event(enable_timing=True) for _ in range(3))
+            one_step(mm, pr, g, e)
+            evs.append(e)
+        mm.sync()
+        torch.cuda.synchronize()
+        barrier()
+        dec = max_over_ranks(sum(a.elapsed_time(b) for a, b, _ in evs))
+        pro = max_over_ranks(sum(c.elapsed_time(a) for a, _, c in evs)) / steps
+        check_err(mm, "after the timed runs")
+        return dec, pro
+
+    # ---- headline: the decode workload (config 3 at N = 1, its tensor-parallel split at N > 1)
+    sampler = ClockSampler(",".join(str(i) for i in range(world)) if rank == 0 else local)
     # the ranks start together: the prefill's and the decode step's cross-rank waits are bounded
     torch.cuda.synchronize()
     barrier()
     for _ in range(args.warmup):
-        one_step()
+        one_step(m, prompt, G)
     m.sync()
-    err = int(max_over_ranks(float(m.device_error())))  # every rank takes the same exit
-    if err:
-        raise RuntimeError(f"device error word 0x{err:x} after warm-up")
-
-    sampler = ClockSampler(",".join(str(i) for i in range(world)) if rank == 0 else local)
+    check_err(m, "after warm-up")
     if rank == 0:
         sampler.start()
     torch.cuda.synchronize()
@@ -501,7 +645,7 @@ def run_decode(args):
     evs = []
     for _ in range(args.steps):
         e = tuple(torch.cuda.Event(enable_timing=True) for _ in range(3))
-        one_step(e)
+        one_step(m, prompt, G, e)
         evs.append(e)
     m.sync()
     torch.cuda.synchronize()
@@ -510,9 +654,7 @@ def run_decode(args):
     clocks = sampler.stop() if rank == 0 else None
     decode_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b, _ in evs))
     prompt_ms = max_over_ranks(sum(c.elapsed_time(a) for a, _, c in evs)) / args.steps
-    err = int(max_over_ranks(float(m.device_error())))
-    if err:
-        raise RuntimeError(f"device error word 0x{err:x}")
+    check_err(m, "after the timed steps")
     toks = m.get_tokens(P + G)
 
     value = G * args.steps / (decode_ms / 1e3)
@@ -535,15 +677,57 @@ def run_decode(args):
         n_gen = len(gen)
     e2e = n_gen * len(e2e_times) / sum(e2e_times)
     kernels_per_step = m.kernels_per_step
+
+    # ---- config 4: 2048-token prompt prefilled on the tensor cores, then 256 tokens at long context
+    long_ctx = None
+    if args.model == "7b" and not args.no_extra and not args.layers:
+        Lp = min(LONG_PROMPT, cfg.seq_len - G)
+        lprompt = synth.seeded_prompt(SEED + 1, Lp, cfg.vocab_size)
+        s2 = ClockSampler(",".join(str(i) for i in range(world)) if rank == 0 else local)
+        if rank == 0:
+            s2.start()
+        dec, pro = timed_decode(m, lprompt, G, 2, 1)
+        c2 = s2.stop() if rank == 0 else None
+        mt = dec / (2 * G)
+        long_ctx = {"workload": f"llama2-7b-shape: {Lp}-token seeded prompt, its {Lp - 1} forced positions prefilled "
+                                f"(int8 tensor-core matmuls{', tensor parallel' if world > 1 else ''}), then {G} greedy "
+                                f"tokens at positions {Lp - 1}..{Lp - 2 + G}",
+                    "value": round(G / (mt / 1e3), 2), "unit": "tok/s", "ms_per_token": round(mt, 4),
+                    "prefill_ms": round(pro, 3), "prefill_positions_per_s": round((Lp - 1) / (pro / 1e3), 1),
+                    "roofline": decode_roofline(cfg, Lp, G, mt, world, kv_f32), "steps": 2, "warmup": 1,
+                    "clocks": c2}
+
     long_prefill = prefill_bench(m, cfg) if world == 1 and not args.no_prefill else None
     m.close()  # every rank leaves the exchange at the same point
     barrier()
+
+    # ---- config 5: the 70B-shape GQA model, 512-token prompt, 128 greedy tokens
+    big = None
+    if args.model == "7b" and not args.no_extra and not args.layers:
+        c70, P70, G70, name70 = _models()["70b"]
+        m70 = build_model(c70, kv_f32, SEED, rank, world, local)
+        stream_of[id(m70)] = torch.cuda.ExternalStream(m70.stream)
+        pr70 = synth.seeded_prompt(SEED, P70, c70.vocab_size)
+        s3 = ClockSampler(",".join(str(i) for i in range(world)) if rank == 0 else local)
+        if rank == 0:
+            s3.start()
+        dec, pro = timed_decode(m70, pr70, G70, 2, 1)
+        c3 = s3.stop() if rank == 0 else None
+        mt = dec / (2 * G70)
+        big = {"workload": f"{name70} (dim {c70.dim}, hidden {c70.hidden_dim}, {c70.n_layers} layers, {c70.n_heads} "
+                           f"heads over {c70.n_kv_heads} KV heads): {P70}-token prompt prefilled, then {G70} greedy "
+                           f"tokens", "value": round(G70 / (mt / 1e3), 2), "unit": "tok/s", "ms_per_token": round(mt, 4),
+               "prefill_ms": round(pro, 3), "roofline": decode_roofline(c70, P70, G70, mt, world, kv_f32),
+               "weight_gb": round(weight_bytes_per_token(c70) / 1e9, 2), "steps": 2, "warmup": 1, "clocks": c3}
+        m70.close()
+        barrier()
+
     if dist is not None:
         dist.destroy_process_group()
     if rank != 0:
         return 0
 
-    # The dominant kernel: the GEMV, over this rank's shapes and launch counts of one decode step.
+    # The dominant kernel's companion: the GEMV over this rank's shapes and launch counts of one decode step.
     sh = tp.shard(cfg, rank, world)
     ld, lkv, lh = sh.q_rows[1] - sh.q_rows[0], sh.kv_rows[1] - sh.kv_rows[0], sh.hidden_rows[1] - sh.hidden_rows[0]
     lv = sh.vocab_rows[1] - sh.vocab_rows[0]
@@ -556,32 +740,36 @@ def run_decode(args):
     mix_us = sum(c * mix[f"{d}x{n}"]["us"] for d, n, c in decode_gemvs)
     launches = sum(c for _, _, c in decode_gemvs)
     gemv_gbps = mix_bytes / mix_us / 1e3
-    cpu = None
-    if not args.no_cpu_baseline and world == 1 and args.model == "7b":
+
+    # ---- the reference on the host cores (N = 1): one full run of the workload; its greedy stream
+    cpu, checks = None, {}
+    gpu_toks = [int(t) for t in toks[P:P + G]]
+    if not args.no_cpu_baseline and world == 1 and args.model == "7b" and not args.layers:
         try:
             cb = CpuReference(cfg)
-            cb.sample()
-            v = statistics.mean(cb.sample() for _ in range(2))
-            cpu = {"value": round(v, 3), "unit": "tok/s", "cores": cb.cores, "kind": cb.kind, "sample": cb.describe()}
+            cb.warm(prompt)
+            rt, secs, top2 = cb.generate(prompt, P - 1 + G)
+            v = len(rt) / secs
+            cpu = {"value": round(v, 3), "unit": "tok/s", "cores": cb.cores, "kind": cb.kind,
+                   "sample": cb.describe(P, G) + "; one full run of the workload"}
+            checks["this_run"] = token_check(gpu_toks, rt, top2, f"this run's {cb.kind} ({cb.variant} build)")
         except Exception as ex:  # the baseline is reported, never required
-            cpu = {"value": None, "unit": "tok/s", "cores": os.cpu_count(), "kind": "reference",
+            cpu = {"value": None, "unit": "tok/s", "cores": physical_cores(), "kind": "reference",
                    "sample": f"not run: {ex}"}
+    if args.model == "7b" and not args.layers and os.path.exists(STREAM_FIXTURE):
+        with open(STREAM_FIXTURE) as f:
+            fx = json.load(f)
+        if fx.get("seed") == SEED and fx.get("prompt") == [int(t) for t in prompt]:
+            checks["fixture"] = token_check(gpu_toks, fx["tokens"], fx.get("top2"),
+                                            f"{os.path.relpath(STREAM_FIXTURE, ROOT)} ({fx.get('reference')})")
 
     line = {
         "metric": "Q8_0 decode tok/s batch 1", "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(decode_ms / args.steps, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
         "data": "synthetic (seeded N(0,0.02) weights, seeded prompt)",
-        "config": {"workload": f"{model_name} q8_0 decode: {P}-token prompt, then {G} greedy tokens timed"
-                               + (f" ({cfg.n_layers} layers: profiling case)" if args.layers else ""),
-                   "model": model_name, "dim": cfg.dim, "hidden": cfg.hidden_dim, "layers": cfg.n_layers,
-                   "heads": cfg.n_heads, "kv_heads": cfg.n_kv_heads, "vocab": cfg.vocab_size,
-                   "seq_len": cfg.seq_len, "kv_cache": args.kv, "global_batch": 1,
-                   "parallelism": "single GPU" if world == 1 else
-                   f"tp{world}: heads / w1,w3 rows / classifier rows per GPU, wo and w2 partial sums "
-                   f"exchanged inside the GEMVs over NVLink peer memory",
-                   "l2": f"weights ({weight_bytes_per_token(cfg) / 1e9:.1f} GB) exceed L2; every token streams them "
-                         f"from HBM"},
+        "config": workload_config(cfg, model_name, P, G, args.kv, world,
+                                  f" ({cfg.n_layers} layers: profiling case)" if args.layers else ""),
         "ms_per_token": round(ms_per_tok, 4),
         # the prefill launches per chunk 10 kernels per layer (activation, matmul, KV write, attention, then
         # activation + matmul for wo, w1|w3, w2; tensor parallel: + scatter, signal, wait, reduce after wo
@@ -597,19 +785,21 @@ def run_decode(args):
                              f"(CUDA events around back-to-back steps); peak = {peak_kind} HBM copy bandwidth; "
                              f"traffic = DRAM bytes per launch"},
         "gemv_roofline": {"bound": "hbm", "achieved": round(gemv_gbps, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(gemv_gbps / hbm, 4),
-                     "traffic": (round(NCU_GEMV_TRAFFIC_RATIO * mix_bytes / launches)
-                                 if NCU_GEMV_TRAFFIC_RATIO else None),
-                     "kernel": "gemv_q8_kernel",
-                     "what": f"Q8_0 GEMV over one decode step's {launches} launches on rank 0 (shapes "
-                             f"{decode_gemvs}): "
-                             f"{mix_bytes / launches / 1e6:.2f} MB algorithmic bytes per launch / "
-                             f"{mix_us / launches:.2f} us average launch (CUDA events, back-to-back batches); "
-                             f"peak = {peak_kind} HBM copy bandwidth; traffic = DRAM bytes per launch"},
+                          "frac": round(gemv_gbps / hbm, 4),
+                          "traffic": (round(NCU_GEMV_TRAFFIC_RATIO * mix_bytes / launches)
+                                      if NCU_GEMV_TRAFFIC_RATIO else None),
+                          "kernel": "gemv_q8_kernel",
+                          "what": f"Q8_0 GEMV over one decode step's {launches} launches on rank 0 (shapes "
+                                  f"{decode_gemvs}): {mix_bytes / launches / 1e6:.2f} MB algorithmic bytes per launch / "
+                                  f"{mix_us / launches:.2f} us average launch (CUDA events, back-to-back batches); "
+                                  f"peak = {peak_kind} HBM copy bandwidth; traffic = DRAM bytes per launch"},
         "step_roofline": {"achieved": round(achieved, 1), "frac": round(achieved / (hbm * world), 4),
                           "unit": "GB/s",
                           "what": f"whole decode step: weight + KV bytes per token ({bytes_tok / 1e9:.3f} GB) / "
                                   f"time per token, against {world} x the HBM peak"},
+        "tokens_check": checks or None,
+        "long_context": long_ctx,
+        "llama70b": big,
         "gemv": gemv,
         "gemv_decode_shapes": mix,
         "prompt_prefill_ms": round(prompt_ms, 3),
@@ -621,7 +811,7 @@ def run_decode(args):
         "cpu_baseline": cpu,
         "clocks": clocks,
         "wall_s_timed_region": round(wall, 3),
-        "tokens_sample": [int(t) for t in toks[P:P + 8]],
+        "tokens_sample": gpu_toks[:8],
     }
     print(json.dumps(line), flush=True)
     return 0

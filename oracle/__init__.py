@@ -224,7 +224,10 @@ class Ref:
         L.oref_forward.argtypes = [C.c_void_p, C.c_int, C.c_int, _f32p]
         L.oref_state_x.argtypes = [C.c_void_p, _f32p]
         L.oref_kv_rows.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, _u16p, _u16p]
-        L.oref_generate.argtypes = [C.c_void_p, _i32p, C.c_int, C.c_int, _i32p, C.POINTER(C.c_double)]
+        L.oref_generate.argtypes = [C.c_void_p, _i32p, C.c_int, C.c_int, _i32p, C.POINTER(C.c_double),
+                                    C.POINTER(C.c_double), C.c_void_p]
+        L.oref_threads.argtypes = [C.c_int]
+        L.oref_threads.restype = C.c_int
         L.oref_generate.restype = C.c_int
         L.oref_quant_f32.argtypes = [_f32p, C.c_size_t, _i8p, _f32p]
         L.oref_quant_bf16.argtypes = [_u16p, C.c_size_t, _i8p, _f32p]
@@ -240,6 +243,10 @@ class Ref:
         L.oref_argmax.restype = C.c_int
         L.oref_sample.argtypes = [_f32p, C.c_int, C.c_float, C.c_float, C.POINTER(C.c_ulonglong)]
         L.oref_sample.restype = C.c_int
+
+    def threads(self, n: int = 0) -> int:
+        """Set (n > 0) and return the OpenMP thread count of the reference's parallel loops."""
+        return int(self.lib.oref_threads(n))
 
     def quant_f32(self, x):
         x = np.ascontiguousarray(x, np.float32).ravel()
@@ -305,8 +312,18 @@ class RefModel:
         p = np.ascontiguousarray(prompt, np.int32)
         out = np.empty(max(steps, 1), np.int32)
         tps = C.c_double(0.0)
-        n = self.ref.lib.oref_generate(self.h, p, p.size, steps, out, C.byref(tps))
+        n = self.ref.lib.oref_generate(self.h, p, p.size, steps, out, C.byref(tps), None, None)
         return out[:n].copy(), tps.value
+
+    def generate_timed(self, prompt, steps):
+        """The reference's generate loop: (generated tokens, wall seconds of the positions that produced
+        them, top-2 logits per generated token [n][2])."""
+        p = np.ascontiguousarray(prompt, np.int32)
+        out = np.empty(max(steps, 1), np.int32)
+        top2 = np.empty((max(steps, 1), 2), np.float32)
+        tps, gs = C.c_double(0.0), C.c_double(0.0)
+        n = self.ref.lib.oref_generate(self.h, p, p.size, steps, out, C.byref(tps), C.byref(gs), top2.ctypes.data)
+        return out[:n].copy(), gs.value, top2[:n].copy()
 
     def kv_rows(self, layer, pos0, n):
         """The reference's bf16 KV-cache rows (uint16 bits) of positions pos0 .. pos0+n-1: (k, v), [n][kv_dim]."""

@@ -10,6 +10,7 @@
 #define _GNU_SOURCE
 #include <errno.h>
 #include <limits.h>
+#include <math.h>
 #include <stdint.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -17,6 +18,8 @@
 #include <sys/stat.h>
 #include <time.h>
 #include <unistd.h>
+
+#include <omp.h>
 
 #include "safetensors.h"
 #include "sampler.h"
@@ -96,21 +99,45 @@ static double now_s(void) {
     return (double)ts.tv_sec + 1e-9 * (double)ts.tv_nsec;
 }
 
+/* The OpenMP thread count the reference's parallel loops use: n > 0 sets it (omp_set_num_threads,
+ * overriding OMP_NUM_THREADS, which a multi-process launcher may have set to 1); returns the count
+ * in effect. */
+int oref_threads(int n) {
+    if (n > 0) omp_set_num_threads(n);
+    return omp_get_max_threads();
+}
+
 /* The greedy token loop of generate (localinfer.c:42-99) fed with token ids instead of a text
  * prompt: prompt tokens are forced one position at a time, the next token is sampled with the
  * reference's sample() at temperature 0 once the prompt is consumed, the loop stops when the
  * sampled token is 1, and the clock starts after the first forward.  Returns the number of
- * generated (non-forced) tokens written to out; *tok_s gets the reference's tok/s figure. */
-int oref_generate(void *hp, const int *prompt, int n_prompt, int steps, int *out, double *tok_s) {
+ * generated (non-forced) tokens written to out; *tok_s gets the reference's tok/s figure.
+ * Optional (NULL: skipped): *gen_s = wall seconds of the positions that produced the generated
+ * tokens (forward + sample, from position n_prompt-1 on); top2[2*i], top2[2*i+1] = the two largest
+ * logits at the position that produced generated token i. */
+int oref_generate(void *hp, const int *prompt, int n_prompt, int steps, int *out, double *tok_s, double *gen_s,
+                  float *top2) {
     ORef *h = hp;
+    const int vocab = h->t.config.vocab_size;
     int token = prompt[0], pos = 0, n_out = 0;
-    double start = 0.0;
+    double start = 0.0, gen0 = 0.0;
     while (pos < steps) {
+        if (pos == n_prompt - 1) gen0 = now_s();
         Tensor *lg = forward(&h->t, token, pos);
         int next;
         if (pos < n_prompt - 1) {
             next = prompt[pos + 1];
         } else {
+            if (top2) {
+                const float *l = (const float *)lg->data;
+                float a = -INFINITY, b = -INFINITY;
+                for (int i = 0; i < vocab; i++) {
+                    if (l[i] > a) { b = a; a = l[i]; }
+                    else if (l[i] > b) b = l[i];
+                }
+                top2[2 * n_out] = a;
+                top2[2 * n_out + 1] = b;
+            }
             next = sample(&h->greedy, (float *)lg->data);
             out[n_out++] = next;
         }
@@ -119,7 +146,9 @@ int oref_generate(void *hp, const int *prompt, int n_prompt, int steps, int *out
         token = next;
         if (start == 0.0) start = now_s();
     }
-    if (tok_s) *tok_s = (pos > 1) ? (double)(pos - 1) / (now_s() - start) : 0.0;
+    const double end = now_s();
+    if (tok_s) *tok_s = (pos > 1) ? (double)(pos - 1) / (end - start) : 0.0;
+    if (gen_s) *gen_s = (n_out > 0) ? end - gen0 : 0.0;
     return n_out;
 }
 
