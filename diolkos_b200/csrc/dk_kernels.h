@@ -262,7 +262,13 @@ struct StepArgs {
     int seq_len = 0;
     int *err = nullptr;
     unsigned long long *trace = nullptr;  // optional timeline [grid][nops][8] (globaltimer, ns)
+    // optional per-stage timeline of ops stage_op0 .. stage_op0 + kStageTraceOps - 1 on the first
+    // kStageTraceCtas CTAs: [op][cta][stage][4] = data landed, terms computed, running sums received, passed on
+    unsigned long long *stage_trace = nullptr;
+    int stage_op0 = 0;
 };
+constexpr int kStageTraceOps = 5, kStageTraceCtas = 4, kStageTraceStages = 64;
+constexpr size_t kStageTraceEntries = (size_t)kStageTraceOps * kStageTraceCtas * kStageTraceStages * 4;
 size_t step_ctl_bytes();
 size_t step_attn_scratch_bytes(int n_heads, int n_kv_heads, int head_size);
 int step_attn_item_slots(int num_ctas);

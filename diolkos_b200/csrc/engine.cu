@@ -715,10 +715,12 @@ static int build_step(dk_model *m) {
     sa.nops = m->n_ops;
     if (const char *e = getenv("DIOLKOS_STEP_TRACE"))
         if (atoi(e) > 0) {
-            const size_t tb = (size_t)m->num_sms * m->n_ops * 8 * 8;
+            const size_t tb = ((size_t)m->num_sms * m->n_ops * 8 + kStageTraceEntries) * 8;
             if (cudaMalloc(&m->d_trace, tb) != cudaSuccess || cudaMemset(m->d_trace, 0, tb) != cudaSuccess)
                 return set_error(DK_ERR_NOMEM, "persistent step: trace buffer");
             sa.trace = m->d_trace;
+            sa.stage_trace = m->d_trace + (size_t)m->num_sms * m->n_ops * 8;
+            sa.stage_op0 = m->n_layers > 1 ? 5 : 0;  // the second layer's five ops
         }
     const int per_sm = step_max_ctas_per_sm(sa.smem);
     if (per_sm < 1)
@@ -887,8 +889,9 @@ int dk_model_trace(dk_model *m, unsigned long long *out, size_t n, int *grid, in
     if (grid) *grid = m->num_sms;
     if (n_ops) *n_ops = m->n_ops;
     if (!m->d_trace) return set_error(DK_ERR_STATE, "dk_model_trace: tracing is off (DIOLKOS_STEP_TRACE=1 at creation)");
-    const size_t total = (size_t)m->num_sms * m->n_ops * 8;
+    size_t total = (size_t)m->num_sms * m->n_ops * 8;
     if (!out || n < total) return set_error(DK_ERR_INVALID, "dk_model_trace: need %zu entries", total);
+    if (n >= total + kStageTraceEntries) total += kStageTraceEntries;  // the per-stage timeline too
     return cuda_status(cudaMemcpy(out, m->d_trace, total * 8, cudaMemcpyDeviceToHost), "dk_model_trace");
 }
 

@@ -27,6 +27,7 @@
 #include "gemv_core.cuh"
 
 #include <algorithm>
+#include <cstdlib>
 #include <cmath>
 
 namespace dk {
@@ -282,9 +283,9 @@ __global__ void __launch_bounds__(32 * kMinWarps, 2) gemv_q8_kernel(const GemvAr
     float *red = xs + ((n / 32 + 3) & ~3);                           // [kMinWarps]
     uint64_t *full = reinterpret_cast<uint64_t *>(red + kMinWarps);  // [kMaxSlots]
     uint64_t *empty = full + kMaxSlots;                              // [kMaxSlots]
-    int *tokflag = reinterpret_cast<int *>(empty + kMaxSlots);       // [kMaxConsumers] (padded to 8 B each)
-    float *tokval = reinterpret_cast<float *>(tokflag + 2 * kMaxConsumers);  // [kMaxConsumers][32]
-    unsigned long long *wkey = reinterpret_cast<unsigned long long *>(tokval + kMaxConsumers * 32);
+    // running row sums handed to each consumer warp: per lane one word = (stage index << 32) | sum bits
+    unsigned long long *tok = reinterpret_cast<unsigned long long *>(empty + kMaxSlots);  // [kMaxConsumers][32]
+    unsigned long long *wkey = tok + kMaxConsumers * 32;
     int *flags = reinterpret_cast<int *>(wkey + kMaxConsumers);      // [0] abort, [1] last CTA
     const uint32_t ring_s = smem_u32(ring), xq_s = smem_u32(xq), xs_s = smem_u32(xs);
 
@@ -302,7 +303,7 @@ __global__ void __launch_bounds__(32 * kMinWarps, 2) gemv_q8_kernel(const GemvAr
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
         }
-        for (int i = 0; i < NC; ++i) tokflag[2 * i] = -1;
+        for (int i = 0; i < NC * 32; ++i) tok[i] = 0xFFFFFFFF00000000ull;  // tag -1
         flags[0] = 0;
         flags[1] = 0;
         mbar_fence_init();
@@ -392,12 +393,13 @@ __global__ void __launch_bounds__(32 * kMinWarps, 2) gemv_q8_kernel(const GemvAr
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
             float sum = 0.0f;
-            if (s > 0) {  // the running sums of stage s-1
-                if (!__all_sync(FULL, token_wait(&tokflag[2 * c], s, a.err, flags))) {
+            if (s > 0) {  // the running sum of this lane's row after stage s-1
+                float prev = 0.0f;
+                if (!__all_sync(FULL, lane_token_wait(&tok[c * 32], lane, s, prev, a.err, flags))) {
                     if (lane == 0) flags[0] = 1;
                     break;
                 }
-                if (b > 0) sum = tokval[c * 32 + lane];
+                if (b > 0) sum = prev;
             }
             if (live) {
                 if (wb == 512) {
@@ -434,12 +436,10 @@ __global__ void __launch_bounds__(32 * kMinWarps, 2) gemv_q8_kernel(const GemvAr
                     }
                 }
             }
-            if (s + 1 < sc.nst) {  // pass the running sums to the warp of stage s+1
+            if (s + 1 < sc.nst) {  // pass this row's running sum to the warp of stage s+1: one tagged word
                 const int cn = (c + 1) % NC;
-                tokval[cn * 32 + lane] = sum;
-                __threadfence_block();
-                __syncwarp();
-                if (lane == 0) *reinterpret_cast<volatile int *>(&tokflag[2 * cn]) = s + 1;
+                *reinterpret_cast<volatile unsigned long long *>(&tok[cn * 32 + lane]) =
+                    ((unsigned long long)(unsigned)(s + 1) << 32) | (unsigned long long)__float_as_uint(sum);
             }
         }
         if constexpr (EPI == EPI_ARGMAX) {
@@ -547,8 +547,8 @@ bool gemv_supported(int n, int d, int epi) {
 }
 
 size_t gemv_smem_tail(int n) {
-    return gemv_x_bytes(n) + kMinWarps * 4 + 2 * kMaxSlots * 8 + kMaxConsumers * 8 + kMaxConsumers * 32 * 4 +
-           kMaxConsumers * 8 + 16;  // activation, red, full/empty, token flags, token sums, warp keys, flags
+    return gemv_x_bytes(n) + kMinWarps * 4 + 2 * kMaxSlots * 8 + kMaxConsumers * 32 * 8 + kMaxConsumers * 8 +
+           16;  // activation, red, full/empty, tagged token words, warp keys, flags
 }
 
 GemvPlan plan_gemv(int n, int d, int epi, int num_sms) {
@@ -568,7 +568,9 @@ GemvPlan plan_gemv(int n, int d, int epi, int num_sms) {
     p.S = std::max(1, std::min({kMaxSlots, (int)(ring / p.slot), stages}));
     if (p.S >= 2) p.S -= p.S % p.NP;
     else p.NP = 1;
-    p.NW = std::max(1, std::min({4, p.S, stages}));
+    int nc = 4;
+    if (const char *e = getenv("DIOLKOS_GEMV_NC")) nc = std::max(1, std::min(atoi(e), kMaxConsumers));
+    p.NW = std::max(1, std::min({nc, p.S, stages}));
     p.PF = kPrefetchStages;
     p.xoff = (size_t)p.S * p.slot;
     p.smem = p.xoff + tail;

@@ -40,20 +40,28 @@ __device__ __forceinline__ void load_quad(Quad &d, int q, uint32_t seg, uint32_t
     }
 }
 
-// Wait until the token flag says the running sums of stage s-1 have been handed to this warp (the flag
-// holds the index of the stage they are for).  A plain shared-memory flag: a hand-off is on the
-// critical path of every stage, and polling a volatile word sees it sooner than an mbarrier phase.
-// Bounded like every wait, and abandoned as soon as another warp raised the CTA's abort flag.
-__device__ __forceinline__ bool token_wait(const int *flag, int s, int *err, const int *abort) {
-    const volatile int *f = flag;
-    if (*f == s) {
-        __threadfence_block();
-        return true;
-    }
+// Wait until this lane's token word carries stage G's tag, then take the running sum from it.  The
+// sender warp stores all 32 words with one instruction, so the warp first polls word 0 (one broadcast
+// read per poll: polling warps then cost the consumers computing terms little shared-memory bandwidth),
+// then reads its own word, polling on only in the rare case that it has not landed yet.  A word is
+// single-copy atomic, so the sum and its tag arrive together: no fence, no separate flag.  Bounded, and
+// abandoned on the CTA's abort flag.
+__device__ __forceinline__ bool lane_token_wait(const unsigned long long *row0, int lane, int G, float &sum, int *err,
+                                                const int *abort) {
+    const volatile unsigned long long *p0 = row0;
+    const volatile unsigned long long *p = row0 + lane;
     const long long t0 = clock64();
+    while ((unsigned)(p0[0] >> 32) != (unsigned)G) {
+        if (*reinterpret_cast<const volatile int *>(abort)) return false;
+        if (clock64() - t0 > DK_WAIT_LIMIT_CYCLES) {
+            atomicOr(err, DK_ERR_TIMEOUT);
+            return false;
+        }
+    }
     for (;;) {
-        if (*f == s) {
-            __threadfence_block();
+        const unsigned long long v = *p;
+        if ((unsigned)(v >> 32) == (unsigned)G) {
+            sum = __uint_as_float((unsigned)v);
             return true;
         }
         if (*reinterpret_cast<const volatile int *>(abort)) return false;

@@ -61,12 +61,19 @@ struct StepCtl {  // shared-memory control block
     uint64_t empty[kStepMaxSlots];   // ring slot read by its consumer
     unsigned long long wkey[kStepMaxConsumers];  // consumers' best greedy-token keys of the op
     float red[kStepWarps];
-    float tokval[kStepMaxConsumers][32];  // running row sums handed to each consumer warp
-    int tokflag[kStepMaxConsumers];       // global index of the stage they are for
+    // running row sums handed to each consumer warp, one 64-bit word per lane: the global index of the
+    // stage they are for (high half) and the sum's bits (low half), stored and polled as one word
+    unsigned long long tok[kStepMaxConsumers][32];
     int abort;      // any wait gave up: every warp leaves
     int last;       // this CTA took the classifier's last ticket
     int grp_last[kAttnGroups];
+    // The compute warps' copies of the op descriptors: op i sits in opbuf[i % 3].  Op i+1 is loaded into
+    // registers while op i runs and stored here before op i's last barrier, so no read of a descriptor
+    // waits on the L2 at an op boundary; three slots keep op i-1's descriptor intact for its stragglers.
+    alignas(16) unsigned long long opbuf[3][(sizeof(StepOp) + 7) / 8];
 };
+constexpr int kOpWords = (int)((sizeof(StepOp) + 7) / 8);
+static_assert(kOpWords <= kComputeThreads - 32, "one descriptor word per thread of warps 1..");
 
 // Self-checking build (-DDK_STEP_CHECKS): every global and shared access below whose index is not
 // trivially in range is tested first; a failed test records the site and value (first one only, with
@@ -100,6 +107,21 @@ __device__ __forceinline__ void trace_mark(const StepArgs &sa, int op, int k) {
 
 __device__ __forceinline__ void bar_compute() {
     asm volatile("bar.sync %0, %1;" ::"n"(kBarCompute), "n"(kComputeThreads) : "memory");
+}
+// The compute warps' barrier that also tells every thread whether any of them passed v != 0: a flag
+// that another warp may raise while the compute warps arrive (the producers' abort) is read once per
+// thread before the barrier, and the OR makes the decision to leave the op loop the same everywhere.
+__device__ __forceinline__ bool bar_compute_or(int v) {
+    unsigned r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.s32 q, %1, 0;\n\t"
+        "bar.red.or.pred p, %2, %3, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"(v), "n"(kBarCompute), "n"(kComputeThreads)
+        : "memory");
+    return r != 0;
 }
 __device__ __forceinline__ void bar_group(int g) {
     asm volatile("bar.sync %0, %1;" ::"r"(2 + g), "n"(kAttnGroupThreads) : "memory");
@@ -364,7 +386,7 @@ __device__ bool step_activation(const GemvArgs &a, int tok, int8_t *xq, float *x
 // reference's group order while the terms of NC stages are computed at once.  Returns false on abort.
 __device__ bool gemv_consume(const StepOp &op, const Sched &sc, int gbase, int S, int NC, size_t slot_bytes,
                              uint32_t ring_s, uint32_t xq_s, uint32_t xs_s, StepCtl &ctl, int c, int lane,
-                             unsigned long long &best) {
+                             unsigned long long &best, unsigned long long *strace) {
     const GemvArgs &a = op.g;
     const int n = a.n;
     for (int s = c; s < sc.nst; s += NC) {
@@ -373,6 +395,8 @@ __device__ bool gemv_consume(const StepOp &op, const Sched &sc, int gbase, int S
             if (lane == 0) ctl.abort = 1;
             return false;
         }
+        unsigned long long *st = (strace && s < kStageTraceStages && lane == 0) ? strace + 4 * s : nullptr;
+        if (st) st[0] = globaltimer();
         const int b = s % sc.nblk;
         const int row = (sc.t0 + s / sc.nblk) * op.T + lane;
         const bool live = lane < op.T && row < a.d;
@@ -391,14 +415,17 @@ __device__ bool gemv_consume(const StepOp &op, const Sched &sc, int gbase, int S
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&ctl.empty[slot]);
+        if (st) st[1] = globaltimer();
         float sum = 0.0f;
-        if (s > 0) {  // the running sums of stage s-1
-            if (!__all_sync(FULL, token_wait(&ctl.tokflag[c], G, a.err, &ctl.abort))) {
+        if (s > 0) {  // the running sum of this lane's row after stage s-1
+            float prev = 0.0f;
+            if (!__all_sync(FULL, lane_token_wait(ctl.tok[c], lane, G, prev, a.err, &ctl.abort))) {
                 if (lane == 0) ctl.abort = 1;
                 return false;
             }
-            if (b > 0) sum = ctl.tokval[c][lane];
+            if (b > 0) sum = prev;
         }
+        if (st) st[2] = globaltimer();
         if (live) {
             if (wb == 512) {
                 #pragma unroll
@@ -431,13 +458,12 @@ __device__ bool gemv_consume(const StepOp &op, const Sched &sc, int gbase, int S
                 }
             }
         }
-        if (s + 1 < sc.nst) {  // hand the running sums to the warp of stage s+1
+        if (s + 1 < sc.nst) {  // hand this row's running sum to the warp of stage s+1: one tagged word
             const int cn = (c + 1) % NC;
-            ctl.tokval[cn][lane] = sum;
-            __threadfence_block();
-            __syncwarp();
-            if (lane == 0) *reinterpret_cast<volatile int *>(&ctl.tokflag[cn]) = G + 1;
+            *reinterpret_cast<volatile unsigned long long *>(&ctl.tok[cn][lane]) =
+                ((unsigned long long)(unsigned)(G + 1) << 32) | (unsigned long long)__float_as_uint(sum);
         }
+        if (st) st[3] = globaltimer();
     }
     return true;
 }
@@ -706,7 +732,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa
             mbar_init(&ctl.full[i], 1);
             mbar_init(&ctl.empty[i], 1);
         }
-        for (int i = 0; i < kStepMaxConsumers; ++i) ctl.tokflag[i] = -1;
+        for (int i = 0; i < kStepMaxConsumers * 32; ++i) (&ctl.tok[0][0])[i] = 0xFFFFFFFF00000000ull;  // tag -1
         ctl.abort = 0;
         ctl.last = 0;
         mbar_fence_init();
@@ -789,9 +815,16 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa
         if (tid == 0 && blockIdx.x == 0) atomicOr(sa.err, DK_ERR_INVALID);
         return;
     }
+    // op descriptors: op 0 now, op i+1 in registers of threads 32 .. 32+kOpWords-1 during op i
+    const bool op_copier = tid >= 32 && tid < 32 + kOpWords;
+    if (op_copier) ctl.opbuf[0][tid - 32] = __ldg(reinterpret_cast<const unsigned long long *>(sa.ops) + (tid - 32));
+    bar_compute();
     int gbase = 0;
     for (int i = 0; i < sa.nops; ++i) {
-        const StepOp &op = sa.ops[i];
+        const StepOp &op = *reinterpret_cast<const StepOp *>(ctl.opbuf[i % 3]);
+        unsigned long long next_word = 0;
+        if (op_copier && i + 1 < sa.nops)
+            next_word = __ldg(reinterpret_cast<const unsigned long long *>(sa.ops + i + 1) + (tid - 32));
         if (op.kind == OP_GEMV) {
             const GemvArgs &a = op.g;
             const Sched sc = op_sched(op);
@@ -806,15 +839,14 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa
                 if (op.wait_cnt && tid == 0 && !wait_local(op.wait_cnt, (epoch + 1ull) * op.wait_units, sa.err))
                     ctl.abort = 1;
                 if (tid == 0) trace_mark(sa, i, 4);
-                bar_compute();  // the polling thread's acquire, then this barrier, order every thread's reads
-                if (*reinterpret_cast<volatile int *>(&ctl.abort)) break;
+                // the polling thread's acquire, then this barrier, order every thread's reads
+                if (bar_compute_or(*reinterpret_cast<volatile int *>(&ctl.abort))) break;
                 if (tid == 0) trace_mark(sa, i, 0);
                 int8_t *xq = reinterpret_cast<int8_t *>(act);
                 float *xs = reinterpret_cast<float *>(act + ((a.n + 15) & ~15));
                 const int tok = a.pro == PRO_EMB_RMS ? __ldcg(a.tokens + pos) : 0;
                 const bool ok = step_activation(a, tok, xq, xs, ctl, tid, epoch, sc.t0 == 0, nw);
-                bar_compute();
-                if (!ok || *reinterpret_cast<volatile int *>(&ctl.abort)) break;
+                if (bar_compute_or(!ok || *reinterpret_cast<volatile int *>(&ctl.abort))) break;
                 if (tid == 0) trace_mark(sa, i, 1);
                 if (a.dump_q && sc.t0 == 0) {  // diagnostics: the op's input and activation, one CTA
                     const float *src = a.pro == PRO_RMS_REDUCE ? a.x_out : a.x;
@@ -825,7 +857,13 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa
                     for (int j = tid; j < (a.n >> 5); j += kComputeThreads) a.dump_s[j] = xs[j];
                 }
                 if (warp < NC) {
-                    gemv_consume(op, sc, gbase, S, NC, sa.slot, ring_s, smem_u32(xq), smem_u32(xs), ctl, warp, lane, best);
+                    unsigned long long *strace = nullptr;
+                    if (sa.stage_trace && i >= sa.stage_op0 && i < sa.stage_op0 + kStageTraceOps &&
+                        (int)blockIdx.x < kStageTraceCtas)
+                        strace = sa.stage_trace + (((size_t)(i - sa.stage_op0) * kStageTraceCtas + blockIdx.x) *
+                                                   kStageTraceStages) * 4;
+                    gemv_consume(op, sc, gbase, S, NC, sa.slot, ring_s, smem_u32(xq), smem_u32(xs), ctl, warp, lane, best,
+                                 strace);
                     if (a.epi == EPI_ARGMAX) {
                         #pragma unroll
                         for (int o = 16; o > 0; o >>= 1) {
@@ -835,8 +873,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa
                         if (lane == 0) ctl.wkey[warp] = best;
                     }
                 }
-                bar_compute();  // every row stored, the activation no longer read
-                if (*reinterpret_cast<volatile int *>(&ctl.abort)) break;
+                // every row stored, the activation no longer read
+                if (bar_compute_or(*reinterpret_cast<volatile int *>(&ctl.abort))) break;
                 if (tid == 0) {
                     trace_mark(sa, i, 2);
                     const int lo = sc.t0 * op.T, hi = min(a.d, (sc.t0 + sc.nt) * op.T);
@@ -895,8 +933,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa
             const AttnArgs &at = op.at;
             if (op.wait_cnt && tid == 0 && !wait_local(op.wait_cnt, (epoch + 1ull) * op.wait_units, sa.err)) ctl.abort = 1;
             if (tid == 0) trace_mark(sa, i, 4);
-            bar_compute();
-            if (*reinterpret_cast<volatile int *>(&ctl.abort)) break;
+            if (bar_compute_or(*reinterpret_cast<volatile int *>(&ctl.abort))) break;
             if (tid == 0) trace_mark(sa, i, 0);
             const int T = pos + 1;
             int nsplit, chunk;
@@ -915,6 +952,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa
             bar_compute();  // the scratch (the activation area) is free again
             if (tid == 0) trace_mark(sa, i, 2);
         }
+        // the next op's descriptor (its slot last held op i-2, which every thread has left)
+        if (op_copier && i + 1 < sa.nops) ctl.opbuf[(i + 1) % 3][tid - 32] = next_word;
+        bar_compute();
     }
 }
 

@@ -253,7 +253,10 @@ int dk_model_kv_read(dk_model *m, int layer, int pos0, int n_pos, void *k, void 
  * with DIOLKOS_STEP_TRACE=1 in the environment: out[(cta * n_ops + op) * 8 + k] = GPU global timer (ns)
  * when, on that CTA, k = 0: the op's input was ready, 1: its activation was built, 2: it finished,
  * 3: the op's last weight stage was issued, 4: the input counter was seen (0: not recorded).
- * *grid and *n_ops give the dimensions. */
+ * *grid and *n_ops give the dimensions.  When n also covers 5 * 4 * 64 * 4 more entries, these follow:
+ * the GEMV consumers' per-stage timeline of the second layer's five ops on CTAs 0..3,
+ * [op][cta][stage][k] with k = 0: the stage's weights landed, 1: its group terms were computed, 2: the
+ * running row sums of the previous stage were received, 3: this stage's sums were passed on. */
 int dk_model_trace(dk_model *m, unsigned long long *out, size_t n, int *grid, int *n_ops);
 /* Diagnostics: the timeline of the last pipelined tensor-core matmul launched on this device while
  * DIOLKOS_GEMM_TRACE=1 was set at the first launch: out[(cta * blocks + b) * 5 + k] = GPU global timer
