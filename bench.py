@@ -576,7 +576,7 @@ def run_decode(args):
 
         if int(os.environ.get("WORLD_SIZE", "1")) != world:
             raise RuntimeError(f"--gpus {world} needs {world} ranks (torchrun --nproc-per-node {world})")
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
 
     def barrier():
         if dist is not None:

@@ -68,6 +68,22 @@ struct GemvArgs {
     unsigned long long *epoch_rw = nullptr;     // the classifier's writable view of epoch
     int row_offset = 0;                         // global index of this rank's first classifier row
     int vocab = 0;                              // rows of the whole classifier (0: d)
+    // ---- tensor parallel, persistent step: the tagged exchange (tagged != 0) ----
+    // Partial rows and the residual travel as 64-bit words, (tag << 32) | value bits, so that a reader
+    // tells a new value from an old one by the word alone: no fences and no counters.  The tag of event k
+    // of a step (k = 0: the embedding row, k = 2l+1: the reduce after layer l's wo, k = 2l+2: after its w2)
+    // is epoch * tag_period + k + 1 (tag_period = 2 * layers + 1).
+    //   EPI_PEER:       each row's partial sum into every rank's peer_recv64[q][tp_rank * d + row], tag k;
+    //   PRO_RMS_REDUCE: gatherer CTAs 0 .. n_gather-1 each take a slice of the rows: wait for every rank's
+    //                   partial (recv64[q][row], tag k) and the residual (x64[row], tag k-1), sum in rank
+    //                   order and store x64_out[row] (tag k); then every CTA reads x64_out (tag k);
+    //   PRO_EMB_RMS:    the CTA that owns tile 0 stores the embedding row to x64_out (tag 0).
+    int tagged = 0, n_gather = 0;
+    int tag_k = 0, tag_period = 0;
+    const unsigned long long *x64 = nullptr;
+    unsigned long long *x64_out = nullptr;
+    const unsigned long long *recv64 = nullptr;
+    unsigned long long *const *peer_recv64 = nullptr;
     // Diagnostics (persistent step only; nullptr: off): the CTA that owns tile 0 copies the op's fp32
     // input vector (n floats; the residual written by the prologue where it writes one) and the Q8_0
     // activation it built (n int8, n/32 scales) here, for per-layer parity checks.

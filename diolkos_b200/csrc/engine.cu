@@ -107,6 +107,8 @@ struct dk_model {
     std::vector<bool> peer_opened;
     void **d_ptrs = nullptr;              // device pointer tables (see comm_tables)
     float *x2 = nullptr;                  // second residual buffer (the reduces ping-pong x <-> x2)
+    unsigned long long *x64 = nullptr;    // persistent step, tensor parallel: the tagged residual, [2][dim]
+    size_t comm_t64 = 0;                  // offset of the tagged receive areas, u64 [2][world][dim]
     unsigned long long *epoch = nullptr;  // decode steps completed (the exchange counters' epoch)
     bool connected = false;
     // persistent decode step (step.cu): the op list on the device, its dependency counters and plan
@@ -283,8 +285,9 @@ dk_model *dk_model_create(const int *cfg, int kv_type, int device, int tp_rank, 
     const size_t sz_cnt = align256((size_t)m->l_kv_heads * 4);
     const size_t sz_part = align256((size_t)kMaxGemvGrid * m->num_sms * 8);
     const size_t sz_tok = align256((size_t)(S + 1) * 4);
+    const size_t sz_x64 = tp_world > 1 ? 2 * align256((size_t)dim * 8) : 0;
     const size_t total = sz_x * 3 + sz_qkv + sz_hb + sz_logits + sz_rope + sz_work + sz_cnt + sz_part + 256 + sz_tok +
-                         4 * 256 + sz_stepcnt;
+                         4 * 256 + sz_stepcnt + sz_x64;
     if (cudaMalloc(&m->aarena, total) != cudaSuccess) return fail("activation memory");
     cudaMemsetAsync(m->aarena, 0, total, m->stream);
     p = m->aarena;
@@ -305,16 +308,22 @@ dk_model *dk_model_create(const int *cfg, int kv_type, int device, int tp_rank, 
     m->err = reinterpret_cast<int *>(p); p += 256;
     m->epoch = reinterpret_cast<unsigned long long *>(p); p += 256;
     m->step_cnt = reinterpret_cast<unsigned long long *>(p); p += sz_stepcnt;
+    if (sz_x64) {  // zeroed with the arena: tag 0 is never a live tag
+        m->x64 = reinterpret_cast<unsigned long long *>(p);
+        p += sz_x64;
+    }
 
     // ---- tensor-parallel exchange area (its own allocation: it is exported to the peers over IPC)
     if (tp_world > 1) {
         m->comm_ctl = align256((size_t)2 * tp_world * dim * 4);
         // then the prefill's two receive areas, [rank][chunk position][dim] floats each
         m->comm_pre = m->comm_ctl + 256;
-        m->comm_bytes = m->comm_pre + 2 * align256((size_t)tp_world * std::min(kPrefillChunk, S) * dim * 4);
+        m->comm_t64 = m->comm_pre + 2 * align256((size_t)tp_world * std::min(kPrefillChunk, S) * dim * 4);
+        // then the persistent step's tagged receive areas (zeroed: tag 0 is never a live tag)
+        m->comm_bytes = m->comm_t64 + 2 * align256((size_t)tp_world * dim * 8);
         if (cudaMalloc(&m->comm, m->comm_bytes) != cudaSuccess) return fail("exchange area");
         if (cudaMemset(m->comm, 0, m->comm_bytes) != cudaSuccess) return fail("exchange area clear");
-        if (cudaMalloc(&m->d_ptrs, 10 * 8 * sizeof(void *)) != cudaSuccess) return fail("peer pointer tables");
+        if (cudaMalloc(&m->d_ptrs, 12 * 8 * sizeof(void *)) != cudaSuccess) return fail("peer pointer tables");
         m->peer_base.assign(tp_world, nullptr);
         m->peer_opened.assign(tp_world, false);
         m->peer_base[tp_rank] = m->comm;
@@ -455,12 +464,16 @@ static int set_weight_impl(dk_model *m, int which, int layer, const void *q, con
 
 // Offsets inside a rank's exchange area and the device pointer tables built from the peers' mappings:
 // table t (8 entries, one per rank) at d_ptrs + 8*t: 0/1 receive areas of parity 0/1, 2/3 their
-// counters, 4 the argmax key arrays, 5 their counters.
+// counters, 4 the argmax key arrays, 5 their counters, 6..9 the prefill's receive areas and counters,
+// 10/11 the persistent step's tagged receive areas of parity 0/1.
 static size_t comm_recv_off(const dk_model *m, int par) { return (size_t)par * m->world * m->dim * 4; }
 static size_t comm_cnt_off(const dk_model *m, int par) { return m->comm_ctl + 8 * (size_t)par; }
 static size_t comm_keys_off(const dk_model *m) { return m->comm_ctl + 16; }
 static size_t comm_keys_cnt_off(const dk_model *m) { return m->comm_ctl + 16 + 64; }
 static size_t comm_pcnt_off(const dk_model *m, int par) { return m->comm_ctl + 128 + 8 * (size_t)par; }
+static size_t comm_t64_off(const dk_model *m, int par) {
+    return m->comm_t64 + (size_t)par * align256((size_t)m->world * m->dim * 8);
+}
 static size_t comm_pre_off(const dk_model *m, int par) {
     return m->comm_pre + (size_t)par * align256((size_t)m->world * std::min(kPrefillChunk, m->seq_len) * m->dim * 4);
 }
@@ -588,20 +601,28 @@ static int build_step(dk_model *m) {
     };
     float *X[2] = {m->x, m->x2};
     int cur = 0;
-    auto reduce_pro = [&](StepOp &op, int par, int index) {
+    // Tensor parallel: the tagged exchange (dk_kernels.h, GemvArgs::tagged).  Event k of a step: 0 the
+    // embedding row, 2l+1 the reduce after layer l's wo, 2l+2 the reduce after its w2; the reduce of event
+    // k reads the tagged residual x64[(k-1) & 1] and writes x64[k & 1].
+    const int n_gather = std::min(16, m->num_sms);
+    auto x64 = [&](int k) { return m->x64 + (size_t)(k & 1) * (align256((size_t)m->dim * 8) / 8); };
+    auto tagged = [&](GemvArgs &a, int k) {
+        a.tagged = 1;
+        a.tag_k = k;
+        a.tag_period = 2 * m->n_layers + 1;
+        a.n_gather = n_gather;
+    };
+    auto reduce_pro = [&](StepOp &op, int par, int k) {
         GemvArgs &a = op.g;
         a.pro = PRO_RMS_REDUCE;
-        a.x = X[cur];
-        a.x_out = X[1 - cur];
-        a.recv = reinterpret_cast<const float *>(m->comm + comm_recv_off(m, par));
-        a.cnt = reinterpret_cast<const unsigned long long *>(m->comm + comm_cnt_off(m, par));
-        a.red_index = index;
-        a.red_period = m->n_layers;
-        cur = 1 - cur;
+        tagged(a, k);
+        a.x64 = x64(k - 1);
+        a.x64_out = x64(k);
+        a.recv64 = reinterpret_cast<const unsigned long long *>(m->comm + comm_t64_off(m, par));
     };
-    auto peer_epi = [&](StepOp &op, int par) {
-        op.g.peer_recv = reinterpret_cast<float *const *>(tab + 8 * par);
-        op.g.peer_cnt = reinterpret_cast<unsigned long long *const *>(tab + 8 * (2 + par));
+    auto peer_epi = [&](StepOp &op, int par, int k) {
+        tagged(op.g, k);
+        op.g.peer_recv64 = reinterpret_cast<unsigned long long *const *>(tab + 8 * (10 + par));
     };
     const int qkv_rows = m->l_dim + 2 * m->l_kv_dim;
     const size_t esz = m->kv_type == DK_KV_F32 ? 4 : 2;
@@ -609,9 +630,13 @@ static int build_step(dk_model *m) {
         const dk_layer &ly = m->layers[l];
         StepOp q = gemv_op(ly.wqkv, m->dim, qkv_rows, l == 0 ? PRO_EMB_RMS : PRO_RMS, EPI_STORE, X[cur], ly.rms_att,
                            m->qkv, m->p_qkv);
+        if (l == 0 && tp) {  // the embedding row starts the tagged residual chain (event 0)
+            tagged(q.g, 0);
+            q.g.x64_out = x64(0);
+        }
         if (l > 0) {
             if (tp) {
-                reduce_pro(q, 1, l - 1);
+                reduce_pro(q, 1, 2 * l);
             } else {
                 q.wait_cnt = cnt(l - 1, 4);
                 q.wait_units = (unsigned long long)m->dim;
@@ -637,13 +662,13 @@ static int build_step(dk_model *m) {
         StepOp o = gemv_op(ly.wo, m->l_dim, m->dim, PRO_F32, tp ? EPI_PEER : EPI_ADD, m->xb, nullptr, X[cur], m->p_wo);
         o.wait_cnt = cnt(l, 1);
         o.wait_units = (unsigned long long)m->l_dim;
-        if (tp) peer_epi(o, 0);
+        if (tp) peer_epi(o, 0, 2 * l + 1);
         else o.done_cnt = cnt(l, 2);
         ops.push_back(o);
 
         StepOp u = gemv_op(ly.w13, m->dim, 2 * m->l_hidden, PRO_RMS, EPI_SWIGLU, X[cur], ly.rms_ffn, m->hb, m->p_w13);
         if (tp) {
-            reduce_pro(u, 0, l);
+            reduce_pro(u, 0, 2 * l + 1);
         } else {
             u.wait_cnt = cnt(l, 2);
             u.wait_units = (unsigned long long)m->dim;
@@ -654,14 +679,14 @@ static int build_step(dk_model *m) {
         StepOp d = gemv_op(ly.w2, m->l_hidden, m->dim, PRO_F32, tp ? EPI_PEER : EPI_ADD, m->hb, nullptr, X[cur], m->p_w2);
         d.wait_cnt = cnt(l, 3);
         d.wait_units = (unsigned long long)m->l_hidden;
-        if (tp) peer_epi(d, 1);
+        if (tp) peer_epi(d, 1, 2 * l + 2);
         else d.done_cnt = cnt(l, 4);
         ops.push_back(d);
     }
     {
         StepOp c = gemv_op(m->wcls, m->dim, m->l_vocab, PRO_RMS, EPI_ARGMAX, X[cur], m->rms_final, m->logits, m->p_cls);
         if (tp) {
-            reduce_pro(c, 1, m->n_layers - 1);
+            reduce_pro(c, 1, 2 * m->n_layers);
             c.g.peer_amax = reinterpret_cast<unsigned long long *const *>(tab + 8 * 4);
             c.g.peer_amax_cnt = reinterpret_cast<unsigned long long *const *>(tab + 8 * 5);
             c.g.amax_keys = reinterpret_cast<const unsigned long long *>(m->comm + comm_keys_off(m));
@@ -771,7 +796,7 @@ int dk_model_comm_connect(dk_model *m, const void *handles) {
         m->peer_base[q] = ptr;
         m->peer_opened[q] = true;
     }
-    std::vector<void *> t(10 * 8, nullptr);
+    std::vector<void *> t(12 * 8, nullptr);
     for (int q = 0; q < m->world; ++q) {
         uint8_t *b = static_cast<uint8_t *>(m->peer_base[q]);
         t[0 * 8 + q] = b + comm_recv_off(m, 0);
@@ -784,6 +809,8 @@ int dk_model_comm_connect(dk_model *m, const void *handles) {
         t[7 * 8 + q] = b + comm_pre_off(m, 1);
         t[8 * 8 + q] = b + comm_pcnt_off(m, 0);
         t[9 * 8 + q] = b + comm_pcnt_off(m, 1);
+        t[10 * 8 + q] = b + comm_t64_off(m, 0);  // the persistent step's tagged receive areas
+        t[11 * 8 + q] = b + comm_t64_off(m, 1);
     }
     if (int r = cuda_status(cudaMemcpy(m->d_ptrs, t.data(), t.size() * sizeof(void *), cudaMemcpyHostToDevice),
                             "peer table upload"))

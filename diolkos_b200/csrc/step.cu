@@ -166,10 +166,82 @@ __device__ __forceinline__ size_t gemv_x_bytes_dev(int n) {
     return (((size_t)n + 15) & ~(size_t)15) + (size_t)((n / 32 + 3) & ~3) * 4;
 }
 
+// ---- tensor parallel: the tagged exchange (GemvArgs::tagged) ------------------------------------------
+__device__ __forceinline__ unsigned tp_tag(unsigned long long epoch, const GemvArgs &a, int k) {
+    return (unsigned)(epoch * (unsigned long long)a.tag_period + (unsigned long long)(k + 1));
+}
+__device__ __forceinline__ void ld_v2u64(const unsigned long long *p, unsigned long long &x, unsigned long long &y) {
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(x), "=l"(y) : "l"(p) : "memory");
+}
+__device__ __forceinline__ void st_v2u64(unsigned long long *p, unsigned long long x, unsigned long long y) {
+    asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(x), "l"(y) : "memory");
+}
+__device__ __forceinline__ void st_u64(unsigned long long *p, unsigned long long x) {
+    asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(x) : "memory");
+}
+__device__ __forceinline__ unsigned long long tagged_word(unsigned T, float v) {
+    return ((unsigned long long)T << 32) | (unsigned long long)__float_as_uint(v);
+}
+// Wait (bounded) until the N words at p (16-byte aligned) all carry tag T, and take their values.  A word
+// is single-copy atomic, so a value arrives with its tag whether a peer GPU or another CTA wrote it.  On a
+// timeout: DK_ERR_COMM, zeros, false -- the caller carries on through its barriers and aborts after them.
+template <int N>
+__device__ __forceinline__ bool wait_tagged(const unsigned long long *p, unsigned T, float (&v)[N], int *err) {
+    static_assert(N % 2 == 0, "pairs of words");
+    unsigned long long w[N];
+    const long long t0 = clock64();
+    for (;;) {
+        #pragma unroll
+        for (int i = 0; i < N; i += 2) ld_v2u64(p + i, w[i], w[i + 1]);
+        bool ok = true;
+        #pragma unroll
+        for (int i = 0; i < N; ++i) ok &= (unsigned)(w[i] >> 32) == T;
+        if (ok) {
+            #pragma unroll
+            for (int i = 0; i < N; ++i) v[i] = __uint_as_float((unsigned)w[i]);
+            return true;
+        }
+        if (clock64() - t0 > DK_WAIT_LIMIT_CYCLES) {
+            atomicOr(err, DK_ERR_COMM);
+            #pragma unroll
+            for (int i = 0; i < N; ++i) v[i] = 0.0f;
+            return false;
+        }
+    }
+}
+// Gatherer CTA (blockIdx.x < n_gather) of a reduce: for its slice of the rows, every rank's partial sum
+// (event tag_k) added in rank order onto the residual (event tag_k - 1), x + (p_0 + p_1 + ...) as the
+// counter exchange computes it, published as the new tagged residual.
+__device__ bool tp_gather(const GemvArgs &a, unsigned long long epoch, int tid) {
+    const int n = a.n, NG = a.n_gather;
+    const int per = ((n + NG - 1) / NG + 3) & ~3;
+    const int r0 = (int)blockIdx.x * per, r1 = min(n, r0 + per);
+    const unsigned T = tp_tag(epoch, a, a.tag_k), Tx = tp_tag(epoch, a, a.tag_k - 1);
+    bool ok = true;
+    for (int r = r0 + 4 * tid; r + 4 <= r1; r += 4 * kComputeThreads) {
+        float x[4], t[4], u[4];
+        ok &= wait_tagged<4>(a.x64 + r, Tx, x, a.err);
+        ok &= wait_tagged<4>(a.recv64 + r, T, t, a.err);
+        for (int q = 1; q < a.tp_world; ++q) {
+            ok &= wait_tagged<4>(a.recv64 + (size_t)q * n + r, T, u, a.err);
+            #pragma unroll
+            for (int j = 0; j < 4; ++j) t[j] = __fadd_rn(t[j], u[j]);
+        }
+        st_v2u64(a.x64_out + r, tagged_word(T, __fadd_rn(x[0], t[0])), tagged_word(T, __fadd_rn(x[1], t[1])));
+        st_v2u64(a.x64_out + r + 2, tagged_word(T, __fadd_rn(x[2], t[2])), tagged_word(T, __fadd_rn(x[3], t[3])));
+    }
+    return ok;
+}
+
 // ---- activation prologue (compute threads) ------------------------------------------------------
-// 16 consecutive values of the op's input, half-group hg (values 16hg .. 16hg+15).
-__device__ __forceinline__ void load16(const GemvArgs &a, int tok, int hg, float (&f)[16]) {
+// 16 consecutive values of the op's input, half-group hg (values 16hg .. 16hg+15).  The tagged reduce reads
+// the new residual its gatherers published (tag T; ok = false on a timeout).
+__device__ __forceinline__ void load16(const GemvArgs &a, int tok, int hg, float (&f)[16], unsigned T, bool &ok) {
     const int n = a.n;
+    if (a.pro == PRO_RMS_REDUCE && a.tagged) {
+        ok &= wait_tagged<16>(a.x64_out + 16 * hg, T, f, a.err);
+        return;
+    }
     if (a.pro == PRO_EMB_RMS) {
         if (!DK_CHK(tok >= 0 && tok < (a.vocab > 0 ? a.vocab : 1) && hg < (n >> 4), a.err, 10, tok)) {
             #pragma unroll
@@ -241,7 +313,9 @@ __device__ __forceinline__ void quant16(float (&f)[16], int hg, bool live, int8_
 __device__ bool step_activation(const GemvArgs &a, int tok, int8_t *xq, float *xs, StepCtl &ctl, int tid,
                                 unsigned long long epoch, bool writer, const float4 (&nw0)[4]) {
     const int n = a.n, nhg = n >> 4, warp = tid >> 5, lane = tid & 31;
-    if (a.pro == PRO_RMS_REDUCE) {
+    bool ok = true;  // false: a tagged wait gave up (every barrier below is still taken)
+    const unsigned T = a.tagged ? tp_tag(epoch, a, a.tag_k) : 0u;
+    if (a.pro == PRO_RMS_REDUCE && !a.tagged) {
         // every rank's partial rows for this exchange point have landed once the counter reaches this
         if (tid == 0) {
             const unsigned long long target =
@@ -249,12 +323,14 @@ __device__ bool step_activation(const GemvArgs &a, int tok, int8_t *xq, float *x
                 (unsigned long long)a.tp_world * (unsigned long long)n;
             if (!wait_counter(a.cnt, target, a.err)) ctl.abort = 1;
         }
-        bar_compute();
-        if (*reinterpret_cast<volatile int *>(&ctl.abort)) return false;
+        if (bar_compute_or(*reinterpret_cast<volatile int *>(&ctl.abort))) return false;  // the same for every thread
         __threadfence();
     }
     const bool rms = a.pro == PRO_RMS || a.pro == PRO_EMB_RMS || a.pro == PRO_RMS_REDUCE;
-    const bool write_x = (a.pro == PRO_EMB_RMS || a.pro == PRO_RMS_REDUCE) && writer;
+    // the residual the prologue produces, stored by one CTA: the embedding row (tagged under the tagged
+    // exchange), or the untagged reduce's sum (the tagged reduce's gatherers stored theirs)
+    const bool write_x = writer && (a.pro == PRO_EMB_RMS || (a.pro == PRO_RMS_REDUCE && !a.tagged));
+    const bool write_x64 = write_x && a.tagged;
     float *xdst = a.pro == PRO_RMS_REDUCE ? a.x_out : const_cast<float *>(a.x);
     const int rounds = (nhg + kComputeThreads - 1) / kComputeThreads;
     if (rms && rounds <= 2) {
@@ -266,8 +342,12 @@ __device__ bool step_activation(const GemvArgs &a, int tok, int8_t *xq, float *x
             const int hg = k * kComputeThreads + tid;
             const bool live = k < rounds && hg < nhg;
             if (live) {
-                load16(a, tok, hg, f);
-                if (write_x) {
+                load16(a, tok, hg, f, T, ok);
+                if (write_x64) {
+                    #pragma unroll
+                    for (int j = 0; j < 16; j += 2)
+                        st_v2u64(a.x64_out + 16 * hg + j, tagged_word(T, f[j]), tagged_word(T, f[j + 1]));
+                } else if (write_x) {
                     #pragma unroll
                     for (int j = 0; j < 4; ++j)
                         reinterpret_cast<float4 *>(xdst + 16 * hg)[j] =
@@ -307,7 +387,7 @@ __device__ bool step_activation(const GemvArgs &a, int tok, int8_t *xq, float *x
             }
             quant16(f, hg, live, xq, xs);
         }
-        return true;
+        return ok;
     }
     if (!rms && rounds <= 3) {
         // plain quantisation of up to three rounds: every load is issued before any is used
@@ -316,7 +396,7 @@ __device__ bool step_activation(const GemvArgs &a, int tok, int8_t *xq, float *x
         for (int k = 0; k < 3; ++k) {
             const int hg = k * kComputeThreads + tid;
             if (k < rounds && hg < nhg) {
-                load16(a, tok, hg, f[k]);
+                load16(a, tok, hg, f[k], T, ok);
             } else {
                 #pragma unroll
                 for (int j = 0; j < 16; ++j) f[k][j] = 0.0f;
@@ -328,15 +408,19 @@ __device__ bool step_activation(const GemvArgs &a, int tok, int8_t *xq, float *x
             const int hg = k * kComputeThreads + tid;
             quant16(f[k], hg, hg < nhg, xq, xs);
         }
-        return true;
+        return ok;
     }
     float r = 1.0f;
     if (rms) {  // wide rmsnorm input: sum of squares first, values re-read below
         float ss = 0.0f;
         for (int hg = tid; hg < nhg; hg += kComputeThreads) {
             float f[16];
-            load16(a, tok, hg, f);
-            if (write_x) {
+            load16(a, tok, hg, f, T, ok);
+            if (write_x64) {
+                #pragma unroll
+                for (int j = 0; j < 16; j += 2)
+                    st_v2u64(a.x64_out + 16 * hg + j, tagged_word(T, f[j]), tagged_word(T, f[j + 1]));
+            } else if (write_x) {
                 #pragma unroll
                 for (int j = 0; j < 4; ++j)
                     reinterpret_cast<float4 *>(xdst + 16 * hg)[j] = make_float4(f[4 * j], f[4 * j + 1], f[4 * j + 2], f[4 * j + 3]);
@@ -358,7 +442,7 @@ __device__ bool step_activation(const GemvArgs &a, int tok, int8_t *xq, float *x
         const bool live = hg < nhg;
         float f[16];
         if (live) {
-            load16(a, tok, hg, f);
+            load16(a, tok, hg, f, T, ok);
             if (rms) {
                 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
@@ -375,7 +459,7 @@ __device__ bool step_activation(const GemvArgs &a, int tok, int8_t *xq, float *x
         }
         quant16(f, hg, live, xq, xs);
     }
-    return true;
+    return ok;
 }
 
 // ---- GEMV op: consumers ---------------------------------------------------------------------------
@@ -386,9 +470,10 @@ __device__ bool step_activation(const GemvArgs &a, int tok, int8_t *xq, float *x
 // reference's group order while the terms of NC stages are computed at once.  Returns false on abort.
 __device__ bool gemv_consume(const StepOp &op, const Sched &sc, int gbase, int S, int NC, size_t slot_bytes,
                              uint32_t ring_s, uint32_t xq_s, uint32_t xs_s, StepCtl &ctl, int c, int lane,
-                             unsigned long long &best, unsigned long long *strace) {
+                             unsigned long long &best, unsigned long long *strace, unsigned long long epoch) {
     const GemvArgs &a = op.g;
     const int n = a.n;
+    const unsigned T = a.tagged ? tp_tag(epoch, a, a.tag_k) : 0u;
     for (int s = c; s < sc.nst; s += NC) {
         const int G = gbase + s, slot = G % S;
         if (!__all_sync(FULL, mbar_wait_abortable(&ctl.full[slot], (uint32_t)((G / S) & 1), a.err, &ctl.abort, false))) {
@@ -448,7 +533,12 @@ __device__ bool gemv_consume(const StepOp &op, const Sched &sc, int gbase, int S
                 if (a.epi == EPI_ADD) {
                     a.out[row] = __fadd_rn(__ldcg(a.out + row), sum);
                 } else if (a.epi == EPI_PEER) {
-                    for (int q = 0; q < a.tp_world; ++q) a.peer_recv[q][(size_t)a.tp_rank * a.d + row] = sum;
+                    if (a.tagged) {  // one tagged word per rank: its own validity, no fence, no count
+                        const unsigned long long wv = tagged_word(T, sum);
+                        for (int q = 0; q < a.tp_world; ++q) st_u64(a.peer_recv64[q] + (size_t)a.tp_rank * a.d + row, wv);
+                    } else {
+                        for (int q = 0; q < a.tp_world; ++q) a.peer_recv[q][(size_t)a.tp_rank * a.d + row] = sum;
+                    }
                 } else {
                     a.out[row] = sum;
                 }
@@ -830,6 +920,11 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa
             const Sched sc = op_sched(op);
             const bool mine = sc.nst > 0;
             unsigned long long best = 0ull;
+            if (a.tagged && a.pro == PRO_RMS_REDUCE && (int)blockIdx.x < a.n_gather) {
+                // a gatherer of the tagged exchange, whether or not it owns rows of this op
+                const bool gok = tp_gather(a, epoch, tid);
+                if (bar_compute_or(!gok || *reinterpret_cast<volatile int *>(&ctl.abort))) break;
+            }
             if (mine) {
                 float4 nw[4];
                 #pragma unroll
@@ -850,8 +945,13 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa
                 if (tid == 0) trace_mark(sa, i, 1);
                 if (a.dump_q && sc.t0 == 0) {  // diagnostics: the op's input and activation, one CTA
                     const float *src = a.pro == PRO_RMS_REDUCE ? a.x_out : a.x;
-                    for (int j = tid; j < (a.n >> 2); j += kComputeThreads)
-                        reinterpret_cast<float4 *>(a.dump_in)[j] = __ldcg(reinterpret_cast<const float4 *>(src) + j);
+                    if (a.tagged && (a.pro == PRO_RMS_REDUCE || a.pro == PRO_EMB_RMS)) {
+                        for (int j = tid; j < a.n; j += kComputeThreads)
+                            a.dump_in[j] = __uint_as_float((unsigned)__ldcg(a.x64_out + j));
+                    } else {
+                        for (int j = tid; j < (a.n >> 2); j += kComputeThreads)
+                            reinterpret_cast<float4 *>(a.dump_in)[j] = __ldcg(reinterpret_cast<const float4 *>(src) + j);
+                    }
                     for (int j = tid; j < (a.n >> 4); j += kComputeThreads)
                         reinterpret_cast<uint4 *>(a.dump_q)[j] = reinterpret_cast<const uint4 *>(xq)[j];
                     for (int j = tid; j < (a.n >> 5); j += kComputeThreads) a.dump_s[j] = xs[j];
@@ -863,7 +963,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa
                         strace = sa.stage_trace + (((size_t)(i - sa.stage_op0) * kStageTraceCtas + blockIdx.x) *
                                                    kStageTraceStages) * 4;
                     gemv_consume(op, sc, gbase, S, NC, sa.slot, ring_s, smem_u32(xq), smem_u32(xs), ctl, warp, lane, best,
-                                 strace);
+                                 strace, epoch);
                     if (a.epi == EPI_ARGMAX) {
                         #pragma unroll
                         for (int o = 16; o > 0; o >>= 1) {
@@ -879,7 +979,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa
                     trace_mark(sa, i, 2);
                     const int lo = sc.t0 * op.T, hi = min(a.d, (sc.t0 + sc.nt) * op.T);
                     const unsigned long long rows = hi > lo ? (unsigned long long)(hi - lo) : 0ull;
-                    if (a.epi == EPI_PEER) {
+                    if (a.epi == EPI_PEER && !a.tagged) {
                         // count this CTA's rows on every rank: a rank that sees the count sees the rows
                         __threadfence_system();
                         for (int r = 0; r < a.tp_world; ++r) atomicAdd_system(a.peer_cnt[r], rows);

@@ -1,4 +1,4 @@
-"""Tensor-parallel host logic on CPU: two gloo ranks (no GPU).
+"""Tensor-parallel host logic on CPU: 2, 4 and 8 gloo ranks (no GPU).
 
 * The shard plan (diolkos_b200.tp) covers every row / column exactly once.
 * Column-split partial GEMVs (wo, w2) summed over the ranks equal the full GEMV: each rank runs the
@@ -16,6 +16,8 @@ import torch.multiprocessing as mp
 from diolkos_b200 import synth, tp
 
 CFG = synth.Config(dim=512, hidden_dim=1024, n_layers=2, n_heads=8, n_kv_heads=2, vocab_size=1000, seq_len=64)
+# divisible 8 ways: 8 heads and 8 KV heads, hidden 1024 = 8 * 128, 64 q / kv columns per rank
+CFG8 = synth.Config(dim=512, hidden_dim=1024, n_layers=2, n_heads=8, n_kv_heads=8, vocab_size=1000, seq_len=64)
 
 
 def _free_port() -> int:
@@ -26,7 +28,8 @@ def _free_port() -> int:
     return port
 
 
-def _worker(rank, world, port, out_q):
+def _worker(rank, world, port, out_q, cfg=None):
+    CFG_ = cfg or CFG
     import torch
     import torch.distributed as dist
 
@@ -37,11 +40,11 @@ def _worker(rank, world, port, out_q):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         port_ = Port()
-        sh = tp.shard(CFG, rank, world)
+        sh = tp.shard(CFG_, rank, world)
         rng = np.random.default_rng(5)
         res = {}
-        for name, n, cols in (("wo", CFG.dim, sh.q_rows), ("w2", CFG.hidden_dim, sh.hidden_rows)):
-            d = CFG.dim
+        for name, n, cols in (("wo", CFG_.dim, sh.q_rows), ("w2", CFG_.hidden_dim, sh.hidden_rows)):
+            d = CFG_.dim
             wq = rng.integers(-127, 128, (d, n), dtype=np.int8)
             ws = (rng.random((d, n // 32), dtype=np.float32) * 0.01).astype(np.float32)
             x = rng.standard_normal(n).astype(np.float32)
@@ -60,23 +63,37 @@ def _worker(rank, world, port, out_q):
 
 def test_shard_plan_covers_everything():
     for world in (1, 2):
-        sh = [tp.shard(CFG, r, world) for r in range(world)]
-        for field, total in (("q_rows", CFG.dim), ("kv_rows", CFG.dim * CFG.n_kv_heads // CFG.n_heads),
-                             ("hidden_rows", CFG.hidden_dim), ("vocab_rows", CFG.vocab_size)):
-            ranges = [getattr(s, field) for s in sh]
-            assert ranges[0][0] == 0 and ranges[-1][1] == total
-            assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
+        _covers(CFG, world)
+    for world in (4, 8):
+        _covers(CFG8, world)
+    # the 7B and 70B shapes split 1, 2, 4 and 8 ways (heads, KV heads, hidden and vocabulary rows)
+    for cfg in (synth.LLAMA7B, synth.LLAMA70B):
+        for world in (1, 2, 4, 8):
+            _covers(cfg, world)
     for world in (8, 16):
         with pytest.raises(ValueError):
             tp.shard(CFG, 0, world)  # 2 kv heads cannot be split 8 or 16 ways
 
 
-def test_column_split_partials_sum_to_full_gemv():
-    world = 2
+def _covers(cfg, world):
+    sh = [tp.shard(cfg, r, world) for r in range(world)]
+    for field, total in (("q_rows", cfg.dim), ("kv_rows", cfg.dim * cfg.n_kv_heads // cfg.n_heads),
+                         ("hidden_rows", cfg.hidden_dim), ("vocab_rows", cfg.vocab_size)):
+        ranges = [getattr(s, field) for s in sh]
+        assert ranges[0][0] == 0 and ranges[-1][1] == total
+        assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
+        # column slices start on Q8_0 group boundaries (the activation's groups stay the reference's)
+        if field in ("q_rows", "hidden_rows"):
+            assert all(a % 32 == 0 for a, _ in ranges)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_column_split_partials_sum_to_full_gemv(world):
+    cfg = CFG if world == 2 else CFG8
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, cfg)) for r in range(world)]
     for p in procs:
         p.start()
     results = dict(q.get(timeout=180) for _ in range(world))
