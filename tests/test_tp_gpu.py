@@ -37,7 +37,7 @@ def _free_port() -> int:
     return port
 
 
-def _rank(rank, world, port, out_q, cfg_name):
+def _rank(rank, world, port, out_q, cfg_name, kv_f32=True):
     CFG = CFGS[cfg_name]
     import torch.distributed as dist
 
@@ -53,7 +53,7 @@ def _rank(rank, world, port, out_q, cfg_name):
     try:
         port_ = Port()
         w, by_name = load_port_weights(port_, CFG, SEED)
-        m = Model(CFG, kv_f32=True, device=rank, tp_rank=rank, tp_world=world)
+        m = Model(CFG, kv_f32=kv_f32, device=rank, tp_rank=rank, tp_world=world)
         m.load_named(by_name)
         tp.connect(m)
         m.finalize()
@@ -65,22 +65,28 @@ def _rank(rank, world, port, out_q, cfg_name):
             norms += [np.asarray(w[(PW_RMS_ATT, l)], np.float32), None, np.asarray(w[(PW_RMS_FFN, l)], np.float32), None]
         norms.append(np.asarray(w[(PW_RMS_FINAL, -1)], np.float32))
         seq = list(prompt) + list(np.random.default_rng(4).integers(3, CFG.vocab_size, 32))
-        recs = parity.synced_run_tp(m, PortModel(port_, CFG, w, kv_f32=True), seq, len(seq), port_, norms, CFG,
+        recs = parity.synced_run_tp(m, PortModel(port_, CFG, w, kv_f32=kv_f32), seq, len(seq), port_, norms, CFG,
                                     rank, world)
+        # teacher-forced (not synchronised) along the oracle's greedy stream: this rank's logit rows
+        ref_toks = PortModel(port_, CFG, w, kv_f32=kv_f32).generate(prompt, STEPS)
+        tf_seq = list(prompt) + list(ref_toks)
+        m.dump_enable(False)
+        tf = np.stack([m.forward(int(tf_seq[p]), p) for p in range(min(len(tf_seq), STEPS))])
         err = m.device_error()
         m.close()
         try:
-            summ = parity.check_tp(recs, f"tp{world} {cfg_name} rank {rank}")
+            summ = parity.check_tp(recs, f"tp{world} {cfg_name} {'fp32' if kv_f32 else 'bf16'} KV rank {rank}")
         except AssertionError as e:
             summ = f"FAILED: {e}"
-        out_q.put((rank, toks, summ, err))
+        out_q.put((rank, toks, summ, err, tf))
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("kv_f32", [True, False])
 @pytest.mark.parametrize("cfg_name", sorted(CFGS))
-def test_tp2_vs_oracle(cfg_name):
+def test_tp2_vs_oracle(cfg_name, kv_f32):
     CFG = CFGS[cfg_name]
     from oracle import Port, PortModel, load_port_weights
 
@@ -88,13 +94,13 @@ def test_tp2_vs_oracle(cfg_name):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, world, port, q, cfg_name)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, q, cfg_name, kv_f32)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
     for _ in range(world):
-        r, toks, summ, err = q.get(timeout=600)
-        res[r] = (toks, summ, err)
+        r, toks, summ, err, tf = q.get(timeout=600)
+        res[r] = (toks, summ, err, tf)
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
@@ -107,22 +113,26 @@ def test_tp2_vs_oracle(cfg_name):
     port_ = Port()
     w, _ = load_port_weights(port_, CFG, SEED)
     prompt = synth.seeded_prompt(3, 8, CFG.vocab_size)
-    ref_toks = PortModel(port_, CFG, w, kv_f32=True).generate(prompt, STEPS)
+    ref_toks = PortModel(port_, CFG, w, kv_f32=kv_f32).generate(prompt, STEPS)
     gpu = res[0][0]
     n = min(len(ref_toks), len(gpu))
     first_div = next((i for i in range(n) if ref_toks[i] != gpu[i]), n)
     print(f"tp{world} {cfg_name}: {first_div} identical greedy tokens of {n}")
     if first_div < n:
-        pm = PortModel(port_, CFG, w, kv_f32=True)
+        # the histories agree up to the divergence: the oracle's margin between its token and the GPU's must
+        # lie within the measured GPU-vs-oracle logit difference there (a near-tie)
+        pm = PortModel(port_, CFG, w, kv_f32=kv_f32)
         seq = list(prompt) + list(ref_toks)
         p_div = len(prompt) - 1 + first_div
         for pos in range(p_div + 1):
             lo = pm.forward(int(seq[pos]), pos)
-        top = np.sort(lo)[-2:]
-        assert lo[int(gpu[first_div])] >= top[1] - 2e-2 * abs(top[1]), (first_div, top, lo[int(gpu[first_div])])
+        lg = np.where(np.isnan(res[0][3][p_div]), res[1][3][p_div], res[0][3][p_div])  # both ranks' rows
+        a_ref, a_gpu = int(ref_toks[first_div]), int(gpu[first_div])
+        margin, diff = float(lo[a_ref] - lo[a_gpu]), float(np.max(np.abs(lg - lo)))
+        assert margin <= 2.0 * diff, (first_div, margin, diff)
 
 
-def _rank_prefill(rank, world, port, out_q, cfg_name):
+def _rank_prefill(rank, world, port, out_q, cfg_name, kv_f32=True):
     CFG = CFGS[cfg_name]
     import torch.distributed as dist
 
@@ -136,7 +146,7 @@ def _rank_prefill(rank, world, port, out_q, cfg_name):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         _, by_name = load_port_weights(Port(), CFG, SEED)
-        m = Model(CFG, kv_f32=True, device=rank, tp_rank=rank, tp_world=world)
+        m = Model(CFG, kv_f32=kv_f32, device=rank, tp_rank=rank, tp_world=world)
         m.load_named(by_name)
         tp.connect(m)
         m.finalize()
@@ -159,8 +169,9 @@ def _rank_prefill(rank, world, port, out_q, cfg_name):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("kv_f32", [True, False])
 @pytest.mark.parametrize("cfg_name", sorted(CFGS))
-def test_tp2_prefill_equals_stepped_decode(cfg_name):
+def test_tp2_prefill_equals_stepped_decode(cfg_name, kv_f32):
     """Tensor-parallel prefill: the wo / w2 partial rows of a chunk cross NVLink and are summed in rank
     order, as the decode step sums them; so the KV cache after a prefill is the one stepped decode leaves
     on every rank (bit-exact logits of this rank's classifier rows after it), and generate gives the same
@@ -169,7 +180,7 @@ def test_tp2_prefill_equals_stepped_decode(cfg_name):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_prefill, args=(r, world, port, q, cfg_name)) for r in range(world)]
+    procs = [ctx.Process(target=_rank_prefill, args=(r, world, port, q, cfg_name, kv_f32)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
