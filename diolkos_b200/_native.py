@@ -57,7 +57,8 @@ SIGNATURES = {
     "dk_model_prefill": (_i, [_vp, _i, _i]),
     "dk_gemm_trace": (_i, [_vp, _sz, _vp, _vp]),
     "dk_attn_split_plan": (_i, [_i, _i, _i, _vp, _vp]),
-    "dk_prefill_attn_plan": (_i, [_i, _i, _i, _i, _i, _i, _vp, _vp]),
+    "dk_step_attn_plan": (_i, [_i, _vp, _vp, _vp]),
+    "dk_prefill_attn_plan": (_i, [_i, _i, _vp, _i, _i, _vp, _vp, _vp]),
     "dk_model_get_tokens": (_i, [_vp, _vp, _i]),
     "dk_model_sync": (_i, [_vp]),
     "dk_model_stream": (_vp, [_vp]),

@@ -187,25 +187,42 @@ int dk_attn_split_plan(int T, int max_splits, int min_chunk, int *nsplit, int *c
     return DK_OK;
 }
 
-int dk_prefill_attn_plan(int n_heads, int n_kv_heads, int max_splits, int min_chunk, int pos0, int ntok,
-                         int *groups_out, long long *items) {
-    if (n_heads < 1 || n_kv_heads < 1 || n_heads % n_kv_heads || max_splits < 1 || min_chunk < 1 || pos0 < 0 ||
-        ntok < 1 || !groups_out)
-        return -set_error(DK_ERR_INVALID, "dk_prefill_attn_plan: bad arguments");
+static bool step_plan_args(const int *plan, AttnArgs &a) {
+    if (!plan || plan[0] < 1 || plan[1] < 1 || plan[2] < 1 || plan[3] < 1 || plan[4] < 0) return false;
+    a.narrow_max_splits = plan[0];
+    a.narrow_min_chunk = plan[1];
+    a.wide_max_splits = plan[2];
+    a.wide_min_chunk = plan[3];
+    a.wide_from = plan[4];
+    a.max_splits = std::max(plan[0], plan[2]);
+    return true;
+}
+
+int dk_step_attn_plan(int T, const int *plan, int *nsplit, int *chunk) {
     AttnArgs a;
+    if (T < 1 || !nsplit || !chunk || !step_plan_args(plan, a))
+        return -set_error(DK_ERR_INVALID, "dk_step_attn_plan: bad arguments");
+    return step_attn_plan(a, T, *nsplit, *chunk);
+}
+
+int dk_prefill_attn_plan(int n_heads, int n_kv_heads, const int *plan, int pos0, int ntok, int *groups_out,
+                         long long *items, long long *narrow_items) {
+    AttnArgs a;
+    if (n_heads < 1 || n_kv_heads < 1 || n_heads % n_kv_heads || pos0 < 0 || ntok < 1 || !groups_out ||
+        !step_plan_args(plan, a))
+        return -set_error(DK_ERR_INVALID, "dk_prefill_attn_plan: bad arguments");
     a.n_heads = n_heads;
     a.n_kv_heads = n_kv_heads;
-    a.max_splits = max_splits;
-    a.min_chunk = min_chunk;
     std::vector<PrefillGroup> g((size_t)ntok);
-    const int n = prefill_attn_plan(a, pos0, ntok, g.data(), items);
+    const int n = prefill_attn_plan(a, pos0, ntok, g.data(), items, narrow_items);
     for (int i = 0; i < n; ++i) {
-        int *o = groups_out + 5 * (size_t)i;
+        int *o = groups_out + 6 * (size_t)i;
         o[0] = g[i].first;
         o[1] = g[i].count;
         o[2] = g[i].nsplit;
         o[3] = g[i].chunk;
         o[4] = g[i].item0;
+        o[5] = g[i].warps;
     }
     return n;
 }

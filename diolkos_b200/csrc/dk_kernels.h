@@ -231,9 +231,37 @@ struct AttnArgs {
     const int *pos = nullptr;
     int n_heads = 0, n_kv_heads = 0, head_size = 0, seq_len = 0;
     int kv_f32 = 0;
+    // max_splits: the split capacity of `work` (its layout stride) and, for the standalone kernel, the cap of
+    // its plan; min_chunk: that plan's shortest split.
     int max_splits = 1, min_chunk = kAttnMinChunk;
+    // The persistent step's attention (and the prompt prefill's, which follows it) has two forms, chosen by
+    // the number of positions T (step_attn_plan): up to wide_from positions, narrow items of
+    // kAttnNarrowWarps warps over short splits (many items, a split merge); beyond, wide items on every
+    // compute warp of a CTA over at most one wave of long splits.
+    int narrow_max_splits = 1, narrow_min_chunk = 16;
+    int wide_max_splits = 1, wide_min_chunk = 16;
+    int wide_from = 0x7fffffff;
     int *err = nullptr;
 };
+constexpr int kAttnNarrowWarps = 2;   // warps of a narrow attention item
+constexpr int kAttnWideWarps = 10;    // warps of a wide one: every compute warp of the persistent step's CTA
+// The persistent step's attention form and split plan over T positions: returns the warps of an item.
+__host__ __device__ inline int step_attn_plan(const AttnArgs &a, int T, int &nsplit, int &chunk) {
+    if (T <= a.wide_from) {
+        attn_split_plan(T, a.narrow_max_splits, a.narrow_min_chunk, nsplit, chunk);
+        return kAttnNarrowWarps;
+    }
+    attn_split_plan(T, a.wide_max_splits, a.wide_min_chunk, nsplit, chunk);
+    // A chunk rounded up to whole 8-position batches: an item's warps run the same batch rounds (a round
+    // is 80 positions), and the chunk stays the same over runs of 8 x nsplit positions, so the prompt
+    // prefill can group 8 positions per item.
+    if (nsplit > 1) {
+        chunk = (chunk + 7) & ~7;
+        nsplit = (T + chunk - 1) / chunk;
+        if (nsplit == 1) chunk = T;
+    }
+    return kAttnWideWarps;
+}
 int attn_max_splits(int seq_len, int n_kv_heads, int num_sms);
 size_t attn_smem_bytes(const AttnArgs &a);
 // Scratch of one attention launch: split partials (n_heads * max_splits * (head_size + 2) floats)
@@ -250,7 +278,21 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st, bool pdl);
 constexpr int kStepProducers = 2;     // producer warps per CTA (one issuing thread each)
 constexpr int kStepMaxSlots = 16;     // ring slots
 constexpr int kStepMaxConsumers = 10; // GEMV consumer warps (at most the compute warps)
-constexpr int kStepMinChunk = 16;     // positions of the shortest attention split in the persistent step
+// Positions of the shortest split of the wide attention form (step_attn_plan): a wide item (one KV head, one
+// split) runs on all compute warps of a CTA, 8 positions per warp per round, 80 per round.  A split takes up
+// to 4 rounds (320 positions) before the plan cuts it -- a split merge costs two L2 round trips, a round
+// about a third of one -- or fewer under grouped-query attention, where a round covers kv_mul query heads;
+// never less than one round, so that no warp of an item idles (70B shape: 80 positions measured 2.6 % faster
+// per token than 40, and 160 slower).
+__host__ __device__ inline int step_min_chunk(int kv_mul) {
+    const int c = 320 / (kv_mul > 0 ? kv_mul : 1);
+    return c > 80 ? c : 80;
+}
+// Contexts up to this many positions take the narrow attention form (step_attn_plan), longer ones the wide.
+// Short contexts have too few positions to fill CTA-wide items; at 2048 positions and beyond the wide form
+// measured 13 % more 7B tokens/s.  Switching at 256, 384 or 640 positions measured the same on the 7B and
+// 70B decode workloads.
+constexpr int kStepWideFrom = 384;
 enum StepOpKind : int { OP_GEMV = 0, OP_ATTN = 1 };
 struct StepOp {
     int kind = OP_GEMV;
@@ -287,7 +329,8 @@ constexpr int kStageTraceOps = 5, kStageTraceCtas = 4, kStageTraceStages = 64;
 constexpr size_t kStageTraceEntries = (size_t)kStageTraceOps * kStageTraceCtas * kStageTraceStages * 4;
 size_t step_ctl_bytes();
 size_t step_attn_scratch_bytes(int n_heads, int n_kv_heads, int head_size);
-int step_attn_item_slots(int num_ctas);
+// attention items one wave of the persistent step runs: num_ctas x the CTA's groups of `warps` warps
+int step_attn_item_slots(int num_ctas, int warps);
 int step_threads();
 int step_max_ctas_per_sm(size_t smem);
 cudaError_t launch_step(const StepArgs &sa, int grid, cudaStream_t st);
@@ -298,14 +341,15 @@ cudaError_t launch_step(const StepArgs &sa, int grid, cudaStream_t st);
 // the decode step's split plan, batch order and merges, K/V rows loaded once for a group of positions.
 cudaError_t launch_prefill_act(const GemvArgs &a, int ntok, const int *tokens, int8_t *xq, float *xs, cudaStream_t st);
 cudaError_t launch_prefill_kv(const AttnArgs &a, int pos0, int ntok, size_t qkv_stride, cudaStream_t st);
-// Prefill attention items: the prompt positions that share the decode step's split plan (split count and
-// chunk; any chunk when there is one split) go together, at most kPrefillRows (query, head) rows, and
+// Prefill attention items: the prompt positions that share the decode step's attention form and split plan
+// (split count and chunk; any chunk when there is one split) go together, at most kPrefillRows (query, head) rows, and
 // one item = (group, KV head, split).
 constexpr int kPrefillRows = 8;
 struct PrefillGroup {
     int first, count;   // positions first .. first+count-1
     int nsplit, chunk;  // their split plan (one split: chunk = the last position + 1)
     int item0;          // index of the group's first item
+    int warps;          // the attention form of their positions (kAttnNarrowWarps or kAttnWideWarps)
 };
 // Tensor-parallel prefill exchange (wo / w2 partial sums of a chunk, over NVLink peer memory):
 // scatter: dst[q] + off receives this rank's nf partial floats, for every rank q (system fence after);
@@ -316,10 +360,13 @@ cudaError_t launch_prefill_scatter(const float *src, float *const *dst, int worl
 cudaError_t launch_prefill_signal(unsigned long long *const *cnt, int world, cudaStream_t st);
 cudaError_t launch_prefill_wait(const unsigned long long *cnt, unsigned long long target, int *err, cudaStream_t st);
 cudaError_t launch_prefill_reduce(float *x, const float *recv, size_t stride, int world, size_t nf, cudaStream_t st);
-// Fills groups[0 .. n) (capacity ntok) for positions pos0 .. pos0+ntok-1; returns n, *items = total items.
-int prefill_attn_plan(const AttnArgs &a, int pos0, int ntok, PrefillGroup *groups, long long *items);
+// Fills groups[0 .. n) (capacity ntok) for positions pos0 .. pos0+ntok-1 with the persistent step's attention
+// form and split plan (step_attn_plan); returns n, *items = total items, *narrow_items = the items of the narrow
+// groups, which come first.
+int prefill_attn_plan(const AttnArgs &a, int pos0, int ntok, PrefillGroup *groups, long long *items,
+                      long long *narrow_items = nullptr);
 cudaError_t launch_prefill_attn(const AttnArgs &a, int pos0, const PrefillGroup *d_groups, int ngroups,
-                                long long items, size_t qkv_stride, size_t out_stride, size_t work_stride,
-                                size_t count_stride, cudaStream_t st);
+                                long long items, long long narrow_items, size_t qkv_stride, size_t out_stride,
+                                size_t work_stride, size_t count_stride, cudaStream_t st);
 
 }  // namespace dk

@@ -116,7 +116,10 @@ struct dk_model {
     StepOp *d_ops = nullptr;
     int n_ops = 0;
     unsigned long long *step_cnt = nullptr;  // [n_layers][5]: qkv, attention, wo, w1|w3, w2
-    int step_splits = 1;                  // attention splits per KV head in the persistent step
+    // the persistent step's attention plan (step_attn_plan): narrow items up to step_wide_from positions,
+    // wide ones beyond; step_splits = the larger split count, the layout stride of the split scratch
+    int step_narrow_splits = 1, step_wide_splits = 1, step_wide_chunk = 16, step_wide_from = 0x7fffffff;
+    int step_splits = 1;
     StepArgs step;
     unsigned long long *d_trace = nullptr;  // DIOLKOS_STEP_TRACE=1: the persistent step's timeline
     std::vector<StepOp> h_ops;            // the op list as uploaded (diagnostics rewrite it)
@@ -273,9 +276,25 @@ dk_model *dk_model_create(const int *cfg, int kv_type, int device, int tp_rank, 
         const char *mode = getenv("DIOLKOS_STEP");
         m->use_step = !(mode && strcmp(mode, "kernels") == 0);
     }
-    // the persistent step's attention: one (KV head, split) item per attention group of the grid
-    m->step_splits = std::max(1, std::min((step_attn_item_slots(m->num_sms) + m->l_kv_heads - 1) / m->l_kv_heads,
-                                          (S + kStepMinChunk - 1) / kStepMinChunk));
+    // The persistent step's attention.  Narrow form (contexts up to step_wide_from positions): one
+    // (KV head, split) item per 2-warp group of the grid, splits of at least 16 positions.  Wide form: at most
+    // one wave of CTA-wide items, splits of at least step_min_chunk positions.  DIOLKOS_ATTN_WIDE_FROM moves
+    // the switch (0: the wide form throughout; a value >= the context: the narrow form throughout);
+    // DIOLKOS_ATTN_WIDE_CHUNK sets the wide form's shortest split (positions).
+    {
+        const int kv_mul = m->l_heads / m->l_kv_heads;
+        m->step_narrow_splits =
+            std::max(1, std::min((step_attn_item_slots(m->num_sms, kAttnNarrowWarps) + m->l_kv_heads - 1) / m->l_kv_heads,
+                                 (S + 15) / 16));
+        m->step_wide_chunk = step_min_chunk(kv_mul);
+        if (const char *e = getenv("DIOLKOS_ATTN_WIDE_CHUNK")) m->step_wide_chunk = std::max(16, atoi(e));
+        m->step_wide_splits =
+            std::max(1, std::min(step_attn_item_slots(m->num_sms, kAttnWideWarps) / m->l_kv_heads,
+                                 (S + m->step_wide_chunk - 1) / m->step_wide_chunk));
+        m->step_wide_from = kStepWideFrom;
+        if (const char *e = getenv("DIOLKOS_ATTN_WIDE_FROM")) m->step_wide_from = std::max(0, atoi(e));
+        m->step_splits = std::max(m->step_narrow_splits, m->step_wide_splits);
+    }
     const int work_splits = std::max(m->attn_splits, m->step_splits);
     const size_t sz_x = align256((size_t)dim * 4), sz_qkv = align256((size_t)qkv_rows * 4);
     const size_t sz_hb = align256((size_t)lh * 4), sz_logits = align256((size_t)m->l_vocab * 4);
@@ -580,6 +599,17 @@ static int enqueue_step(dk_model *m, cudaStream_t st) {
 // The persistent step (step.cu): the step's op list -- per layer q|k|v GEMV, attention, wo GEMV, w1|w3
 // GEMV, w2 GEMV; then the classifier -- with the same arguments the per-kernel path gives each launch,
 // the dependency counters that replace the kernel boundaries, and the shared-memory plan.
+// The persistent step's attention plan, shared by the decode step and the prompt prefill (step_attn_plan).
+static void step_attn_fields(const dk_model *m, AttnArgs &t) {
+    t.max_splits = m->step_splits;
+    t.min_chunk = 16;
+    t.narrow_max_splits = m->step_narrow_splits;
+    t.narrow_min_chunk = 16;
+    t.wide_max_splits = m->step_wide_splits;
+    t.wide_min_chunk = m->step_wide_chunk;
+    t.wide_from = m->step_wide_from;
+}
+
 static int build_step(dk_model *m) {
     const bool tp = m->world > 1;
     void *const *tab = reinterpret_cast<void *const *>(m->d_ptrs);
@@ -653,7 +683,7 @@ static int build_step(dk_model *m) {
         t.v_cache = static_cast<uint8_t *>(m->vcache) + (size_t)l * m->kv_layer_elems * esz;
         t.out = m->xb; t.work = m->attn_work; t.count = m->attn_count; t.pos = m->pos;
         t.n_heads = m->l_heads; t.n_kv_heads = m->l_kv_heads; t.head_size = m->hs; t.seq_len = m->seq_len;
-        t.kv_f32 = m->kv_type == DK_KV_F32; t.max_splits = m->step_splits; t.min_chunk = kStepMinChunk; t.err = m->err;
+        t.kv_f32 = m->kv_type == DK_KV_F32; step_attn_fields(m, t); t.err = m->err;
         at.wait_cnt = cnt(l, 0);
         at.wait_units = (unsigned long long)qkv_rows;
         at.done_cnt = cnt(l, 1);
@@ -1182,15 +1212,15 @@ static int prefill_chunk(dk_model *m, int pos0, int n, cudaStream_t st) {
     t.qkv = m->pqkv; t.rope = m->rope;
     t.out = m->pxb; t.work = m->pwork; t.count = m->pcount; t.pos = m->pos;
     t.n_heads = m->l_heads; t.n_kv_heads = m->l_kv_heads; t.head_size = m->hs; t.seq_len = m->seq_len;
-    t.kv_f32 = m->kv_type == DK_KV_F32; t.max_splits = m->step_splits; t.min_chunk = kStepMinChunk; t.err = m->err;
+    t.kv_f32 = m->kv_type == DK_KV_F32; step_attn_fields(m, t); t.err = m->err;
     // the attention's position groups (the same for every layer), planned into this chunk's pinned slot
     // once that slot's previous upload is done; stream order keeps the upload behind the previous
     // chunk's kernels
     const int slot = (pos0 / C) % m->pslots;
     PrefillGroup *hg = m->h_groups + (size_t)slot * C;
     if (int r = cuda_status(cudaEventSynchronize(m->pslot_done[slot]), "prefill: group slot")) return r;
-    long long items = 0;
-    const int ngroups = prefill_attn_plan(t, pos0, n, hg, &items);
+    long long items = 0, narrow_items = 0;
+    const int ngroups = prefill_attn_plan(t, pos0, n, hg, &items, &narrow_items);
     if (int r = cuda_status(cudaMemcpyAsync(m->pgroups, hg, (size_t)ngroups * sizeof(PrefillGroup),
                                             cudaMemcpyHostToDevice, st),
                             "prefill: group table"))
@@ -1206,7 +1236,7 @@ static int prefill_chunk(dk_model *m, int pos0, int n, cudaStream_t st) {
         // The last layer's attention and MLP feed only these positions' logits, which nothing reads: the
         // decode step recomputes the last prompt position.  Its K/V rows are all that is kept.
         if (!e && l == m->n_layers - 1) break;
-        if (!e) e = launch_prefill_attn(t, pos0, m->pgroups, ngroups, items, (size_t)qkv_rows, (size_t)m->l_dim,
+        if (!e) e = launch_prefill_attn(t, pos0, m->pgroups, ngroups, items, narrow_items, (size_t)qkv_rows, (size_t)m->l_dim,
                                         m->pwork_stride, m->pcount_stride, st);
         if (!e) e = act(PRO_F32, m->pxb, nullptr, m->l_dim);
         if (!e) e = tp ? mm(ly.wo, m->l_dim, m->dim, m->p_wo.T, EPI_STORE, m->ppart)

@@ -45,15 +45,16 @@ constexpr int kStepWarps = 12;
 constexpr int kStepThreads = 32 * kStepWarps;
 constexpr int kComputeWarps = kStepWarps - kStepProducers;  // warps 0 .. 9
 constexpr int kComputeThreads = 32 * kComputeWarps;
-constexpr int kAttnGroupWarps = 2;
-constexpr int kAttnGroups = kComputeWarps / kAttnGroupWarps;  // 5
-constexpr int kAttnGroupThreads = 32 * kAttnGroupWarps;
+// Attention items run on groups of GW warps: kAttnNarrowWarps (the narrow form: kComputeWarps / GW groups
+// per CTA) or kAttnWideWarps (the wide form: one group, every compute warp), step_attn_plan.
+constexpr int kAttnGroups = kComputeWarps / kAttnNarrowWarps;  // groups of the narrow form (5)
+static_assert(kAttnWideWarps == kComputeWarps && kComputeWarps % kAttnNarrowWarps == 0, "attention groups");
 constexpr int kBatch = 8;          // positions an attention warp loads at once
 constexpr int kHeadsPerPass = 2;   // query heads of one KV head an attention warp holds at once
 constexpr int kMergeChunk = 12;    // splits whose partials the merging group loads in one round trip
-constexpr int kMergeDims = 2;      // head dims per merging thread (head_size <= 128 on 64 threads)
+// head dims per merging thread of a GW-warp group (head_size <= 128)
+template <int GW> constexpr int merge_dims() { return (128 + 32 * GW - 1) / (32 * GW); }
 constexpr int kBarCompute = 1;     // named barrier of the compute warps; 2 + g: attention group g
-static_assert(kComputeWarps % kAttnGroupWarps == 0, "attention groups");
 static_assert(2 + kAttnGroups <= 16, "named barriers");
 
 struct StepCtl {  // shared-memory control block
@@ -123,8 +124,9 @@ __device__ __forceinline__ bool bar_compute_or(int v) {
         : "memory");
     return r != 0;
 }
+template <int GW>
 __device__ __forceinline__ void bar_group(int g) {
-    asm volatile("bar.sync %0, %1;" ::"r"(2 + g), "n"(kAttnGroupThreads) : "memory");
+    asm volatile("bar.sync %0, %1;" ::"r"(2 + g), "n"(32 * GW) : "memory");
 }
 __device__ __forceinline__ unsigned long long ld_acquire_gpu(const unsigned long long *p) {
     unsigned long long v;
@@ -624,11 +626,11 @@ __device__ __forceinline__ void load_kv_batch(const AttnArgs &a, size_t head_bas
     }
 }
 
-// One (KV head, split) item on attention group grp (kAttnGroupWarps warps): the arithmetic of the
-// standalone attention kernel (attention.cu), with the group's named barrier in place of the CTA's.
-// sm = the group's scratch [kAttnGroupWarps][kv_mul][hs + 4].  The output of a KV head's query heads
-// is complete when its last split has merged; that split counts them on done_cnt.
-template <bool F32>
+// One (KV head, split) item on attention group grp (GW warps): the arithmetic of the standalone attention
+// kernel (attention.cu), with the group's named barrier in place of the CTA's.  sm = the group's scratch
+// [GW][kv_mul][hs + 4].  The output of a KV head's query heads is complete when its last split has
+// merged; that split counts them on done_cnt.
+template <bool F32, int GW>
 __device__ void attn_item(const AttnArgs &a, int pos, int kvh, int split, int nsplit, int chunk, int grp, int gt,
                           float *sm, StepCtl &ctl, unsigned long long *done_cnt, const StepArgs &sa, int opi) {
     const bool mark = grp == 0 && gt == 0 && sa.trace;
@@ -673,7 +675,7 @@ __device__ void attn_item(const AttnArgs &a, int pos, int kvh, int split, int ns
             acc[m] = make_float4(0, 0, 0, 0);
         }
         if (mark && m0 == 0) trace_mark(sa, opi, 5);
-        for (int tb = t0 + warp * kBatch; tb < t1; tb += kAttnGroupWarps * kBatch) {
+        for (int tb = t0 + warp * kBatch; tb < t1; tb += GW * kBatch) {
             float4 kk[kBatch], vv[kBatch];
             load_kv_batch<F32>(a, head_base, hs, tb, t1, pos, act, kp, vp, kk, vv);
             #pragma unroll
@@ -721,18 +723,18 @@ __device__ void attn_item(const AttnArgs &a, int pos, int kvh, int split, int ns
     }
     const int W = hs + 2;
     if (mark) trace_mark(sa, opi, 6);
-    bar_group(grp);
+    bar_group<GW>(grp);
     for (int m = 0; m < kv_mul; ++m) {
         float M = -INFINITY;
-        for (int w = 0; w < kAttnGroupWarps; ++w) M = fmaxf(M, sm[(size_t)(w * kv_mul + m) * SW]);
+        for (int w = 0; w < GW; ++w) M = fmaxf(M, sm[(size_t)(w * kv_mul + m) * SW]);
         float L = 0.0f;
-        for (int w = 0; w < kAttnGroupWarps; ++w) {
+        for (int w = 0; w < GW; ++w) {
             const float *cw = sm + (size_t)(w * kv_mul + m) * SW;
             L = __fmaf_rn(cw[1], expf(cw[0] - M), L);
         }
-        for (int e = gt; e < hs; e += kAttnGroupThreads) {
+        for (int e = gt; e < hs; e += (32 * GW)) {
             float o = 0.0f;
-            for (int w = 0; w < kAttnGroupWarps; ++w) {
+            for (int w = 0; w < GW; ++w) {
                 const float *cw = sm + (size_t)(w * kv_mul + m) * SW;
                 o = __fmaf_rn(cw[4 + e], expf(cw[0] - M), o);
             }
@@ -749,25 +751,25 @@ __device__ void attn_item(const AttnArgs &a, int pos, int kvh, int split, int ns
         }
     }
     __threadfence();
-    bar_group(grp);  // the scratch is reused by the next item; every store above is fenced
+    bar_group<GW>(grp);  // the scratch is reused by the next item; every store above is fenced
     if (mark) trace_mark(sa, opi, 7);
     if (nsplit > 1) {
         if (gt == 0) {
             const unsigned ticket = atomicAdd(a.count + kvh, 1u);
             ctl.grp_last[grp] = ticket == (unsigned)nsplit - 1u;
         }
-        bar_group(grp);
+        bar_group<GW>(grp);
         if (!ctl.grp_last[grp]) return;
         __threadfence();
         // Merge the splits: every split's (max, sum) and this thread's accumulators are loaded together
         // (one round trip per kMergeChunk splits), folded with an online rescale.
         for (int m = 0; m < kv_mul; ++m) {
             const float *wb = a.work + (size_t)(kvh * kv_mul + m) * a.max_splits * W;
-            float M = -INFINITY, L = 0.0f, o[kMergeDims];
+            float M = -INFINITY, L = 0.0f, o[merge_dims<GW>()];
             #pragma unroll
-            for (int k = 0; k < kMergeDims; ++k) o[k] = 0.0f;
+            for (int k = 0; k < merge_dims<GW>(); ++k) o[k] = 0.0f;
             for (int s0 = 0; s0 < nsplit; s0 += kMergeChunk) {
-                float cm[kMergeChunk], cl[kMergeChunk], co[kMergeChunk][kMergeDims];
+                float cm[kMergeChunk], cl[kMergeChunk], co[kMergeChunk][merge_dims<GW>()];
                 #pragma unroll
                 for (int j = 0; j < kMergeChunk; ++j) {
                     const bool in = s0 + j < nsplit;
@@ -775,8 +777,8 @@ __device__ void attn_item(const AttnArgs &a, int pos, int kvh, int split, int ns
                     cm[j] = in ? __ldcg(w) : -INFINITY;
                     cl[j] = in ? __ldcg(w + 1) : 0.0f;
                     #pragma unroll
-                    for (int k = 0; k < kMergeDims; ++k) {
-                        const int e = gt + k * kAttnGroupThreads;
+                    for (int k = 0; k < merge_dims<GW>(); ++k) {
+                        const int e = gt + k * (32 * GW);
                         co[j][k] = (in && e < hs) ? __ldcg(w + 2 + e) : 0.0f;
                     }
                 }
@@ -786,26 +788,34 @@ __device__ void attn_item(const AttnArgs &a, int pos, int kvh, int split, int ns
                 const float r = expf(M - cmax);  // 0 while M is -inf
                 L = __fmul_rn(L, r);
                 #pragma unroll
-                for (int k = 0; k < kMergeDims; ++k) o[k] = __fmul_rn(o[k], r);
+                for (int k = 0; k < merge_dims<GW>(); ++k) o[k] = __fmul_rn(o[k], r);
                 #pragma unroll
                 for (int j = 0; j < kMergeChunk; ++j) {
                     const float f = expf(cm[j] - cmax);  // 0 for the padding entries
                     L = __fmaf_rn(cl[j], f, L);
                     #pragma unroll
-                    for (int k = 0; k < kMergeDims; ++k) o[k] = __fmaf_rn(co[j][k], f, o[k]);
+                    for (int k = 0; k < merge_dims<GW>(); ++k) o[k] = __fmaf_rn(co[j][k], f, o[k]);
                 }
                 M = cmax;
             }
             #pragma unroll
-            for (int k = 0; k < kMergeDims; ++k) {
-                const int e = gt + k * kAttnGroupThreads;
+            for (int k = 0; k < merge_dims<GW>(); ++k) {
+                const int e = gt + k * (32 * GW);
                 if (e < hs) a.out[(size_t)(kvh * kv_mul + m) * hs + e] = __fdiv_rn(o[k], L);
             }
         }
         if (gt == 0) a.count[kvh] = 0u;
-        bar_group(grp);
+        bar_group<GW>(grp);
     }
     if (gt == 0) red_release_add(done_cnt, (unsigned long long)kv_mul * hs);
+}
+// The wide form out of line: inlined, its code would share the kernel's register allocation with the
+// GEMV consumers and slow every op (measured); a call per CTA-wide item costs little.
+template <bool F32>
+__device__ __noinline__ void attn_item_wide(const AttnArgs &a, int pos, int kvh, int split, int nsplit, int chunk,
+                                            int tid, float *sm, StepCtl &ctl, unsigned long long *done_cnt,
+                                            const StepArgs &sa, int opi) {
+    attn_item<F32, kAttnWideWarps>(a, pos, kvh, split, nsplit, chunk, 0, tid, sm, ctl, done_cnt, sa, opi);
 }
 
 __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa) {
@@ -849,9 +859,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa
                     const AttnArgs &at = op.at;
                     const int T = pos + 1;
                     int nsplit, chunk;
-                    attn_split_plan(T, at.max_splits, at.min_chunk, nsplit, chunk);
+                    const int groups = kComputeWarps / step_attn_plan(at, T, nsplit, chunk);
                     const size_t row = (size_t)at.head_size * (at.kv_f32 ? 4 : 2);
-                    for (int g = 0; g < kAttnGroups; ++g) {
+                    for (int g = 0; g < groups; ++g) {
                         const int it = g * (int)gridDim.x + (int)blockIdx.x;
                         if (it >= at.n_kv_heads * nsplit) break;
                         const int kvh = it / nsplit, t0 = (it % nsplit) * chunk, t1 = min(pos, t0 + chunk);
@@ -1037,17 +1047,28 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa
             if (tid == 0) trace_mark(sa, i, 0);
             const int T = pos + 1;
             int nsplit, chunk;
-            attn_split_plan(T, at.max_splits, at.min_chunk, nsplit, chunk);
+            const int gw = step_attn_plan(at, T, nsplit, chunk);  // the same on every thread
             const int items = at.n_kv_heads * nsplit;
-            const int grp = warp / kAttnGroupWarps, gt = tid - grp * kAttnGroupThreads;
             const int kv_mul = at.n_heads / at.n_kv_heads;
-            float *sm = reinterpret_cast<float *>(act) + (size_t)grp * kAttnGroupWarps * kv_mul * (at.head_size + 4);
             // item it runs on CTA it % grid: consecutive items (the splits of one head, then the next
             // head) spread over all SMs, so every SM's share of the KV cache is loaded at once
-            for (int it = grp * (int)gridDim.x + (int)blockIdx.x; it < items; it += gridDim.x * kAttnGroups) {
-                const int kvh = it / nsplit, split = it % nsplit;
-                if (at.kv_f32) attn_item<true>(at, pos, kvh, split, nsplit, chunk, grp, gt, sm, ctl, op.done_cnt, sa, i);
-                else attn_item<false>(at, pos, kvh, split, nsplit, chunk, grp, gt, sm, ctl, op.done_cnt, sa, i);
+            if (gw == kAttnNarrowWarps) {
+                const int grp = warp / kAttnNarrowWarps, gt = tid - grp * 32 * kAttnNarrowWarps;
+                float *sm = reinterpret_cast<float *>(act) + (size_t)grp * kAttnNarrowWarps * kv_mul * (at.head_size + 4);
+                for (int it = grp * (int)gridDim.x + (int)blockIdx.x; it < items; it += gridDim.x * kAttnGroups) {
+                    const int kvh = it / nsplit, split = it % nsplit;
+                    if (at.kv_f32)
+                        attn_item<true, kAttnNarrowWarps>(at, pos, kvh, split, nsplit, chunk, grp, gt, sm, ctl, op.done_cnt, sa, i);
+                    else
+                        attn_item<false, kAttnNarrowWarps>(at, pos, kvh, split, nsplit, chunk, grp, gt, sm, ctl, op.done_cnt, sa, i);
+                }
+            } else {
+                float *sm = reinterpret_cast<float *>(act);
+                for (int it = (int)blockIdx.x; it < items; it += gridDim.x) {
+                    const int kvh = it / nsplit, split = it % nsplit;
+                    if (at.kv_f32) attn_item_wide<true>(at, pos, kvh, split, nsplit, chunk, tid, sm, ctl, op.done_cnt, sa, i);
+                    else attn_item_wide<false>(at, pos, kvh, split, nsplit, chunk, tid, sm, ctl, op.done_cnt, sa, i);
+                }
             }
             bar_compute();  // the scratch (the activation area) is free again
             if (tid == 0) trace_mark(sa, i, 2);
@@ -1112,8 +1133,9 @@ constexpr int kPreRowChunk = 4;
 static_assert(kPreRowChunk * kBatch == 32, "one score per lane");
 constexpr int kPrePartStride = 36;  // floats per (row, position) block of lane partials: 16-byte reads without conflicts
 
-// Attention of the prompt positions of one group (positions that share the decode step's split plan)
-// for one (KV head, split): item = blockIdx.x, one attention group of kAttnGroupWarps warps.  Each K/V
+// Attention of the prompt positions of one group (positions that share the decode step's attention form
+// and split plan) for one (KV head, split): item = item_base + blockIdx.x, one attention group of GW warps
+// (the form's item size: its positions' decode steps run their items on GW warps).  Each K/V
 // batch is loaded once and used for every (position, query head) row of the group; each row keeps the
 // decode step's own arithmetic (attn_item): the same batches in the same order per warp, the same
 // masked tail, the warp merge, the split partials and the last split's merge -- so every output equals
@@ -1128,18 +1150,17 @@ constexpr int kPrePartStride = 36;  // floats per (row, position) block of lane 
 //       the batch max over the row's 8 lanes, the rescale and exp, and the running sum in position order
 //       through shuffles;
 //   (c) lanes over head dims: acc = acc * rescale, then acc = fma(p_j, v_j, acc) in position order.
-template <bool F32>
-__global__ void __launch_bounds__(kAttnGroupThreads, 8) prefill_attn_kernel(const AttnArgs a, int pos0,
-                                                                         const PrefillGroup *groups, int ngroups,
-                                                                         size_t qkv_stride, size_t out_stride,
-                                                                         size_t work_stride, size_t count_stride) {
+template <bool F32, int GW>
+__global__ void __launch_bounds__(32 * GW, GW == kAttnNarrowWarps ? 8 : 2)
+    prefill_attn_kernel(const AttnArgs a, int pos0, const PrefillGroup *groups, int ngroups, long long item_base,
+                        size_t qkv_stride, size_t out_stride, size_t work_stride, size_t count_stride) {
     extern __shared__ __align__(16) float psm[];
     __shared__ int last_split[kPrefillRows];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int hs = a.head_size, half = hs >> 1, d0 = 4 * lane;
     const bool act = d0 < hs;
     const int kv_mul = a.n_heads / a.n_kv_heads;
-    const long long item = blockIdx.x;
+    const long long item = item_base + blockIdx.x;
     int lo = 0, hi = ngroups - 1;  // the group holding this item: the last with item0 <= item
     while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
@@ -1153,8 +1174,8 @@ __global__ void __launch_bounds__(kAttnGroupThreads, 8) prefill_attn_kernel(cons
     const int t0 = split * g.chunk, tmax = min(g.first + g.count, t0 + g.chunk);
     const int SW = hs + 4, W = hs + 2;
     float *qs = psm;                           // [kPrefillRows][hs]
-    float *stt = psm + (size_t)kPrefillRows * hs;  // [kAttnGroupWarps][kPrefillRows][SW]
-    for (int r = warp; r < rows; r += kAttnGroupWarps) {
+    float *stt = psm + (size_t)kPrefillRows * hs;  // [GW][kPrefillRows][SW]
+    for (int r = warp; r < rows; r += GW) {
         const int q = r / kv_mul, m = r % kv_mul, pos = g.first + q;
         if (act)
             *reinterpret_cast<float4 *>(qs + (size_t)r * hs + d0) =
@@ -1172,12 +1193,12 @@ __global__ void __launch_bounds__(kAttnGroupThreads, 8) prefill_attn_kernel(cons
     __syncthreads();
     const float sq = __fsqrt_rn((float)hs);
     const size_t head_base = (size_t)kvh * a.seq_len * hs + d0;
-    float *part = psm + (size_t)kPrefillRows * hs + (size_t)kAttnGroupWarps * kPrefillRows * SW +
+    float *part = psm + (size_t)kPrefillRows * hs + (size_t)GW * kPrefillRows * SW +
                   (size_t)warp * kPreRowChunk * kBatch * kPrePartStride;  // this warp's [32][36] partials
-    float *pjs = psm + (size_t)kPrefillRows * hs + (size_t)kAttnGroupWarps * kPrefillRows * SW +
-                 (size_t)kAttnGroupWarps * kPreRowChunk * kBatch * kPrePartStride + (size_t)warp * 40;  // [4][8], [4]
+    float *pjs = psm + (size_t)kPrefillRows * hs + (size_t)GW * kPrefillRows * SW +
+                 (size_t)GW * kPreRowChunk * kBatch * kPrePartStride + (size_t)warp * 40;  // [4][8], [4]
     auto row_end = [&](int r) { return min(g.first + r / kv_mul + 1, t0 + g.chunk); };
-    for (int tb = t0 + warp * kBatch; tb < tmax; tb += kAttnGroupWarps * kBatch) {
+    for (int tb = t0 + warp * kBatch; tb < tmax; tb += GW * kBatch) {
         float4 kk[kBatch], vv[kBatch];
         #pragma unroll
         for (int j = 0; j < kBatch; ++j) {
@@ -1272,16 +1293,16 @@ __global__ void __launch_bounds__(kAttnGroupThreads, 8) prefill_attn_kernel(cons
         const int q = r / kv_mul, m = r % kv_mul, pos = g.first + q;
         const float *s0 = stt + (size_t)r * SW;
         float M = -INFINITY;
-        for (int w = 0; w < kAttnGroupWarps; ++w) M = fmaxf(M, s0[(size_t)w * kPrefillRows * SW]);
+        for (int w = 0; w < GW; ++w) M = fmaxf(M, s0[(size_t)w * kPrefillRows * SW]);
         float L = 0.0f;
-        for (int w = 0; w < kAttnGroupWarps; ++w) {
+        for (int w = 0; w < GW; ++w) {
             const float *cw = s0 + (size_t)w * kPrefillRows * SW;
             L = __fmaf_rn(cw[1], expf(cw[0] - M), L);
         }
         const size_t hrow = (size_t)(kvh * kv_mul + m);
-        for (int e = tid; e < hs; e += kAttnGroupThreads) {
+        for (int e = tid; e < hs; e += (32 * GW)) {
             float o = 0.0f;
-            for (int w = 0; w < kAttnGroupWarps; ++w) {
+            for (int w = 0; w < GW; ++w) {
                 const float *cw = s0 + (size_t)w * kPrefillRows * SW;
                 o = __fmaf_rn(cw[4 + e], expf(cw[0] - M), o);
             }
@@ -1310,11 +1331,11 @@ __global__ void __launch_bounds__(kAttnGroupThreads, 8) prefill_attn_kernel(cons
         const float *work = a.work + (size_t)(pos - pos0) * work_stride;
         for (int m = 0; m < kv_mul; ++m) {
             const float *wb = work + (size_t)(kvh * kv_mul + m) * a.max_splits * W;
-            float M = -INFINITY, L = 0.0f, o[kMergeDims];
+            float M = -INFINITY, L = 0.0f, o[merge_dims<GW>()];
             #pragma unroll
-            for (int k = 0; k < kMergeDims; ++k) o[k] = 0.0f;
+            for (int k = 0; k < merge_dims<GW>(); ++k) o[k] = 0.0f;
             for (int s0 = 0; s0 < g.nsplit; s0 += kMergeChunk) {
-                float cm[kMergeChunk], cl[kMergeChunk], co[kMergeChunk][kMergeDims];
+                float cm[kMergeChunk], cl[kMergeChunk], co[kMergeChunk][merge_dims<GW>()];
                 #pragma unroll
                 for (int j = 0; j < kMergeChunk; ++j) {
                     const bool in = s0 + j < g.nsplit;
@@ -1322,8 +1343,8 @@ __global__ void __launch_bounds__(kAttnGroupThreads, 8) prefill_attn_kernel(cons
                     cm[j] = in ? __ldcg(w) : -INFINITY;
                     cl[j] = in ? __ldcg(w + 1) : 0.0f;
                     #pragma unroll
-                    for (int k = 0; k < kMergeDims; ++k) {
-                        const int e = tid + k * kAttnGroupThreads;
+                    for (int k = 0; k < merge_dims<GW>(); ++k) {
+                        const int e = tid + k * (32 * GW);
                         co[j][k] = (in && e < hs) ? __ldcg(w + 2 + e) : 0.0f;
                     }
                 }
@@ -1333,19 +1354,19 @@ __global__ void __launch_bounds__(kAttnGroupThreads, 8) prefill_attn_kernel(cons
                 const float rr = expf(M - cmax);
                 L = __fmul_rn(L, rr);
                 #pragma unroll
-                for (int k = 0; k < kMergeDims; ++k) o[k] = __fmul_rn(o[k], rr);
+                for (int k = 0; k < merge_dims<GW>(); ++k) o[k] = __fmul_rn(o[k], rr);
                 #pragma unroll
                 for (int j = 0; j < kMergeChunk; ++j) {
                     const float f = expf(cm[j] - cmax);
                     L = __fmaf_rn(cl[j], f, L);
                     #pragma unroll
-                    for (int k = 0; k < kMergeDims; ++k) o[k] = __fmaf_rn(co[j][k], f, o[k]);
+                    for (int k = 0; k < merge_dims<GW>(); ++k) o[k] = __fmaf_rn(co[j][k], f, o[k]);
                 }
                 M = cmax;
             }
             #pragma unroll
-            for (int k = 0; k < kMergeDims; ++k) {
-                const int e = tid + k * kAttnGroupThreads;
+            for (int k = 0; k < merge_dims<GW>(); ++k) {
+                const int e = tid + k * (32 * GW);
                 if (e < hs) a.out[(size_t)(pos - pos0) * out_stride + (size_t)(kvh * kv_mul + m) * hs + e] = __fdiv_rn(o[k], L);
             }
         }
@@ -1415,19 +1436,21 @@ cudaError_t launch_prefill_reduce(float *x, const float *recv, size_t stride, in
     return cudaGetLastError();
 }
 
-int prefill_attn_plan(const AttnArgs &a, int pos0, int ntok, PrefillGroup *groups, long long *items) {
+int prefill_attn_plan(const AttnArgs &a, int pos0, int ntok, PrefillGroup *groups, long long *items,
+                      long long *narrow_items) {
     const int kv_mul = a.n_heads / a.n_kv_heads;
     const int qmax = std::max(1, kPrefillRows / kv_mul);
     int n = 0;
-    long long total = 0;
+    long long total = 0, narrow = 0;
     for (int t = 0; t < ntok; ++t) {
         const int pos = pos0 + t, T = pos + 1;
         int ns, ch;
-        attn_split_plan(T, a.max_splits, a.min_chunk, ns, ch);
+        const int gw = step_attn_plan(a, T, ns, ch);
         if (n > 0) {
             PrefillGroup &b = groups[n - 1];
-            // one split: the run is [0, T) whatever the chunk; more: the same chunk, the same split starts
-            if (b.count < qmax && b.nsplit == ns && (ns == 1 || b.chunk == ch)) {
+            // the same form; one split: the run is [0, T) whatever the chunk; more: the same chunk, the same
+            // split starts
+            if (b.count < qmax && b.warps == gw && b.nsplit == ns && (ns == 1 || b.chunk == ch)) {
                 ++b.count;
                 if (ns == 1) b.chunk = T;
                 continue;
@@ -1439,10 +1462,13 @@ int prefill_attn_plan(const AttnArgs &a, int pos0, int ntok, PrefillGroup *group
         groups[n].nsplit = ns;
         groups[n].chunk = ch;
         groups[n].item0 = (int)total;
+        groups[n].warps = gw;
+        if (gw == kAttnNarrowWarps) narrow = total + (long long)a.n_kv_heads * ns;
         ++n;
     }
     if (n > 0) total += (long long)a.n_kv_heads * groups[n - 1].nsplit;
     if (items) *items = total;
+    if (narrow_items) *narrow_items = narrow;
     return n;
 }
 
@@ -1463,37 +1489,55 @@ cudaError_t launch_prefill_kv(const AttnArgs &a, int pos0, int ntok, size_t qkv_
     return cudaGetLastError();
 }
 
-cudaError_t launch_prefill_attn(const AttnArgs &a, int pos0, const PrefillGroup *d_groups, int ngroups,
-                                long long items, size_t qkv_stride, size_t out_stride, size_t work_stride,
-                                size_t count_stride, cudaStream_t st) {
-    if (ngroups < 1 || items < 1 || items > 0x7FFFFFFFLL || a.head_size > 128 || a.head_size % 4) return cudaErrorInvalidValue;
+template <bool F32, int GW>
+static cudaError_t launch_prefill_attn_form(const AttnArgs &a, int pos0, const PrefillGroup *d_groups, int ngroups,
+                                            long long item0, long long items, size_t qkv_stride, size_t out_stride,
+                                            size_t work_stride, size_t count_stride, cudaStream_t st) {
+    if (items <= 0) return cudaSuccess;
     const size_t smem = sizeof(float) * ((size_t)kPrefillRows * a.head_size +
-                                         (size_t)kAttnGroupWarps * kPrefillRows * (a.head_size + 4) +
-                                         (size_t)kAttnGroupWarps * kPreRowChunk * kBatch * kPrePartStride +
-                                         (size_t)kAttnGroupWarps * 40);
-    if (a.kv_f32) {
-        if (smem > 48 * 1024) {
-            const cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (e != cudaSuccess) return e;
-        }
-        prefill_attn_kernel<true><<<(unsigned)items, kAttnGroupThreads, smem, st>>>(a, pos0, d_groups, ngroups, qkv_stride,
-                                                                                   out_stride, work_stride, count_stride);
-    } else {
-        if (smem > 48 * 1024) {
-            const cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (e != cudaSuccess) return e;
-        }
-        prefill_attn_kernel<false><<<(unsigned)items, kAttnGroupThreads, smem, st>>>(a, pos0, d_groups, ngroups, qkv_stride,
-                                                                                    out_stride, work_stride, count_stride);
+                                         (size_t)GW * kPrefillRows * (a.head_size + 4) +
+                                         (size_t)GW * kPreRowChunk * kBatch * kPrePartStride + (size_t)GW * 40);
+    if (smem > 48 * 1024) {
+        const cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel<F32, GW>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
     }
+    prefill_attn_kernel<F32, GW><<<(unsigned)items, 32 * GW, smem, st>>>(a, pos0, d_groups, ngroups, item0, qkv_stride,
+                                                                        out_stride, work_stride, count_stride);
     return cudaGetLastError();
+}
+
+cudaError_t launch_prefill_attn(const AttnArgs &a, int pos0, const PrefillGroup *d_groups, int ngroups,
+                                long long items, long long narrow_items, size_t qkv_stride, size_t out_stride,
+                                size_t work_stride, size_t count_stride, cudaStream_t st) {
+    if (ngroups < 1 || items < 1 || items > 0x7FFFFFFFLL || narrow_items < 0 || narrow_items > items ||
+        a.head_size > 128 || a.head_size % 4)
+        return cudaErrorInvalidValue;
+    // the narrow groups' items first (the positions before wide_from), then the wide ones'
+    cudaError_t e;
+    if (a.kv_f32) {
+        e = launch_prefill_attn_form<true, kAttnNarrowWarps>(a, pos0, d_groups, ngroups, 0, narrow_items, qkv_stride,
+                                                             out_stride, work_stride, count_stride, st);
+        if (e == cudaSuccess)
+            e = launch_prefill_attn_form<true, kAttnWideWarps>(a, pos0, d_groups, ngroups, narrow_items,
+                                                               items - narrow_items, qkv_stride, out_stride,
+                                                               work_stride, count_stride, st);
+    } else {
+        e = launch_prefill_attn_form<false, kAttnNarrowWarps>(a, pos0, d_groups, ngroups, 0, narrow_items, qkv_stride,
+                                                              out_stride, work_stride, count_stride, st);
+        if (e == cudaSuccess)
+            e = launch_prefill_attn_form<false, kAttnWideWarps>(a, pos0, d_groups, ngroups, narrow_items,
+                                                                items - narrow_items, qkv_stride, out_stride,
+                                                                work_stride, count_stride, st);
+    }
+    return e;
 }
 
 size_t step_ctl_bytes() { return (sizeof(StepCtl) + 127) & ~(size_t)127; }
 size_t step_attn_scratch_bytes(int n_heads, int n_kv_heads, int head_size) {
-    return sizeof(float) * (size_t)kAttnGroups * kAttnGroupWarps * (n_heads / n_kv_heads) * (head_size + 4);
+    return sizeof(float) * (size_t)kComputeWarps * (n_heads / n_kv_heads) * (head_size + 4);
 }
-int step_attn_item_slots(int num_ctas) { return num_ctas * kAttnGroups; }
+int step_attn_item_slots(int num_ctas, int warps) { return num_ctas * (kComputeWarps / warps); }
 int step_threads() { return kStepThreads; }
 
 cudaError_t launch_step(const StepArgs &sa, int grid, cudaStream_t st) {

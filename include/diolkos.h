@@ -265,13 +265,20 @@ int dk_model_trace(dk_model *m, unsigned long long *out, size_t n, int *grid, in
  * (0: not recorded).  *ctas and *blocks give the dimensions (the first 148 CTAs, 32 blocks). */
 int dk_gemm_trace(unsigned long long *out, size_t n, int *ctas, int *blocks);
 /* Diagnostics (host only, no GPU): the attention's split plan over T positions (the count of splits and
- * their length; the decode step's attention, src/transformer.c:149-193, split for the GPU), and the
- * prefill attention's position groups for positions pos0 .. pos0+ntok-1: groups_out receives 5 ints
- * per group (first position, count, split count, chunk, first item index), capacity ntok groups;
- * returns the group count and *items the total (group, KV head, split) items. */
+ * their length; the decode step's attention, src/transformer.c:149-193, split for the GPU).
+ * dk_attn_split_plan: one plan (the standalone attention kernel's form).
+ * dk_step_attn_plan: the persistent step's two forms, plan[5] = {narrow max splits, narrow shortest
+ * split, wide max splits, wide shortest split, wide_from}: T <= wide_from takes the narrow form (items of
+ * 2 warps), beyond the wide one (items of 10 warps, the chunk rounded up to whole 8-position batches);
+ * returns the item's warps.
+ * dk_prefill_attn_plan: the prefill attention's position groups for positions pos0 .. pos0+ntok-1 under
+ * the step's plan: groups_out receives 6 ints per group (first position, count, split count, chunk,
+ * first item index, item warps), capacity ntok groups; returns the group count, *items the total
+ * (group, KV head, split) items and *narrow_items those of the narrow groups, which come first. */
 int dk_attn_split_plan(int T, int max_splits, int min_chunk, int *nsplit, int *chunk);
-int dk_prefill_attn_plan(int n_heads, int n_kv_heads, int max_splits, int min_chunk, int pos0, int ntok,
-                         int *groups_out, long long *items);
+int dk_step_attn_plan(int T, const int *plan, int *nsplit, int *chunk);
+int dk_prefill_attn_plan(int n_heads, int n_kv_heads, const int *plan, int pos0, int ntok, int *groups_out,
+                         long long *items, long long *narrow_items);
 /* Bytes of weights one decode step reads on this rank. */
 size_t dk_model_weight_bytes(dk_model *m);
 

@@ -185,12 +185,15 @@ def test_generate_equals_forward_argmax(tiny_weights):
     np.testing.assert_array_equal(gen, np.array(out, np.int32))
 
 
-def test_kv_f32_and_gqa_vs_oracle(port):
+@pytest.mark.parametrize("wide_from", [None, 100])
+def test_kv_f32_and_gqa_vs_oracle(port, wide_from, monkeypatch):
     """fp32 KV cache and grouped-query attention (8 query heads per KV head, as in 70B), against the
     restatement with the same cache type, state-synchronised over 300 positions (several attention
-    splits)."""
+    splits); with wide_from = 100 the attention takes its wide form (CTA-wide items) from position 100."""
     from oracle import PortModel, load_port_weights
 
+    if wide_from is not None:
+        monkeypatch.setenv("DIOLKOS_ATTN_WIDE_FROM", str(wide_from))
     cfg = synth.Config(dim=512, hidden_dim=1024, n_layers=2, n_heads=8, n_kv_heads=1, vocab_size=2048, seq_len=512)
     w, by_name = load_port_weights(port, cfg, 77)
     for kv_f32 in (True, False):
@@ -283,23 +286,33 @@ def _logits_bits(a):
 
 
 @pytest.mark.parametrize(
-    "shape,kv_f32,P",
+    "shape,kv_f32,P,wide_from",
     [
-        ("tiny", False, 8),
-        ("tiny", False, 200),
-        ("gqa", True, 300),   # two prefill chunks (256 + 43 positions), many attention splits
-        ("gqa", False, 300),
-        ("wide", True, 40),   # dim 4096: the one-round-trip rmsnorm prologue
-        ("capped", False, 540),  # 32 KV heads: the split count is capped (24 on 148 SMs) from position 384
-        ("swiglu", True, 100),   # hidden 4096: w1|w3 (8192 rows) on the pipelined tensor-core matmul
+        ("tiny", False, 8, None),
+        ("tiny", False, 200, None),
+        ("tiny", True, 200, 0),      # the wide attention form at every position
+        ("gqa", True, 300, None),    # two prefill chunks (256 + 43 positions), many attention splits
+        ("gqa", False, 300, None),
+        ("gqa", True, 300, 0),       # wide items over 8 query heads, 80-position splits
+        ("gqa", False, 300, 100),    # the form switches inside the first chunk
+        ("wide", True, 40, None),    # dim 4096: the one-round-trip rmsnorm prologue
+        ("capped", False, 540, None),  # 32 KV heads: the narrow split count is capped (24 on 148 SMs) from
+                                       # position 384, where the wide form takes over
+        ("capped", True, 540, 1000),   # the narrow form throughout
+        ("swiglu", True, 100, None),   # hidden 4096: w1|w3 (8192 rows) on the pipelined tensor-core matmul
     ],
 )
-def test_prefill_equals_decode_steps(port, tiny_weights, shape, kv_f32, P):
+def test_prefill_equals_decode_steps(port, tiny_weights, shape, kv_f32, P, wide_from, monkeypatch):
     """The batched prefill (tensor-core matmuls over the prompt positions) leaves the KV cache exactly
     as decode steps at those positions do (every model here has 2 layers or more: the prefill stops
-    after the last layer's K/V rows, so only earlier layers run attention and the MLP): the logits of the last prompt position, decoded after the
-    prefill, equal bit for bit those decoded after stepping every prompt position."""
+    after the last layer's K/V rows, so only earlier layers run attention and the MLP): the logits of the
+    last prompt position, decoded after the prefill, equal bit for bit those decoded after stepping every
+    prompt position.  wide_from moves the position from which the attention runs in its wide form
+    (DIOLKOS_ATTN_WIDE_FROM; None: the default, 384)."""
     from oracle import load_port_weights
+
+    if wide_from is not None:
+        monkeypatch.setenv("DIOLKOS_ATTN_WIDE_FROM", str(wide_from))
 
     if shape == "tiny":
         cfg, by_name = synth.TINY, tiny_weights[1]
