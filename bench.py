@@ -266,18 +266,10 @@ class CpuReference:
             md = write_reference_model(self.tmp, cfg, seed)
             self.m = ref.load(md, self.tmp)
         else:
-            from oracle import Port, PortModel
-
             os.environ["OMP_NUM_THREADS"] = str(self.want)
             self.variant = "port"
             self.cores = self.want
-            port = Port()
-            w = {}
-            from diolkos_b200.model import weight_id
-
-            for tname, kind, val in host_weights(cfg, seed):
-                w[(_port_key(weight_id(tname)[0]), weight_id(tname)[1])] = val
-            self.m = PortModel(port, cfg, w)
+            self.m = port_model(cfg, seed)
 
     def generate(self, prompt, steps):
         """(generated tokens, seconds of the positions that produced them, top-2 logits per token)."""
@@ -307,6 +299,19 @@ class CpuReference:
                 f"prompt forced one position at a time, then {G} greedy tokens; tok/s = generated tokens / wall "
                 f"time of the positions that produced them; bf16 KV (the reference's); {self.cores} OpenMP threads "
                 f"({self.want} physical cores)")
+
+
+def port_model(cfg, seed: int, kv_f32: bool = False):
+    """The oracle's restatement (oracle/port.c) loaded with the decode workload's weights (bf16 KV, the
+    reference's cache type, unless kv_f32)."""
+    from oracle import Port, PortModel
+
+    from diolkos_b200.model import weight_id
+
+    w = {}
+    for tname, kind, val in host_weights(cfg, seed):
+        w[(_port_key(weight_id(tname)[0]), weight_id(tname)[1])] = val
+    return PortModel(Port(), cfg, w, kv_f32=kv_f32)
 
 
 def _port_key(which: int) -> int:
@@ -339,6 +344,51 @@ def token_check(gpu_toks, ref_toks, ref_top2, source: str) -> dict:
 
 
 # ------------------------------------------------------------------ GEMV microbenchmark (config 2)
+def forced_check(m, prompt, ref_toks, ref_top2, world: int, source: str) -> dict:
+    """Teacher-forced agreement with a reference stream: the model is fed the prompt and then the
+    reference's own tokens, and at every generated position its greedy choice (the first index of the
+    largest logit, over all ranks' classifier rows) is compared with the reference's.  A free-running
+    stream diverges for good at its first near-tie; this count shows whether every disagreement is one.
+    Each disagreement lists the reference's top-2 gap and the model's own gap between its choice and the
+    reference's token (both relative to the top logit).  Every rank calls it (forward exchanges)."""
+    import torch.distributed as dist
+
+    P = len(prompt)
+    seq = [int(t) for t in prompt] + [int(t) for t in ref_toks]
+    local = []  # per generated position: (best value, best global index, value of the reference's token)
+    for pos in range(P - 1 + len(ref_toks)):
+        lg = m.forward(seq[pos], pos)
+        if pos < P - 1:
+            continue
+        ok = np.isfinite(lg)  # tensor parallel: this rank's classifier rows
+        idx = np.flatnonzero(ok)
+        b = int(idx[np.argmax(lg[idx])])
+        rt = seq[pos + 1]
+        local.append((float(lg[b]), b, float(lg[rt]) if ok[rt] else float("nan")))
+    if world > 1:
+        allr = [None] * world
+        dist.all_gather_object(allr, local)
+    else:
+        allr = [local]
+    agree, dis = 0, []
+    for j in range(len(ref_toks)):
+        cands = [r[j] for r in allr]
+        top = max(c[0] for c in cands)
+        best = min(c[1] for c in cands if c[0] == top)
+        rv = next(c[2] for c in cands if c[2] == c[2])
+        if best == int(ref_toks[j]):
+            agree += 1
+            continue
+        d = {"index": j, "gpu": best, "ref": int(ref_toks[j]), "gpu_gap": round((top - rv) / abs(top), 7)}
+        if ref_top2 is not None and j < len(ref_top2):
+            a, b2 = float(ref_top2[j][0]), float(ref_top2[j][1])
+            d["ref_top2_gap"] = round((a - b2) / abs(a), 7) if a else None
+        dis.append(d)
+    return {"agree": agree, "of": len(ref_toks), "vs": source,
+            "max_gap_at_disagreement": max((max(d["gpu_gap"], d.get("ref_top2_gap") or 0.0) for d in dis), default=None),
+            "disagreements": dis[:16]}
+
+
 def gemv_alg_bytes(d: int, n: int) -> float:
     """Algorithmic bytes of one [d x n] Q8_0 GEMV: weights + scales, the activation, the output."""
     return d * n * 1.125 + n * 1.125 + d * 4
@@ -708,13 +758,24 @@ def run_decode(args):
     m.close()  # every rank leaves the exchange at the same point
     barrier()
 
-    # ---- the greedy stream with the reference's cache type (bf16 KV), for the token check against it
-    bf16_toks = None
+    # ---- the greedy stream with the reference's cache type (bf16 KV), for the token check against it, and
+    # the same model teacher-forced with the reference's stream
+    bf16_toks, forced = None, None
+    fx = None
+    if args.model == "7b" and not args.layers and os.path.exists(STREAM_FIXTURE):
+        with open(STREAM_FIXTURE) as f:
+            fx = json.load(f)
+        if not (fx.get("seed") == SEED and fx.get("prompt") == [int(t) for t in prompt]):
+            fx = None
     if args.model == "7b" and not args.layers:
         mb = build_model(cfg, False, SEED, rank, world, local)
         barrier()
         bf16_toks = [int(t) for t in mb.generate(prompt, P - 1 + G)]
         check_err(mb, "after the bf16-KV generate")
+        if fx is not None:
+            forced = forced_check(mb, prompt, fx["tokens"], fx.get("top2"), world,
+                                  f"{os.path.relpath(STREAM_FIXTURE, ROOT)} ({fx.get('reference')})")
+            check_err(mb, "after the teacher-forced check")
         mb.close()
         barrier()
 
@@ -775,12 +836,14 @@ def run_decode(args):
         except Exception as ex:  # the baseline is reported, never required
             cpu = {"value": None, "unit": "tok/s", "cores": physical_cores(), "kind": "reference",
                    "sample": f"not run: {ex}"}
-    if args.model == "7b" and not args.layers and os.path.exists(STREAM_FIXTURE):
-        with open(STREAM_FIXTURE) as f:
-            fx = json.load(f)
-        if fx.get("seed") == SEED and fx.get("prompt") == [int(t) for t in prompt]:
-            checks["fixture"] = token_check(cmp_toks, fx["tokens"], fx.get("top2"),
-                                            f"{os.path.relpath(STREAM_FIXTURE, ROOT)} ({fx.get('reference')})")
+    if fx is not None:
+        checks["fixture"] = token_check(cmp_toks, fx["tokens"], fx.get("top2"),
+                                        f"{os.path.relpath(STREAM_FIXTURE, ROOT)} ({fx.get('reference')})")
+    if forced is not None:
+        if fx.get("control_forced"):
+            c = fx["control_forced"]
+            forced["control"] = {k: c.get(k) for k in ("what", "agree", "of", "max_gap_at_disagreement")}
+        checks["forced"] = forced
     if bf16_toks is not None:
         checks["gpu_stream"] = ("greedy tokens of the same model with the reference's bf16 KV cache (dk_model_generate), "
                                 "compared with the reference's stream; the headline decode uses an fp32 cache, "
