@@ -747,7 +747,9 @@ static int build_step(dk_model *m) {
     sa.S = S;
     int nc = 4;  // measured best on B200 for the LLaMA shapes (more warps spin on the token flags)
     if (const char *e = getenv("DIOLKOS_STEP_NC")) nc = atoi(e);
-    sa.NC = std::max(1, std::min(std::min(nc, S), kStepMaxConsumers));
+    // A consumer waits on a slot's full barrier by parity, which is sound once the slot's previous stage
+    // has landed: the token chain guarantees that for S >= 2 NC + 2 (units of two stages, step.cu).
+    sa.NC = std::max(1, std::min(std::min(nc, (S - 2) / 2), kStepMaxConsumers));
     sa.xoff = (size_t)S * sa.slot;
     sa.ctl_off = sa.xoff + ((act + 127) & ~(size_t)127);
     sa.smem = sa.ctl_off + step_ctl_bytes();

@@ -40,34 +40,32 @@ __device__ __forceinline__ void load_quad(Quad &d, int q, uint32_t seg, uint32_t
     }
 }
 
-// Wait until this lane's token word carries stage G's tag, then take the running sum from it.  The
-// sender warp stores all 32 words with one instruction, so the warp first polls word 0 (one broadcast
-// read per poll: polling warps then cost the consumers computing terms little shared-memory bandwidth),
-// then reads its own word, polling on only in the rare case that it has not landed yet.  A word is
-// single-copy atomic, so the sum and its tag arrive together: no fence, no separate flag.  Bounded, and
-// abandoned on the CTA's abort flag.
+// Wait until this lane's token word carries stage G's tag, then take the running sum from it.  Every
+// lane polls its own word: one shared-memory round trip when the sums have landed, which is what the
+// hand-off costs on the row sums' serial path (the warp's 32 words are two wavefronts).  A word is
+// single-copy atomic, so the sum and its tag arrive together: no fence, no separate flag.  The abort
+// flag and the clock are looked at every 16 polls only, so a poll is one load.  Bounded.
 __device__ __forceinline__ bool lane_token_wait(const unsigned long long *row0, int lane, int G, float &sum, int *err,
                                                 const int *abort) {
-    const volatile unsigned long long *p0 = row0;
     const volatile unsigned long long *p = row0 + lane;
-    const long long t0 = clock64();
-    while ((unsigned)(p0[0] >> 32) != (unsigned)G) {
-        if (*reinterpret_cast<const volatile int *>(abort)) return false;
-        if (clock64() - t0 > DK_WAIT_LIMIT_CYCLES) {
-            atomicOr(err, DK_ERR_TIMEOUT);
-            return false;
-        }
+    unsigned long long v = *p;
+    if ((unsigned)(v >> 32) == (unsigned)G) {
+        sum = __uint_as_float((unsigned)v);
+        return true;
     }
-    for (;;) {
-        const unsigned long long v = *p;
+    const long long t0 = clock64();
+    for (int k = 1;; ++k) {
+        v = *p;
         if ((unsigned)(v >> 32) == (unsigned)G) {
             sum = __uint_as_float((unsigned)v);
             return true;
         }
-        if (*reinterpret_cast<const volatile int *>(abort)) return false;
-        if (clock64() - t0 > DK_WAIT_LIMIT_CYCLES) {
-            atomicOr(err, DK_ERR_TIMEOUT);
-            return false;
+        if (!(k & 15)) {
+            if (*reinterpret_cast<const volatile int *>(abort)) return false;
+            if (clock64() - t0 > DK_WAIT_LIMIT_CYCLES) {
+                atomicOr(err, DK_ERR_TIMEOUT);
+                return false;
+            }
         }
     }
 }

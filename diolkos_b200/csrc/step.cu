@@ -465,65 +465,89 @@ __device__ bool step_activation(const GemvArgs &a, int tok, int8_t *xq, float *x
 }
 
 // ---- GEMV op: consumers ---------------------------------------------------------------------------
-// Consume this CTA's stages of the op (compute warp c < NC): the standalone GEMV's consumer loop
-// (gemv_core.cuh) with the ring position continuing from `gbase` (stages of earlier ops).  Stage s of
-// the op goes to warp s % NC; the rows' running sums travel from the warp of stage s to the warp of
-// stage s+1 (the TOKEN, flagged with the global stage index), so every row is summed in the
-// reference's group order while the terms of NC stages are computed at once.  Returns false on abort.
+// Consume this CTA's stages of the op (compute warp c < NC): the standalone GEMV's arithmetic
+// (gemv_core.cuh) with the ring position continuing from `gbase` (stages of earlier ops).  The stages
+// are taken in UNITS of two consecutive blocks of one tile (one block where a tile has an odd count):
+// unit u goes to warp u % NC, which computes both stages' group terms, frees their ring slots, and then
+// waits for the rows' running sums after unit u-1 (the TOKEN, flagged with the global index of the
+// unit's first stage), adds its 32 terms in group order, and passes the sums on.  So every row is
+// summed in the reference's group order while the terms of NC units are computed at once, and the
+// sums cross between warps once per two blocks.  Returns false on abort.
+
+// The terms of stage G (block b of the tile whose row this lane owns) into t, then its slot freed.
+__device__ __forceinline__ bool stage_terms(const GemvArgs &a, int G, int b, int S, size_t slot_bytes, uint32_t ring_s,
+                                            uint32_t xq_s, uint32_t xs_s, StepCtl &ctl, int lane, bool live,
+                                            float (&t)[16], unsigned long long *st) {
+    const int slot = G % S;
+    if (!__all_sync(FULL, mbar_wait_abortable(&ctl.full[slot], (uint32_t)((G / S) & 1), a.err, &ctl.abort, false))) {
+        if (lane == 0) ctl.abort = 1;
+        return false;
+    }
+    if (st) st[0] = globaltimer();
+    const int wb = q8_blk_width(a.n, b);
+    if (live && DK_CHK((size_t)slot * slot_bytes + (size_t)(lane + 1) * q8_blk_bytes(wb) <= (size_t)S * slot_bytes &&
+                           512 * b + wb <= a.n,
+                       a.err, 2, G)) {
+        const uint32_t seg = ring_s + (uint32_t)(slot * slot_bytes + lane * q8_blk_bytes(wb));
+        const uint32_t xqb = xq_s + 512u * b, xsb = xs_s + 64u * b;
+        if (wb == 512) block_terms_full(t, seg, xqb, xsb, lane);
+        else block_terms_part(t, seg, xqb, xsb, wb, lane);
+        // pinned here: otherwise the compiler may sink the term arithmetic past the token wait
+        #pragma unroll
+        for (int g = 0; g < 16; ++g) asm volatile("" : "+f"(t[g]));
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&ctl.empty[slot]);
+    if (st) st[1] = globaltimer();
+    return true;
+}
+__device__ __forceinline__ float add_terms(float sum, const float (&t)[16], int wb) {
+    if (wb == 512) {
+        #pragma unroll
+        for (int g = 0; g < 16; ++g) sum = __fadd_rn(sum, t[g]);
+    } else {
+        #pragma unroll
+        for (int g = 0; g < 16; ++g)
+            if (g < (wb >> 5)) sum = __fadd_rn(sum, t[g]);
+    }
+    return sum;
+}
+
 __device__ bool gemv_consume(const StepOp &op, const Sched &sc, int gbase, int S, int NC, size_t slot_bytes,
                              uint32_t ring_s, uint32_t xq_s, uint32_t xs_s, StepCtl &ctl, int c, int lane,
                              unsigned long long &best, unsigned long long *strace, unsigned long long epoch) {
     const GemvArgs &a = op.g;
     const int n = a.n;
     const unsigned T = a.tagged ? tp_tag(epoch, a, a.tag_k) : 0u;
-    for (int s = c; s < sc.nst; s += NC) {
-        const int G = gbase + s, slot = G % S;
-        if (!__all_sync(FULL, mbar_wait_abortable(&ctl.full[slot], (uint32_t)((G / S) & 1), a.err, &ctl.abort, false))) {
-            if (lane == 0) ctl.abort = 1;
-            return false;
-        }
-        unsigned long long *st = (strace && s < kStageTraceStages && lane == 0) ? strace + 4 * s : nullptr;
-        if (st) st[0] = globaltimer();
-        const int b = s % sc.nblk;
-        const int row = (sc.t0 + s / sc.nblk) * op.T + lane;
+    const int upt = (sc.nblk + 1) >> 1;  // units per tile
+    const int nunits = sc.nt * upt;
+    for (int u = c; u < nunits; u += NC) {
+        const int tile = u / upt, b0 = 2 * (u - tile * upt);
+        const bool two = b0 + 1 < sc.nblk;
+        const int s0 = tile * sc.nblk + b0, G0 = gbase + s0;
+        const int row = (sc.t0 + tile) * op.T + lane;
         const bool live = lane < op.T && row < a.d;
-        const int wb = q8_blk_width(n, b);
-        float t[16] = {};
-        if (live && DK_CHK((size_t)slot * slot_bytes + (size_t)(lane + 1) * q8_blk_bytes(wb) <= (size_t)S * slot_bytes &&
-                               512 * b + wb <= n,
-                           a.err, 2, G)) {
-            const uint32_t seg = ring_s + (uint32_t)(slot * slot_bytes + lane * q8_blk_bytes(wb));
-            const uint32_t xqb = xq_s + 512u * b, xsb = xs_s + 64u * b;
-            if (wb == 512) block_terms_full(t, seg, xqb, xsb, lane);
-            else block_terms_part(t, seg, xqb, xsb, wb, lane);
-            // pinned here: otherwise the compiler may sink the term arithmetic past the token wait
-            #pragma unroll
-            for (int g = 0; g < 16; ++g) asm volatile("" : "+f"(t[g]));
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&ctl.empty[slot]);
-        if (st) st[1] = globaltimer();
+        unsigned long long *st0 = (strace && s0 < kStageTraceStages && lane == 0) ? strace + 4 * s0 : nullptr;
+        unsigned long long *st1 = (strace && s0 + 1 < kStageTraceStages && lane == 0 && two) ? strace + 4 * (s0 + 1) : nullptr;
+        float t0[16] = {}, t1[16] = {};
+        if (!stage_terms(a, G0, b0, S, slot_bytes, ring_s, xq_s, xs_s, ctl, lane, live, t0, st0)) return false;
+        if (two && !stage_terms(a, G0 + 1, b0 + 1, S, slot_bytes, ring_s, xq_s, xs_s, ctl, lane, live, t1, st1))
+            return false;
         float sum = 0.0f;
-        if (s > 0) {  // the running sum of this lane's row after stage s-1
+        if (u > 0) {  // the running sum of this lane's row after unit u-1
             float prev = 0.0f;
-            if (!__all_sync(FULL, lane_token_wait(ctl.tok[c], lane, G, prev, a.err, &ctl.abort))) {
+            if (!__all_sync(FULL, lane_token_wait(ctl.tok[c], lane, G0, prev, a.err, &ctl.abort))) {
                 if (lane == 0) ctl.abort = 1;
                 return false;
             }
-            if (b > 0) sum = prev;
+            if (b0 > 0) sum = prev;
         }
-        if (st) st[2] = globaltimer();
+        if (st0) st0[2] = globaltimer();
         if (live) {
-            if (wb == 512) {
-                #pragma unroll
-                for (int g = 0; g < 16; ++g) sum = __fadd_rn(sum, t[g]);
-            } else {
-                #pragma unroll
-                for (int g = 0; g < 16; ++g)
-                    if (g < (wb >> 5)) sum = __fadd_rn(sum, t[g]);
-            }
+            sum = add_terms(sum, t0, q8_blk_width(n, b0));
+            if (two) sum = add_terms(sum, t1, q8_blk_width(n, b0 + 1));
         }
-        if (b == sc.nblk - 1) {  // the tile's rows are finished
+        if (b0 + (two ? 1 : 0) == sc.nblk - 1) {  // the tile's rows are finished
             if (a.epi == EPI_SWIGLU) {
                 const float h3 = __shfl_down_sync(FULL, sum, 1);
                 if (live && !(lane & 1) && DK_CHK((row >> 1) < (a.d >> 1), a.err, 4, row)) {
@@ -550,12 +574,12 @@ __device__ bool gemv_consume(const StepOp &op, const Sched &sc, int gbase, int S
                 }
             }
         }
-        if (s + 1 < sc.nst) {  // hand this row's running sum to the warp of stage s+1: one tagged word
+        if (u + 1 < nunits) {  // hand this row's running sum to the warp of unit u+1: one tagged word
             const int cn = (c + 1) % NC;
             *reinterpret_cast<volatile unsigned long long *>(&ctl.tok[cn][lane]) =
-                ((unsigned long long)(unsigned)(G + 1) << 32) | (unsigned long long)__float_as_uint(sum);
+                ((unsigned long long)(unsigned)(G0 + (two ? 2 : 1)) << 32) | (unsigned long long)__float_as_uint(sum);
         }
-        if (st) st[3] = globaltimer();
+        if (st0) st0[3] = globaltimer();
     }
     return true;
 }
@@ -1542,7 +1566,7 @@ int step_threads() { return kStepThreads; }
 
 cudaError_t launch_step(const StepArgs &sa, int grid, cudaStream_t st) {
     if (sa.S < 1 || sa.S > kStepMaxSlots || sa.S < kStepProducers || sa.S % kStepProducers || sa.NC < 1 ||
-        sa.NC > kStepMaxConsumers || sa.NC > kComputeWarps || sa.S < sa.NC || sa.smem > 227 * 1024 ||
+        sa.NC > kStepMaxConsumers || sa.NC > kComputeWarps || sa.S < 2 * sa.NC + 2 || sa.smem > 227 * 1024 ||
         sa.ctl_off + step_ctl_bytes() > sa.smem || sa.xoff < (size_t)sa.S * sa.slot || sa.ctl_off < sa.xoff)
         return cudaErrorInvalidValue;
     static int attr_bytes[64] = {0};
