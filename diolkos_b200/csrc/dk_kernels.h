@@ -310,6 +310,10 @@ struct StepArgs {
     const StepOp *ops = nullptr;  // device array
     int nops = 0;
     int S = 2, NC = 1;            // ring slots, GEMV consumer warps
+    // copies a CTA's producers keep in flight (issued, not landed; a multiple of kStepProducers, or 0: as
+    // many as the ring has free slots), so that the weight stream does not queue the step's own
+    // dependent stores and loads behind it at the memory controllers
+    int inflight = 0;
     size_t slot = 0;              // bytes of one ring slot (>= the largest stage)
     size_t xoff = 0;              // activation / attention scratch
     size_t ctl_off = 0;           // control block

@@ -529,6 +529,11 @@ __device__ bool gemv_consume(const StepOp &op, const Sched &sc, int gbase, int S
         const bool live = lane < op.T && row < a.d;
         unsigned long long *st0 = (strace && s0 < kStageTraceStages && lane == 0) ? strace + 4 * s0 : nullptr;
         unsigned long long *st1 = (strace && s0 + 1 < kStageTraceStages && lane == 0 && two) ? strace + 4 * (s0 + 1) : nullptr;
+        const bool last = b0 + (two ? 1 : 0) == sc.nblk - 1;  // this unit finishes the tile's rows
+        // the residual the rows add to, loaded before the terms: it is constant during the op (the
+        // previous residual add completed before this op's input did), and its L2 round trip would
+        // otherwise sit on the tile's last hand-off
+        const float res = (last && a.epi == EPI_ADD && live) ? __ldcg(a.out + row) : 0.0f;
         float t0[16] = {}, t1[16] = {};
         if (!stage_terms(a, G0, b0, S, slot_bytes, ring_s, xq_s, xs_s, ctl, lane, live, t0, st0)) return false;
         if (two && !stage_terms(a, G0 + 1, b0 + 1, S, slot_bytes, ring_s, xq_s, xs_s, ctl, lane, live, t1, st1))
@@ -547,7 +552,7 @@ __device__ bool gemv_consume(const StepOp &op, const Sched &sc, int gbase, int S
             sum = add_terms(sum, t0, q8_blk_width(n, b0));
             if (two) sum = add_terms(sum, t1, q8_blk_width(n, b0 + 1));
         }
-        if (b0 + (two ? 1 : 0) == sc.nblk - 1) {  // the tile's rows are finished
+        if (last) {  // the tile's rows are finished
             if (a.epi == EPI_SWIGLU) {
                 const float h3 = __shfl_down_sync(FULL, sum, 1);
                 if (live && !(lane & 1) && DK_CHK((row >> 1) < (a.d >> 1), a.err, 4, row)) {
@@ -557,7 +562,7 @@ __device__ bool gemv_consume(const StepOp &op, const Sched &sc, int gbase, int S
                 }
             } else if (live) {
                 if (a.epi == EPI_ADD) {
-                    a.out[row] = __fadd_rn(__ldcg(a.out + row), sum);
+                    a.out[row] = __fadd_rn(res, sum);
                 } else if (a.epi == EPI_PEER) {
                     if (a.tagged) {  // one tagged word per rank: its own validity, no fence, no count
                         const unsigned long long wv = tagged_word(T, sum);
@@ -904,6 +909,15 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa
             for (; s < sc.nst; s += kStepProducers) {
                 const int G = gbase + s, slot = G % S;
                 if (G >= S && !mbar_wait_abortable(&ctl.empty[slot], (uint32_t)(((G / S) - 1) & 1), op.g.err, &ctl.abort, false)) {
+                    ctl.abort = 1;
+                    ok = false;
+                    break;
+                }
+                // at most sa.inflight copies in flight: stage G - inflight (this producer's own, issued by
+                // it and not yet refilled, so its phase is the slot's latest) must have landed
+                const int K = sa.inflight;
+                if (K > 0 && G >= K &&
+                    !mbar_wait_abortable(&ctl.full[(G - K) % S], (uint32_t)(((G - K) / S) & 1), op.g.err, &ctl.abort, false)) {
                     ctl.abort = 1;
                     ok = false;
                     break;
@@ -1566,7 +1580,7 @@ int step_threads() { return kStepThreads; }
 
 cudaError_t launch_step(const StepArgs &sa, int grid, cudaStream_t st) {
     if (sa.S < 1 || sa.S > kStepMaxSlots || sa.S < kStepProducers || sa.S % kStepProducers || sa.NC < 1 ||
-        sa.NC > kStepMaxConsumers || sa.NC > kComputeWarps || sa.S < 2 * sa.NC + 2 || sa.smem > 227 * 1024 ||
+        sa.NC > kStepMaxConsumers || sa.NC > kComputeWarps || sa.S < 2 * sa.NC + 2 || sa.inflight < 0 || sa.inflight % kStepProducers || sa.inflight > sa.S || sa.smem > 227 * 1024 ||
         sa.ctl_off + step_ctl_bytes() > sa.smem || sa.xoff < (size_t)sa.S * sa.slot || sa.ctl_off < sa.xoff)
         return cudaErrorInvalidValue;
     static int attr_bytes[64] = {0};
