@@ -300,16 +300,20 @@ def _gpus() -> int:
 
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
-def test_client_cli_two_gpus(tiny_dir, loaded, tmp_path):
+def test_client_cli_two_gpus(loaded, tmp_path):
     """Two ranks (one process per GPU, the sums exchanged over NVLink) run the same generate loop; the
     tensor-parallel sum order moves logits by ~1e-6 relative, so the greedy text agrees with one GPU's
-    except after a near-tie: the first pieces are compared."""
-    root, d = tiny_dir
+    except after a near-tie: the first pieces are compared.  The model is a small one that splits over
+    two ranks (4 heads of 64 dims, hidden 768: 128 dims and 384 hidden rows per rank; the tiny model's
+    6 heads of 48 do not split into 32-multiples)."""
+    cfg = synth.TINY.replace(dim=256, n_heads=4, n_kv_heads=4)
+    d = str(tmp_path / "tp-model")
+    synth.write_model(d, cfg, SEED)
     tok_path = str(tmp_path / "tokenizer.bin")
-    synth.write_tokenizer(tok_path, synth.TINY.vocab_size)
+    synth.write_tokenizer(tok_path, cfg.vocab_size)
     exe = os.path.join(ROOT, "diolkos_b200", "bin", "client")
-    one = _run_cli(exe, d, tok_path, "abc de fgh", 24, root, ("-g", "1"))
-    two = _run_cli(exe, d, tok_path, "abc de fgh", 24, root, ("-g", "2"))
+    one = _run_cli(exe, d, tok_path, "abc de fgh", 24, str(tmp_path), ("-g", "1"))
+    two = _run_cli(exe, d, tok_path, "abc de fgh", 24, str(tmp_path), ("-g", "2"))
     assert b"(2 GPUs)" in two.stderr
     t1 = one.stdout.rstrip(b"\n").rsplit(b"Loaded", 1)[-1].split(b"\n", 1)[-1]
     t2 = two.stdout.rstrip(b"\n").rsplit(b"Loaded", 1)[-1].split(b"\n", 1)[-1]
