@@ -56,7 +56,7 @@ DECODE_GEMVS = [(12288, 4096, 32), (4096, 4096, 32), (22016, 4096, 32), (4096, 1
 NCU_GEMV_TRAFFIC_RATIO = 1.003
 # DRAM bytes / algorithmic bytes of one persistent decode-step launch (step_kernel), from the ncu
 # capture summarised in profiles/step_kernel_7b.txt (full 7B shape, positions 40-43).
-NCU_STEP_TRAFFIC_RATIO = 1.001
+NCU_STEP_TRAFFIC_RATIO = 1.005
 
 
 def parse():
@@ -65,7 +65,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "gemv", "gemm"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "gemv", "gemm", "attention"], default="decode")
     ap.add_argument("--kv", choices=["f32", "bf16"], default="f32")
     ap.add_argument("--model", choices=["7b", "70b"], default="7b",
                     help="7b: the headline workload; 70b: the 70B-shape GQA model, 512-token prompt, 128 tokens")
@@ -937,6 +937,76 @@ def run_gemm(args):
     return 0
 
 
+ATTN_POSITIONS = (200, 2047, 4000)  # a short context, the long-prompt workload's, near seq_len
+
+
+def attention_bench(reps: int = 32, kv: str = "f32"):
+    """The decode attention kernel alone (dk_attention_decode: RoPE, KV-cache write, split-K softmax.V;
+    the per-kernel decode path's attention, the same arithmetic as the persistent step's) at the 7B shape
+    (32 heads of 128, seq_len 4096) at a few positions.  `reps` calls back to back rotate over enough
+    layers' KV caches that the working set is over 3x the L2; CUDA events on the launching stream, best
+    of 3 batches.  GB/s = the KV bytes a call reads (2 * (pos+1) * kv_dim * element size) / time."""
+    import torch
+
+    from diolkos_b200 import ops, synth
+
+    cfg = synth.LLAMA7B
+    H, KVH, hs, seq = cfg.n_heads, cfg.n_kv_heads, cfg.dim // cfg.n_heads, cfg.seq_len
+    esz = 4 if kv == "f32" else 2
+    layer_bytes = 2 * KVH * seq * hs * esz
+    copies = max(2, int(3 * 126e6 // layer_bytes) + 1)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    dt = torch.float32 if kv == "f32" else torch.bfloat16
+    ks = [(torch.randn(KVH * seq * hs, generator=g, device="cuda") * 0.5).to(dt) for _ in range(copies)]
+    vs = [(torch.randn(KVH * seq * hs, generator=g, device="cuda") * 0.5).to(dt) for _ in range(copies)]
+    if kv != "f32":
+        ks = [k.view(torch.int16) for k in ks]
+        vs = [v.view(torch.int16) for v in vs]
+    half = hs // 2
+    inv = 1.0 / (10000.0 ** (torch.arange(half, dtype=torch.float64) * 2 / hs))
+    ang = torch.arange(seq, dtype=torch.float64)[:, None] * inv[None, :]
+    rope = torch.stack([torch.cos(ang), torch.sin(ang)], -1).to(torch.float32).reshape(-1).cuda()
+    qkv = torch.randn((H + 2 * KVH) * hs, generator=g, device="cuda")
+    work = torch.zeros(ops.attention_work_bytes(H, KVH, hs, seq), dtype=torch.uint8, device="cuda")
+    out = torch.empty(H * hs, device="cuda")
+    hbm, kind = peaks()
+    res = {}
+    for pos in ATTN_POSITIONS:
+        p = torch.tensor([pos], dtype=torch.int32, device="cuda")
+        for i in range(copies):  # warm-up: every cache once
+            ops.attention_decode(qkv, rope, ks[i], vs[i], p, H, KVH, hs, seq, work, out)
+        torch.cuda.synchronize()
+        best = float("inf")
+        for _ in range(3):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(reps):
+                ops.attention_decode(qkv, rope, ks[i % copies], vs[i % copies], p, H, KVH, hs, seq, work, out)
+            e1.record()
+            torch.cuda.synchronize()
+            best = min(best, e0.elapsed_time(e1) * 1e3 / reps)
+        alg = 2.0 * (pos + 1) * KVH * hs * esz
+        res[str(pos)] = {"us": round(best, 2), "kv_mb": round(alg / 1e6, 2), "GBps": round(alg / best / 1e3, 1),
+                         "frac": round(alg / best / 1e3 / hbm, 4)}
+    return {"kernel": "attention_kernel", "kv": kv, "positions": res, "peak": hbm, "peak_kind": kind,
+            "what": f"dk_attention_decode at 32 heads x 128, seq_len {seq}, {kv} KV cache: KV bytes read per call / "
+                    f"time per call ({reps} calls back to back over {copies} layers' caches, best of 3)"}
+
+
+def run_attention(args):
+    import torch
+
+    torch.cuda.set_device(0)
+    a = attention_bench(kv=args.kv)
+    best = max(a["positions"].values(), key=lambda v: v["GBps"])
+    line = {"metric": "decode attention HBM GB/s", "value": best["GBps"], "unit": "GB/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": args.kv, "data": "synthetic",
+            "config": {"workload": "decode attention, LLaMA-2-7B heads, one layer per call"}, "attention": a}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -945,6 +1015,8 @@ def main():
         return run_gemv(args)
     if args.workload == "gemm":
         return run_gemm(args)
+    if args.workload == "attention":
+        return run_attention(args)
     return run_decode(args)
 
 
