@@ -282,6 +282,7 @@ int dk_matmul_q8_0_batch(float *out, const float *x, const uint8_t *const *w_pac
     for (int i = 0; i < count; ++i) {
         a.w = w_packed[i];
         a.out = out + (size_t)i * d;
+        a.early_input = i > 0;  // x was complete before GEMV 0 (launched without programmatic dependence) began
         // The first GEMV waits for whatever wrote its weights; the later ones may start streaming their
         // weights while the previous GEMV of the batch runs (nothing in the batch writes weights).
         if (int r = cuda_status(launch_gemv(a, p, (cudaStream_t)stream, i > 0), "dk_matmul_q8_0_batch")) return r;

@@ -84,6 +84,11 @@ struct GemvArgs {
     unsigned long long *x64_out = nullptr;
     const unsigned long long *recv64 = nullptr;
     unsigned long long *const *peer_recv64 = nullptr;
+    // Standalone kernel, PRO_F32 / EPI_STORE only: the input x was complete before the previous kernel in
+    // the stream started (the later GEMVs of dk_matmul_q8_0_batch, whose first GEMV is launched without
+    // programmatic dependence), so the activation is built and the terms computed before the dependency
+    // wait, which only the output stores take.
+    int early_input = 0;
     // Diagnostics (persistent step only; nullptr: off): the CTA that owns tile 0 copies the op's fp32
     // input vector (n floats; the residual written by the prologue where it writes one) and the Q8_0
     // activation it built (n int8, n/32 scales) here, for per-layer parity checks.

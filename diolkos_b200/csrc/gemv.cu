@@ -340,7 +340,12 @@ __global__ void __launch_bounds__(32 * kMinWarps, 2) gemv_q8_kernel(const GemvAr
     // was last written or read by kernels that an earlier kernel of the step already waited for.  So
     // it starts on the partials as soon as the last rank's rows land, not when the producing kernel's
     // last CTA has drained its fence and exited.
-    if constexpr (PRO != PRO_RMS_REDUCE) pdl_wait();
+    // A batch's later GEMV (early_input) reads only weights and an input that was complete before the
+    // previous kernel started: it waits for that kernel only before its first output store (below).
+    const bool early = PRO == PRO_F32 && EPI == EPI_STORE && a.early_input;
+    if constexpr (PRO != PRO_RMS_REDUCE) {
+        if (!early) pdl_wait();
+    }
     pdl_trigger();
     if (half) {
         if constexpr (kRmsFamily) build_activation_half<PRO>(a, xq, xs, red, nw);
@@ -369,6 +374,7 @@ __global__ void __launch_bounds__(32 * kMinWarps, 2) gemv_q8_kernel(const GemvAr
     } else if (warp < NC) {
         const int c = warp;
         unsigned long long best = 0ull;
+        bool waited = !early;  // the dependency wait before this thread's first output store
         for (int s = c; s < sc.nst; s += NC) {
             const int slot = s % S;
             if (!__all_sync(FULL, mbar_wait_abortable(&full[slot], (uint32_t)((s / S) & 1), a.err, flags, false))) {
@@ -428,6 +434,10 @@ __global__ void __launch_bounds__(32 * kMinWarps, 2) gemv_q8_kernel(const GemvAr
                         // over NVLink; the local one for this rank).
                         for (int q = 0; q < a.tp_world; ++q) a.peer_recv[q][(size_t)a.tp_rank * a.d + row] = sum;
                     } else {
+                        if (!waited) {
+                            pdl_wait();
+                            waited = true;
+                        }
                         a.out[row] = sum;
                     }
                     if constexpr (EPI == EPI_ARGMAX) {
