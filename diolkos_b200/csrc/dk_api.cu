@@ -278,14 +278,18 @@ int dk_matmul_q8_0_batch(float *out, const float *x, const uint8_t *const *w_pac
     a.x = x;
     a.err = device_error_word();
     if (!a.err) return set_error(DK_ERR_CUDA, "dk_matmul_q8_0_batch: could not allocate the device error word");
-    const GemvPlan p = plan_gemv(n, d, EPI_STORE, current_num_sms());
-    for (int i = 0; i < count; ++i) {
-        a.w = w_packed[i];
-        a.out = out + (size_t)i * d;
-        a.early_input = i > 0;  // x was complete before GEMV 0 (launched without programmatic dependence) began
-        // The first GEMV waits for whatever wrote its weights; the later ones may start streaming their
-        // weights while the previous GEMV of the batch runs (nothing in the batch writes weights).
-        if (int r = cuda_status(launch_gemv(a, p, (cudaStream_t)stream, i > 0), "dk_matmul_q8_0_batch")) return r;
+    // One launch per kGemvBatchMax matrices: each CTA streams its tiles of every matrix of the launch
+    // through one ring, the activation built once.  A later launch starts while the previous one runs
+    // (x was complete before the first began): it waits for it only before its first output store.
+    const GemvPlan p = plan_gemv_batch(n, d, std::min(count, kGemvBatchMax), current_num_sms());
+    for (int i0 = 0, k = 0; i0 < count; i0 += kGemvBatchMax, ++k) {
+        GemvBatch b;
+        b.count = std::min(kGemvBatchMax, count - i0);
+        b.groups = b.count > 1 ? 2 : 1;  // two CTAs per SM, alternate matrices: two rings, two row-sum chains
+        for (int j = 0; j < b.count; ++j) b.w[j] = w_packed[i0 + j];
+        a.out = out + (size_t)i0 * d;
+        a.early_input = k > 0;
+        if (int r = cuda_status(launch_gemv_batch(a, b, p, (cudaStream_t)stream, k > 0), "dk_matmul_q8_0_batch")) return r;
     }
     return DK_OK;
 }

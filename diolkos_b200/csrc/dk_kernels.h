@@ -173,6 +173,19 @@ int gemv_tile_rows(int d, int epi, int num_sms);
 GemvPlan plan_gemv(int n, int d, int epi, int num_sms);
 bool gemv_supported(int n, int d, int epi);
 cudaError_t launch_gemv(const GemvArgs &a, const GemvPlan &p, cudaStream_t st, bool pdl);
+// A batch of same-shape matrices against one input in ONE launch (dk_matmul_q8_0_batch): every CTA
+// streams its tiles of matrix 0, then of matrix 1, ... through one ring, the activation built once,
+// out[i * d + row] for matrix i.  PRO_F32 or PRO_Q8 with EPI_STORE.
+constexpr int kGemvBatchMax = 32;
+struct GemvBatch {
+    int count = 0;  // 0: the single matrix GemvArgs::w
+    // CTA groups: group g (CTAs g * grid .. (g+1) * grid - 1 of the launch) takes matrices g, g + groups, ...
+    // over the same tiles, so that `groups` CTAs share each SM, each with its own ring and row-sum chains
+    int groups = 1;
+    const uint8_t *w[kGemvBatchMax] = {};
+};
+GemvPlan plan_gemv_batch(int n, int d, int count, int num_sms);
+cudaError_t launch_gemv_batch(const GemvArgs &a, const GemvBatch &b, const GemvPlan &p, cudaStream_t st, bool pdl);
 
 // ---------------- batched Q8_0 matmul on the tensor cores (prefill) --------------------------
 struct GemmArgs {

@@ -272,7 +272,8 @@ __device__ __forceinline__ void build_activation_half(const GemvArgs &a, int8_t 
 // ALL stages of the CTA (across tile boundaries too, where the sums restart at 0), so a warp is never
 // handed a second token before it has taken the first.
 template <int PRO, int EPI>
-__global__ void __launch_bounds__(32 * kMinWarps, 2) gemv_q8_kernel(const GemvArgs a, const GemvPlan p) {
+__global__ void __launch_bounds__(32 * kMinWarps, 2) gemv_q8_kernel(const GemvArgs a, const GemvPlan p,
+                                                                     const GemvBatch bt) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int n = a.n, NC = p.NW, S = p.S;
@@ -289,14 +290,28 @@ __global__ void __launch_bounds__(32 * kMinWarps, 2) gemv_q8_kernel(const GemvAr
     int *flags = reinterpret_cast<int *>(wkey + kMaxConsumers);      // [0] abort, [1] last CTA
     const uint32_t ring_s = smem_u32(ring), xq_s = smem_u32(xq), xs_s = smem_u32(xs);
 
+    // A batch's CTA groups cover the same tiles: CTA index within the group, and the group
+    const int cgrid = bt.count > 0 ? p.grid : (int)gridDim.x;
+    const int cidx = (int)blockIdx.x % cgrid, grp = (int)blockIdx.x / cgrid;
     Sched sc;
-    sc.t0 = (int)((long long)blockIdx.x * p.ntiles / gridDim.x);
-    sc.nt = (int)((long long)(blockIdx.x + 1) * p.ntiles / gridDim.x) - sc.t0;
+    sc.t0 = (int)((long long)cidx * p.ntiles / cgrid);
+    sc.nt = (int)((long long)(cidx + 1) * p.ntiles / cgrid) - sc.t0;
     sc.nblk = (n + 511) >> 9;
     sc.T = p.T;
     sc.n = n;
     sc.nst = sc.nt * sc.nblk;
     sc.tile_bytes = (size_t)p.T * q8_row_bytes(n);
+    // A batch (bt.count matrices of the same shape): this CTA's stages of its group's matrices -- k-th
+    // matrix grp + k * groups -- one after another in one sequence, so the ring streams from one matrix
+    // into the next.
+    const int G = bt.count > 0 ? bt.groups : 1;
+    const int nmat = bt.count > 0 ? (bt.count - grp + G - 1) / G : 1;
+    const int total = nmat * sc.nst;
+    auto wsrc = [&](int s) -> const uint8_t * {
+        if (bt.count == 0) return sc.src(a.w, s);
+        const int k = s / sc.nst;
+        return sc.src(bt.w[grp + k * G], s - k * sc.nst);
+    };
 
     if (tid == 0) {
         for (int i = 0; i < S; ++i) {
@@ -319,11 +334,11 @@ __global__ void __launch_bounds__(32 * kMinWarps, 2) gemv_q8_kernel(const GemvAr
     int next = q;  // this producer's next stage to issue
     if (producer) {
         policy = l2_evict_first_policy();
-        for (; next < min(S, sc.nst); next += NP) {
+        for (; next < min(S, total); next += NP) {
             mbar_arrive_expect_tx(&full[next], sc.bytes(next));
-            bulk_g2s(ring + (size_t)next * p.slot, sc.src(a.w, next), sc.bytes(next), &full[next], policy);
+            bulk_g2s(ring + (size_t)next * p.slot, wsrc(next), sc.bytes(next), &full[next], policy);
         }
-        for (int s = S + q; s < min(S + p.PF, sc.nst); s += NP) bulk_prefetch_l2(sc.src(a.w, s), sc.bytes(s));
+        for (int s = S + q; s < min(S + p.PF, total); s += NP) bulk_prefetch_l2(wsrc(s), sc.bytes(s));
     }
 
     // The rmsnorm family on n == 16 * threads takes the one-round-trip prologue; its norm weights are
@@ -356,15 +371,15 @@ __global__ void __launch_bounds__(32 * kMinWarps, 2) gemv_q8_kernel(const GemvAr
 
     if (q >= 0 && q < NP) {
         if (lane == 0) {
-            for (; next < sc.nst; next += NP) {
+            for (; next < total; next += NP) {
                 const int slot = next % S;
                 if (!mbar_wait_abortable(&empty[slot], (uint32_t)(((next / S) - 1) & 1), a.err, flags, false)) {
                     flags[0] = 1;
                     break;
                 }
                 mbar_arrive_expect_tx(&full[slot], sc.bytes(next));
-                bulk_g2s(ring + (size_t)slot * p.slot, sc.src(a.w, next), sc.bytes(next), &full[slot], policy);
-                if (next + p.PF < sc.nst) bulk_prefetch_l2(sc.src(a.w, next + p.PF), sc.bytes(next + p.PF));
+                bulk_g2s(ring + (size_t)slot * p.slot, wsrc(next), sc.bytes(next), &full[slot], policy);
+                if (next + p.PF < total) bulk_prefetch_l2(wsrc(next + p.PF), sc.bytes(next + p.PF));
             }
             // Never leave a copy in flight into the shared memory of an exiting CTA: each of this
             // producer's slots has at most one outstanding copy, the last one issued into it.
@@ -375,14 +390,16 @@ __global__ void __launch_bounds__(32 * kMinWarps, 2) gemv_q8_kernel(const GemvAr
         const int c = warp;
         unsigned long long best = 0ull;
         bool waited = !early;  // the dependency wait before this thread's first output store
-        for (int s = c; s < sc.nst; s += NC) {
+        for (int s = c; s < total; s += NC) {
             const int slot = s % S;
+            const int k = s / sc.nst;                   // this CTA's k-th matrix of the batch
+            const int m = bt.count > 0 ? grp + k * G : 0;  // its index in the batch (0 without a batch)
             if (!__all_sync(FULL, mbar_wait_abortable(&full[slot], (uint32_t)((s / S) & 1), a.err, flags, false))) {
                 if (lane == 0) flags[0] = 1;
                 break;
             }
             const int b = s % sc.nblk;
-            const int row = (sc.t0 + s / sc.nblk) * p.T + lane;
+            const int row = (sc.t0 + (s - k * sc.nst) / sc.nblk) * p.T + lane;
             const bool live = lane < p.T && row < a.d;
             const int wb = q8_blk_width(n, b);
             float t[16] = {};
@@ -438,7 +455,7 @@ __global__ void __launch_bounds__(32 * kMinWarps, 2) gemv_q8_kernel(const GemvAr
                             pdl_wait();
                             waited = true;
                         }
-                        a.out[row] = sum;
+                        a.out[(size_t)m * a.d + row] = sum;
                     }
                     if constexpr (EPI == EPI_ARGMAX) {
                         const unsigned long long key = argmax_key(sum, row + a.row_offset);
@@ -446,7 +463,7 @@ __global__ void __launch_bounds__(32 * kMinWarps, 2) gemv_q8_kernel(const GemvAr
                     }
                 }
             }
-            if (s + 1 < sc.nst) {  // pass this row's running sum to the warp of stage s+1: one tagged word
+            if (s + 1 < total) {  // pass this row's running sum to the warp of stage s+1: one tagged word
                 const int cn = (c + 1) % NC;
                 *reinterpret_cast<volatile unsigned long long *>(&tok[cn * 32 + lane]) =
                     ((unsigned long long)(unsigned)(s + 1) << 32) | (unsigned long long)__float_as_uint(sum);
@@ -519,7 +536,7 @@ __global__ void __launch_bounds__(32 * kMinWarps, 2) gemv_q8_kernel(const GemvAr
 }
 
 template <int PRO, int EPI>
-cudaError_t launch_t(const GemvArgs &a, const GemvPlan &p, cudaStream_t st, bool pdl) {
+cudaError_t launch_t(const GemvArgs &a, const GemvPlan &p, cudaStream_t st, bool pdl, const GemvBatch &bt = GemvBatch()) {
     auto kern = gemv_q8_kernel<PRO, EPI>;
     // Opt in to the dynamic shared memory this launch needs (raised monotonically, per device).
     static int attr_bytes[64] = {0};
@@ -532,7 +549,7 @@ cudaError_t launch_t(const GemvArgs &a, const GemvPlan &p, cudaStream_t st, bool
         attr_bytes[dev] = (int)p.smem;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(p.grid);
+    cfg.gridDim = dim3(p.grid * (bt.count > 0 ? bt.groups : 1));
     cfg.blockDim = dim3(32 * kMinWarps);
     cfg.dynamicSmemBytes = p.smem;
     cfg.stream = st;
@@ -541,7 +558,7 @@ cudaError_t launch_t(const GemvArgs &a, const GemvPlan &p, cudaStream_t st, bool
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, a, p);
+    return cudaLaunchKernelEx(&cfg, kern, a, p, bt);
 }
 
 }  // namespace
@@ -585,6 +602,34 @@ GemvPlan plan_gemv(int n, int d, int epi, int num_sms) {
     p.xoff = (size_t)p.S * p.slot;
     p.smem = p.xoff + tail;
     return p;
+}
+
+GemvPlan plan_gemv_batch(int n, int d, int count, int num_sms) {
+    GemvPlan p = plan_gemv(n, d, EPI_STORE, num_sms);
+    // the ring as deep as the budget allows: the batch's stages run on from one matrix into the next
+    const int stages = ((p.ntiles + p.grid - 1) / p.grid) * ((n + 511) / 512) * std::max(1, count);
+    const size_t tail = gemv_smem_tail(n);
+    const size_t ring = kSmemBudget > tail ? kSmemBudget - tail : 0;
+    p.S = std::max(1, std::min({kMaxSlots, (int)(ring / p.slot), stages}));
+    if (p.S >= 2) p.S -= p.S % p.NP;
+    int nc = 4;
+    if (const char *e = getenv("DIOLKOS_GEMV_NC")) nc = std::max(1, std::min(atoi(e), kMaxConsumers));
+    p.NW = std::max(1, std::min({nc, p.S, stages}));
+    p.xoff = (size_t)p.S * p.slot;
+    p.smem = p.xoff + tail;
+    return p;
+}
+
+cudaError_t launch_gemv_batch(const GemvArgs &a, const GemvBatch &b, const GemvPlan &p, cudaStream_t st, bool pdl) {
+    if (b.count < 1 || b.count > kGemvBatchMax || b.groups < 1 || b.groups > 2 || b.groups > b.count || a.epi != EPI_STORE || (a.pro != PRO_F32 && a.pro != PRO_Q8) ||
+        !gemv_supported(a.n, a.d, a.epi) || p.smem > 227 * 1024 || p.NW < 1 || p.NW > kMaxConsumers || p.S < p.NW ||
+        p.NP < 1 || p.NW + p.NP > kMinWarps || p.S % p.NP || p.S > kMaxSlots || p.T < 1 || p.T > 32 || p.PF < 0 ||
+        p.smem < (size_t)p.S * p.slot + gemv_smem_tail(a.n))
+        return cudaErrorInvalidValue;
+    for (int i = 0; i < b.count; ++i)
+        if (!b.w[i]) return cudaErrorInvalidValue;
+    if (a.pro == PRO_Q8) return launch_t<PRO_Q8, EPI_STORE>(a, p, st, pdl, b);
+    return launch_t<PRO_F32, EPI_STORE>(a, p, st, pdl, b);
 }
 
 cudaError_t launch_gemv(const GemvArgs &a, const GemvPlan &p, cudaStream_t st, bool pdl) {

@@ -79,8 +79,10 @@ int dk_matmul_q8_0_q(float *out, const int8_t *xq, const float *xs, const uint8_
                      int d, void *stream);
 /* `count` GEMVs of the same activation x against count packed [d x n] matrices (the reference calls
  * matmul once per matrix, e.g. wq, wk, wv on the same xb, src/transformer.c:83-85): out[i*d .. (i+1)*d)
- * = W_i * quant(x).  Launched back to back; from the second GEMV on, each one starts streaming its
- * weights while the previous one finishes, which is how the decode engine runs the kernel. */
+ * = W_i * quant(x), each bit-identical to dk_matmul_q8_0.  One launch per 32 matrices: every SM runs two
+ * CTAs that stream their tiles of alternate matrices, one matrix after another, through their rings (the
+ * activation built once); a later launch starts while the previous one runs and waits for it only before
+ * its first output store. */
 int dk_matmul_q8_0_batch(float *out, const float *x, const uint8_t *const *w_packed, int count, int n,
                          int d, void *stream);
 /* matmul_Q8_0 (src/utils.c:106-138) for a batch of `ntok` already-quantised activation vectors
