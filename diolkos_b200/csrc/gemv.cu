@@ -36,7 +36,7 @@ namespace {
 constexpr int kMaxConsumers = 6;
 constexpr int kMinWarps = 8;   // warps launched per CTA (consumers + producer + helpers for the activation)
 constexpr int kMaxSlots = 16;
-constexpr size_t kSmemBudget = 104 * 1024;    // two of these fit on an SM (this kernel + the next)
+constexpr size_t kSmemBudget = 112 * 1024;    // two of these fit on an SM (228 KB: this kernel + the next, or a batch's two CTA groups)
 constexpr int kPrefetchStages = 3;           // L2 prefetch distance beyond the ring, in stages
 
 // Build the Q8_0 activation in shared memory: xq int8[n] then xs fp32[n/32].  One thread per
