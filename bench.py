@@ -51,9 +51,10 @@ GEMV_SHAPES = [(4096, 4096), (11008, 4096), (4096, 11008), (32000, 4096)]  # [ou
 # The GEMVs of one 7B-shape decode step: (rows, cols, launches per step) -- fused q|k|v, wo, the
 # row-interleaved w1|w3, w2, and the classifier.
 DECODE_GEMVS = [(12288, 4096, 32), (4096, 4096, 32), (22016, 4096, 32), (4096, 11008, 32), (32000, 4096, 1)]
-# DRAM bytes / algorithmic bytes of one GEMV launch, from the ncu capture of every decode shape
-# summarised in profiles/gemv_q8_decode_shapes.txt (dram__bytes_read.sum + dram__bytes_write.sum).
-NCU_GEMV_TRAFFIC_RATIO = 1.003
+# DRAM bytes / algorithmic bytes of one batched GEMV launch, from the ncu capture of every bench shape
+# summarised in profiles/gemv_q8_batch.txt (dram__bytes_read.sum + dram__bytes_write.sum: 0.995-1.004
+# for the 4096- and 11008-row shapes).
+NCU_GEMV_TRAFFIC_RATIO = 1.000
 # DRAM bytes / algorithmic bytes of one persistent decode-step launch (step_kernel), from the ncu
 # capture summarised in profiles/step_kernel_7b.txt (full 7B shape, positions 40-43).
 NCU_STEP_TRAFFIC_RATIO = 1.005
