@@ -298,6 +298,33 @@ def test_gemv_batch_equals_single(torch_cuda):
         np.testing.assert_array_equal(got[i].view(np.uint32), one.view(np.uint32))
 
 
+@pytest.mark.parametrize("n,d,count", [(4096, 4096, 33), (4160, 1000, 70), (288, 96, 2), (512, 4096, 1)])
+def test_gemv_batch_launches_bit_exact(torch_cuda, n, d, count):
+    """The batch's launch structure: one launch per 32 matrices (count 33 and 70: a second and third
+    launch that start early and wait only before their stores), two CTA groups taking alternate matrices
+    (an odd count leaves the second group one short; count 1 runs one group), a partial last block
+    (n = 4160), a tile range with fewer tiles than SMs (d = 96).  Every output row equals one
+    dk_matmul_q8_0 call's, bit for bit, and nothing is written past the last matrix's rows."""
+    from diolkos_b200 import ops
+
+    torch = torch_cuda
+    rng = np.random.default_rng(n + d + count)
+    ws = []
+    for _ in range(5):
+        q = rng.integers(-127, 128, n * d, dtype=np.int8)
+        s = (rng.random(n * d // 32, dtype=np.float32) * 0.001 + 1e-6).astype(np.float32)
+        ws.append(ops.pack(_dev(torch, q), _dev(torch, s), n, d))
+    x = _dev(torch, rng.standard_normal(n).astype(np.float32))
+    idx = [int(i) for i in rng.integers(0, len(ws), count)]
+    out = torch.full((count + 1, d), float("nan"), dtype=torch.float32, device="cuda")
+    ops.matmul_batch(x, [ws[i] for i in idx], n, d, out[:count])
+    got = out.cpu().numpy()
+    singles = [ops.matmul(x, w, n, d).cpu().numpy() for w in ws]
+    for i, k in enumerate(idx):
+        np.testing.assert_array_equal(got[i].view(np.uint32), singles[k].view(np.uint32), err_msg=f"matrix {i}")
+    assert np.isnan(got[count]).all()
+
+
 # Tile heights on 148 SMs: d 4096 / 12288 -> 28, d 4736 -> 32 (the pipelined TMA form, n % 128 == 0);
 # d 300 / 1001 -> 3 / 7 and n 288 -> the simple form.
 @pytest.mark.parametrize("n,d,ntok", [(4096, 4096, 32), (4096, 4096, 5), (11008, 4096, 37), (288, 864, 70),
