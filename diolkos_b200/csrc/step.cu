@@ -55,6 +55,7 @@ constexpr int kMergeChunk = 12;    // splits whose partials the merging group lo
 // head dims per merging thread of a GW-warp group (head_size <= 128)
 template <int GW> constexpr int merge_dims() { return (128 + 32 * GW - 1) / (32 * GW); }
 constexpr int kBarCompute = 1;     // named barrier of the compute warps; 2 + g: attention group g
+constexpr int kStepActBlocks = 64; // 512-column blocks of an activation built block by block (n <= 32768)
 static_assert(2 + kAttnGroups <= 16, "named barriers");
 
 struct StepCtl {  // shared-memory control block
@@ -68,6 +69,9 @@ struct StepCtl {  // shared-memory control block
     int abort;      // any wait gave up: every warp leaves
     int last;       // this CTA took the classifier's last ticket
     int grp_last[kAttnGroups];
+    // per 512-column block of a PRO_F32 op's activation: the op index + 1 once its values and scales are in
+    // shared memory (step_activation_blocks)
+    int act_ready[kStepActBlocks];
     // The compute warps' copies of the op descriptors: op i sits in opbuf[i % 3].  Op i+1 is loaded into
     // registers while op i runs and stored here before op i's last barrier, so no read of a descriptor
     // waits on the L2 at an op boundary; three slots keep op i-1's descriptor intact for its stragglers.
@@ -464,6 +468,52 @@ __device__ bool step_activation(const GemvArgs &a, int tok, int8_t *xq, float *x
     return ok;
 }
 
+// The Q8_0 activation of a PRO_F32 op (a plain per-group quantisation, no norm: wo on the attention
+// output, w2 on the SwiGLU output) built block by block by the compute warps that do not consume, in
+// block order (builder k of NB takes blocks k, k + NB, ...), each block published with act_ready[b] =
+// tag.  The consumers start on block 0 as soon as it is there instead of waiting for the whole vector.
+// The arithmetic is step_activation's (load16 / quant16): the same bits.
+__device__ void step_activation_blocks(const GemvArgs &a, int8_t *xq, float *xs, StepCtl &ctl, int k, int NB,
+                                       int lane, int tag) {
+    const int nhg = a.n >> 4, nblk = (a.n + 511) >> 9;
+    bool ok = true;
+    for (int b = k; b < nblk; b += NB) {
+        const int hg = 32 * b + lane;  // half-group: 16 values; the partner half is the neighbouring lane
+        float f[16];
+        if (hg < nhg) {
+            load16(a, 0, hg, f, 0u, ok);
+        } else {
+            #pragma unroll
+            for (int j = 0; j < 16; ++j) f[j] = 0.0f;
+        }
+        quant16(f, hg, hg < nhg, xq, xs);
+        __threadfence_block();  // this lane's values and scale before the block's flag
+        __syncwarp();
+        if (lane == 0)
+            asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(&ctl.act_ready[b])), "r"(tag)
+                         : "memory");
+    }
+}
+// Bounded wait (acquire) until block b of the activation is published; abandoned on the abort flag.
+__device__ __forceinline__ bool wait_act_block(const StepCtl &ctl, int b, int tag, int *err, const int *abort) {
+    const uint32_t w = smem_u32(&ctl.act_ready[b]);
+    int v;
+    asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(w) : "memory");
+    if (v == tag) return true;
+    const long long t0 = clock64();
+    for (int it = 1;; ++it) {
+        asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(w) : "memory");
+        if (v == tag) return true;
+        if (!(it & 15)) {
+            if (*reinterpret_cast<const volatile int *>(abort)) return false;
+            if (clock64() - t0 > DK_WAIT_LIMIT_CYCLES) {
+                atomicOr(err, DK_ERR_TIMEOUT);
+                return false;
+            }
+        }
+    }
+}
+
 // ---- GEMV op: consumers ---------------------------------------------------------------------------
 // Consume this CTA's stages of the op (compute warp c < NC): the standalone GEMV's arithmetic
 // (gemv_core.cuh) with the ring position continuing from `gbase` (stages of earlier ops).  The stages
@@ -477,9 +527,10 @@ __device__ bool step_activation(const GemvArgs &a, int tok, int8_t *xq, float *x
 // The terms of stage G (block b of the tile whose row this lane owns) into t, then its slot freed.
 __device__ __forceinline__ bool stage_terms(const GemvArgs &a, int G, int b, int S, size_t slot_bytes, uint32_t ring_s,
                                             uint32_t xq_s, uint32_t xs_s, StepCtl &ctl, int lane, bool live,
-                                            float (&t)[16], unsigned long long *st) {
+                                            float (&t)[16], unsigned long long *st, int act_tag) {
     const int slot = G % S;
-    if (!__all_sync(FULL, mbar_wait_abortable(&ctl.full[slot], (uint32_t)((G / S) & 1), a.err, &ctl.abort, false))) {
+    if (!__all_sync(FULL, mbar_wait_abortable(&ctl.full[slot], (uint32_t)((G / S) & 1), a.err, &ctl.abort, false) &&
+                              (act_tag == 0 || wait_act_block(ctl, b, act_tag, a.err, &ctl.abort)))) {
         if (lane == 0) ctl.abort = 1;
         return false;
     }
@@ -515,7 +566,8 @@ __device__ __forceinline__ float add_terms(float sum, const float (&t)[16], int 
 
 __device__ bool gemv_consume(const StepOp &op, const Sched &sc, int gbase, int S, int NC, size_t slot_bytes,
                              uint32_t ring_s, uint32_t xq_s, uint32_t xs_s, StepCtl &ctl, int c, int lane,
-                             unsigned long long &best, unsigned long long *strace, unsigned long long epoch) {
+                             unsigned long long &best, unsigned long long *strace, unsigned long long epoch,
+                             int act_tag) {
     const GemvArgs &a = op.g;
     const int n = a.n;
     const unsigned T = a.tagged ? tp_tag(epoch, a, a.tag_k) : 0u;
@@ -535,8 +587,8 @@ __device__ bool gemv_consume(const StepOp &op, const Sched &sc, int gbase, int S
         // otherwise sit on the tile's last hand-off
         const float res = (last && a.epi == EPI_ADD && live) ? __ldcg(a.out + row) : 0.0f;
         float t0[16] = {}, t1[16] = {};
-        if (!stage_terms(a, G0, b0, S, slot_bytes, ring_s, xq_s, xs_s, ctl, lane, live, t0, st0)) return false;
-        if (two && !stage_terms(a, G0 + 1, b0 + 1, S, slot_bytes, ring_s, xq_s, xs_s, ctl, lane, live, t1, st1))
+        if (!stage_terms(a, G0, b0, S, slot_bytes, ring_s, xq_s, xs_s, ctl, lane, live, t0, st0, act_tag)) return false;
+        if (two && !stage_terms(a, G0 + 1, b0 + 1, S, slot_bytes, ring_s, xq_s, xs_s, ctl, lane, live, t1, st1, act_tag))
             return false;
         float sum = 0.0f;
         if (u > 0) {  // the running sum of this lane's row after unit u-1
@@ -864,6 +916,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa
         for (int i = 0; i < kStepMaxConsumers * 32; ++i) (&ctl.tok[0][0])[i] = 0xFFFFFFFF00000000ull;  // tag -1
         ctl.abort = 0;
         ctl.last = 0;
+        for (int b = 0; b < kStepActBlocks; ++b) ctl.act_ready[b] = 0;
         mbar_fence_init();
     }
     __syncthreads();
@@ -987,9 +1040,17 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa
                 if (tid == 0) trace_mark(sa, i, 0);
                 int8_t *xq = reinterpret_cast<int8_t *>(act);
                 float *xs = reinterpret_cast<float *>(act + ((a.n + 15) & ~15));
-                const int tok = a.pro == PRO_EMB_RMS ? __ldcg(a.tokens + pos) : 0;
-                const bool ok = step_activation(a, tok, xq, xs, ctl, tid, epoch, sc.t0 == 0, nw);
-                if (bar_compute_or(!ok || *reinterpret_cast<volatile int *>(&ctl.abort))) break;
+                // PRO_F32 (wo, w2): the activation block by block beside the consumers (the same for every
+                // thread of the CTA, so every thread takes the same barriers)
+                const bool blockwise = a.pro == PRO_F32 && !a.dump_q && ((a.n + 511) >> 9) <= kStepActBlocks;
+                const int act_tag = blockwise ? i + 1 : 0;
+                if (blockwise) {
+                    if (warp >= NC) step_activation_blocks(a, xq, xs, ctl, warp - NC, kComputeWarps - NC, lane, act_tag);
+                } else {
+                    const int tok = a.pro == PRO_EMB_RMS ? __ldcg(a.tokens + pos) : 0;
+                    const bool ok = step_activation(a, tok, xq, xs, ctl, tid, epoch, sc.t0 == 0, nw);
+                    if (bar_compute_or(!ok || *reinterpret_cast<volatile int *>(&ctl.abort))) break;
+                }
                 if (tid == 0) trace_mark(sa, i, 1);
                 if (a.dump_q && sc.t0 == 0) {  // diagnostics: the op's input and activation, one CTA
                     const float *src = a.pro == PRO_RMS_REDUCE ? a.x_out : a.x;
@@ -1011,7 +1072,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa
                         strace = sa.stage_trace + (((size_t)(i - sa.stage_op0) * kStageTraceCtas + blockIdx.x) *
                                                    kStageTraceStages) * 4;
                     gemv_consume(op, sc, gbase, S, NC, sa.slot, ring_s, smem_u32(xq), smem_u32(xs), ctl, warp, lane, best,
-                                 strace, epoch);
+                                 strace, epoch, act_tag);
                     if (a.epi == EPI_ARGMAX) {
                         #pragma unroll
                         for (int o = 16; o > 0; o >>= 1) {
