@@ -312,9 +312,16 @@ def test_client_cli_two_gpus(loaded, tmp_path):
     tok_path = str(tmp_path / "tokenizer.bin")
     synth.write_tokenizer(tok_path, cfg.vocab_size)
     exe = os.path.join(ROOT, "diolkos_b200", "bin", "client")
-    one = _run_cli(exe, d, tok_path, "abc de fgh", 24, str(tmp_path), ("-g", "1"))
-    two = _run_cli(exe, d, tok_path, "abc de fgh", 24, str(tmp_path), ("-g", "2"))
+    prompt = b"abc de fgh"
+    one = _run_cli(exe, d, tok_path, prompt.decode(), 24, str(tmp_path), ("-g", "1"))
+    two = _run_cli(exe, d, tok_path, prompt.decode(), 24, str(tmp_path), ("-g", "2"))
     assert b"(2 GPUs)" in two.stderr
-    t1 = one.stdout.rstrip(b"\n").rsplit(b"Loaded", 1)[-1].split(b"\n", 1)[-1]
-    t2 = two.stdout.rstrip(b"\n").rsplit(b"Loaded", 1)[-1].split(b"\n", 1)[-1]
-    assert len(t2) > 0 and t1[:8] == t2[:8], (t1[:80], t2[:80])
+
+    def generated(out: bytes) -> bytes:  # rank 0 echoes the prompt, then prints the pieces; other ranks
+        i = out.find(prompt)              # may print their loading lines anywhere around it
+        assert i >= 0, out[-300:]
+        return out[i + len(prompt):].split(b"\n", 1)[0]
+
+    g1, g2 = generated(one.stdout), generated(two.stdout)
+    first = g1.split(b" ", 1)[0]  # the first generated piece(s) before a space
+    assert len(g2) > 0 and len(first) > 0 and g2.startswith(first), (g1[:80], g2[:80])
