@@ -395,10 +395,40 @@ def gemv_alg_bytes(d: int, n: int) -> float:
     return d * n * 1.125 + n * 1.125 + d * 4
 
 
+def graph_time_us(enqueue, calls: int, reps: int = 3) -> float:
+    """Device time per call of `enqueue` (which issues `calls` library calls on torch's current stream),
+    captured once in a CUDA graph so that host launch overhead is not timed: one untimed replay keeps
+    the stream busy while the timed replay is enqueued behind an event; CUDA events, best of `reps`."""
+    import torch
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        enqueue()  # outside capture: any first-call setup of the library happens here
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        enqueue()
+    graph.replay()
+    torch.cuda.synchronize()
+    best = float("inf")
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        graph.replay()
+        e0.record()
+        graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1) * 1e3 / calls)
+    del graph
+    return best
+
+
 def gemv_bench(reps: int = 64, shapes=None):
-    """GEMV shapes through dk_matmul_q8_0_batch: `reps` GEMVs back to back, rotating over enough
-    packed copies of the matrix that the working set is over 3x the L2, timed with CUDA events on
-    the launching stream (best of 3 batches)."""
+    """GEMV shapes through dk_matmul_q8_0_batch: `reps` GEMVs in one call, rotating over enough
+    packed copies of the matrix that the working set is over 3x the L2; device time per GEMV
+    (graph_time_us: CUDA graph, CUDA events on the launching stream, best of 3)."""
     import torch
 
     from diolkos_b200 import ops
@@ -416,16 +446,7 @@ def gemv_bench(reps: int = 64, shapes=None):
         x = torch.randn(n, generator=g, device="cuda")
         batch = [ws[i % copies] for i in range(reps)]
         y = torch.empty((reps, d), device="cuda")
-        ops.matmul_batch(x, batch, n, d, y)
-        torch.cuda.synchronize()
-        best = float("inf")
-        for _ in range(3):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            ops.matmul_batch(x, batch, n, d, y)
-            e1.record()
-            torch.cuda.synchronize()
-            best = min(best, e0.elapsed_time(e1) * 1e3 / reps)
+        best = graph_time_us(lambda: ops.matmul_batch(x, batch, n, d, y), reps)
         alg = gemv_alg_bytes(d, n)
         out[f"{d}x{n}"] = {"us": round(best, 2), "GBps": round(alg / best / 1e3, 1)}
         del ws, batch, y
@@ -484,7 +505,8 @@ def prefill_bench(m, cfg, reps: int = 3):
 
 def gemm_bench(cfg, ntok: int = GEMM_TOKENS, reps: int = 8):
     """The prefill matmul (dk_matmul_q8_0_tokens) on one layer's shapes at ntok positions: reps
-    launches back to back rotating over packed copies (working set > 3x L2), CUDA events, best of 3."""
+    launches back to back rotating over packed copies (working set > 3x L2), behind one untimed launch
+    so that the first timed one does not wait for the host; CUDA events, best of 3."""
     import torch
 
     from diolkos_b200 import ops
@@ -510,6 +532,7 @@ def gemm_bench(cfg, ntok: int = GEMM_TOKENS, reps: int = 8):
         best = float("inf")
         for _ in range(3):
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ops.matmul_tokens(xq, xs, ws[copies - 1], n, d, out=y)  # the stream is busy when e0 is reached
             e0.record()
             for i in range(reps):
                 ops.matmul_tokens(xq, xs, ws[i % copies], n, d, out=y)
@@ -944,9 +967,10 @@ ATTN_POSITIONS = (200, 2047, 4000)  # a short context, the long-prompt workload'
 def attention_bench(reps: int = 32, kv: str = "f32"):
     """The decode attention kernel alone (dk_attention_decode: RoPE, KV-cache write, split-K softmax.V;
     the per-kernel decode path's attention, the same arithmetic as the persistent step's) at the 7B shape
-    (32 heads of 128, seq_len 4096) at a few positions.  `reps` calls back to back rotate over enough
-    layers' KV caches that the working set is over 3x the L2; CUDA events on the launching stream, best
-    of 3 batches.  GB/s = the KV bytes a call reads (2 * (pos+1) * kv_dim * element size) / time."""
+    (32 heads of 128, seq_len 4096) at a few positions.  At each position the calls rotate over enough
+    layers' KV caches that the rows they read are over 3x the L2 (at least `reps` calls); device time
+    per call (graph_time_us: CUDA graph, CUDA events, best of 3).  GB/s = the KV bytes a call reads
+    (2 * (pos+1) * kv_dim * element size) / time."""
     import torch
 
     from diolkos_b200 import ops, synth
@@ -954,8 +978,14 @@ def attention_bench(reps: int = 32, kv: str = "f32"):
     cfg = synth.LLAMA7B
     H, KVH, hs, seq = cfg.n_heads, cfg.n_kv_heads, cfg.dim // cfg.n_heads, cfg.seq_len
     esz = 4 if kv == "f32" else 2
-    layer_bytes = 2 * KVH * seq * hs * esz
-    copies = max(2, int(3 * 126e6 // layer_bytes) + 1)
+
+    def alg_bytes(pos):
+        return 2.0 * (pos + 1) * KVH * hs * esz
+
+    def n_copies(pos):
+        return max(2, int(3 * 126e6 // alg_bytes(pos)) + 1)
+
+    copies = max(n_copies(pos) for pos in ATTN_POSITIONS)
     g = torch.Generator(device="cuda").manual_seed(5)
     dt = torch.float32 if kv == "f32" else torch.bfloat16
     ks = [(torch.randn(KVH * seq * hs, generator=g, device="cuda") * 0.5).to(dt) for _ in range(copies)]
@@ -974,24 +1004,23 @@ def attention_bench(reps: int = 32, kv: str = "f32"):
     res = {}
     for pos in ATTN_POSITIONS:
         p = torch.tensor([pos], dtype=torch.int32, device="cuda")
-        for i in range(copies):  # warm-up: every cache once
-            ops.attention_decode(qkv, rope, ks[i], vs[i], p, H, KVH, hs, seq, work, out)
-        torch.cuda.synchronize()
-        best = float("inf")
-        for _ in range(3):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            for i in range(reps):
-                ops.attention_decode(qkv, rope, ks[i % copies], vs[i % copies], p, H, KVH, hs, seq, work, out)
-            e1.record()
-            torch.cuda.synchronize()
-            best = min(best, e0.elapsed_time(e1) * 1e3 / reps)
-        alg = 2.0 * (pos + 1) * KVH * hs * esz
+        c = n_copies(pos)
+        calls = max(reps, c)
+
+        def enqueue():
+            for i in range(calls):
+                ops.attention_decode(qkv, rope, ks[i % c], vs[i % c], p, H, KVH, hs, seq, work, out)
+
+        best = graph_time_us(enqueue, calls)
+        alg = alg_bytes(pos)
         res[str(pos)] = {"us": round(best, 2), "kv_mb": round(alg / 1e6, 2), "GBps": round(alg / best / 1e3, 1),
-                         "frac": round(alg / best / 1e3 / hbm, 4)}
+                         "frac": round(alg / best / 1e3 / hbm, 4), "calls": calls, "caches": c}
+    del ks, vs
+    torch.cuda.empty_cache()
     return {"kernel": "attention_kernel", "kv": kv, "positions": res, "peak": hbm, "peak_kind": kind,
             "what": f"dk_attention_decode at 32 heads x 128, seq_len {seq}, {kv} KV cache: KV bytes read per call / "
-                    f"time per call ({reps} calls back to back over {copies} layers' caches, best of 3)"}
+                    "device time per call (the calls of one position captured in a CUDA graph, rotating over "
+                    "enough layers' caches that the rows read exceed 3x the L2; best of 3)"}
 
 
 def run_attention(args):
