@@ -395,10 +395,11 @@ def gemv_alg_bytes(d: int, n: int) -> float:
     return d * n * 1.125 + n * 1.125 + d * 4
 
 
-def graph_time_us(enqueue, calls: int, reps: int = 3) -> float:
+def graph_time_us(enqueue, calls: int, reps: int = 10) -> float:
     """Device time per call of `enqueue` (which issues `calls` library calls on torch's current stream),
-    captured once in a CUDA graph so that host launch overhead is not timed: one untimed replay keeps
-    the stream busy while the timed replay is enqueued behind an event; CUDA events, best of `reps`."""
+    captured once in a CUDA graph so that host launch overhead is not timed: `reps` replays back to back,
+    each between its own pair of CUDA events, behind one untimed replay that keeps the stream busy while
+    the host enqueues the rest; the median replay over `calls`."""
     import torch
 
     side = torch.cuda.Stream()
@@ -412,23 +413,22 @@ def graph_time_us(enqueue, calls: int, reps: int = 3) -> float:
         enqueue()
     graph.replay()
     torch.cuda.synchronize()
-    best = float("inf")
-    for _ in range(reps):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        graph.replay()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    graph.replay()
+    for e0, e1 in ev:
         e0.record()
         graph.replay()
         e1.record()
-        torch.cuda.synchronize()
-        best = min(best, e0.elapsed_time(e1) * 1e3 / calls)
+    torch.cuda.synchronize()
     del graph
-    return best
+    times = sorted(e0.elapsed_time(e1) * 1e3 / calls for e0, e1 in ev)
+    return times[len(times) // 2]
 
 
 def gemv_bench(reps: int = 64, shapes=None):
     """GEMV shapes through dk_matmul_q8_0_batch: `reps` GEMVs in one call, rotating over enough
     packed copies of the matrix that the working set is over 3x the L2; device time per GEMV
-    (graph_time_us: CUDA graph, CUDA events on the launching stream, best of 3)."""
+    (graph_time_us: CUDA graph, CUDA events on the launching stream, median of 10 replays)."""
     import torch
 
     from diolkos_b200 import ops
@@ -969,7 +969,7 @@ def attention_bench(reps: int = 32, kv: str = "f32"):
     the per-kernel decode path's attention, the same arithmetic as the persistent step's) at the 7B shape
     (32 heads of 128, seq_len 4096) at a few positions.  At each position the calls rotate over enough
     layers' KV caches that the rows they read are over 3x the L2 (at least `reps` calls); device time
-    per call (graph_time_us: CUDA graph, CUDA events, best of 3).  GB/s = the KV bytes a call reads
+    per call (graph_time_us: CUDA graph, CUDA events, median of 10 replays).  GB/s = the KV bytes a call reads
     (2 * (pos+1) * kv_dim * element size) / time."""
     import torch
 
@@ -1020,7 +1020,7 @@ def attention_bench(reps: int = 32, kv: str = "f32"):
     return {"kernel": "attention_kernel", "kv": kv, "positions": res, "peak": hbm, "peak_kind": kind,
             "what": f"dk_attention_decode at 32 heads x 128, seq_len {seq}, {kv} KV cache: KV bytes read per call / "
                     "device time per call (the calls of one position captured in a CUDA graph, rotating over "
-                    "enough layers' caches that the rows read exceed 3x the L2; best of 3)"}
+                    "enough layers' caches that the rows read exceed 3x the L2; median of 10 replays)"}
 
 
 def run_attention(args):
