@@ -306,10 +306,12 @@ __host__ __device__ inline int step_min_chunk(int kv_mul) {
     const int c = 320 / (kv_mul > 0 ? kv_mul : 1);
     return c > 80 ? c : 80;
 }
-// Contexts up to this many positions take the narrow attention form (step_attn_plan), longer ones the wide.
-// Short contexts have too few positions to fill CTA-wide items; at 2048 positions and beyond the wide form
-// measured 13 % more 7B tokens/s.  Switching at 256, 384 or 640 positions measured the same on the 7B and
-// 70B decode workloads.
+// Contexts up to this many positions take the narrow attention form (step_attn_plan), longer ones the wide
+// (unless the wide items would leave more than a tenth of the CTAs idle; the engine then keeps the narrow
+// form throughout).  Short contexts have too few positions to fill CTA-wide items.  Measured at 2048+
+// positions on B200: the 70B shape (144 wide items on 148 SMs) 63.8 tok/s wide against 60.6 narrow; the 7B
+// shape on 2 GPUs (144 items) 514 against 508; the 7B shape on one GPU (128 items) 388 against 396.
+// Switching at 256, 384 or 640 positions measured the same on the 7B and 70B decode workloads.
 constexpr int kStepWideFrom = 384;
 enum StepOpKind : int { OP_GEMV = 0, OP_ATTN = 1 };
 struct StepOp {

@@ -277,21 +277,26 @@ dk_model *dk_model_create(const int *cfg, int kv_type, int device, int tp_rank, 
         m->use_step = !(mode && strcmp(mode, "kernels") == 0);
     }
     // The persistent step's attention.  Narrow form (contexts up to step_wide_from positions): one
-    // (KV head, split) item per 2-warp group of the grid, splits of at least 16 positions.  Wide form: at most
+    // (KV head, split) item per 2-warp group of the grid (at most one wave: the split count is rounded
+    // down), splits of at least 16 positions.  Wide form: at most
     // one wave of CTA-wide items, splits of at least step_min_chunk positions.  DIOLKOS_ATTN_WIDE_FROM moves
     // the switch (0: the wide form throughout; a value >= the context: the narrow form throughout);
     // DIOLKOS_ATTN_WIDE_CHUNK sets the wide form's shortest split (positions).
     {
         const int kv_mul = m->l_heads / m->l_kv_heads;
         m->step_narrow_splits =
-            std::max(1, std::min((step_attn_item_slots(m->num_sms, kAttnNarrowWarps) + m->l_kv_heads - 1) / m->l_kv_heads,
-                                 (S + 15) / 16));
+            std::max(1, std::min(step_attn_item_slots(m->num_sms, kAttnNarrowWarps) / m->l_kv_heads, (S + 15) / 16));
         m->step_wide_chunk = step_min_chunk(kv_mul);
         if (const char *e = getenv("DIOLKOS_ATTN_WIDE_CHUNK")) m->step_wide_chunk = std::max(16, atoi(e));
         m->step_wide_splits =
             std::max(1, std::min(step_attn_item_slots(m->num_sms, kAttnWideWarps) / m->l_kv_heads,
                                  (S + m->step_wide_chunk - 1) / m->step_wide_chunk));
         m->step_wide_from = kStepWideFrom;
+        // The wide form runs one wave of CTA-wide items.  Where they would leave more than a tenth of the
+        // CTAs idle (the 7B shape on one GPU: 4 splits x 32 KV heads = 128 of 148), the narrow form's
+        // full wave is the faster one at every context length.
+        if ((long long)m->step_wide_splits * m->l_kv_heads * 10 < (long long)m->num_sms * 9)
+            m->step_wide_from = 0x7fffffff;
         if (const char *e = getenv("DIOLKOS_ATTN_WIDE_FROM")) m->step_wide_from = std::max(0, atoi(e));
         m->step_splits = std::max(m->step_narrow_splits, m->step_wide_splits);
     }

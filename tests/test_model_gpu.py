@@ -296,9 +296,10 @@ def _logits_bits(a):
         ("gqa", True, 300, 0),       # wide items over 8 query heads, 80-position splits
         ("gqa", False, 300, 100),    # the form switches inside the first chunk
         ("wide", True, 40, None),    # dim 4096: the one-round-trip rmsnorm prologue
-        ("capped", False, 540, None),  # 32 KV heads: the narrow split count is capped (24 on 148 SMs) from
-                                       # position 384, where the wide form takes over
-        ("capped", True, 540, 1000),   # the narrow form throughout
+        ("capped", False, 540, 384),   # 32 KV heads: the narrow split count is capped (23 on 148 SMs) from
+                                       # position 369; the wide form takes over at 384
+        ("capped", True, 540, None),   # the default: on 148 SMs the narrow form throughout (4 x 32 wide
+                                       # items would leave 20 CTAs idle)
         ("swiglu", True, 100, None),   # hidden 4096: w1|w3 (8192 rows) on the pipelined tensor-core matmul
     ],
 )
