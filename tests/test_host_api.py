@@ -312,3 +312,54 @@ def test_loader_size_mismatch_and_bad_config_exit(tmp_path):
         f.write('{"hidden_size": 64, "num_hidden_layers": ')
     r = _run_loader(d, str(tmp_path))
     assert r.returncode == 1 and "config.json" in r.stderr, r.stderr
+
+
+# ---- corrupt inputs: the loader stops with a message (exit status 1), no GPU needed -------------
+def _cached_small_model(tmp_path, port, name="small-model"):
+    """The small model with every Q8_0 tensor in the cache (the loader then needs no GPU)."""
+    d = _write_small_model(str(tmp_path), name=name)
+    cache = os.path.join(str(tmp_path), "cache", name)
+    for n, v in _expected_tensors(port).items():
+        if v[0] == "q8":
+            synth.write_q8_cache(cache, n, v[1], v[2])
+    return d, cache
+
+
+def test_loader_truncated_cache_file_exits(tmp_path, port):
+    d, cache = _cached_small_model(tmp_path, port)
+    victim = os.path.join(cache, "model.layers.1.mlp.down_proj.weight-Q8_0.tensor")
+    size = os.path.getsize(victim)
+    with open(victim, "r+b") as f:
+        f.truncate(size - 4)  # the last scale cut short
+    r = _run_loader(d, str(tmp_path))
+    assert r.returncode == 1 and "is truncated" in r.stderr and "down_proj" in r.stderr, r.stderr
+
+
+def test_loader_truncated_safetensors_exits(tmp_path, port):
+    """A header length past the end of the file: the file is skipped with a message, and the loader
+    then stops because the directory holds no usable safetensors file."""
+    d, _ = _cached_small_model(tmp_path, port)
+    path = os.path.join(d, "model.safetensors")
+    with open(path, "rb") as f:
+        hlen = struct.unpack("<Q", f.read(8))[0]
+    with open(path, "r+b") as f:
+        f.truncate(8 + hlen // 2)
+    r = _run_loader(d, str(tmp_path))
+    assert r.returncode == 1, r.stderr
+    assert "not a safetensors file" in r.stderr and "No safetensors files found" in r.stderr, r.stderr
+
+
+def test_loader_short_data_section_exits(tmp_path, port):
+    """The header is intact but the tensor data stops early: a tensor that is not cached (a norm,
+    widened from bf16 on the host) whose bytes lie past the end of the file."""
+    d, _ = _cached_small_model(tmp_path, port)
+    path = os.path.join(d, "model.safetensors")
+    with open(path, "rb") as f:
+        hlen = struct.unpack("<Q", f.read(8))[0]
+        header = json.loads(f.read(hlen))
+    ends = {k: v["data_offsets"][1] for k, v in header.items() if k != "__metadata__"}
+    norm = max((k for k in ends if k.endswith("layernorm.weight")), key=lambda k: ends[k])
+    with open(path, "r+b") as f:
+        f.truncate(8 + hlen + ends[norm] - 2)
+    r = _run_loader(d, str(tmp_path))
+    assert r.returncode == 1 and "Data size mismatch" in r.stderr, r.stderr

@@ -4,7 +4,8 @@
 * Column-split partial GEMVs (wo, w2) summed over the ranks equal the full GEMV: each rank runs the
   oracle's matmul_Q8_0 on its column slice -- the slices start at multiples of 32, so the activation's
   Q8_0 groups are the reference's -- and the gloo all-reduce adds them.
-* The exchange-area handshake returns every rank's handle in rank order.
+* The exchange-area handshake returns every rank's handle in rank order, and a rank that never
+  reaches it makes the others' handshake end with an error within the process group's timeout.
 """
 import os
 import socket
@@ -103,3 +104,48 @@ def test_column_split_partials_sum_to_full_gemv(world):
     for rank, res in results.items():
         assert res["wo"] < 1e-5 and res["w2"] < 1e-5, (rank, res)
         assert res["handles"] == [bytes([r]) * 64 for r in range(world)]
+
+
+def _handshake_worker(rank, world, port, out_q, absent):
+    """Rank `absent` leaves before the exchange-area handshake; the others must get an error from it
+    within the process group's timeout, not wait for good."""
+    import datetime
+    import time
+
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    if rank == absent:
+        out_q.put((rank, "left"))
+        time.sleep(15)  # alive but never joins: the others' collective runs out of time
+        return
+    t0 = time.monotonic()
+    try:
+        tp.exchange_handles(bytes([rank]) * 64)
+        out_q.put((rank, ("completed", time.monotonic() - t0, "")))
+    except Exception as e:  # the backend's timeout or connection error
+        out_q.put((rank, ("error", time.monotonic() - t0, type(e).__name__)))
+
+
+def test_handshake_fails_when_a_rank_never_arrives():
+    world, absent = 3, 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_handshake_worker, args=(r, world, port, q, absent)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        results = dict(q.get(timeout=120) for _ in range(world))
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    assert results[absent] == "left"
+    for r in range(world):
+        if r != absent:
+            what, seconds, _ = results[r]
+            assert what == "error" and seconds < 60, results
