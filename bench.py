@@ -409,7 +409,9 @@ def graph_time_us(enqueue, calls: int, reps: int = 10) -> float:
     torch.cuda.current_stream().wait_stream(side)
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
+    # thread_local: CUDA calls of other threads (a process group's watchdog under torchrun) stay legal
+    # while this thread captures
+    with torch.cuda.graph(graph, capture_error_mode="thread_local"):
         enqueue()
     graph.replay()
     torch.cuda.synchronize()
