@@ -334,6 +334,9 @@ struct StepArgs {
     // many as the ring has free slots), so that the weight stream does not queue the step's own
     // dependent stores and loads behind it at the memory controllers
     int inflight = 0;
+    // the same while the compute warps wait for an op's input, build its activation or run attention
+    // (StepCtl::crit; 0: inflight throughout)
+    int inflight_crit = 0;
     size_t slot = 0;              // bytes of one ring slot (>= the largest stage)
     size_t xoff = 0;              // activation / attention scratch
     size_t ctl_off = 0;           // control block

@@ -755,10 +755,16 @@ static int build_step(dk_model *m) {
     // A consumer waits on a slot's full barrier by parity, which is sound once the slot's previous stage
     // has landed: the token chain guarantees that for S >= 2 NC + 2 (units of two stages, step.cu).
     sa.NC = std::max(1, std::min(std::min(nc, (S - 2) / 2), kStepMaxConsumers));
-    // copies in flight per CTA: 4 measured best on B200 (7B decode 505 tok/s with as many as the ring
-    // allows, 515 with 4, 512 with 6, 470 with 2)
-    sa.inflight = std::min(S, 4);
+    // Copies in flight per CTA.  While the compute warps wait for an op's input, build its activation or
+    // run attention, the stream's queued copies delay their stores and L2 loads, so the producers keep
+    // fewer in flight then (2) than while the stages are consumed (8).  Measured on B200, 7B decode:
+    // one cap throughout 505 / 515 / 512 / 470 tok/s (as many as the ring allows / 4 / 6 / 2); 2 in the
+    // waits with 4 / 6 / 8 otherwise 541 / 544 / 544, with 4 otherwise and 8 in the waits 523.
+    sa.inflight = std::min(S, 8);
     if (const char *e = getenv("DIOLKOS_STEP_INFLIGHT")) sa.inflight = std::max(0, std::min(S, atoi(e) & ~(kStepProducers - 1)));
+    sa.inflight_crit = std::min(S, 2);
+    if (const char *e = getenv("DIOLKOS_STEP_INFLIGHT_CRIT"))
+        sa.inflight_crit = std::max(0, std::min(S, atoi(e) & ~(kStepProducers - 1)));
     sa.xoff = (size_t)S * sa.slot;
     sa.ctl_off = sa.xoff + ((act + 127) & ~(size_t)127);
     sa.smem = sa.ctl_off + step_ctl_bytes();

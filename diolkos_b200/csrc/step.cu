@@ -68,6 +68,7 @@ struct StepCtl {  // shared-memory control block
     unsigned long long tok[kStepMaxConsumers][32];
     int abort;      // any wait gave up: every warp leaves
     int last;       // this CTA took the classifier's last ticket
+    int crit;       // the compute warps wait for an op's input, build its activation or run attention
     int grp_last[kAttnGroups];
     // per 512-column block of a PRO_F32 op's activation: the op index + 1 once its values and scales are in
     // shared memory (step_activation_blocks)
@@ -916,6 +917,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa
         for (int i = 0; i < kStepMaxConsumers * 32; ++i) (&ctl.tok[0][0])[i] = 0xFFFFFFFF00000000ull;  // tag -1
         ctl.abort = 0;
         ctl.last = 0;
+        ctl.crit = 1;
         for (int b = 0; b < kStepActBlocks; ++b) ctl.act_ready[b] = 0;
         mbar_fence_init();
     }
@@ -966,9 +968,12 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa
                     ok = false;
                     break;
                 }
-                // at most sa.inflight copies in flight: stage G - inflight (this producer's own, issued by
-                // it and not yet refilled, so its phase is the slot's latest) must have landed
-                const int K = sa.inflight;
+                // at most K copies in flight (inflight_crit while the compute warps are in a wait, an
+                // activation build or attention; inflight while they consume): stage G - K (this
+                // producer's own, issued by it and not yet refilled, so its phase is the slot's latest)
+                // must have landed
+                const int K = (sa.inflight_crit > 0 && *reinterpret_cast<volatile int *>(&ctl.crit)) ? sa.inflight_crit
+                                                                                                : sa.inflight;
                 if (K > 0 && G >= K &&
                     !mbar_wait_abortable(&ctl.full[(G - K) % S], (uint32_t)(((G - K) / S) & 1), op.g.err, &ctl.abort, false)) {
                     ctl.abort = 1;
@@ -1016,6 +1021,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa
         unsigned long long next_word = 0;
         if (op_copier && i + 1 < sa.nops)
             next_word = __ldg(reinterpret_cast<const unsigned long long *>(sa.ops + i + 1) + (tid - 32));
+        if (tid == 0) *reinterpret_cast<volatile int *>(&ctl.crit) = 1;
         if (op.kind == OP_GEMV) {
             const GemvArgs &a = op.g;
             const Sched sc = op_sched(op);
@@ -1065,6 +1071,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa
                         reinterpret_cast<uint4 *>(a.dump_q)[j] = reinterpret_cast<const uint4 *>(xq)[j];
                     for (int j = tid; j < (a.n >> 5); j += kComputeThreads) a.dump_s[j] = xs[j];
                 }
+                if (tid == 0) *reinterpret_cast<volatile int *>(&ctl.crit) = 0;
                 if (warp < NC) {
                     unsigned long long *strace = nullptr;
                     if (sa.stage_trace && i >= sa.stage_op0 && i < sa.stage_op0 + kStageTraceOps &&
@@ -1085,6 +1092,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs sa
                 // every row stored, the activation no longer read
                 if (bar_compute_or(*reinterpret_cast<volatile int *>(&ctl.abort))) break;
                 if (tid == 0) {
+                    *reinterpret_cast<volatile int *>(&ctl.crit) = 1;
                     trace_mark(sa, i, 2);
                     const int lo = sc.t0 * op.T, hi = min(a.d, (sc.t0 + sc.nt) * op.T);
                     const unsigned long long rows = hi > lo ? (unsigned long long)(hi - lo) : 0ull;
@@ -1641,7 +1649,8 @@ int step_threads() { return kStepThreads; }
 
 cudaError_t launch_step(const StepArgs &sa, int grid, cudaStream_t st) {
     if (sa.S < 1 || sa.S > kStepMaxSlots || sa.S < kStepProducers || sa.S % kStepProducers || sa.NC < 1 ||
-        sa.NC > kStepMaxConsumers || sa.NC > kComputeWarps || sa.S < 2 * sa.NC + 2 || sa.inflight < 0 || sa.inflight % kStepProducers || sa.inflight > sa.S || sa.smem > 227 * 1024 ||
+        sa.NC > kStepMaxConsumers || sa.NC > kComputeWarps || sa.S < 2 * sa.NC + 2 || sa.inflight < 0 || sa.inflight % kStepProducers || sa.inflight > sa.S ||
+        sa.inflight_crit < 0 || sa.inflight_crit % kStepProducers || sa.inflight_crit > sa.S || sa.smem > 227 * 1024 ||
         sa.ctl_off + step_ctl_bytes() > sa.smem || sa.xoff < (size_t)sa.S * sa.slot || sa.ctl_off < sa.xoff)
         return cudaErrorInvalidValue;
     static int attr_bytes[64] = {0};
