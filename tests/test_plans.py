@@ -33,14 +33,39 @@ def test_split_plan_capped_example():
     assert split_plan(384, 24, 16) == (24, 16)
 
 
-def step_plan_args(n_kv_heads, kv_mul, seq_len, num_sms=148, wide_from=384):
+NEVER = 0x7FFFFFFF
+
+
+def step_plan_args(n_kv_heads, kv_mul, seq_len, num_sms=148, wide_from=None):
     """The persistent step's plan as dk_model_create sets it (engine.cu): narrow items of 2 warps, 5 per
-    SM, splits of at least 16 positions; wide items of 10 warps, one per SM, splits of at least
-    step_min_chunk(kv_mul) = max(80, 320 / kv_mul) positions."""
-    narrow = max(1, min(-(-5 * num_sms // n_kv_heads), -(-seq_len // 16)))
+    SM, splits of at least 16 positions, at most one wave of items; wide items of 10 warps, one per SM,
+    splits of at least step_min_chunk(kv_mul) = max(80, 320 / kv_mul) positions, from 384 positions on
+    unless the wide items would leave more than a tenth of the SMs idle (wide_from given: the
+    DIOLKOS_ATTN_WIDE_FROM override)."""
+    narrow = max(1, min(5 * num_sms // n_kv_heads, -(-seq_len // 16)))
     wide_chunk = max(80, 320 // kv_mul)
     wide = max(1, min(num_sms // n_kv_heads, -(-seq_len // wide_chunk)))
+    if wide_from is None:
+        wide_from = NEVER if wide * n_kv_heads * 10 < num_sms * 9 else 384
     return np.array([narrow, 16, wide, wide_chunk, wide_from], np.int32)
+
+
+@pytest.mark.parametrize("n_kv_heads,num_sms", [(32, 148), (16, 148), (8, 148), (4, 148), (6, 148), (32, 132)])
+def test_narrow_items_fit_one_wave(n_kv_heads, num_sms):
+    """Every narrow item of a position has a 2-warp group of its own (5 per SM): no second wave."""
+    plan = step_plan_args(n_kv_heads, 1, 4096, num_sms=num_sms, wide_from=NEVER)
+    for T in range(1, 4097):
+        warps, ns, ch = step_plan(T, plan)
+        assert warps == 2 and ns * n_kv_heads <= 5 * num_sms, (T, ns)
+
+
+def test_default_form_choice():
+    """The 7B shape on one GPU (32 KV heads: 4 wide splits = 128 items on 148 SMs) keeps the narrow form;
+    with 16 KV heads per rank (2 GPUs, 144 items) or the 70B shape's 8 (144 items) the wide form starts at
+    384 positions."""
+    assert step_plan_args(32, 1, 4096)[4] == NEVER
+    assert step_plan_args(16, 1, 4096)[4] == 384
+    assert step_plan_args(8, 8, 4096)[4] == 384
 
 
 def step_plan(T, plan):
@@ -126,8 +151,9 @@ def test_prefill_groups_cover_each_item_once_with_the_decode_plan(n_heads, n_kv_
 
 
 def test_wide_prefill_groups_hold_eight_positions():
-    """Past the split cap the wide chunk changes only every 8 x nsplit positions: 7B groups are full."""
-    plan = step_plan_args(32, 1, 4096)
+    """Past the split cap the wide chunk changes only every 8 x nsplit positions: 7B groups are full
+    (the 7B shape with the wide form forced from 384 positions)."""
+    plan = step_plan_args(32, 1, 4096, wide_from=384)
     g, _, _ = prefill_plan(32, 32, plan, 1792, 256)
     assert (g[:, 5] == 10).all()
     assert np.mean(g[:, 1]) > 7.0, g[:, 1]
