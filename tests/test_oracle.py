@@ -82,6 +82,17 @@ def test_port_vs_reference_live_quant_and_gemv(port, ref):
                                   ref.matmul(xv, wq, ws, n, d).view(np.uint32))
 
 
+@pytest.mark.parametrize("n,d", [(8192, 64), (28672, 32), (11008, 48), (32, 33)])
+def test_port_vs_reference_live_gemv_widths(port, ref, n, d):
+    """The restatement's GEMV against the compiled reference at the 70B shape's input widths (dim 8192,
+    hidden 28672), the 7B hidden width and the narrowest input: bit for bit."""
+    rng = np.random.default_rng(n + d)
+    wq, ws = port.quant_bf16(synth.f32_to_bf16_bits(rng.standard_normal(n * d, dtype=np.float32) * np.float32(0.02)))
+    xv = rng.standard_normal(n, dtype=np.float32)
+    np.testing.assert_array_equal(port.matmul(xv, wq, ws, n, d).view(np.uint32),
+                                  ref.matmul(xv, wq, ws, n, d).view(np.uint32))
+
+
 def test_port_group_dots_exact(port):
     rng = np.random.default_rng(5)
     n, d = 256, 7
