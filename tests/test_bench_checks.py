@@ -1,6 +1,6 @@
-"""bench.py's token checks on CPU (no GPU): the free-running comparison and the teacher-forced agreement
-with a reference stream, on a fake model, at 1 and 2 gloo ranks (tensor parallel: each rank sees only
-its classifier rows)."""
+"""bench.py's checks on CPU (no GPU): the free-running comparison and the teacher-forced agreement with a
+reference stream, on a fake model, at 1 and 2 gloo ranks (tensor parallel: each rank sees only its
+classifier rows); and the byte accounting behind the roofline fractions."""
 import os
 import socket
 import sys
@@ -102,3 +102,28 @@ def test_forced_check_two_ranks_gathers_the_global_choice():
         assert d["gpu"] == (d["ref"] + 1) % V and 0 < d["gpu_gap"] < 1e-5
         assert "ref_top2_gap" not in d
     assert sorted(d["index"] for d in r0["disagreements"]) == [p - (P - 1) for p in ties]
+
+
+def test_roofline_byte_accounting():
+    """The algorithmic bytes behind the roofline fractions: the 7B-shape weights once per token at 1.125 B
+    per value (6.607 G matmul values -> 7.433 GB, plus activations, norms and one embedding row), the KV
+    rows 2 * L * (pos + 1) * kv_dim * element size, and the GEMV shapes' d*n*1.125 + n*1.125 + d*4."""
+    from diolkos_b200 import synth
+
+    cfg = synth.LLAMA7B
+    mat_values = cfg.n_layers * (4 * cfg.dim * cfg.dim + 3 * cfg.hidden_dim * cfg.dim) + cfg.vocab_size * cfg.dim
+    assert mat_values == 6_607_077_376
+    wb = bench.weight_bytes_per_token(cfg)
+    gemvs = [(cfg.dim, cfg.dim), (cfg.kv_dim, cfg.dim), (cfg.kv_dim, cfg.dim), (cfg.dim, cfg.dim),
+             (cfg.hidden_dim, cfg.dim), (cfg.dim, cfg.hidden_dim), (cfg.hidden_dim, cfg.dim)]
+    want = (cfg.n_layers * (sum(bench.gemv_alg_bytes(d, n) for d, n in gemvs) + 2 * cfg.dim * 4)
+            + bench.gemv_alg_bytes(cfg.vocab_size, cfg.dim) + cfg.dim * 1.125 + cfg.dim * 4)
+    assert wb == want
+    assert 0 < wb - mat_values * 1.125 < 10e6, wb  # activations, outputs, norms, one embedding row
+    assert bench.kv_bytes_read(cfg, 0, 1, 4) == 2 * 32 * 4096 * 4
+    # the decode workload: 256 tokens at positions 31 .. 286, fp32 KV
+    kv = bench.kv_bytes_read(cfg, 31, 287, 4)
+    assert kv == 2.0 * 32 * 4096 * 4 * sum(p + 1 for p in range(31, 287))
+    assert abs((wb + kv / 256) / 1e9 - 7.608) < 0.001  # the step roofline's bytes per token
+    assert bench.gemv_alg_bytes(4096, 4096) == 4096 * 4096 * 1.125 + 4096 * 1.125 + 4096 * 4
+    assert abs(bench.gemv_alg_bytes(32000, 4096) / 1e6 - 147.59) < 0.01
