@@ -77,6 +77,41 @@ def build(verbose: bool = True) -> str:
     return LIB
 
 
+SAN_FLAGS = ["-fsanitize=address,undefined", "-fno-sanitize-recover=undefined", "-fno-omit-frame-pointer", "-g",
+             "-O1"]
+SAN_LIB = os.path.join(BUILD, "libdiolkos_san.so")
+
+
+def build_sanitized() -> str:
+    """The same library with the host C code (the reference API: loader, JSON reader, tokenizer, sampler,
+    tensor helpers) built under AddressSanitizer and UndefinedBehaviorSanitizer, the CUDA objects
+    unchanged: _build/libdiolkos_san.so, for the CPU tests of the host code.  A process that loads it
+    preloads the gcc sanitizer runtimes (sanitizer_runtimes())."""
+    build(verbose=False)
+    headers = glob.glob(os.path.join(CSRC, "host", "*.h")) + glob.glob(os.path.join(INCLUDE, "*.h"))
+    objs = [os.path.join(BUILD, os.path.basename(src) + ".o") for src in sorted(glob.glob(os.path.join(CSRC, "*.cu")))]
+    for src in sorted(glob.glob(os.path.join(CSRC, "host", "*.c"))):
+        obj = os.path.join(BUILD, "san_" + os.path.basename(src) + ".o")
+        if _newer(obj, [src] + headers):
+            _run([HOST_CC, *CC_FLAGS, *SAN_FLAGS, "-c", src, "-o", obj])
+        objs.append(obj)
+    if _newer(SAN_LIB, objs):
+        _run([NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-Xlinker", "-Bsymbolic", "-o", SAN_LIB,
+              *objs, "-lasan", "-lubsan", "-lcudart_static", "-lrt", "-lpthread", "-ldl", "-lm"])
+    return SAN_LIB
+
+
+def sanitizer_runtimes() -> list:
+    """The gcc ASan and UBSan runtimes to preload (ASan first), or [] when this gcc has none."""
+    out = []
+    for name in ("libasan.so", "libubsan.so"):
+        path = subprocess.run([HOST_CC, f"-print-file-name={name}"], capture_output=True, text=True).stdout.strip()
+        if not os.path.isabs(path) or not os.path.exists(path):
+            return []
+        out.append(path)
+    return out
+
+
 if __name__ == "__main__":
     build()
     sys.exit(0)
