@@ -363,3 +363,17 @@ def test_loader_short_data_section_exits(tmp_path, port):
         f.truncate(8 + hlen + ends[norm] - 2)
     r = _run_loader(d, str(tmp_path))
     assert r.returncode == 1 and "Data size mismatch" in r.stderr, r.stderr
+
+
+def test_tokenizer_truncated_file_exits(tmp_path):
+    """tokenizer.bin cut inside a piece, or inside the header: exit status 1 and a message naming the file."""
+    pieces, scores, _ = make_vocab(3)
+    path = str(tmp_path / "tokenizer.bin")
+    write_tokenizer_bin(path, pieces, scores)
+    code = f"from diolkos_b200 import refapi; refapi.load_tokenizer({path!r})"
+    for cut, what in ((os.path.getsize(path) - 3, "short piece"), (10, "short header")):
+        with open(path, "r+b") as f:
+            f.truncate(cut)
+        r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                           env={**os.environ, "PYTHONPATH": ROOT})
+        assert r.returncode == 1 and what in r.stderr and "tokenizer.bin" in r.stderr, r.stderr
